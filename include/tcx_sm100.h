@@ -1,0 +1,223 @@
+/*
+ * tcx_sm100.h — C ABI of the B200 (sm_100a) CUDA backend for tensor.cx.
+ *
+ * This is the drop-in boundary under tensor.cx's backend execution ABI
+ * (`Backend::execute(const BackendExecution&)`, cpp/tensorcx/core/backend.h:67-73).
+ * Each entry point replaces one `launch_*` function of the reference CUDA backend
+ * (cpp/tensorcx/backends/cuda/cuda_kernels.h, cuda_math.h) or one composite that the
+ * reference runs as several backend calls (cpp/tensorcx/core/inference.cpp). The
+ * citation above each declaration names the interface it replaces.
+ *
+ * Conventions
+ *  - Plain device pointers and sizes; no C++ or torch types. Element counts and
+ *    extents are int64_t, like tensorcx::Dim (cpp/tensorcx/core/shape.h:8).
+ *  - Every call is stream-ordered on `stream` (a cudaStream_t; NULL is the legacy
+ *    default stream) and returns once the work is enqueued. The reference launches
+ *    finish with cudaDeviceSynchronize (cuda_profiling.h:66-77); the host backend
+ *    keeps that synchronous contract by synchronizing its own stream instead.
+ *  - Calls never allocate device memory. Where a kernel needs scratch, the caller
+ *    passes `workspace` of at least the size the matching *_workspace_bytes query
+ *    returns (the host backend takes it from its stream-ordered pool).
+ *  - Metadata arrays (shapes, strides) are HOST pointers read during the call; they
+ *    travel to the GPU as kernel parameters. The reference instead allocated and
+ *    copied them with cudaMalloc + cudaMemcpy on every call (cuda_backend.cpp:590-599).
+ *  - Return value: TCX_OK, or a status mirroring tensorcx::StatusCode
+ *    (cpp/tensorcx/core/status.h:8-13). TCX_INVALID_ARGUMENT is raised before any
+ *    work is enqueued, so outputs are untouched, as the reference requires of failed
+ *    execution (cuda_backend.cpp:612-613). The message of the last failure on the
+ *    calling thread is returned by tcx_sm100_last_error().
+ */
+#ifndef TCX_SM100_H_
+#define TCX_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tcx_stream_t;
+
+/* tensorcx::StatusCode */
+enum { TCX_OK = 0, TCX_INVALID_ARGUMENT = 1, TCX_UNAVAILABLE = 2, TCX_INTERNAL = 3 };
+
+/* tensorcx::DType (cpp/tensorcx/core/dtype.h:8-12); bool is not on this path. */
+enum { TCX_FLOAT32 = 0, TCX_INT32 = 1 };
+
+/* tensorcx::OpKind values (cpp/tensorcx/core/operation.h:12-63) for the ops on this
+ * path, so a host backend can pass OpDesc::kind through unchanged. */
+enum {
+  TCX_OP_ADD = 1, TCX_OP_MULTIPLY = 2, TCX_OP_MATMUL = 3, TCX_OP_SUM = 4, TCX_OP_MAX = 5,
+  TCX_OP_MEAN = 6, TCX_OP_EXP = 7, TCX_OP_GELU = 8, TCX_OP_SILU = 9, TCX_OP_SOFTMAX = 10,
+  TCX_OP_RMSNORM = 11, TCX_OP_LAYERNORM = 12, TCX_OP_SUBTRACT = 13, TCX_OP_DIVIDE = 14,
+  TCX_OP_MIN = 41, TCX_OP_ARGMAX = 42, TCX_OP_CLIP = 43
+};
+
+/* Activation applied after the bias add in fused chains. ReLU is tensor.cx's
+ * clip(x, lower=0) (python/tensorcx/tensor.py:858-876; cpu_math.cpp:42-47). */
+enum { TCX_ACT_NONE = 0, TCX_ACT_SILU = 1, TCX_ACT_RELU = 2 };
+
+/* Matmul kernel selection: automatic, the SIMT FFMA kernel, or the tcgen05 3xTF32
+ * tensor-core kernel (the latter two for tests and measurement). */
+enum { TCX_MATMUL_AUTO = 0, TCX_MATMUL_FFMA = 1, TCX_MATMUL_TENSOR = 2 };
+
+/* ------------------------------------------------------------------ runtime --- */
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+const char* tcx_sm100_last_error(void);
+
+/* ABI revision of this library (bumped on any signature change). */
+int tcx_sm100_abi_version(void);
+
+/* TCX_OK when `device` is an sm_100 GPU this library's kernels can run on.
+ * Replaces the availability probe of cuda::available() (cuda_backend.cpp:166-169). */
+int tcx_sm100_device_supported(int device);
+
+/* Reads and clears the device-side error word of `device`: kernels with bounded
+ * waits record a timeout there instead of hanging (0 = no error). */
+int tcx_sm100_device_error(int device, int* code);
+
+/* --------------------------------------------------------------- reductions --- */
+
+/* One-axis reduction or normalization over a contiguous tensor viewed as
+ * [outer, reduce, inner] (axis extent `reduce`, element stride `inner`).
+ * Replaces launch_axis (cuda_kernels.h:34-36; primitives.cu:290-306).
+ *   op  TCX_OP_SUM / TCX_OP_MAX (float32, int32), TCX_OP_MEAN (float32): output
+ *       [outer, inner]. For float32 sum/mean the order of additions is the CPU
+ *       reference's left-to-right order, bit for bit, whenever reduce <= 65536 or
+ *       there are at least 4096 independent rows; otherwise (few very long rows) a
+ *       fixed-shape pairwise tree (relative error <= 1e-5 against the CPU result).
+ *       Max is exact in every case (first NaN, first of equal values).
+ *   op  TCX_OP_SOFTMAX / TCX_OP_RMSNORM / TCX_OP_LAYERNORM (float32): output has the
+ *       input's shape; `epsilon` is the already-validated float32 epsilon
+ *       (cpu_backend.cpp:30-42 checks it on the host side). */
+int tcx_sm100_axis(tcx_stream_t stream, int op, int dtype, const void* input, void* output,
+                   int64_t outer, int64_t reduce, int64_t inner, float epsilon,
+                   void* workspace, size_t workspace_bytes);
+
+/* Scratch for tcx_sm100_axis (non-zero only for sum/max/mean over few long rows,
+ * which run the parallel tree; with less workspace those run the ordered kernel). */
+size_t tcx_sm100_axis_workspace_bytes(int op, int64_t outer, int64_t reduce, int64_t inner);
+
+/* Affine normalization fused into one pass: normalize, multiply by weight[reduce]
+ * (if non-NULL), then add bias[reduce] (if non-NULL), each a separately rounded
+ * float32 operation. Replaces the three-call kAffineRmsNorm / kAffineLayerNorm
+ * composite (core/inference.cpp:103-122). op is TCX_OP_RMSNORM or TCX_OP_LAYERNORM. */
+int tcx_sm100_affine_norm(tcx_stream_t stream, int op, const float* input, float* output,
+                          int64_t outer, int64_t reduce, int64_t inner, float epsilon,
+                          const float* weight, const float* bias);
+
+/* Multi-axis reduction (sum / max / mean) described by the reduction plan's index
+ * metadata: `rank` (extent, element stride) pairs, kept axes first, reduced axes last
+ * (core/shape.h:59-70). groups = number of outputs, reduction_size = elements per
+ * output. Replaces launch_reduce_axes (cuda_kernels.h:37-40). A reduction over every
+ * axis (groups == 1) runs the bandwidth-bound two-stage kernel: exact for int32 and
+ * max, fixed-order pairwise tree for float32 sum/mean (relative error <= 1e-5).
+ * Other selections keep the CPU order exactly. `workspace` >= the bytes returned by
+ * tcx_sm100_reduce_workspace_bytes(groups * reduction_size). */
+int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* input,
+                          void* output, int64_t groups, int64_t reduction_size,
+                          const int64_t* index_metadata, int32_t outer_rank, int32_t rank,
+                          void* workspace, size_t workspace_bytes);
+
+/* min (op TCX_OP_MIN, output dtype = input dtype) or argmax (TCX_OP_ARGMAX, int32
+ * output) over the plan's metadata, as make_math_plan builds it (core/math.cpp:39-56).
+ * Replaces math_kernel codes 3 and 4 (math.cu:56-60). The first NaN wins; otherwise
+ * the first extremum (lowest index) wins, with -0 == +0, as cpu_math.cpp:48-54. */
+int tcx_sm100_min_argmax(tcx_stream_t stream, int op, int dtype, const void* input,
+                         void* output, int64_t groups, int64_t reduction_size,
+                         const int64_t* index_metadata, int32_t rank, void* workspace,
+                         size_t workspace_bytes);
+
+/* Scratch needed by the full-tensor reduction kernels for `count` input elements. */
+size_t tcx_sm100_reduce_workspace_bytes(int64_t count);
+
+/* Full-tensor reduction of a contiguous buffer of `count` elements:
+ * op in {SUM, MAX, MEAN, MIN, ARGMAX}. Equivalent to tcx_sm100_reduce_axes /
+ * tcx_sm100_min_argmax over every axis; `output` holds one element (int32 for
+ * ARGMAX). */
+int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* input,
+                         int64_t count, void* output, void* workspace,
+                         size_t workspace_bytes);
+
+/* Per-shard partial of a full-tensor reduction, for combining across GPUs. The
+ * record is produced on the device; shards are combined in rank order by
+ * tcx_sm100_reduce_combine, so the result does not depend on collective ordering.
+ * `index_base` is the global index of this shard's first element. */
+typedef struct tcx_partial {
+  uint32_t key;    /* order key of the best element (min/max/argmax) */
+  uint32_t bits;   /* raw bits of the best element, or of the float32/int32 sum */
+  int64_t index;   /* global index of the best element (lowest among ties) */
+} tcx_partial;
+
+int tcx_sm100_reduce_partial(tcx_stream_t stream, int op, int dtype, const void* input,
+                             int64_t count, int64_t index_base, tcx_partial* partial,
+                             void* workspace, size_t workspace_bytes);
+
+/* Combines `nparts` device records in order into the final one-element output of
+ * a reduction over `total_count` elements (the mean divides by it once). */
+int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype,
+                             const tcx_partial* partials, int32_t nparts,
+                             int64_t total_count, void* output);
+
+/* -------------------------------------------------------------- elementwise --- */
+
+/* exp / gelu (tanh form) / silu, float32. Replaces launch_unary (cuda_kernels.h:32-33;
+ * primitives.cu:14-27). Arithmetic follows cpu_backend.cpp:990-1010 operation by
+ * operation (no contraction into FMA). */
+int tcx_sm100_unary(tcx_stream_t stream, int op, const float* input, float* output,
+                    int64_t count);
+
+/* add / subtract / multiply / divide with NumPy broadcasting. `metadata` holds the
+ * output shape, then the lhs element strides, then the rhs element strides (zero for
+ * broadcast axes), 3*rank values (core/shape.h:14-22). rank 0 or identical shapes may
+ * pass metadata = NULL, rank = 0. int32 wraps through uint32; divide is float32 only.
+ * Replaces launch_binary / launch_broadcast_binary (cuda_kernels.h:15-22). */
+int tcx_sm100_binary(tcx_stream_t stream, int op, int dtype, const void* lhs,
+                     const void* rhs, void* output, int64_t count, const int64_t* metadata,
+                     int32_t rank);
+
+/* clip(x, lower, upper) with broadcast bounds: metadata = output shape then the
+ * element strides of x, lower and upper (4*rank values), as make_math_plan builds it
+ * (core/math.cpp:33-38). Replaces math_kernel code 5 (math.cu:51-55). */
+int tcx_sm100_clip(tcx_stream_t stream, int dtype, const void* input, const void* lower,
+                   const void* upper, void* output, int64_t count, const int64_t* metadata,
+                   int32_t rank);
+
+/* Fused elementwise chain out[r, c] = act(x[r, c] + bias[c]) over a [rows, cols]
+ * buffer (bias may be NULL). Replaces the broadcast add + activation pair of calls
+ * (cuda_backend.cpp:557-578 then 604-605) with one read and one write. */
+int tcx_sm100_bias_act(tcx_stream_t stream, const float* input, const float* bias,
+                       float* output, int64_t rows, int64_t cols, int act);
+
+/* ------------------------------------------------------------------- matmul --- */
+
+/* Scratch for tcx_sm100_matmul: the tf32 hi/lo split of both operands (K-major).
+ * lhs_batches / rhs_batches are the operands' own batch counts (numel / (m*k),
+ * numel / (k*n)). Zero when the FFMA kernel will be used. */
+size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k,
+                                        int64_t lhs_batches, int64_t rhs_batches, int path);
+
+/* Batched float32 matmul with NumPy broadcasting, as planned by make_matmul_plan
+ * (core/shape.cpp:49-76): output [batches, m, n] contiguous; batch b reads
+ * lhs + offset(b, lhs_batch_strides) and rhs + offset(b, rhs_batch_strides), offsets
+ * as matmul_batch_offset (shape.cpp:78-85) over `batch_shape` (batch_rank entries;
+ * batches = its product). Optional fused epilogue: out = act(acc + bias[n]) when
+ * bias != NULL or act != TCX_ACT_NONE. Replaces launch_matmul (cuda_kernels.h:43-45)
+ * and, with an epilogue, the matmul -> add -> activation call chain.
+ * Large products run on tcgen05 tensor cores with a 3xTF32 split
+ * (hi*hi + hi*lo + lo*hi, float32 accumulation): relative Frobenius error
+ * <= 1e-4 * sqrt(k / 1024) against the CPU reference. Inputs holding inf or NaN are
+ * computed by the FFMA kernel instead (IEEE semantics), decided on the device. */
+int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output,
+                     int64_t m, int64_t n, int64_t k, int64_t batches,
+                     const int64_t* batch_shape, const int64_t* lhs_batch_strides,
+                     const int64_t* rhs_batch_strides, int32_t batch_rank,
+                     const float* bias, int act, int path, void* workspace,
+                     size_t workspace_bytes);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+#endif  /* TCX_SM100_H_ */

@@ -1,0 +1,79 @@
+// Shared helpers of the sm_100a backend: error reporting across the C ABI, launch
+// geometry and the float32/int32 order keys used by the reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "tcx_sm100.h"
+
+namespace tcx {
+
+// Thread-local last-error message behind tcx_sm100_last_error().
+void set_error(const std::string& message);
+void clear_error();
+
+inline int invalid(const char* message) {
+  set_error(message);
+  return TCX_INVALID_ARGUMENT;
+}
+
+// Maps the launch status of the kernels just enqueued to a C-ABI status.
+inline int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return TCX_OK;
+  set_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return TCX_INTERNAL;
+}
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Device-side error word (see tcx_sm100_device_error); bounded waits set it.
+__device__ __forceinline__ void record_device_error(int* word, int code) {
+  if (word) atomicCAS(word, 0, code);
+}
+int* device_error_word();
+
+constexpr int kMaxRank = 16;
+
+// Small by-value metadata block passed as a kernel parameter (no per-call
+// device allocation, unlike the reference's cudaMalloc + cudaMemcpy uploads).
+struct Meta {
+  int32_t rank;
+  int64_t v[4 * kMaxRank];
+};
+
+// ------------------------------------------------------------ order keys
+// 32-bit keys whose unsigned order is the reduction's preference order:
+// a larger key wins; equal keys fall back to the lower index. NaN maps to the
+// largest key (the first NaN wins), both zeros share one key (they compare equal),
+// as cpu_math.cpp:14-21 and std::max in cpu_backend.cpp:1190-1196.
+__device__ __forceinline__ uint32_t ordered_f32(uint32_t b) {
+  if ((b & 0x7fffffffu) == 0) b = 0;  // -0 == +0
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ bool is_nan_bits(uint32_t b) {
+  return (b & 0x7fffffffu) > 0x7f800000u;
+}
+// key for "largest wins" (max, argmax)
+__device__ __forceinline__ uint32_t key_max(uint32_t b, bool fp) {
+  if (!fp) return b ^ 0x80000000u;
+  return is_nan_bits(b) ? 0xffffffffu : ordered_f32(b);
+}
+// key for "smallest wins" (min); NaN still wins.
+__device__ __forceinline__ uint32_t key_min(uint32_t b, bool fp) {
+  if (!fp) return ~(b ^ 0x80000000u);
+  return is_nan_bits(b) ? 0xffffffffu : ~ordered_f32(b);
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// One-axis sum/max/mean over [outer, reduce, inner] (reduce.cu).
+int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* output,
+                int64_t outer, int64_t reduce, int64_t inner, void* ws, size_t ws_bytes);
+size_t axis_reduce_workspace(int64_t outer, int64_t reduce, int64_t inner);
+
+}  // namespace tcx

@@ -1,0 +1,687 @@
+// float32 matmul / batched matmul for sm_100a.
+//
+// Tensor-core path (3xTF32 on tcgen05):
+//   1. Split pre-pass (HBM-bound): every operand element x becomes
+//      hi = rna_tf32(x), lo = rna_tf32(x - hi), written K-major into the caller's
+//      workspace ([plane][rows][Kp], planes hi/lo per operand batch, K padded with
+//      zeros to a multiple of 32). B is transposed on the way, so both operands are
+//      K-major. The pass also flags any inf/NaN input.
+//   2. GEMM: a persistent, warp-specialized kernel, one CTA per SM:
+//        warp 0      TMA producer: 4 tiles per k-block (A hi/lo 128x32, B hi/lo 256x32,
+//                    128B-swizzled) into a 2-stage shared-memory ring (mbarriers);
+//        warp 1      MMA issuer: per 8-wide k step, three tcgen05.mma.kind::tf32
+//                    (lo*hi, hi*lo, hi*hi) into one float32 TMEM accumulator;
+//                    tcgen05.commit releases the stage / publishes the accumulator;
+//        warps 2-5   epilogue: tcgen05.ld 32x32b from TMEM, bias + activation,
+//                    float32 stores. Two TMEM accumulators (2 x 256 columns) let the
+//                    epilogue of tile t overlap the main loop of tile t+1.
+//      No TMA multicast anywhere (this code also runs in multi-GPU jobs).
+//   3. If the pre-pass saw inf/NaN, the GEMM exits at once and the FFMA kernel
+//      (launched behind it, idle otherwise) computes the product with IEEE
+//      semantics: 3xTF32 cross terms would turn inf*0 into NaN.
+// FFMA path: a 64x64x16 register-blocked SIMT kernel for skinny or small products.
+//
+// Every spin-wait is bounded (a few seconds of %globaltimer); on expiry the kernel
+// records the site in the device error word, stops issuing, drains what it issued
+// and frees its TMEM before returning.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace tcx {
+namespace {
+
+constexpr int kMaxBatchRank = 8;
+
+struct BatchMap {
+  int32_t rank;
+  int64_t shape[kMaxBatchRank];
+  int64_t lhs[kMaxBatchRank];  // element strides (plan strides)
+  int64_t rhs[kMaxBatchRank];
+};
+
+__device__ __forceinline__ int64_t batch_off(int64_t b, const int64_t* shape, const int64_t* st, int rank) {
+  int64_t off = 0;
+  for (int a = rank - 1; a >= 0; --a) {
+    off += (b % shape[a]) * st[a];
+    b /= shape[a];
+  }
+  return off;
+}
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legal wait
+
+// Bounded wait: false when the CTA is aborting or the limit passed (then it records
+// `site` in the device error word and raises the CTA abort flag).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             int* err, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - start > kWaitLimitNs) {
+      *abort_flag = 1;
+      record_device_error(err, site);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte-swizzled operand tile: rows of 128 bytes, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);        // start address
+  d |= static_cast<uint64_t>(1) << 16;                       // leading byte offset (unused)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;               // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;                       // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+#define TCX_LD32(r, taddr)                                                                          \
+  asm volatile(                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"               \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),               \
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),               \
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                \
+      : "r"(taddr))
+
+__device__ __forceinline__ float silu_e(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+__device__ __forceinline__ float relu_e(float v) {
+  // clip(v, +0, +inf) of cpu_math.cpp:42-47: NaN kept, v <= 0 (incl. -0) -> +0
+  return (v != v) ? v : (v > 0.0f ? v : 0.0f);
+}
+__device__ __forceinline__ float epilogue_op(float v, const float* bias, int64_t col, int act) {
+  if (bias) v = __fadd_rn(v, __ldg(bias + col));
+  if (act == TCX_ACT_SILU) v = silu_e(v);
+  else if (act == TCX_ACT_RELU) v = relu_e(v);
+  return v;
+}
+
+// ------------------------------------------------------------------- pre-pass
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// A [nb][M][K] -> W [2*nb][M][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
+__global__ void split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows,
+                           int64_t k, int64_t kp, int* __restrict__ nonfinite) {
+  const int64_t total = nb * rows * kp;
+  const int64_t plane = rows * kp;
+  bool bad = false;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = i / plane, rem = i % plane, r = rem / kp, c = rem % kp;
+    const float x = c < k ? __ldg(a + (b * rows + r) * k + c) : 0.0f;
+    bad |= !isfinite(x);
+    const float hi = tf32_rna(x);
+    const float lo = tf32_rna(__fsub_rn(x, hi));
+    w[(2 * b) * plane + rem] = hi;
+    w[(2 * b + 1) * plane + rem] = lo;
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
+}
+
+// B [nb][K][N] -> W [2*nb][N][Kp] (transposed, K-major), 32x32 tiles through smem.
+__global__ void split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k,
+                           int64_t n, int64_t kp, int* __restrict__ nonfinite) {
+  __shared__ float tile[32][33];
+  const int64_t plane = n * kp;
+  const int64_t tiles_n = (n + 31) / 32, tiles_k = kp / 32;
+  bool bad = false;
+  for (int64_t t = blockIdx.x; t < nb * tiles_n * tiles_k; t += gridDim.x) {
+    const int64_t b = t / (tiles_n * tiles_k), rem = t % (tiles_n * tiles_k);
+    const int64_t n0 = (rem % tiles_n) * 32, k0 = (rem / tiles_n) * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+      const int64_t kk = k0 + j, nn = n0 + threadIdx.x;
+      float x = 0.0f;
+      if (kk < k && nn < n) x = __ldg(bsrc + (b * k + kk) * n + nn);
+      bad |= !isfinite(x);
+      tile[j][threadIdx.x] = x;
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+      const int64_t nn = n0 + j, kk = k0 + threadIdx.x;
+      if (nn < n) {
+        const float x = tile[threadIdx.x][j];
+        const float hi = tf32_rna(x);
+        const float lo = tf32_rna(__fsub_rn(x, hi));
+        w[(2 * b) * plane + nn * kp + kk] = hi;
+        w[(2 * b + 1) * plane + nn * kp + kk] = lo;
+      }
+    }
+    __syncthreads();
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
+}
+
+// ------------------------------------------------------------ tcgen05 GEMM
+constexpr int kBM = 128, kBN = 256, kBK = 32, kStages = 2;
+constexpr int kTileA = kBM * kBK * 4;                   // 16 KB
+constexpr int kTileB = kBN * kBK * 4;                   // 32 KB
+constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;    // 96 KB
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 2 * kBN;                      // two accumulators
+constexpr int kGemmSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kGroupM = 8;
+
+// Instruction descriptor: kind::tf32, D f32, A/B tf32, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                            (static_cast<uint32_t>(kBM >> 4) << 24);
+
+struct GemmArgs {
+  float* c;
+  const float* bias;
+  const int* nonfinite;
+  int* err;
+  int64_t m, n, k_elems;  // output extents
+  int64_t lhs_mk, rhs_kn; // elements per operand batch (m*k, k*n)
+  int32_t num_kb, tiles_m, tiles_n, act, vec_store;
+  int64_t batches;
+  BatchMap bm;
+};
+
+__device__ __forceinline__ void tile_coords(int64_t t, const GemmArgs& g, int64_t& batch, int& mt, int& nt) {
+  const int64_t per_batch = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
+  batch = t / per_batch;
+  const int64_t r = t % per_batch;
+  const int64_t group_span = static_cast<int64_t>(kGroupM) * g.tiles_n;
+  const int64_t group = r / group_span;
+  const int first_m = static_cast<int>(group * kGroupM);
+  const int gsize = min(kGroupM, g.tiles_m - first_m);
+  const int64_t in_group = r % group_span;
+  mt = first_m + static_cast<int>(in_group % gsize);
+  nt = static_cast<int>(in_group / gsize);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const GemmArgs g) {
+  if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = bars;                  // [kStages]
+  uint64_t* empty = bars + kStages;       // [kStages]
+  uint64_t* acc_full = bars + 2 * kStages;      // [2]
+  uint64_t* acc_empty = bars + 2 * kStages + 2; // [2]
+  uint64_t* drain = bars + 2 * kStages + 4;     // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 4); }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t total_tiles = g.batches * g.tiles_m * g.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- TMA producer
+      int64_t kb_global = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int64_t batch; int mt, nt;
+        tile_coords(t, g, batch, mt, nt);
+        const int64_t pa = batch_off(batch, g.bm.shape, g.bm.lhs, g.bm.rank) / (g.lhs_mk > 0 ? g.lhs_mk : 1);
+        const int64_t pb = batch_off(batch, g.bm.shape, g.bm.rhs, g.bm.rank) / (g.rhs_kn > 0 ? g.rhs_kn : 1);
+        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+          const int s = static_cast<int>(kb_global % kStages);
+          const uint32_t phase = static_cast<uint32_t>((kb_global / kStages) & 1);
+          if (!wait_bounded(smem_u32(&empty[s]), phase ^ 1u, abort_flag, g.err, 0x101)) { ok = false; break; }
+          uint8_t* st = smem + s * kStageBytes;
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, kStageBytes);
+          const int kc = kb * kBK;
+          tma_load_3d(smem_u32(st), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa));
+          tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa + 1));
+          tma_load_3d(smem_u32(st + 2 * kTileA), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb));
+          tma_load_3d(smem_u32(st + 2 * kTileA + kTileB), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb + 1));
+        }
+      }
+      // Drain: every stage this thread filled must have landed before the CTA exits.
+      if (!ok) {
+        for (int s = 0; s < kStages; ++s) {
+          const int64_t fills = kb_global > s ? (kb_global - s + kStages - 1) / kStages : 0;
+          if (fills == 0) continue;
+          const uint32_t parity = static_cast<uint32_t>((fills - 1) & 1);
+          const uint64_t start = globaltimer();
+          while (!mbar_try_wait(smem_u32(&full[s]), parity))
+            if (globaltimer() - start > kWaitLimitNs) { record_device_error(g.err, 0x1ff); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      int64_t kb_global = 0;
+      int64_t local = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = static_cast<int>(local & 1);
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_flag, g.err, 0x102)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+          const int s = static_cast<int>(kb_global % kStages);
+          const uint32_t phase = static_cast<uint32_t>((kb_global / kStages) & 1);
+          if (!wait_bounded(smem_u32(&full[s]), phase, abort_flag, g.err, 0x103)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + s * kStageBytes);
+          const uint32_t a_lo = a_hi + kTileA;
+          const uint32_t b_hi = a_hi + 2 * kTileA;
+          const uint32_t b_lo = b_hi + kTileB;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            mma_tf32(d_tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(b_hi + off), kIdesc, first);
+            mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_lo + off), kIdesc, 1u);
+            mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_hi + off), kIdesc, 1u);
+          }
+          mma_commit(smem_u32(&empty[s]));  // stage free once these MMAs have read it
+        }
+        mma_commit(smem_u32(&acc_full[acc]));  // accumulator ready (or drained on abort)
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int64_t local = 0;
+    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      const int acc = static_cast<int>(local & 1);
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!wait_bounded(smem_u32(&acc_full[acc]), acc_phase, abort_flag, g.err, 0x104)) break;
+      tc_fence_after();
+      int64_t batch; int mt, nt;
+      tile_coords(t, g, batch, mt, nt);
+      const int64_t row = static_cast<int64_t>(mt) * kBM + q * 32 + lane;
+      const int64_t col0 = static_cast<int64_t>(nt) * kBN;
+      float* crow = g.c + (batch * g.m + row) * g.n;
+      const bool row_ok = row < g.m;
+      const bool vec = g.vec_store != 0;
+#pragma unroll 1
+      for (int cc = 0; cc < kBN; cc += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN + cc);
+        TCX_LD32(r, taddr);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (cc + 32 >= kBN) {
+          // all TMEM reads of this accumulator are done: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+        }
+        if (row_ok && !*abort_flag) {
+          const int64_t c = col0 + cc;
+          if (vec && c + 32 <= g.n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v;
+              v.x = epilogue_op(__uint_as_float(r[j + 0]), g.bias, c + j + 0, g.act);
+              v.y = epilogue_op(__uint_as_float(r[j + 1]), g.bias, c + j + 1, g.act);
+              v.z = epilogue_op(__uint_as_float(r[j + 2]), g.bias, c + j + 2, g.act);
+              v.w = epilogue_op(__uint_as_float(r[j + 3]), g.bias, c + j + 3, g.act);
+              *reinterpret_cast<float4*>(crow + c + j) = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), g.bias, c + j, g.act);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) {
+      // every MMA this thread issued must complete before TMEM is released
+      mma_commit(smem_u32(drain));
+      const uint64_t start = globaltimer();
+      while (!mbar_try_wait(smem_u32(drain), 0))
+        if (globaltimer() - start > kWaitLimitNs) { record_device_error(g.err, 0x1fe); break; }
+    }
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// --------------------------------------------------------------- FFMA GEMM
+constexpr int kFM = 64, kFN = 64, kFK = 16;
+
+// mode 0: always compute; mode 1: only when *nonfinite is set (fallback behind the
+// tensor-core kernel).
+__global__ void __launch_bounds__(256)
+gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ c,
+                 int64_t m, int64_t n, int64_t k, int64_t batches, BatchMap bm,
+                 const float* __restrict__ bias, int act, const int* __restrict__ nonfinite, int mode) {
+  if (mode == 1 && !*nonfinite) return;
+  __shared__ float as[kFK][kFM + 4];
+  __shared__ float bs[kFK][kFN + 4];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int64_t tiles_m = (m + kFM - 1) / kFM, tiles_n = (n + kFN - 1) / kFN;
+  const int64_t total = batches * tiles_m * tiles_n;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t batch = t / (tiles_m * tiles_n), r = t % (tiles_m * tiles_n);
+    const int64_t m0 = (r / tiles_n) * kFM, n0 = (r % tiles_n) * kFN;
+    const float* ab = a + batch_off(batch, bm.shape, bm.lhs, bm.rank);
+    const float* bb = b + batch_off(batch, bm.shape, bm.rhs, bm.rank);
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int64_t k0 = 0; k0 < k; k0 += kFK) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int e = threadIdx.x + i * 256;
+        const int rr = e / kFK, cc = e % kFK;
+        const int64_t gm = m0 + rr, gk = k0 + cc;
+        as[cc][rr] = (gm < m && gk < k) ? __ldg(ab + gm * k + gk) : 0.0f;
+        const int br = e / kFN, bc = e % kFN;
+        const int64_t bk = k0 + br, bn = n0 + bc;
+        bs[br][bc] = (bk < k && bn < n) ? __ldg(bb + bk * n + bn) : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < kFK; ++kk) {
+        float av[4], bv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) av[i] = as[kk][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bv[j] = bs[kk][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t gm = m0 + ty * 4 + i;
+      if (gm >= m) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t gn = n0 + tx * 4 + j;
+        if (gn < n) c[(batch * m + gm) * n + gn] = epilogue_op(acc[i][j], bias, gn, act);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map over [planes][rows][kp] float32, box {32, box_rows, 1}, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kp), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kp * 4), static_cast<cuuint64_t>(rows * kp * 4)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows), 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct Layout {
+  int64_t kp;
+  size_t off_flag, off_a, off_b, total;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+Layout tensor_layout(int64_t m, int64_t n, int64_t k, int64_t nba, int64_t nbb) {
+  Layout l;
+  l.kp = (k + kBK - 1) / kBK * kBK;
+  l.off_flag = 0;
+  l.off_a = 1024;
+  l.off_b = align_up(l.off_a + static_cast<size_t>(2 * nba * m * l.kp) * 4, 1024);
+  l.total = align_up(l.off_b + static_cast<size_t>(2 * nbb * n * l.kp) * 4, 1024);
+  return l;
+}
+
+bool use_tensor(int64_t m, int64_t n, int64_t k, int path) {
+  if (path == TCX_MATMUL_FFMA) return false;
+  if (m == 0 || n == 0 || k == 0) return false;
+  if (path == TCX_MATMUL_TENSOR) return true;
+  return m >= 128 && n >= 128 && k >= 128 && static_cast<double>(m) * n >= 4.0 * kBM * kBN;
+}
+
+int collapse_batches(int64_t batches, const int64_t* shape, const int64_t* ls, const int64_t* rs, int rank,
+                     BatchMap& bm) {
+  bm.rank = 0;
+  for (int a = 0; a < rank; ++a) {
+    if (shape[a] == 1) continue;
+    if (bm.rank > 0) {
+      const int p = bm.rank - 1;
+      if (bm.lhs[p] == ls[a] * shape[a] && bm.rhs[p] == rs[a] * shape[a]) {
+        bm.shape[p] *= shape[a];
+        bm.lhs[p] = ls[a];
+        bm.rhs[p] = rs[a];
+        continue;
+      }
+    }
+    if (bm.rank == kMaxBatchRank) return invalid("matmul batch rank exceeds 8 after collapsing");
+    bm.shape[bm.rank] = shape[a];
+    bm.lhs[bm.rank] = ls[a];
+    bm.rhs[bm.rank] = rs[a];
+    ++bm.rank;
+  }
+  (void)batches;
+  return TCX_OK;
+}
+
+}  // namespace
+}  // namespace tcx
+
+using namespace tcx;
+
+namespace {
+// Number of distinct operand batches = (largest offset / batch size) + 1.
+int64_t distinct_batches(const BatchMap& bm, bool lhs, int64_t per) {
+  if (per == 0) return 1;
+  int64_t max_off = 0;
+  for (int a = 0; a < bm.rank; ++a) max_off += (bm.shape[a] - 1) * (lhs ? bm.lhs[a] : bm.rhs[a]);
+  return max_off / per + 1;
+}
+}  // namespace
+
+extern "C" {
+
+size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t lhs_batches,
+                                        int64_t rhs_batches, int path) {
+  if (!use_tensor(m, n, k, path)) return 0;
+  return tensor_layout(m, n, k, std::max<int64_t>(lhs_batches, 1), std::max<int64_t>(rhs_batches, 1)).total;
+}
+
+int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
+                     int64_t n, int64_t k, int64_t batches, const int64_t* batch_shape,
+                     const int64_t* lhs_batch_strides, const int64_t* rhs_batch_strides, int32_t batch_rank,
+                     const float* bias, int act, int path, void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (m < 0 || n < 0 || k < 0 || batches < 0 || batch_rank < 0) return invalid("negative matmul extents");
+  if (act != TCX_ACT_NONE && act != TCX_ACT_SILU && act != TCX_ACT_RELU) return invalid("unsupported activation");
+  if (path != TCX_MATMUL_AUTO && path != TCX_MATMUL_FFMA && path != TCX_MATMUL_TENSOR)
+    return invalid("unknown matmul path");
+  if (batch_rank > 0 && (!batch_shape || !lhs_batch_strides || !rhs_batch_strides))
+    return invalid("missing matmul batch metadata");
+  BatchMap bm;
+  if (int st = collapse_batches(batches, batch_shape, lhs_batch_strides, rhs_batch_strides, batch_rank, bm)) return st;
+  if (m == 0 || n == 0 || batches == 0) return TCX_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = sm_count();
+
+  if (!use_tensor(m, n, k, path)) {
+    const int64_t tiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
+    gemm_ffma_kernel<<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
+    return launch_status("ffma matmul");
+  }
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return invalid("matmul extent too large for the tensor path");
+  const int64_t nba = distinct_batches(bm, true, m * k), nbb = distinct_batches(bm, false, k * n);
+  const Layout lay = tensor_layout(m, n, k, nba, nbb);
+  if (!workspace || workspace_bytes < lay.total) return invalid("matmul workspace is missing or too small");
+  if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("matmul workspace must be 1024-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* flag = reinterpret_cast<int*>(ws + lay.off_flag);
+  float* wa = reinterpret_cast<float*>(ws + lay.off_a);
+  float* wb = reinterpret_cast<float*>(ws + lay.off_b);
+  if (2 * std::max(nba, nbb) > INT32_MAX) return invalid("too many operand batches for the tensor path");
+
+  if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
+  {
+    const int64_t total = nba * m * lay.kp;
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 16LL * sms));
+    split_rows<<<grid, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
+    const int64_t tiles = nbb * ceil_div(n, 32) * (lay.kp / 32);
+    const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 32LL * sms));
+    split_cols<<<grid_b, dim3(32, 8), 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
+  }
+  if (int st = launch_status("matmul split pre-pass")) return st;
+
+  alignas(64) CUtensorMap map_a, map_b;
+  if (!make_map(&map_a, wa, 2 * nba, m, lay.kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, lay.kp, kBN))
+    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
+        cudaSuccess)
+      return launch_status("gemm smem attribute");
+    attr_done[dev] = true;
+  }
+  GemmArgs g;
+  g.c = output;
+  g.bias = bias;
+  g.nonfinite = flag;
+  g.err = device_error_word();
+  g.m = m; g.n = n; g.k_elems = k;
+  g.lhs_mk = m * k; g.rhs_kn = k * n;
+  g.num_kb = static_cast<int32_t>(lay.kp / kBK);
+  g.tiles_m = static_cast<int32_t>(ceil_div(m, kBM));
+  g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
+  g.act = act;
+  g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
+  g.batches = batches;
+  g.bm = bm;
+  const int64_t tiles = batches * g.tiles_m * g.tiles_n;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
+  if (int st = launch_status("tcgen05 matmul")) return st;
+  // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
+  const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
+  const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
+  gemm_ffma_kernel<<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+  return launch_status("matmul fallback");
+}
+
+}  // extern "C"

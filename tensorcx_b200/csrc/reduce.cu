@@ -1,0 +1,684 @@
+// Reductions of the tensor.cx hot path on sm_100a.
+//
+//  * Full-tensor and long-row reductions (sum / mean / max / min / argmax, float32
+//    and int32): a two-stage, bandwidth-bound design. Stage 1 runs a fixed grid of
+//    4 CTAs per SM; each CTA streams one contiguous chunk with 128-bit
+//    non-allocating loads, 4 loads in flight per thread, and reduces it to one
+//    16-byte record (warp shuffles, then shared memory). Stage 2 folds the records
+//    of each row in a fixed tree order. Shape-fixed order => results are
+//    deterministic run to run. Index-carrying keys keep the reference semantics:
+//    the first NaN wins, both zeros compare equal, ties go to the lowest index
+//    (cpu_math.cpp:48-54; cpu_backend.cpp:1184-1196).
+//  * Ordered row reductions (float32 sum / mean where the CPU order must be kept
+//    bit for bit, tests/python/test_cuda_primitives.py:114-125 of the reference):
+//    32 rows per CTA staged through shared memory in coalesced 32x128 tiles, one
+//    thread per row adding left to right.
+//  * Strided axes and general multi-axis selections: one thread per output, walking
+//    the reduction in the reference's index order (exact).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace tcx {
+namespace {
+
+constexpr int kStage1Threads = 512;
+constexpr int kUnroll = 4;
+
+enum Kind { kSumF = 0, kSumI = 1, kBestMax = 2, kBestMin = 3 };
+
+template <typename T>
+__device__ __forceinline__ T max_identity() {
+  if constexpr (std::is_same<T, float>::value) return -INFINITY;
+  else return INT32_MIN;
+}
+
+__device__ __forceinline__ float4 ldg_stream(const float4* p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+struct Acc {
+  float f[4 * kUnroll];
+  uint32_t u[4 * kUnroll];
+  uint32_t key;
+  int64_t idx;
+};
+
+template <int K, bool FP>
+__device__ __forceinline__ void take(Acc& a, int slot, uint32_t bits, int64_t index) {
+  if (K == kSumF) {
+    a.f[slot] = __fadd_rn(a.f[slot], __uint_as_float(bits));
+  } else if (K == kSumI) {
+    a.u[slot] += bits;
+  } else {
+    const uint32_t k = (K == kBestMax) ? key_max(bits, FP) : key_min(bits, FP);
+    if (k > a.key) {  // strict: earlier indices win ties within a thread
+      a.key = k;
+      a.idx = index;
+    }
+  }
+}
+
+__device__ __forceinline__ bool better(uint32_t ka, int64_t ia, uint32_t kb, int64_t ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+// Folds (sum or key/index) across the CTA in a fixed order; result in thread 0.
+template <int K>
+__device__ __forceinline__ void block_fold(uint32_t& bits, uint32_t& key, int64_t& idx) {
+  __shared__ uint32_t s_bits[32], s_key[32];
+  __shared__ int64_t s_idx[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const uint32_t ob = __shfl_xor_sync(0xffffffffu, bits, off);
+    const uint32_t ok = __shfl_xor_sync(0xffffffffu, key, off);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, off);
+    if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(ob)));
+    else if (K == kSumI) bits += ob;
+    else if (better(ok, oi, key, idx)) { key = ok; idx = oi; }
+  }
+  if (lane == 0) { s_bits[warp] = bits; s_key[warp] = key; s_idx[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < nwarps) { bits = s_bits[lane]; key = s_key[lane]; idx = s_idx[lane]; }
+    else { bits = K == kSumF ? __float_as_uint(0.0f) : 0u; key = 0; idx = INT64_MAX; }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint32_t ob = __shfl_xor_sync(0xffffffffu, bits, off);
+      const uint32_t ok = __shfl_xor_sync(0xffffffffu, key, off);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, off);
+      if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(ob)));
+      else if (K == kSumI) bits += ob;
+      else if (better(ok, oi, key, idx)) { key = ok; idx = oi; }
+    }
+  }
+  __syncthreads();
+}
+
+// Stage 1: CTA (blockIdx.x, row) reduces elements [blockIdx.x*chunk, +chunk) of a
+// row of `n` elements into part[row * gridDim.x + blockIdx.x]. `chunk` is a multiple
+// of 4 so every chunk starts 16-byte aligned when VEC (row start aligned).
+template <int K, bool FP, bool VEC>
+__global__ void __launch_bounds__(kStage1Threads)
+reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t chunk,
+              int64_t index_base, tcx_partial* __restrict__ part) {
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const uint32_t* xr = x + row * n;
+    const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
+    const int64_t end = min(begin + chunk, n);
+    Acc a;
+#pragma unroll
+    for (int s = 0; s < 4 * kUnroll; ++s) { a.f[s] = 0.0f; a.u[s] = 0u; }
+    a.key = 0; a.idx = INT64_MAX;
+    const int tid = threadIdx.x;
+    int64_t tail_begin = begin;
+    if (VEC && end > begin) {
+      const float4* xv = reinterpret_cast<const float4*>(xr + begin);
+      const int64_t nvec = (end - begin) >> 2;
+      int64_t i = tid;
+      for (; i + (kUnroll - 1) * kStage1Threads < nvec; i += kUnroll * kStage1Threads) {
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) v[u] = ldg_stream(xv + i + u * kStage1Threads);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t e = begin + 4 * (i + u * kStage1Threads) + index_base;
+          take<K, FP>(a, 4 * u + 0, __float_as_uint(v[u].x), e + 0);
+          take<K, FP>(a, 4 * u + 1, __float_as_uint(v[u].y), e + 1);
+          take<K, FP>(a, 4 * u + 2, __float_as_uint(v[u].z), e + 2);
+          take<K, FP>(a, 4 * u + 3, __float_as_uint(v[u].w), e + 3);
+        }
+      }
+      for (; i < nvec; i += kStage1Threads) {
+        const float4 v = ldg_stream(xv + i);
+        const int64_t e = begin + 4 * i + index_base;
+        take<K, FP>(a, 0, __float_as_uint(v.x), e + 0);
+        take<K, FP>(a, 1, __float_as_uint(v.y), e + 1);
+        take<K, FP>(a, 2, __float_as_uint(v.z), e + 2);
+        take<K, FP>(a, 3, __float_as_uint(v.w), e + 3);
+      }
+      tail_begin = begin + nvec * 4;
+    }
+    for (int64_t j = tail_begin + tid; j < end; j += kStage1Threads)
+      take<K, FP>(a, 0, __ldg(xr + j), j + index_base);
+
+    uint32_t bits = 0, key = a.key;
+    int64_t idx = a.idx;
+    if (K == kSumF) {
+      // fixed pairwise order over the 16 accumulators
+      float t[4 * kUnroll];
+#pragma unroll
+      for (int s = 0; s < 4 * kUnroll; ++s) t[s] = a.f[s];
+#pragma unroll
+      for (int w = 4 * kUnroll / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int s = 0; s < w; ++s) t[s] = __fadd_rn(t[s], t[s + w]);
+      bits = __float_as_uint(t[0]);
+    } else if (K == kSumI) {
+      uint32_t s = 0;
+#pragma unroll
+      for (int q = 0; q < 4 * kUnroll; ++q) s += a.u[q];
+      bits = s;
+    }
+    block_fold<K>(bits, key, idx);
+    if (threadIdx.x == 0) {
+      tcx_partial p;
+      p.key = key;
+      p.bits = bits;
+      p.index = idx;
+      part[row * gridDim.x + blockIdx.x] = p;
+    }
+  }
+}
+
+// Output modes of stage 2 and the rank combine.
+enum OutMode { kOutValue = 0, kOutMean = 1, kOutIndex = 2, kOutRecord = 3 };
+
+__device__ __forceinline__ void emit(int mode, const uint32_t* xr, int64_t index_base,
+                                     uint32_t bits, uint32_t key, int64_t idx, int64_t count,
+                                     bool sum_kind, void* out, int64_t slot) {
+  if (mode == kOutRecord) {
+    tcx_partial p;
+    p.key = key;
+    p.index = idx;
+    p.bits = sum_kind ? bits : (idx == INT64_MAX ? 0u : xr[idx - index_base]);
+    static_cast<tcx_partial*>(out)[slot] = p;
+  } else if (mode == kOutIndex) {
+    static_cast<int32_t*>(out)[slot] = static_cast<int32_t>(idx - index_base);
+  } else if (mode == kOutMean) {
+    static_cast<float*>(out)[slot] =
+        count ? __fdiv_rn(__uint_as_float(bits), static_cast<float>(count)) : __int_as_float(0x7fc00000);
+  } else {
+    static_cast<uint32_t*>(out)[slot] = sum_kind ? bits : xr[idx - index_base];
+  }
+}
+
+// Stage 2: one CTA per row folds that row's `nparts` records in a fixed order.
+template <int K>
+__global__ void __launch_bounds__(1024)
+reduce_stage2(const tcx_partial* __restrict__ part, int nparts, int64_t rows, int64_t n,
+              const uint32_t* __restrict__ x, int64_t index_base, int mode, void* out) {
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0;
+    int64_t idx = INT64_MAX;
+    // Each thread folds a strided subset in increasing order, then the CTA tree.
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+      const tcx_partial p = part[row * nparts + i];
+      if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(p.bits)));
+      else if (K == kSumI) bits += p.bits;
+      else if (better(p.key, p.index, key, idx)) { key = p.key; idx = p.index; }
+    }
+    block_fold<K>(bits, key, idx);
+    if (threadIdx.x == 0)
+      emit(mode, x + row * n, index_base, bits, key, idx, n, K <= kSumI, out, row);
+  }
+}
+
+// Folds per-rank records in rank order (one thread; nparts is the world size).
+template <int K>
+__global__ void combine_records(const tcx_partial* __restrict__ parts, int nparts,
+                                int64_t total, int mode, void* out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0, best_bits = 0;
+  int64_t idx = INT64_MAX;
+  for (int i = 0; i < nparts; ++i) {
+    const tcx_partial p = parts[i];
+    if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(p.bits)));
+    else if (K == kSumI) bits += p.bits;
+    else if (better(p.key, p.index, key, idx)) { key = p.key; idx = p.index; best_bits = p.bits; }
+  }
+  if (mode == kOutIndex) static_cast<int32_t*>(out)[0] = static_cast<int32_t>(idx);
+  else if (mode == kOutMean)
+    static_cast<float*>(out)[0] =
+        total ? __fdiv_rn(__uint_as_float(bits), static_cast<float>(total)) : __int_as_float(0x7fc00000);
+  else static_cast<uint32_t*>(out)[0] = K <= kSumI ? bits : best_bits;
+}
+
+// ---------------------------------------------------------------- ordered rows
+constexpr int kRowsPerCta = 32, kTileCols = 128;
+
+// One thread per row, left-to-right in float32 (sum/mean) or the reference's max.
+template <typename T, int OP>  // OP: 0 sum, 1 max, 2 mean
+__global__ void __launch_bounds__(256)
+rows_ordered(const T* __restrict__ x, T* __restrict__ out, int64_t rows, int64_t n) {
+  __shared__ T tile[kRowsPerCta][kTileCols + 1];
+  for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRowsPerCta; row0 < rows;
+       row0 += static_cast<int64_t>(gridDim.x) * kRowsPerCta) {
+    T acc;
+    bool seen_nan = false;
+    acc = OP == 1 ? max_identity<T>() : static_cast<T>(0);
+    for (int64_t c0 = 0; c0 < n; c0 += kTileCols) {
+#pragma unroll
+      for (int k = 0; k < kRowsPerCta * kTileCols / 256; ++k) {
+        const int e = threadIdx.x + k * 256;
+        const int r = e / kTileCols, c = e % kTileCols;
+        const int64_t gr = row0 + r, gc = c0 + c;
+        tile[r][c] = (gr < rows && gc < n) ? x[gr * n + gc] : static_cast<T>(0);
+      }
+      __syncthreads();
+      if (threadIdx.x < kRowsPerCta) {
+        const int r = threadIdx.x;
+        const int cols = static_cast<int>(n - c0 < kTileCols ? n - c0 : kTileCols);
+        for (int c = 0; c < cols; ++c) {
+          const T v = tile[r][c];
+          if (OP == 1) {
+            if constexpr (std::is_same<T, float>::value) {
+              if (!seen_nan) {
+                if (isnan(v)) { acc = v; seen_nan = true; }
+                else acc = (acc < v) ? v : acc;
+              }
+            } else {
+              acc = (acc < v) ? v : acc;
+            }
+          } else {
+            if constexpr (std::is_same<T, float>::value) acc = __fadd_rn(acc, v);
+            else acc = static_cast<T>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(v));
+          }
+        }
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x < kRowsPerCta && row0 + threadIdx.x < rows) {
+      if constexpr (std::is_same<T, float>::value) {
+        if (OP == 2) acc = n ? __fdiv_rn(acc, static_cast<float>(n)) : __int_as_float(0x7fc00000);
+      }
+      out[row0 + threadIdx.x] = acc;
+    }
+  }
+}
+
+// Strided axis: one thread per (outer, inner) output, reduce in index order.
+template <typename T, int OP>
+__global__ void axis_strided(const T* __restrict__ x, T* __restrict__ out, int64_t outer,
+                             int64_t reduce, int64_t inner) {
+  const int64_t count = outer * inner;
+  for (int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; id < count;
+       id += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t base = (id / inner) * reduce * inner + id % inner;
+    T acc;
+    acc = OP == 1 ? max_identity<T>() : static_cast<T>(0);
+    for (int64_t r = 0; r < reduce; ++r) {
+      const T v = x[base + r * inner];
+      if (OP == 1) {
+        if constexpr (std::is_same<T, float>::value) {
+          if (isnan(v)) { acc = v; break; }
+        }
+        acc = (acc < v) ? v : acc;
+      } else {
+        if constexpr (std::is_same<T, float>::value) acc = __fadd_rn(acc, v);
+        else acc = static_cast<T>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(v));
+      }
+    }
+    if constexpr (std::is_same<T, float>::value) {
+      if (OP == 2) acc = reduce ? __fdiv_rn(acc, static_cast<float>(reduce)) : __int_as_float(0x7fc00000);
+    }
+    out[id] = acc;
+  }
+}
+
+__device__ __forceinline__ int64_t meta_offset(int64_t index, const Meta& m, int begin, int end) {
+  int64_t value = 0;
+  for (int a = end - 1; a >= begin; --a) {
+    const int64_t extent = m.v[2 * a];
+    value += (index % extent) * m.v[2 * a + 1];
+    index /= extent;
+  }
+  return value;
+}
+
+// General multi-axis sum/max/mean, one thread per output (cpu_backend.cpp:1123-1152).
+template <typename T, int OP>
+__global__ void reduce_axes_general(const T* __restrict__ x, T* __restrict__ out,
+                                    int64_t groups, int64_t size, Meta meta, int outer_rank) {
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t base = meta_offset(g, meta, 0, outer_rank);
+    T acc;
+    acc = OP == 1 ? max_identity<T>() : static_cast<T>(0);
+    for (int64_t r = 0; r < size; ++r) {
+      const T v = x[base + meta_offset(r, meta, outer_rank, meta.rank)];
+      if (OP == 1) {
+        if constexpr (std::is_same<T, float>::value) {
+          if (isnan(v)) { acc = v; break; }
+        }
+        acc = (acc < v) ? v : acc;
+      } else {
+        if constexpr (std::is_same<T, float>::value) acc = __fadd_rn(acc, v);
+        else acc = static_cast<T>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(v));
+      }
+    }
+    if constexpr (std::is_same<T, float>::value) {
+      if (OP == 2) acc = size ? __fdiv_rn(acc, static_cast<float>(size)) : __int_as_float(0x7fc00000);
+    }
+    out[g] = acc;
+  }
+}
+
+// General min/argmax, one thread per output (cpu_math.cpp:48-54).
+template <bool FP, bool ARGMAX>
+__global__ void min_argmax_general(const uint32_t* __restrict__ x, uint32_t* __restrict__ out,
+                                   int64_t groups, int64_t reduce, Meta meta) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < groups;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint32_t best = x[meta_offset(i * reduce, meta, 0, meta.rank)];
+    uint32_t bkey = ARGMAX ? key_max(best, FP) : key_min(best, FP);
+    int64_t index = 0;
+    for (int64_t j = 1; j < reduce; ++j) {
+      const uint32_t a = x[meta_offset(i * reduce + j, meta, 0, meta.rank)];
+      const uint32_t k = ARGMAX ? key_max(a, FP) : key_min(a, FP);
+      if (k > bkey) { best = a; bkey = k; index = j; }
+    }
+    out[i] = ARGMAX ? static_cast<uint32_t>(index) : best;
+  }
+}
+
+__global__ void fill_word(uint32_t* out, uint32_t value) { *out = value; }
+
+
+// ------------------------------------------------------------------- host side
+int kind_of(int op, int dtype) {
+  if (op == TCX_OP_SUM || op == TCX_OP_MEAN) return dtype == TCX_FLOAT32 ? kSumF : kSumI;
+  if (op == TCX_OP_MAX || op == TCX_OP_ARGMAX) return kBestMax;
+  return kBestMin;
+}
+
+struct Stage1Grid {
+  int64_t chunk;
+  int parts;
+  int rows_y;
+};
+
+Stage1Grid stage1_grid(int64_t rows, int64_t n) {
+  const int64_t target_ctas = 4LL * sm_count();
+  int64_t per_row = rows >= target_ctas ? 1 : target_ctas / rows;
+  per_row = std::max<int64_t>(1, std::min<int64_t>(per_row, ceil_div(n, 4096)));
+  int64_t chunk = ceil_div(n, per_row);
+  chunk = (chunk + 3) & ~int64_t(3);
+  if (chunk == 0) chunk = 4;
+  Stage1Grid g;
+  g.chunk = chunk;
+  g.parts = static_cast<int>(std::max<int64_t>(1, ceil_div(n, chunk)));
+  g.rows_y = static_cast<int>(std::min<int64_t>(rows, 65535));
+  return g;
+}
+
+size_t tree_workspace(int64_t rows, int64_t n) {
+  const Stage1Grid g = stage1_grid(rows, n);
+  return static_cast<size_t>(rows) * g.parts * sizeof(tcx_partial);
+}
+
+template <int K, bool FP>
+void launch_stage1(cudaStream_t s, const uint32_t* x, int64_t rows, int64_t n, int64_t index_base,
+                   tcx_partial* parts, const Stage1Grid& g) {
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (n % 4 == 0 || rows == 1);
+  dim3 grid(g.parts, g.rows_y);
+  if (vec) reduce_stage1<K, FP, true><<<grid, kStage1Threads, 0, s>>>(x, rows, n, g.chunk, index_base, parts);
+  else reduce_stage1<K, FP, false><<<grid, kStage1Threads, 0, s>>>(x, rows, n, g.chunk, index_base, parts);
+}
+
+// Row-wise tree reduction of `rows` contiguous rows of `n` elements.
+int tree_reduce(cudaStream_t s, int op, int dtype, const void* input, int64_t rows, int64_t n,
+                int64_t index_base, int mode, void* out, void* ws, size_t ws_bytes) {
+  const Stage1Grid g = stage1_grid(rows, n);
+  const size_t need = static_cast<size_t>(rows) * g.parts * sizeof(tcx_partial);
+  if (!ws || ws_bytes < need) return invalid("reduction workspace is missing or too small");
+  auto* parts = static_cast<tcx_partial*>(ws);
+  const auto* x = static_cast<const uint32_t*>(input);
+  const bool fp = dtype == TCX_FLOAT32;
+  const int kind = kind_of(op, dtype);
+  const int grid2 = static_cast<int>(std::min<int64_t>(rows, 65535));
+  switch (kind) {
+    case kSumF:
+      launch_stage1<kSumF, true>(s, x, rows, n, index_base, parts, g);
+      reduce_stage2<kSumF><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      break;
+    case kSumI:
+      launch_stage1<kSumI, false>(s, x, rows, n, index_base, parts, g);
+      reduce_stage2<kSumI><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      break;
+    case kBestMax:
+      if (fp) launch_stage1<kBestMax, true>(s, x, rows, n, index_base, parts, g);
+      else launch_stage1<kBestMax, false>(s, x, rows, n, index_base, parts, g);
+      reduce_stage2<kBestMax><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      break;
+    default:
+      if (fp) launch_stage1<kBestMin, true>(s, x, rows, n, index_base, parts, g);
+      else launch_stage1<kBestMin, false>(s, x, rows, n, index_base, parts, g);
+      reduce_stage2<kBestMin><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      break;
+  }
+  return launch_status("tree reduction");
+}
+
+int out_mode(int op) {
+  if (op == TCX_OP_MEAN) return kOutMean;
+  if (op == TCX_OP_ARGMAX) return kOutIndex;
+  return kOutValue;
+}
+
+bool valid_reduce_op(int op, int dtype) {
+  if (dtype != TCX_FLOAT32 && dtype != TCX_INT32) return false;
+  switch (op) {
+    case TCX_OP_SUM: case TCX_OP_MAX: case TCX_OP_MIN: case TCX_OP_ARGMAX: return true;
+    case TCX_OP_MEAN: return dtype == TCX_FLOAT32;
+    default: return false;
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t blocks = ceil_div(std::max<int64_t>(work, 1), threads);
+  return static_cast<int>(std::min<int64_t>(blocks, 32LL * sm_count()));
+}
+
+// True when the (extent, stride) pairs enumerate a contiguous buffer in order.
+bool identity_metadata(const int64_t* meta, int rank) {
+  int64_t expect = 1;
+  for (int a = rank - 1; a >= 0; --a) {
+    if (meta[2 * a] == 1) continue;
+    if (meta[2 * a + 1] != expect) return false;
+    expect *= meta[2 * a];
+  }
+  return true;
+}
+
+int load_meta(Meta& m, const int64_t* meta, int rank) {
+  if (rank < 0 || rank > 2 * kMaxRank) return invalid("reduction metadata rank exceeds 32 axes");
+  m.rank = rank;
+  for (int i = 0; i < 2 * rank; ++i) m.v[i] = meta[i];
+  return TCX_OK;
+}
+
+}  // namespace
+
+size_t axis_reduce_workspace(int64_t outer, int64_t reduce, int64_t inner) {
+  if (inner != 1 || reduce <= 65536 || outer >= 4096 || outer <= 0) return 0;
+  return tree_workspace(outer, reduce);
+}
+
+// Shared by tcx_sm100_axis (rows.cu) and reduce_axes: sum/max/mean along one axis.
+int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* output,
+                               int64_t outer, int64_t reduce, int64_t inner, void* ws,
+                               size_t ws_bytes) {
+  const int64_t count = outer * inner;
+  if (count == 0) return TCX_OK;
+  const bool f32 = dtype == TCX_FLOAT32;
+  if (inner == 1) {
+    const int64_t rows = outer;
+    // Few long rows: the parallel tree (exact for int32 and max, 1e-5 for float sums).
+    if (reduce > 65536 && rows < 4096 && ws) {
+      const size_t need = tree_workspace(rows, reduce);
+      if (ws_bytes >= need)
+        return tree_reduce(s, op, dtype, input, rows, reduce, 0, out_mode(op), output, ws, ws_bytes);
+    }
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(rows, kRowsPerCta), 65535LL * 16));
+    if (f32) {
+      auto* x = static_cast<const float*>(input);
+      auto* o = static_cast<float*>(output);
+      if (op == TCX_OP_SUM) rows_ordered<float, 0><<<grid, 256, 0, s>>>(x, o, rows, reduce);
+      else if (op == TCX_OP_MAX) rows_ordered<float, 1><<<grid, 256, 0, s>>>(x, o, rows, reduce);
+      else rows_ordered<float, 2><<<grid, 256, 0, s>>>(x, o, rows, reduce);
+    } else {
+      auto* x = static_cast<const int32_t*>(input);
+      auto* o = static_cast<int32_t*>(output);
+      if (op == TCX_OP_SUM) rows_ordered<int32_t, 0><<<grid, 256, 0, s>>>(x, o, rows, reduce);
+      else rows_ordered<int32_t, 1><<<grid, 256, 0, s>>>(x, o, rows, reduce);
+    }
+    return launch_status("ordered row reduction");
+  }
+  const int grid = grid_for(count, 256);
+  if (f32) {
+    auto* x = static_cast<const float*>(input);
+    auto* o = static_cast<float*>(output);
+    if (op == TCX_OP_SUM) axis_strided<float, 0><<<grid, 256, 0, s>>>(x, o, outer, reduce, inner);
+    else if (op == TCX_OP_MAX) axis_strided<float, 1><<<grid, 256, 0, s>>>(x, o, outer, reduce, inner);
+    else axis_strided<float, 2><<<grid, 256, 0, s>>>(x, o, outer, reduce, inner);
+  } else {
+    auto* x = static_cast<const int32_t*>(input);
+    auto* o = static_cast<int32_t*>(output);
+    if (op == TCX_OP_SUM) axis_strided<int32_t, 0><<<grid, 256, 0, s>>>(x, o, outer, reduce, inner);
+    else axis_strided<int32_t, 1><<<grid, 256, 0, s>>>(x, o, outer, reduce, inner);
+  }
+  return launch_status("strided axis reduction");
+}
+
+
+}  // namespace tcx
+
+using namespace tcx;
+
+extern "C" {
+
+size_t tcx_sm100_reduce_workspace_bytes(int64_t count) {
+  return tree_workspace(1, std::max<int64_t>(count, 1));
+}
+
+int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* input,
+                         int64_t count, void* output, void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (!valid_reduce_op(op, dtype)) return invalid("unsupported full reduction op/dtype");
+  if (count < 0) return invalid("negative element count");
+  if (count == 0) {
+    if (op == TCX_OP_MAX || op == TCX_OP_MIN || op == TCX_OP_ARGMAX)
+      return invalid("reduction requires a non-empty input");
+    // sum of nothing is 0, mean of nothing is NaN (cpu_backend.cpp:1146-1147)
+    fill_word<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint32_t*>(output), op == TCX_OP_MEAN ? 0x7fc00000u : 0u);
+    return launch_status("empty reduction");
+  }
+  if (op == TCX_OP_ARGMAX && count > INT32_MAX) return invalid("argmax index range exceeds int32");
+  return tree_reduce(reinterpret_cast<cudaStream_t>(stream), op, dtype, input, 1, count, 0,
+                     out_mode(op), output, workspace, workspace_bytes);
+}
+
+int tcx_sm100_reduce_partial(tcx_stream_t stream, int op, int dtype, const void* input,
+                             int64_t count, int64_t index_base, tcx_partial* partial,
+                             void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (!valid_reduce_op(op, dtype)) return invalid("unsupported partial reduction op/dtype");
+  if (count <= 0) return invalid("partial reduction requires a non-empty shard");
+  return tree_reduce(reinterpret_cast<cudaStream_t>(stream), op, dtype, input, 1, count, index_base,
+                     kOutRecord, partial, workspace, workspace_bytes);
+}
+
+int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype, const tcx_partial* partials,
+                             int32_t nparts, int64_t total_count, void* output) {
+  clear_error();
+  if (!valid_reduce_op(op, dtype)) return invalid("unsupported combine op/dtype");
+  if (nparts <= 0) return invalid("combine requires at least one record");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int mode = out_mode(op);
+  switch (kind_of(op, dtype)) {
+    case kSumF: combine_records<kSumF><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
+    case kSumI: combine_records<kSumI><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
+    case kBestMax: combine_records<kBestMax><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
+    default: combine_records<kBestMin><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
+  }
+  return launch_status("reduction combine");
+}
+
+int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* input, void* output,
+                          int64_t groups, int64_t reduction_size, const int64_t* index_metadata,
+                          int32_t outer_rank, int32_t rank, void* workspace,
+                          size_t workspace_bytes) {
+  clear_error();
+  if (op != TCX_OP_SUM && op != TCX_OP_MAX && op != TCX_OP_MEAN)
+    return invalid("reduce_axes supports sum, max and mean");
+  if (!valid_reduce_op(op, dtype)) return invalid("mean only supports float32 tensors");
+  if (groups < 0 || reduction_size < 0 || outer_rank < 0 || outer_rank > rank)
+    return invalid("malformed reduction plan");
+  if (op == TCX_OP_MAX && reduction_size == 0) return invalid("max reduction requires non-empty axes");
+  if (groups == 0) return TCX_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (rank > 0 && !index_metadata) return invalid("missing reduction metadata");
+  // A selection whose metadata enumerates the buffer in order is `groups` contiguous
+  // rows of `reduction_size`: the row kernels apply (all-axes is the 1-row case).
+  if (reduction_size > 0 && identity_metadata(index_metadata, rank)) {
+    if (groups == 1 && reduction_size > 65536)
+      return tree_reduce(s, op, dtype, input, 1, reduction_size, 0, out_mode(op), output, workspace,
+                         workspace_bytes);
+    return axis_reduce(s, op, dtype, input, output, groups, reduction_size, 1,
+                       workspace, workspace_bytes);
+  }
+  Meta meta;
+  if (int st = load_meta(meta, index_metadata, rank)) return st;
+  const int grid = grid_for(groups, 256);
+  if (dtype == TCX_FLOAT32) {
+    auto* x = static_cast<const float*>(input);
+    auto* o = static_cast<float*>(output);
+    if (op == TCX_OP_SUM) reduce_axes_general<float, 0><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta, outer_rank);
+    else if (op == TCX_OP_MAX) reduce_axes_general<float, 1><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta, outer_rank);
+    else reduce_axes_general<float, 2><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta, outer_rank);
+  } else {
+    auto* x = static_cast<const int32_t*>(input);
+    auto* o = static_cast<int32_t*>(output);
+    if (op == TCX_OP_SUM) reduce_axes_general<int32_t, 0><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta, outer_rank);
+    else reduce_axes_general<int32_t, 1><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta, outer_rank);
+  }
+  return launch_status("multi-axis reduction");
+}
+
+int tcx_sm100_min_argmax(tcx_stream_t stream, int op, int dtype, const void* input, void* output,
+                         int64_t groups, int64_t reduction_size, const int64_t* index_metadata,
+                         int32_t rank, void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (op != TCX_OP_MIN && op != TCX_OP_ARGMAX) return invalid("min_argmax supports min and argmax");
+  if (dtype != TCX_FLOAT32 && dtype != TCX_INT32)
+    return invalid("math operations require float32 or int32 tensors");
+  if (reduction_size <= 0) return invalid("min/argmax require a non-empty reduction");
+  if (op == TCX_OP_ARGMAX && reduction_size > INT32_MAX) return invalid("argmax index range exceeds int32");
+  if (groups < 0) return invalid("malformed reduction plan");
+  if (groups == 0) return TCX_OK;
+  if (rank > 0 && !index_metadata) return invalid("missing reduction metadata");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool fp = dtype == TCX_FLOAT32;
+  if (identity_metadata(index_metadata, rank) && reduction_size >= 1024) {
+    // contiguous rows: parallel row reduction (exact: index-carrying keys)
+    return tree_reduce(s, op, dtype, input, groups, reduction_size, 0, out_mode(op), output,
+                       workspace, workspace_bytes);
+  }
+  Meta meta;
+  if (int st = load_meta(meta, index_metadata, rank)) return st;
+  const int grid = grid_for(groups, 256);
+  auto* x = static_cast<const uint32_t*>(input);
+  auto* o = static_cast<uint32_t*>(output);
+  if (op == TCX_OP_ARGMAX) {
+    if (fp) min_argmax_general<true, true><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta);
+    else min_argmax_general<false, true><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta);
+  } else {
+    if (fp) min_argmax_general<true, false><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta);
+    else min_argmax_general<false, false><<<grid, 256, 0, s>>>(x, o, groups, reduction_size, meta);
+  }
+  return launch_status("min/argmax");
+}
+
+}  // extern "C"

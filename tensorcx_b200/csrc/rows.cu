@@ -1,0 +1,415 @@
+// Row softmax / rmsnorm / layernorm (+ fused affine) on sm_100a, and the
+// tcx_sm100_axis dispatcher.
+//
+// Contiguous rows (axis = -1, inner == 1) up to 32768 elements: one CTA per row keeps
+// the whole row in registers (128-bit loads when the row is 16-byte aligned), so
+// every element is read from HBM once and written once: 8 bytes per element, the
+// roofline minimum. Statistics use warp shuffles plus one shared-memory hop.
+// Longer rows stream the row from global memory in 2-3 passes; strided axes run one
+// thread per (outer, inner) column in the reference's own order.
+//
+// Special cases follow the CPU reference (cpu_backend.cpp:125-240): a NaN anywhere in
+// a softmax row makes the row NaN; a constant finite layernorm row gives 0 (NaN when
+// epsilon is 0); a zero layernorm denominator gives NaN. Elementwise products and sums
+// that the reference performs as separate float32 operations use _rn intrinsics so
+// nvcc does not contract them into FMAs.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace tcx {
+namespace {
+
+enum RowOp { kSoftmax = 0, kRms = 1, kLayer = 2 };
+
+__device__ __forceinline__ float nan_max(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  return a < b ? b : a;
+}
+
+// CTA-wide reductions; every thread receives the result.
+template <int THREADS>
+struct Block {
+  static constexpr int kWarps = THREADS / 32;
+  __device__ static float sum(float v, float* smem) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (kWarps == 1) return v;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    float t = lane < kWarps ? smem[lane] : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
+    return t;
+  }
+  __device__ static float max(float v, float* smem) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = nan_max(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (kWarps == 1) return v;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    float t = lane < kWarps ? smem[lane] : -INFINITY;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t = nan_max(t, __shfl_xor_sync(0xffffffffu, t, off));
+    return t;
+  }
+  __device__ static bool all(bool v, float* smem) {
+    v = __all_sync(0xffffffffu, v);
+    if (kWarps == 1) return v;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) smem[warp] = v ? 1.0f : 0.0f;
+    __syncthreads();
+    return __all_sync(0xffffffffu, lane < kWarps ? smem[lane] != 0.0f : true);
+  }
+};
+
+// Per-row math on values held by the CTA's threads. E = elements per thread.
+template <int OP, int THREADS, int E>
+__device__ __forceinline__ void row_math(float (&v)[E], const bool (&valid)[E], int64_t n,
+                                         float first, float eps, float* smem) {
+  using B = Block<THREADS>;
+  if (OP == kSoftmax) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < E; ++i) if (valid[i]) m = nan_max(m, v[i]);
+    m = B::max(m, smem);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      v[i] = valid[i] ? expf(__fsub_rn(v[i], m)) : 0.0f;
+      s = __fadd_rn(s, v[i]);
+    }
+    s = B::sum(s, smem);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fdiv_rn(v[i], s);
+  } else if (OP == kRms) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) if (valid[i]) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    ss = B::sum(ss, smem);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], scale);
+  } else {
+    float s = 0.0f;
+    bool eq = true;
+#pragma unroll
+    for (int i = 0; i < E; ++i) if (valid[i]) { s = __fadd_rn(s, v[i]); eq = eq && (v[i] == first); }
+    s = B::sum(s, smem);
+    eq = B::all(eq, smem);
+    if (eq && isfinite(first)) {
+      const float value = eps == 0.0f ? __int_as_float(0x7fc00000) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) v[i] = value;
+      return;
+    }
+    const float mean = __fdiv_rn(s, static_cast<float>(n));
+    float ssd = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      if (valid[i]) {
+        const float d = __fsub_rn(v[i], mean);
+        ssd = __fadd_rn(ssd, __fmul_rn(d, d));
+      }
+    }
+    ssd = B::sum(ssd, smem);
+    const float denom = __fadd_rn(__fdiv_rn(ssd, static_cast<float>(n)), eps);
+    if (denom == 0.0f) {
+#pragma unroll
+      for (int i = 0; i < E; ++i) v[i] = __int_as_float(0x7fc00000);
+      return;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(denom));
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fsub_rn(v[i], mean), scale);
+  }
+}
+
+__device__ __forceinline__ float affine(float y, const float* w, const float* b, int64_t c) {
+  if (w) y = __fmul_rn(y, __ldg(w + c));
+  if (b) y = __fadd_rn(y, __ldg(b + c));
+  return y;
+}
+
+// One CTA per row, the row held in registers. VEC: float4 accesses (row length % 4 == 0
+// and 16-byte aligned rows); otherwise scalar accesses, element tid + THREADS*q.
+template <int OP, int THREADS, int VPT, bool VEC>
+__global__ void __launch_bounds__(THREADS)
+row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n,
+           float eps, const float* __restrict__ w, const float* __restrict__ b) {
+  constexpr int E = VPT * 4;
+  __shared__ float smem[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + row * n;
+    float* orow = out + row * n;
+    float v[E];
+    bool valid[E];
+    if (VEC) {
+      const int64_t n4 = n >> 2;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t i4 = threadIdx.x + static_cast<int64_t>(j) * THREADS;
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool ok = i4 < n4;
+        if (ok) t = __ldcs(reinterpret_cast<const float4*>(xr) + i4);
+        v[4 * j + 0] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+        valid[4 * j + 0] = valid[4 * j + 1] = valid[4 * j + 2] = valid[4 * j + 3] = ok;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < E; ++q) {
+        const int64_t i = threadIdx.x + static_cast<int64_t>(q) * THREADS;
+        valid[q] = i < n;
+        v[q] = valid[q] ? __ldcs(xr + i) : 0.0f;
+      }
+    }
+    const float first = OP == kLayer ? __ldg(xr) : 0.0f;
+    row_math<OP, THREADS, E>(v, valid, n, first, eps, smem);
+    if (VEC) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t i4 = threadIdx.x + static_cast<int64_t>(j) * THREADS;
+        if (i4 < (n >> 2)) {
+          float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          if (w || b) {
+            t.x = affine(t.x, w, b, 4 * i4 + 0); t.y = affine(t.y, w, b, 4 * i4 + 1);
+            t.z = affine(t.z, w, b, 4 * i4 + 2); t.w = affine(t.w, w, b, 4 * i4 + 3);
+          }
+          __stcs(reinterpret_cast<float4*>(orow) + i4, t);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < E; ++q) {
+        const int64_t i = threadIdx.x + static_cast<int64_t>(q) * THREADS;
+        if (i < n) __stcs(orow + i, (w || b) ? affine(v[q], w, b, i) : v[q]);
+      }
+    }
+  }
+}
+
+// Rows longer than the register-resident limit: CTA per row, streaming passes.
+template <int OP>
+__global__ void __launch_bounds__(1024)
+row_stream(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n,
+           float eps, const float* __restrict__ w, const float* __restrict__ b) {
+  using B = Block<1024>;
+  __shared__ float smem[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + row * n;
+    float* orow = out + row * n;
+    if (OP == kSoftmax) {
+      float m = -INFINITY;
+      for (int64_t i = threadIdx.x; i < n; i += 1024) m = nan_max(m, xr[i]);
+      m = B::max(m, smem);
+      float s = 0.0f;
+      for (int64_t i = threadIdx.x; i < n; i += 1024) s = __fadd_rn(s, expf(__fsub_rn(xr[i], m)));
+      s = B::sum(s, smem);
+      for (int64_t i = threadIdx.x; i < n; i += 1024) orow[i] = __fdiv_rn(expf(__fsub_rn(xr[i], m)), s);
+    } else if (OP == kRms) {
+      float ss = 0.0f;
+      for (int64_t i = threadIdx.x; i < n; i += 1024) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+      ss = B::sum(ss, smem);
+      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
+      for (int64_t i = threadIdx.x; i < n; i += 1024) orow[i] = affine(__fmul_rn(xr[i], scale), w, b, i);
+    } else {
+      const float first = xr[0];
+      float s = 0.0f;
+      bool eq = true;
+      for (int64_t i = threadIdx.x; i < n; i += 1024) { s = __fadd_rn(s, xr[i]); eq = eq && xr[i] == first; }
+      s = B::sum(s, smem);
+      eq = B::all(eq, smem);
+      if (eq && isfinite(first)) {
+        const float value = eps == 0.0f ? __int_as_float(0x7fc00000) : 0.0f;
+        for (int64_t i = threadIdx.x; i < n; i += 1024) orow[i] = affine(value, w, b, i);
+        continue;
+      }
+      const float mean = __fdiv_rn(s, static_cast<float>(n));
+      float ssd = 0.0f;
+      for (int64_t i = threadIdx.x; i < n; i += 1024) {
+        const float d = __fsub_rn(xr[i], mean);
+        ssd = __fadd_rn(ssd, __fmul_rn(d, d));
+      }
+      ssd = B::sum(ssd, smem);
+      const float denom = __fadd_rn(__fdiv_rn(ssd, static_cast<float>(n)), eps);
+      const float scale = denom == 0.0f ? __int_as_float(0x7fc00000) : __fdiv_rn(1.0f, __fsqrt_rn(denom));
+      for (int64_t i = threadIdx.x; i < n; i += 1024)
+        orow[i] = affine(denom == 0.0f ? scale : __fmul_rn(__fsub_rn(xr[i], mean), scale), w, b, i);
+    }
+  }
+}
+
+// Strided axis: one thread per (outer, inner) column, the reference's sequential order.
+template <int OP>
+__global__ void row_strided(const float* __restrict__ x, float* __restrict__ out, int64_t outer,
+                            int64_t reduce, int64_t inner, float eps, const float* __restrict__ w,
+                            const float* __restrict__ b) {
+  const int64_t count = outer * inner;
+  for (int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; id < count;
+       id += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t base = (id / inner) * reduce * inner + id % inner;
+    if (OP == kSoftmax) {
+      float m = -INFINITY;
+      for (int64_t r = 0; r < reduce; ++r) {
+        const float v = x[base + r * inner];
+        if (isnan(v)) { m = v; break; }
+        m = m < v ? v : m;
+      }
+      float d = 0.0f;
+      for (int64_t r = 0; r < reduce; ++r) d = __fadd_rn(d, expf(__fsub_rn(x[base + r * inner], m)));
+      for (int64_t r = 0; r < reduce; ++r) {
+        const int64_t i = base + r * inner;
+        out[i] = __fdiv_rn(expf(__fsub_rn(x[i], m)), d);
+      }
+    } else if (OP == kRms) {
+      float ss = 0.0f;
+      for (int64_t r = 0; r < reduce; ++r) {
+        const float v = x[base + r * inner];
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+      }
+      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(reduce)), eps)));
+      for (int64_t r = 0; r < reduce; ++r) {
+        const int64_t i = base + r * inner;
+        out[i] = affine(__fmul_rn(x[i], scale), w, b, r);
+      }
+    } else {
+      float s = 0.0f;
+      const float first = x[base];
+      bool eq = true;
+      for (int64_t r = 0; r < reduce; ++r) {
+        const float v = x[base + r * inner];
+        s = __fadd_rn(s, v);
+        eq = eq && v == first;
+      }
+      if (eq && isfinite(first)) {
+        const float value = eps == 0.0f ? __int_as_float(0x7fc00000) : 0.0f;
+        for (int64_t r = 0; r < reduce; ++r) out[base + r * inner] = affine(value, w, b, r);
+        continue;
+      }
+      const float mean = __fdiv_rn(s, static_cast<float>(reduce));
+      float ssd = 0.0f;
+      for (int64_t r = 0; r < reduce; ++r) {
+        const float d = __fsub_rn(x[base + r * inner], mean);
+        ssd = __fadd_rn(ssd, __fmul_rn(d, d));
+      }
+      const float denom = __fadd_rn(__fdiv_rn(ssd, static_cast<float>(reduce)), eps);
+      if (denom == 0.0f) {
+        for (int64_t r = 0; r < reduce; ++r) out[base + r * inner] = affine(__int_as_float(0x7fc00000), w, b, r);
+        continue;
+      }
+      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(denom));
+      for (int64_t r = 0; r < reduce; ++r) {
+        const int64_t i = base + r * inner;
+        out[i] = affine(__fmul_rn(__fsub_rn(x[i], mean), scale), w, b, r);
+      }
+    }
+  }
+}
+
+template <int OP, int THREADS, int VPT>
+void launch_row(cudaStream_t s, const float* x, float* out, int64_t rows, int64_t n, float eps,
+                const float* w, const float* b, bool vec) {
+  const int grid = static_cast<int>(std::min<int64_t>(rows, 1LL << 20));
+  if (vec) row_kernel<OP, THREADS, VPT, true><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
+  else row_kernel<OP, THREADS, VPT, false><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
+}
+
+template <int OP>
+int run_rows(cudaStream_t s, const float* x, float* out, int64_t outer, int64_t reduce,
+             int64_t inner, float eps, const float* w, const float* b) {
+  if (outer * inner == 0 || reduce == 0) return TCX_OK;
+  if (inner != 1) {
+    const int64_t count = outer * inner;
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(count, 256), 32LL * sm_count()));
+    row_strided<OP><<<grid, 256, 0, s>>>(x, out, outer, reduce, inner, eps, w, b);
+    return launch_status("strided row op");
+  }
+  const int64_t n = reduce;
+  const bool vec = n % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (n <= 1024) launch_row<OP, 128, 2>(s, x, out, outer, n, eps, w, b, vec);
+  else if (n <= 4096) launch_row<OP, 256, 4>(s, x, out, outer, n, eps, w, b, vec);
+  else if (n <= 8192) launch_row<OP, 512, 4>(s, x, out, outer, n, eps, w, b, vec);
+  else if (n <= 16384) launch_row<OP, 512, 8>(s, x, out, outer, n, eps, w, b, vec);
+  else if (n <= 32768) launch_row<OP, 1024, 8>(s, x, out, outer, n, eps, w, b, vec);
+  else {
+    const int grid = static_cast<int>(std::min<int64_t>(outer, 1LL << 20));
+    row_stream<OP><<<grid, 1024, 0, s>>>(x, out, outer, n, eps, w, b);
+  }
+  return launch_status("row op");
+}
+
+int rows_dispatch(cudaStream_t s, int op, const float* x, float* out, int64_t outer,
+                  int64_t reduce, int64_t inner, float eps, const float* w, const float* b) {
+  switch (op) {
+    case TCX_OP_SOFTMAX: return run_rows<kSoftmax>(s, x, out, outer, reduce, inner, eps, w, b);
+    case TCX_OP_RMSNORM: return run_rows<kRms>(s, x, out, outer, reduce, inner, eps, w, b);
+    default: return run_rows<kLayer>(s, x, out, outer, reduce, inner, eps, w, b);
+  }
+}
+
+bool valid_dims(int64_t outer, int64_t reduce, int64_t inner) {
+  return outer >= 0 && reduce >= 0 && inner >= 0;
+}
+
+}  // namespace
+}  // namespace tcx
+
+using namespace tcx;
+
+extern "C" {
+
+size_t tcx_sm100_axis_workspace_bytes(int op, int64_t outer, int64_t reduce, int64_t inner) {
+  if (op != TCX_OP_SUM && op != TCX_OP_MAX && op != TCX_OP_MEAN) return 0;
+  return axis_reduce_workspace(outer, reduce, inner);
+}
+
+int tcx_sm100_axis(tcx_stream_t stream, int op, int dtype, const void* input, void* output,
+                   int64_t outer, int64_t reduce, int64_t inner, float epsilon, void* workspace,
+                   size_t workspace_bytes) {
+  clear_error();
+  if (!valid_dims(outer, reduce, inner)) return invalid("negative axis extents");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (op) {
+    case TCX_OP_SUM:
+    case TCX_OP_MAX:
+      if (dtype != TCX_FLOAT32 && dtype != TCX_INT32) return invalid("CUDA operations only support float32");
+      if (op == TCX_OP_MAX && reduce == 0) return invalid("max reduction requires a non-empty axis");
+      return axis_reduce(s, op, dtype, input, output, outer, reduce, inner, workspace, workspace_bytes);
+    case TCX_OP_MEAN:
+      if (dtype != TCX_FLOAT32) return invalid("mean only supports float32 tensors");
+      return axis_reduce(s, op, dtype, input, output, outer, reduce, inner, workspace, workspace_bytes);
+    case TCX_OP_SOFTMAX:
+    case TCX_OP_RMSNORM:
+    case TCX_OP_LAYERNORM:
+      if (dtype != TCX_FLOAT32) return invalid("CUDA operation only supports float32 for this dtype");
+      if (!(epsilon >= 0.0f) || isinf(epsilon)) return invalid("epsilon must be finite and non-negative and representable as float32");
+      return rows_dispatch(s, op, static_cast<const float*>(input), static_cast<float*>(output), outer,
+                           reduce, inner, epsilon, nullptr, nullptr);
+    default:
+      return invalid("unsupported axis operation");
+  }
+}
+
+int tcx_sm100_affine_norm(tcx_stream_t stream, int op, const float* input, float* output,
+                          int64_t outer, int64_t reduce, int64_t inner, float epsilon,
+                          const float* weight, const float* bias) {
+  clear_error();
+  if (!valid_dims(outer, reduce, inner)) return invalid("negative axis extents");
+  if (op != TCX_OP_RMSNORM && op != TCX_OP_LAYERNORM) return invalid("affine norm supports rmsnorm and layernorm");
+  if (op == TCX_OP_RMSNORM && bias) return invalid("invalid affine normalization parameters");
+  if (!(epsilon >= 0.0f) || isinf(epsilon)) return invalid("epsilon must be finite, non-negative and representable as float32");
+  return rows_dispatch(reinterpret_cast<cudaStream_t>(stream), op, input, output, outer, reduce, inner,
+                       epsilon, weight, bias);
+}
+
+}  // extern "C"

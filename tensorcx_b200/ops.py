@@ -1,0 +1,357 @@
+"""Python host mirror of the tensor.cx op API for device='cuda' on B200.
+
+Names, argument meaning and errors follow python/tensorcx/tensor.py (matmul 500-505,
+sum/max/mean 508-545, softmax/rmsnorm/layernorm 565-584, min/argmax 834-855,
+clip 858-876) and the primitive dispatch of CudaBackend::execute
+(cpp/tensorcx/backends/cuda/cuda_backend.cpp:290-627). Tensors are torch CUDA tensors
+(float32 or int32, contiguous): torch supplies device memory and streams, nothing else.
+Every op calls the C ABI (tensorcx_b200._abi) on torch's current stream; outputs are
+fresh contiguous tensors, and workspace comes from torch's stream-ordered caching
+allocator. Ops are asynchronous like torch ops; call torch.cuda.synchronize() (or
+.cpu()) to observe results.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import plan
+from ._abi import ACT, FLOAT32, INT32, MATMUL_PATH, OP, Partial, check, i64_array, lib
+
+__all__ = ["matmul", "sum", "max", "mean", "min", "argmax", "softmax", "rmsnorm", "layernorm",
+           "exp", "gelu", "silu", "add", "subtract", "multiply", "divide", "clip", "relu",
+           "bias_act", "linear", "reduce_partial", "reduce_combine", "Partial"]
+
+
+def _dtype(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return FLOAT32
+    if t.dtype == torch.int32:
+        return INT32
+    raise ValueError("CUDA operations only support float32 and int32 on this path")
+
+
+def _check_tensor(t: torch.Tensor, name: str = "input") -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise ValueError("device mismatch: tensors must be on the CUDA device")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _workspace(nbytes: int, device, align: int = 1024):
+    """(keep-alive tensor, aligned pointer) for `nbytes` of scratch, or (None, None)."""
+    if nbytes == 0:
+        return None, None
+    buf = torch.empty(nbytes + align, dtype=torch.uint8, device=device)
+    addr = (buf.data_ptr() + align - 1) // align * align
+    return buf, ctypes.c_void_p(addr)
+
+
+# -------------------------------------------------------------------- matmul
+def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = None,
+           act: str = "none", path: str = "auto", out: torch.Tensor | None = None) -> torch.Tensor:
+    """NumPy-semantics float32 matmul; optional fused epilogue act(C + bias[n])."""
+    _check_tensor(lhs, "lhs"), _check_tensor(rhs, "rhs")
+    if lhs.device != rhs.device:
+        raise ValueError("device mismatch for matmul")
+    if lhs.dtype != torch.float32 or rhs.dtype != torch.float32:
+        raise ValueError("matmul only supports float32 tensors")
+    p = plan.matmul(lhs.shape, rhs.shape)
+    if out is None:
+        out = torch.empty(p.output_shape, dtype=torch.float32, device=lhs.device)
+    if bias is not None:
+        _check_tensor(bias, "bias")
+        if bias.shape != (p.n,) or bias.dtype != torch.float32:
+            raise ValueError("bias must be float32 with shape (n,)")
+    nba = lhs.numel() // max(1, p.m * p.k) if p.m * p.k else 1
+    nbb = rhs.numel() // max(1, p.k * p.n) if p.k * p.n else 1
+    ws_bytes = lib().tcx_sm100_matmul_workspace_bytes(p.m, p.n, p.k, nba, nbb, MATMUL_PATH[path])
+    keep, ws = _workspace(ws_bytes, lhs.device)
+    batches = plan.numel(p.batch_shape) if out.numel() else 0
+    check(lib().tcx_sm100_matmul(
+        _stream(), _ptr(lhs), _ptr(rhs), _ptr(out), p.m, p.n, p.k, batches,
+        i64_array(p.batch_shape), i64_array(p.lhs_batch_strides), i64_array(p.rhs_batch_strides),
+        len(p.batch_shape), _ptr(bias), ACT[act], MATMUL_PATH[path], ws, ws_bytes))
+    del keep
+    return out
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           act: str = "none") -> torch.Tensor:
+    """linear(x, w[out, in], b[out]) (core/inference.cpp:89-102) as one matmul with the
+    bias (and optional activation) fused into the epilogue."""
+    _check_tensor(x, "x"), _check_tensor(weight, "weight")
+    if x.dim() == 0 or weight.dim() != 2 or x.shape[-1] != weight.shape[1]:
+        raise ValueError("linear requires (..., in_features) and (out_features, in_features)")
+    if bias is not None and bias.shape != (weight.shape[0],):
+        raise ValueError("linear bias must have shape (out_features,)")
+    return matmul(x, weight.t().contiguous(), bias=bias, act=act)
+
+
+# ---------------------------------------------------------------- reductions
+def _axes_sequence(axis, rank):
+    values = tuple(axis) if isinstance(axis, (tuple, list)) else (axis,)
+    scalar = rank == 0 and len(values) == 1 and values[0] in (0, -1)
+    if scalar:
+        return (), True
+    out = []
+    for v in values:
+        if not -rank <= v < rank:
+            raise ValueError("reduction axis is out of range")
+        out.append(v % rank)
+    return tuple(out), False
+
+
+def _reduce(name: str, x: torch.Tensor, axis) -> torch.Tensor:
+    """tensor.py:_reduce: a single axis uses the one-axis primitive, otherwise the
+    multi-axis plan (every axis when axis is None)."""
+    _check_tensor(x)
+    dt = _dtype(x)
+    if name == "mean" and dt != FLOAT32:
+        raise ValueError("mean only supports float32 tensors")
+    rank = x.dim()
+    if axis is None:
+        axes, scalar = tuple(range(rank)), rank == 0
+    else:
+        axes, scalar = _axes_sequence(axis, rank)
+    if scalar or len(axes) == 1:
+        shape, outer, reduce, inner = plan.axis(list(x.shape), axes[0] if axes else 0)
+        if name == "max" and reduce == 0:
+            raise ValueError("max reduction requires a non-empty axis")
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+        ws_bytes = lib().tcx_sm100_axis_workspace_bytes(OP[name], outer, reduce, inner)
+        keep, ws = _workspace(ws_bytes, x.device)
+        check(lib().tcx_sm100_axis(_stream(), OP[name], dt, _ptr(x), _ptr(out), outer, reduce, inner,
+                                   0.0, ws, ws_bytes))
+        return out
+    p = plan.reduction(list(x.shape), axes)
+    if name == "max" and p.reduction_size == 0:
+        raise ValueError("max reduction requires non-empty axes")
+    if not axes:
+        return x.clone()
+    out = torch.empty(p.output_shape, dtype=x.dtype, device=x.device)
+    groups = plan.numel(p.output_shape)
+    ws_bytes = lib().tcx_sm100_reduce_workspace_bytes(groups * p.reduction_size)
+    keep, ws = _workspace(ws_bytes, x.device)
+    check(lib().tcx_sm100_reduce_axes(_stream(), OP[name], dt, _ptr(x), _ptr(out), groups,
+                                      p.reduction_size, i64_array(p.index_metadata),
+                                      len(p.output_shape), x.dim(), ws, ws_bytes))
+    return out
+
+
+def sum(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001 - tensor.cx name
+    return _reduce("sum", x, axis)
+
+
+def max(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001
+    return _reduce("max", x, axis)
+
+
+def mean(x: torch.Tensor, axis=None) -> torch.Tensor:
+    return _reduce("mean", x, axis)
+
+
+def _min_argmax(name: str, x: torch.Tensor, axis) -> torch.Tensor:
+    """make_math_plan (core/math.cpp:39-56) then the C ABI."""
+    _check_tensor(x)
+    dt = _dtype(x)
+    rank = x.dim()
+    if axis is None:
+        axes = list(range(rank))
+    else:
+        vals = list(axis) if isinstance(axis, (tuple, list)) else [axis]
+        axes = [] if (rank == 0 and len(vals) == 1 and vals[0] in (0, -1)) else vals
+    p = plan.reduction(list(x.shape), axes)
+    if not p.reduction_size:
+        raise ValueError("min/argmax require a non-empty reduction")
+    if name == "argmax":
+        extent = 1
+        for a in axes:
+            a = a + rank if a < 0 else a
+            if x.shape[a] > (2**31 - 1) // extent:
+                raise ValueError("argmax index range exceeds int32")
+            extent *= x.shape[a]
+    out = torch.empty(p.output_shape, dtype=torch.int32 if name == "argmax" else x.dtype, device=x.device)
+    groups = plan.numel(p.output_shape)
+    ws_bytes = lib().tcx_sm100_reduce_workspace_bytes(groups * p.reduction_size)
+    keep, ws = _workspace(ws_bytes, x.device)
+    check(lib().tcx_sm100_min_argmax(_stream(), OP[name], dt, _ptr(x), _ptr(out), groups,
+                                     p.reduction_size, i64_array(p.index_metadata), x.dim(), ws,
+                                     ws_bytes))
+    return out
+
+
+def min(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001
+    return _min_argmax("min", x, axis)
+
+
+def argmax(x: torch.Tensor, axis=None) -> torch.Tensor:
+    return _min_argmax("argmax", x, axis)
+
+
+def reduce_partial(x: torch.Tensor, op: str, index_base: int = 0) -> torch.Tensor:
+    """This shard's 16-byte tcx_partial record (as a uint8[16] device tensor) for a
+    full-tensor reduction combined across GPUs with reduce_combine."""
+    _check_tensor(x)
+    rec = torch.empty(16, dtype=torch.uint8, device=x.device)
+    ws_bytes = lib().tcx_sm100_reduce_workspace_bytes(x.numel())
+    keep, ws = _workspace(ws_bytes, x.device)
+    check(lib().tcx_sm100_reduce_partial(_stream(), OP[op], _dtype(x), _ptr(x), x.numel(), index_base,
+                                         _ptr(rec), ws, ws_bytes))
+    return rec
+
+
+def reduce_combine(records: torch.Tensor, op: str, dtype: torch.dtype, total_count: int) -> torch.Tensor:
+    """Folds gathered records ([nparts, 16] uint8, rank order) into the final value."""
+    out = torch.empty((), dtype=torch.int32 if op == "argmax" else dtype, device=records.device)
+    dt = FLOAT32 if dtype == torch.float32 else INT32
+    check(lib().tcx_sm100_reduce_combine(_stream(), OP[op], dt, _ptr(records.contiguous()),
+                                         records.numel() // 16, total_count, _ptr(out)))
+    return out
+
+
+# ------------------------------------------------------------------ row ops
+def _row_op(name: str, x: torch.Tensor, axis: int, eps: float | None, weight=None, bias=None):
+    _check_tensor(x)
+    if x.dtype != torch.float32:
+        raise ValueError(f"{name} only supports float32 tensors")
+    _, outer, reduce, inner = plan.axis(list(x.shape), axis)
+    e = plan.epsilon(eps) if eps is not None else 0.0
+    out = torch.empty_like(x)
+    if weight is None and bias is None:
+        check(lib().tcx_sm100_axis(_stream(), OP[name], FLOAT32, _ptr(x), _ptr(out), outer, reduce, inner,
+                                   e, None, 0))
+        return out
+    expected = () if x.dim() == 0 else (reduce,)
+    for t in (weight, bias):
+        if t is not None:
+            _check_tensor(t)
+            if tuple(t.shape) != expected or t.dtype != torch.float32:
+                raise ValueError("affine parameters must match the normalized axis")
+    check(lib().tcx_sm100_affine_norm(_stream(), OP[name], _ptr(x), _ptr(out), outer, reduce, inner, e,
+                                      _ptr(weight), _ptr(bias)))
+    return out
+
+
+def softmax(x: torch.Tensor, axis: int = -1) -> torch.Tensor:
+    return _row_op("softmax", x, axis, None)
+
+
+def rmsnorm(x: torch.Tensor, axis: int = -1, eps: float = 1.0e-5, *, weight=None) -> torch.Tensor:
+    return _row_op("rmsnorm", x, axis, eps, weight, None)
+
+
+def layernorm(x: torch.Tensor, axis: int = -1, eps: float = 1.0e-5, *, weight=None, bias=None) -> torch.Tensor:
+    return _row_op("layernorm", x, axis, eps, weight, bias)
+
+
+# -------------------------------------------------------------- elementwise
+def _unary(name: str, x: torch.Tensor) -> torch.Tensor:
+    _check_tensor(x)
+    if x.dtype != torch.float32:
+        raise ValueError(f"{name} only supports float32 tensors")
+    out = torch.empty_like(x)
+    check(lib().tcx_sm100_unary(_stream(), OP[name], _ptr(x), _ptr(out), x.numel()))
+    return out
+
+
+def exp(x):
+    return _unary("exp", x)
+
+
+def gelu(x):
+    return _unary("gelu", x)
+
+
+def silu(x):
+    return _unary("silu", x)
+
+
+def _binary(name: str, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    _check_tensor(a), _check_tensor(b)
+    if a.dtype != b.dtype:
+        raise ValueError("dtype mismatch for binary operation")
+    dt = _dtype(a)
+    if name == "divide" and dt != FLOAT32:
+        raise ValueError("division only supports float32 tensors")
+    shape, ls, rs = plan.broadcast(list(a.shape), list(b.shape))
+    out = torch.empty(shape, dtype=a.dtype, device=a.device)
+    same = list(a.shape) == list(b.shape)
+    meta = [] if same else list(shape) + ls + rs
+    check(lib().tcx_sm100_binary(_stream(), OP[name], dt, _ptr(a), _ptr(b), _ptr(out), out.numel(),
+                                 i64_array(meta) if meta else None, 0 if same else len(shape)))
+    return out
+
+
+def add(a, b):
+    return _binary("add", a, b)
+
+
+def subtract(a, b):
+    return _binary("subtract", a, b)
+
+
+def multiply(a, b):
+    return _binary("multiply", a, b)
+
+
+def divide(a, b):
+    return _binary("divide", a, b)
+
+
+def clip(x: torch.Tensor, lower=None, upper=None) -> torch.Tensor:
+    """tensor.py:858-876: scalar or tensor bounds, None leaves that side open."""
+    _check_tensor(x)
+    dt = _dtype(x)
+    if lower is None and upper is None:
+        raise ValueError("clip requires at least one bound")
+    bounds = []
+    for i, v in enumerate((lower, upper)):
+        if v is None:
+            v = (-math.inf if i == 0 else math.inf) if dt == FLOAT32 else (-(2**31) if i == 0 else 2**31 - 1)
+        if not isinstance(v, torch.Tensor):
+            v = torch.tensor(v, dtype=x.dtype, device=x.device)
+        if v.dtype != x.dtype:
+            raise ValueError("clip input dtypes must match")
+        bounds.append(v.contiguous())
+    shape = list(x.shape)
+    for t in (x, *bounds):
+        shape = plan.broadcast(shape, list(t.shape))[0]
+    meta = list(shape)
+    for t in (x, *bounds):
+        meta += plan.broadcast(list(t.shape), shape)[1]
+    out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    check(lib().tcx_sm100_clip(_stream(), dt, _ptr(x), _ptr(bounds[0]), _ptr(bounds[1]), _ptr(out),
+                               out.numel(), i64_array(meta), len(shape)))
+    return out
+
+
+def relu(x: torch.Tensor) -> torch.Tensor:
+    """ReLU as tensor.cx spells it: clip(x, lower=0)."""
+    return clip(x, 0, None)
+
+
+def bias_act(x: torch.Tensor, bias: torch.Tensor | None, act: str = "silu") -> torch.Tensor:
+    """Fused chain act(x + bias[-1 axis]) in one pass (the add + activation pair)."""
+    _check_tensor(x)
+    cols = x.shape[-1] if x.dim() else 1
+    if bias is not None:
+        _check_tensor(bias, "bias")
+        if tuple(bias.shape) != (cols,):
+            raise ValueError("bias must match the last axis")
+    out = torch.empty_like(x)
+    rows = x.numel() // cols if cols else 0
+    check(lib().tcx_sm100_bias_act(_stream(), _ptr(x), _ptr(bias), _ptr(out), rows, cols, ACT[act]))
+    return out

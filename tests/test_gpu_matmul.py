@@ -1,0 +1,157 @@
+"""GPU parity of float32 matmul against the CPU oracle, both kernels.
+
+Bar: relative Frobenius error <= 1e-4 * sqrt(K / 1024) (at least the 1e-4 floor)
+against the CPU reference, plus the reference tests' elementwise check
+(rtol = atol = 1e-4, tests/python/test_cuda_primitives.py:9-21 and
+test_batched_matmul.py:14-50)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+PATHS = ["ffma", "tensor"]
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def frob_ok(got, ref, k):
+    tol = 1e-4 * math.sqrt(max(k, 1024) / 1024)
+    num = np.linalg.norm((got.astype(np.float64) - ref.astype(np.float64)).ravel())
+    den = np.linalg.norm(ref.astype(np.float64).ravel())
+    assert num <= tol * max(den, 1e-30), (num / max(den, 1e-30), tol)
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (2, 3, 4), (15, 17, 31), (17, 16, 15), (32, 33, 16), (0, 3, 4),
+                                   (3, 0, 4), (3, 4, 0), (65, 129, 67)])
+def test_reference_shapes(tcx, oracle, path, m, k, n):
+    rng = np.random.default_rng(7)
+    a = rng.normal(size=(m, k)).astype(np.float32)
+    b = rng.normal(size=(k, n)).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), path=path))
+    assert got.shape == (m, n)
+    np.testing.assert_allclose(got, oracle.matmul(a, b), rtol=1e-4, atol=1e-4)
+
+
+CASES = [((3,), (3,)), ((2, 3), (3,)), ((3,), (3, 4)), ((2, 3, 4), (2, 4, 5)), ((2, 3, 4), (4, 5)),
+         ((3, 4), (2, 4, 5)), ((4,), (2, 4, 5)), ((2, 3, 4), (4,)), ((2, 1, 3, 4), (1, 5, 4, 6)),
+         ((1, 2, 3, 4), (3, 1, 4, 5)), ((2, 1, 1, 3, 4), (1, 5, 1, 4, 2)), ((2, 17, 19), (1, 19, 33)),
+         ((2, 33, 17), (2, 17, 1)), ((0,), (0,)), ((2, 0), (0,)), ((0,), (0, 3)), ((2, 3, 0), (1, 0, 4)),
+         ((0, 3, 4), (1, 4, 2)), ((1, 3, 4), (0, 4, 2)), ((2, 0, 4), (2, 4, 3)), ((2, 3, 4), (2, 4, 0)),
+         ((0, 2, 3, 0), (1, 2, 0, 4)), ((2, 1, 0, 3), (1, 5, 3, 4)), ((3,), (0, 3, 4)), ((0, 2, 3), (3,)),
+         ((2, 1, 3, 4), (5, 4, 2))]
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("shapes", CASES)
+def test_batched_broadcast(tcx, oracle, path, shapes):
+    rng = np.random.default_rng(741)
+    a, b = [rng.uniform(-1, 1, s).astype(np.float32) for s in shapes]
+    got = host(tcx.matmul(dev(a), dev(b), path=path))
+    expected = oracle.matmul(a, b)
+    assert got.shape == expected.shape
+    np.testing.assert_allclose(got, expected, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_special_values(tcx, oracle, path):
+    a = np.array([[[np.nan, 1]], [[np.inf, 1]], [[-np.inf, -1]], [[-0., 0.]]], np.float32)
+    b = np.array([[1.], [2.]], np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), path=path))
+    np.testing.assert_allclose(got, oracle.matmul(a, b), rtol=1e-4, atol=1e-4, equal_nan=True)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_inf_in_large_product_takes_ieee_path(tcx, oracle, path):
+    rng = np.random.default_rng(2)
+    a = rng.uniform(-1, 1, (256, 512)).astype(np.float32)
+    b = rng.uniform(-1, 1, (512, 256)).astype(np.float32)
+    a[3, 7] = np.inf
+    got = host(tcx.matmul(dev(a), dev(b), path=path))
+    expected = oracle.matmul(a, b)
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(expected))
+    np.testing.assert_array_equal(np.isinf(got), np.isinf(expected))
+    fin = np.isfinite(expected)
+    np.testing.assert_allclose(got[fin], expected[fin], rtol=1e-4, atol=1e-4)
+
+
+def test_high_rank_and_grid_stride(tcx):
+    a = torch.ones((1,) * 300 + (2, 3), device="cuda")
+    b = torch.ones((3, 4), device="cuda")
+    r = tcx.matmul(a, b)
+    assert tuple(r.shape) == (1,) * 300 + (2, 4)
+    np.testing.assert_array_equal(host(r).reshape(2, 4), np.full((2, 4), 3, np.float32))
+    values = (np.arange(65537, dtype=np.float32) % 17).reshape(-1, 1, 1)
+    r = tcx.matmul(dev(values), dev(np.array([[2.]], np.float32)))
+    np.testing.assert_array_equal(host(r), values * 2)
+    with pytest.raises(ValueError):
+        tcx.matmul(torch.empty((2, 3), device="cuda"), torch.empty((2, 3), device="cuda"))
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 32), (256, 512, 128), (300, 300, 300), (129, 257, 33),
+                                   (512, 512, 1024), (1024, 1024, 1024), (2048, 2048, 2048), (1000, 4000, 100),
+                                   (384, 1280, 4096)])
+def test_tensor_path_sizes(tcx, oracle, m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), path="tensor"))
+    rows = slice(0, m) if m * n * k <= (1 << 28) else slice(m // 2 - 64, m // 2 + 64)
+    ref = oracle.matmul(a, b, rows=rows, batches=[0])[0]
+    frob_ok(got[rows], ref, k)
+    np.testing.assert_allclose(got[rows], ref, rtol=2e-4 * math.sqrt(k / 1024) + 1e-4, atol=1e-4 * math.sqrt(k))
+
+
+def test_tensor_path_is_more_accurate_than_tf32(tcx, oracle):
+    """3xTF32 must reach near-fp32 accuracy: far below single-pass TF32 error."""
+    rng = np.random.default_rng(4)
+    a = rng.uniform(-1, 1, (256, 2048)).astype(np.float32)
+    b = rng.uniform(-1, 1, (2048, 256)).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), path="tensor")).astype(np.float64)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    rel = np.linalg.norm(got - exact) / np.linalg.norm(exact)
+    assert rel < 2e-6, rel
+
+
+def test_batched_tensor_and_epilogue(tcx, oracle):
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (4, 256, 384)).astype(np.float32)
+    b = rng.uniform(-1, 1, (4, 384, 512)).astype(np.float32)
+    bias = rng.normal(size=512).astype(np.float32)
+    for path in PATHS:
+        for act in ("none", "silu", "relu"):
+            got = host(tcx.matmul(dev(a), dev(b), bias=dev(bias), act=act, path=path))
+            ref = oracle.add(oracle.matmul(a, b), bias)
+            if act == "silu":
+                ref = oracle.silu(ref)
+            elif act == "relu":
+                ref = oracle.relu(ref)
+            frob_ok(got, ref, 384)
+
+
+def test_broadcast_rhs_tensor_path(tcx, oracle):
+    rng = np.random.default_rng(6)
+    a = rng.uniform(-1, 1, (3, 200, 160)).astype(np.float32)
+    b = rng.uniform(-1, 1, (160, 300)).astype(np.float32)
+    frob_ok(host(tcx.matmul(dev(a), dev(b), path="tensor")), oracle.matmul(a, b), 160)
+    a2 = rng.uniform(-1, 1, (2, 1, 130, 64)).astype(np.float32)
+    b2 = rng.uniform(-1, 1, (1, 3, 64, 140)).astype(np.float32)
+    frob_ok(host(tcx.matmul(dev(a2), dev(b2), path="tensor")), oracle.matmul(a2, b2), 64)
+
+
+def test_linear_fused(tcx, oracle):
+    rng = np.random.default_rng(8)
+    x = rng.normal(size=(256, 784)).astype(np.float32)
+    w = rng.uniform(-1 / 28, 1 / 28, (512, 784)).astype(np.float32)
+    b = rng.normal(size=512).astype(np.float32)
+    frob_ok(host(tcx.linear(dev(x), dev(w), dev(b))), oracle.linear(x, w, b), 784)

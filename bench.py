@@ -1,0 +1,500 @@
+"""Benchmark of the tensor.cx hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (BASELINE.json metric, configs[1] at its largest size): float32 matmul
+C = A @ B at M = N = K = 8192, A, B ~ U(-1, 1) (seeded per rank), in TFLOP/s
+(2*M*N*K flops per step, whole job). A step is one tcx_sm100_matmul call: the
+3xTF32 split pre-pass plus the tcgen05 GEMM. Inputs (256 MiB each) exceed the
+126 MB L2, so no flush is needed between steps.
+
+N > 1 (torchrun, one rank per GPU, NCCL): every rank multiplies its own 8192^3 pair
+(weak scaling, no communication); the timed region is bracketed by barrier +
+synchronize, and the time is the max over ranks.
+
+Also measured in the same run, device-resident, and reported under "workloads"
+(each with its own roofline fraction): row softmax / rmsnorm / layernorm on
+[16384, 4096] (rows sharded over ranks) and softmax on [4096, 32768]; full
+reductions over 2^28 float32 (sum, argmax) and int32 (sum), sharded over ranks and
+combined by an NCCL all-gather of 16-byte partial records; batched matmul
+[64, 2048, 2048]^2 with the fused bias + SiLU epilogue, batch sharded over ranks.
+
+`--impl reference` times the reference's own CPU matmul (cpu::matmul, compiled from
+the tensor.cx sources into oracle/_ref) on row slices of the same 8192^3 product,
+on all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SIZE = 8192
+METRIC = "fp32 matmul TFLOP/s (8192^3, 3xTF32 on tcgen05)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--size", type=int, default=SIZE)
+    p.add_argument("--no-workloads", action="store_true", help="headline only")
+    return p.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_matmul_rate(size: int, threads: int, rows_per_thread: int, a=None, b=None):
+    """Reference cpu::matmul on `threads` disjoint row slices of the size^3 product
+    (identical per-element arithmetic to the full product). Returns (flops/s, rows)."""
+    from oracle.oracle import Reference
+    ref = Reference()
+    rng = np.random.default_rng(0)
+    if a is None:
+        a = (rng.random((threads * rows_per_thread, size), dtype=np.float32) * 2 - 1)
+        b = (rng.random((size, size), dtype=np.float32) * 2 - 1)
+    outs = [None] * threads
+
+    def work(t):
+        r0 = t * rows_per_thread
+        outs[t] = ref.matmul_rows(a, b, r0, r0 + rows_per_thread)
+
+    t0 = time.perf_counter()
+    pool = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    for th in pool:
+        th.start()
+    for th in pool:
+        th.join()
+    dt = time.perf_counter() - t0
+    rows = threads * rows_per_thread
+    return 2.0 * rows * size * size / dt, rows, dt, np.concatenate(outs)
+
+
+def host_threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle.oracle import Reference
+    if not Reference.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtcx_ref.so was not built"}))
+        return
+    threads = host_threads()
+    size = args.size
+    rng = np.random.default_rng(0)
+    a = rng.random((threads, size), dtype=np.float32) * 2 - 1
+    b = rng.random((size, size), dtype=np.float32) * 2 - 1
+    for _ in range(args.warmup):
+        cpu_matmul_rate(size, threads, 1, a, b)
+    times = []
+    for _ in range(args.steps):
+        rate, rows, dt, _ = cpu_matmul_rate(size, threads, 1, a, b)
+        times.append(dt)
+    mean_dt = sum(times) / len(times)
+    value = 2.0 * threads * size * size / mean_dt / 1e12
+    sample = f"cpu::matmul on {threads} disjoint rows of the {size}^3 product per step ({threads} threads)"
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"fp32 matmul {size}^3 (row-sliced sample)", "sample_rows_per_step": threads},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (every 50 ms) of SM clock and throttle reasons."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+        self.windows = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu=timestamp,{self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        self.windows.append((t0, t1))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for ts, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            inside = any(a - 0.05 <= ts <= b + 0.05 for a, b in self.windows)
+            rows.append((inside, parts))
+        use = [p for inside, p in rows if inside] or [p for _, p in rows]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(p[2]) for p in use if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in use for i in range(4) if "Active" in p[6 + i] and "Not" not in p[6 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(use[0][3]) if use[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(use),
+                "power_w_max": max((float(p[4]) for p in use if p[4].replace(".", "").isdigit()), default=None)}
+
+
+# ------------------------------------------------------------------ GPU arm
+class Timer:
+    """CUDA-event timing on the current stream, max over ranks."""
+
+    def __init__(self, torch, dist, world):
+        self.torch, self.dist, self.world = torch, dist, world
+
+    def run(self, step, steps, warmup, sampler=None):
+        torch = self.torch
+        for _ in range(warmup):
+            step()
+        self.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.time()
+        start.record()
+        for _ in range(steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        t1 = time.time()
+        self.barrier()
+        if sampler:
+            sampler.mark(t0, t1)
+        ms = start.elapsed_time(end)
+        return self.max_over_ranks(ms)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, value):
+        if self.world == 1:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def read_timer(lib):
+    names = ctypes.create_string_buffer(64 * 64)
+    launches = (ctypes.c_int64 * 64)()
+    total = (ctypes.c_double * 64)()
+    n = ctypes.c_int32(0)
+    lib.tcx_sm100_timer_read(names, len(names), launches, total, 64, ctypes.byref(n))
+    out = {}
+    raw = names.raw.split(b"\0")
+    for i in range(n.value):
+        out[raw[i].decode()] = (int(launches[i]), float(total[i]))
+    return out
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "of measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "of fallback"
+
+
+def gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+    from tensorcx_b200 import _abi, ops
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    lib = _abi.lib()
+    assert lib.tcx_sm100_device_supported(local) == 0, lib.tcx_sm100_last_error()
+    timer = Timer(torch, dist, world)
+    pk, pk_note = peaks()
+    hbm_peak = float(pk["hbm_gbs"])
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    sampler = ClockSampler(visible[local] if local < len(visible) else str(local))
+    sampler.start()
+    size = args.size
+    flops = 2.0 * size ** 3
+
+    # cuBLAS TF32 rate on this GPU now: the denominator of the 3xTF32 roofline
+    torch.backends.cuda.matmul.allow_tf32 = True
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    ta = torch.rand(size, size, device="cuda", generator=g)
+    tb = torch.rand(size, size, device="cuda", generator=g)
+    tf32_ms = timer.run(lambda: torch.matmul(ta, tb), 10, 3)
+    tf32_tflops = flops * 10 / (tf32_ms * 1e-3) / 1e12
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sgemm_ms = timer.run(lambda: torch.matmul(ta, tb), 3, 1)
+    sgemm_tflops = flops * 3 / (sgemm_ms * 1e-3) / 1e12
+    del ta, tb
+    torch.cuda.empty_cache()
+
+    # headline inputs (host-generated, seeded per rank, then resident in HBM)
+    rng = np.random.default_rng(rank)
+    a_host = torch.from_numpy(rng.random((size, size), dtype=np.float32) * 2 - 1).pin_memory()
+    b_host = torch.from_numpy(rng.random((size, size), dtype=np.float32) * 2 - 1).pin_memory()
+    c_host = torch.empty((size, size), dtype=torch.float32).pin_memory()
+    a = a_host.cuda()
+    b = b_host.cuda()
+    c = torch.empty((size, size), dtype=torch.float32, device="cuda")
+    ws_bytes = lib.tcx_sm100_matmul_workspace_bytes(size, size, size, 1, 1, 0)
+    ws_buf = torch.empty(ws_bytes + 1024, dtype=torch.uint8, device="cuda")
+    ws = ctypes.c_void_p((ws_buf.data_ptr() + 1023) // 1024 * 1024)
+    one = _abi.i64_array([])
+
+    def step():
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        _abi.check(lib.tcx_sm100_matmul(s, ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                                        ctypes.c_void_p(c.data_ptr()), size, size, size, 1, one, one, one, 0,
+                                        None, 0, 0, ws, ws_bytes))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    ms = timer.run(step, args.steps, 0, sampler)
+    lib.tcx_sm100_timer_enable(0)
+    kernels = read_timer(lib)
+    ms_per_step = ms / args.steps
+    value = world * flops / (ms_per_step * 1e-3) / 1e12
+    gemm_launches, gemm_ms = kernels.get("gemm_tf32x3", (0, 0.0))
+    gemm_avg_ms = gemm_ms / max(gemm_launches, 1)
+    gemm_avg_ms = timer.max_over_ranks(gemm_avg_ms)
+    achieved = flops / (gemm_avg_ms * 1e-3) / 1e12
+    peak_3x = tf32_tflops / 3.0
+    launches = sum(v[0] for v in kernels.values())
+
+    # e2e: host buffers in, host result out, through the same C-ABI call
+    def e2e_step():
+        a.copy_(a_host, non_blocking=True)
+        b.copy_(b_host, non_blocking=True)
+        step()
+        c_host.copy_(c, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_ms = timer.run(e2e_step, e2e_steps, 1, sampler) / e2e_steps
+    e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+
+    # CPU baseline (rank 0, N = 1): the reference's cpu::matmul on a row sample
+    cpu = None
+    if rank == 0 and world == 1:
+        from oracle.oracle import Reference
+        if Reference.available():
+            threads = host_threads()
+            a_np = a_host.numpy()
+            b_np = b_host.numpy()
+            # calibrate one row, then size the sample to about 10 s of CPU work
+            r1, _, dt1, _ = cpu_matmul_rate(size, 1, 1, a_np[:1], b_np)
+            per_thread = max(1, min(8, int(10.0 / max(dt1, 1e-3))))
+            rate, rows, dt, got_rows = cpu_matmul_rate(size, threads, per_thread,
+                                                       a_np[:threads * per_thread], b_np)
+            step()
+            torch.cuda.synchronize()
+            gpu_rows = c[:rows].cpu().numpy()
+            rel = float(np.linalg.norm(gpu_rows.astype(np.float64) - got_rows) / np.linalg.norm(got_rows))
+            cpu = {"value": rate / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                   "sample": f"cpu::matmul (reference, -O3) on {rows} rows of the {size}^3 product, "
+                             f"{threads} threads, {dt:.1f} s",
+                   "gpu_rows_rel_frobenius_error": rel,
+                   "tolerance": 1e-4 * math.sqrt(size / 1024)}
+    del a_host, b_host, c_host
+
+    workloads = {} if args.no_workloads else secondary(args, torch, dist, lib, ops, timer, world, rank,
+                                                       hbm_peak, peak_3x, sampler)
+    del a, b, c, ws_buf
+    sampler.stop()
+    clocks = sampler.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (3xTF32 split on tf32 tensor cores, f32 accumulate)",
+            "data": "synthetic (seeded U(-1,1), per-rank seed)",
+            "config": {"workload": f"fp32 matmul M=N=K={size} (BASELINE configs[1], largest size)",
+                       "per_gpu": f"{size}^3", "parallelism": f"independent products, {world} GPU(s)",
+                       "l2": "inputs (256 MiB each) larger than the 126 MB L2; no flush"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
+                         "frac": achieved / peak_3x, "traffic": None,
+                         "kernel": "gemm_tf32x3 (tcgen05.mma kind::tf32 x3 per k-step)",
+                         "kernel_ms": gemm_avg_ms,
+                         "peak_note": f"cuBLAS TF32 GEMM {size}^3 measured in this run = {tf32_tflops:.1f} TFLOP/s, "
+                                      f"/3 for 3xTF32 (MEASURED_PEAKS bf16 {pk.get('bf16_tflops')} TFLOP/s "
+                                      f"{pk_note}; bf16/6 = {float(pk.get('bf16_tflops', 0)) / 6:.1f})"},
+            "context": {"cublas_tf32_tflops": tf32_tflops, "cublas_fp32_sgemm_tflops": sgemm_tflops,
+                        "split_prepass_ms": (kernels.get("split_rows", (0, 0))[1] + kernels.get("split_cols", (0, 0))[1])
+                        / max(args.steps, 1)},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * size * size * 4,
+                    "d2h_bytes_per_step": size * size * 4, "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "kernels_in_timed_region": {k: {"launches": v[0], "total_ms": v[1]} for k, v in kernels.items()},
+            "clocks": clocks,
+            "workloads": workloads,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x, sampler):
+    """The other hot-path workloads of BASELINE configs[2..4], device-resident."""
+    out = {}
+    steps = max(5, args.steps)
+    g = torch.Generator(device="cuda").manual_seed(77 + rank)
+
+    def hbm_entry(name, bytes_per_step, ms_step, kernel, kernels, extra=None):
+        k_launches, k_ms = kernels.get(kernel, (0, 0.0))
+        k_avg = timer.max_over_ranks(k_ms / max(k_launches, 1))
+        achieved = bytes_per_step / (k_avg * 1e-3) / 1e9 if k_avg else None
+        d = {"value": world * bytes_per_step / (ms_step * 1e-3) / 1e9, "unit": "GB/s",
+             "ms_per_step": ms_step,
+             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                          "frac": achieved / hbm_peak if achieved else None, "kernel": kernel,
+                          "kernel_ms": k_avg}}
+        if extra:
+            d.update(extra)
+        out[name] = d
+
+    # row ops, [16384, 4096] and [4096, 32768]: rows sharded over ranks
+    for name, (rows, cols), op in [("softmax_16384x4096", (16384, 4096), "softmax"),
+                                   ("rmsnorm_16384x4096", (16384, 4096), "rmsnorm"),
+                                   ("layernorm_16384x4096", (16384, 4096), "layernorm"),
+                                   ("softmax_4096x32768", (4096, 32768), "softmax")]:
+        r = rows // world
+        x = torch.randn(r, cols, device="cuda", generator=g) * 3
+        y = torch.empty_like(x)
+        fn = getattr(ops, op)
+        kw = {} if op == "softmax" else {"eps": 1e-5}
+
+        def st(x=x, fn=fn, kw=kw):
+            return fn(x, axis=-1, **kw)
+        st()
+        read_timer(lib)
+        lib.tcx_sm100_timer_enable(1)
+        ms = timer.run(st, steps, 2, sampler) / steps
+        lib.tcx_sm100_timer_enable(0)
+        kern = read_timer(lib)
+        hbm_entry(name, 8.0 * r * cols, ms, "row_kernel", kern,
+                  {"config": f"[{rows},{cols}] float32, rows sharded {world} way(s), 8 B/element"})
+        del x, y
+
+    # full reductions over 2^28 elements: shard + per-rank record + NCCL all-gather
+    total = 1 << 28
+    shard = total // world
+    base = rank * shard
+    xf = torch.randn(shard, device="cuda", generator=g)
+    xi = torch.randint(-1000, 1001, (shard,), device="cuda", generator=g, dtype=torch.int32)
+    gathered = torch.empty((world, 16), dtype=torch.uint8, device="cuda")
+    for name, x, op in [("sum_f32_2^28", xf, "sum"), ("argmax_f32_2^28", xf, "argmax"),
+                        ("sum_i32_2^28", xi, "sum"), ("max_i32_2^28", xi, "max")]:
+        def st(x=x, op=op):
+            rec = ops.reduce_partial(x, op, index_base=base)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, rec)
+                recs = gathered
+            else:
+                recs = rec.view(1, 16)
+            return ops.reduce_combine(recs, op, x.dtype, total)
+        st()
+        read_timer(lib)
+        lib.tcx_sm100_timer_enable(1)
+        ms = timer.run(st, steps, 2, sampler) / steps
+        lib.tcx_sm100_timer_enable(0)
+        kern = read_timer(lib)
+        hbm_entry(name, 4.0 * shard, ms, "reduce_stage1", kern,
+                  {"config": f"2^28 elements total, {world} shard(s), partials combined by "
+                             f"{'NCCL all_gather' if world > 1 else 'the combine kernel'} in rank order"})
+    del xf, xi
+
+    # batched matmul + fused bias + SiLU: [64, 2048, 2048]^2, batch sharded
+    nb = 64 // world
+    a = torch.rand(nb, 2048, 2048, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(nb, 2048, 2048, device="cuda", generator=g) * 2 - 1
+    bias = torch.randn(2048, device="cuda", generator=g)
+
+    def st():
+        return ops.matmul(a, b, bias=bias, act="silu")
+    st()
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    ms = timer.run(st, max(3, steps // 2), 1, sampler) / max(3, steps // 2)
+    lib.tcx_sm100_timer_enable(0)
+    kern = read_timer(lib)
+    fl = 2.0 * nb * 2048 ** 3
+    k_launches, k_ms = kern.get("gemm_tf32x3", (0, 0.0))
+    k_avg = timer.max_over_ranks(k_ms / max(k_launches, 1))
+    out["bmm_bias_silu_64x2048^3"] = {
+        "value": world * fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+        "config": f"[64,2048,2048]^2 + bias[2048] + SiLU fused in the GEMM epilogue, batch sharded {world} way(s)",
+        "roofline": {"bound": "tensor", "achieved": fl / (k_avg * 1e-3) / 1e12 if k_avg else None,
+                     "peak": peak_3x, "unit": "TFLOP/s",
+                     "frac": (fl / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
+                     "kernel": "gemm_tf32x3", "kernel_ms": k_avg}}
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

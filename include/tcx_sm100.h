@@ -78,6 +78,17 @@ int tcx_sm100_device_supported(int device);
  * waits record a timeout there instead of hanging (0 = no error). */
 int tcx_sm100_device_error(int device, int* code);
 
+/* Device timing of this library's kernel launches, the reference's DeviceTimer
+ * contract (cpp/tensorcx/backends/cuda/cuda_profiling.h:23-64): while enabled on the
+ * calling thread, every kernel the entry points launch is bracketed by CUDA events
+ * on its own stream. tcx_sm100_timer_read waits for the recorded events and returns
+ * one entry per kernel name: launch count and total device milliseconds. `names`
+ * receives up to `capacity` NUL-separated names (each at most 63 bytes). Reading
+ * clears the records. Disabled by default; costs nothing when disabled. */
+int tcx_sm100_timer_enable(int enable);
+int tcx_sm100_timer_read(char* names, size_t names_bytes, int64_t* launches, double* total_ms,
+                         int32_t capacity, int32_t* entries);
+
 /* --------------------------------------------------------------- reductions --- */
 
 /* One-axis reduction or normalization over a contiguous tensor viewed as

@@ -13,6 +13,6 @@ __all__ = ["lib", "plan", "ops"]
 
 def __getattr__(name):
     if name == "ops":
-        from . import ops
-        return ops
+        import importlib
+        return importlib.import_module(".ops", __name__)
     raise AttributeError(name)

@@ -34,6 +34,9 @@ SIGNATURES = {
     "tcx_sm100_abi_version": (ctypes.c_int, []),
     "tcx_sm100_device_supported": (ctypes.c_int, [ctypes.c_int]),
     "tcx_sm100_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "tcx_sm100_timer_enable": (ctypes.c_int, [ctypes.c_int]),
+    "tcx_sm100_timer_read": (ctypes.c_int, [ctypes.c_char_p, _sz, _i64p, ctypes.POINTER(ctypes.c_double), _i32,
+                                            ctypes.POINTER(ctypes.c_int32)]),
     "tcx_sm100_axis": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _sz]),
     "tcx_sm100_axis_workspace_bytes": (_sz, [ctypes.c_int, _i64, _i64, _i64]),
     "tcx_sm100_affine_norm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),

@@ -37,6 +37,21 @@ __device__ __forceinline__ void record_device_error(int* word, int code) {
 }
 int* device_error_word();
 
+// Brackets the kernel launches of its scope with CUDA events when the calling
+// thread enabled tcx_sm100_timer_enable (runtime.cu); otherwise does nothing.
+class TimedLaunch {
+ public:
+  TimedLaunch(const char* name, cudaStream_t stream);
+  ~TimedLaunch();
+  TimedLaunch(const TimedLaunch&) = delete;
+  TimedLaunch& operator=(const TimedLaunch&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t stream_;
+  cudaEvent_t start_ = nullptr;
+};
+
 constexpr int kMaxRank = 16;
 
 // Small by-value metadata block passed as a kernel parameter (no per-call

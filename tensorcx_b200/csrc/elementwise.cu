@@ -211,6 +211,7 @@ int tcx_sm100_unary(tcx_stream_t stream, int op, const float* input, float* outp
   if (count == 0) return TCX_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int grid = ew_grid(count);
+  TimedLaunch timer("unary", s);
   if (op == TCX_OP_EXP) unary_kernel<TCX_OP_EXP><<<grid, 256, 0, s>>>(input, output, count);
   else if (op == TCX_OP_GELU) unary_kernel<TCX_OP_GELU><<<grid, 256, 0, s>>>(input, output, count);
   else unary_kernel<TCX_OP_SILU><<<grid, 256, 0, s>>>(input, output, count);
@@ -242,6 +243,7 @@ int tcx_sm100_binary(tcx_stream_t stream, int op, int dtype, const void* lhs, co
     m.rank = r;
     for (int a = 0; a < r; ++a) { m.v[a] = shape[a]; m.v[r + a] = st[0][a]; m.v[2 * r + a] = st[1][a]; }
   }
+  TimedLaunch timer("binary", s);
   if (dtype == TCX_FLOAT32) {
     auto* a = static_cast<const float*>(lhs); auto* b = static_cast<const float*>(rhs);
     auto* o = static_cast<float*>(output);
@@ -276,6 +278,7 @@ int tcx_sm100_clip(tcx_stream_t stream, int dtype, const void* input, const void
     for (int k = 0; k < 3; ++k) m.v[(k + 1) * r + a] = st[k][a];
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  TimedLaunch timer("clip", s);
   clip_kernel<<<ew_grid(count), 256, 0, s>>>(dtype == TCX_FLOAT32, static_cast<const uint32_t*>(input),
                                              static_cast<const uint32_t*>(lower),
                                              static_cast<const uint32_t*>(upper),
@@ -294,6 +297,7 @@ int tcx_sm100_bias_act(tcx_stream_t stream, const float* input, const float* bia
                    ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(output) |
                      reinterpret_cast<uintptr_t>(bias)) % 16) == 0;
   const int grid = ew_grid(rows * cols);
+  TimedLaunch timer("bias_act", s);
 #define TCX_BA(A)                                                                              \
   if (vec) bias_act_kernel<A, true><<<grid, 256, 0, s>>>(input, bias, output, rows, cols);     \
   else bias_act_kernel<A, false><<<grid, 256, 0, s>>>(input, bias, output, rows, cols);

@@ -621,7 +621,10 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
   if (!use_tensor(m, n, k, path)) {
     const int64_t tiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
-    gemm_ffma_kernel<<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
+    {
+      TimedLaunch timer("gemm_ffma", s);
+      gemm_ffma_kernel<<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
+    }
     return launch_status("ffma matmul");
   }
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return invalid("matmul extent too large for the tensor path");
@@ -639,10 +642,16 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
   {
     const int64_t total = nba * m * lay.kp;
     const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 16LL * sms));
-    split_rows<<<grid, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
+    {
+      TimedLaunch timer("split_rows", s);
+      split_rows<<<grid, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
+    }
     const int64_t tiles = nbb * ceil_div(n, 32) * (lay.kp / 32);
     const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 32LL * sms));
-    split_cols<<<grid_b, dim3(32, 8), 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
+    {
+      TimedLaunch timer("split_cols", s);
+      split_cols<<<grid_b, dim3(32, 8), 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
+    }
   }
   if (int st = launch_status("matmul split pre-pass")) return st;
 
@@ -675,12 +684,18 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
   g.bm = bm;
   const int64_t tiles = batches * g.tiles_m * g.tiles_n;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
-  gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
+  {
+    TimedLaunch timer("gemm_tf32x3", s);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
+  }
   if (int st = launch_status("tcgen05 matmul")) return st;
   // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
   const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
   const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
-  gemm_ffma_kernel<<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+  {
+    TimedLaunch timer("gemm_ffma_fallback", s);
+    gemm_ffma_kernel<<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+  }
   return launch_status("matmul fallback");
 }
 

@@ -37,10 +37,14 @@ __device__ __forceinline__ T max_identity() {
   else return INT32_MIN;
 }
 
-__device__ __forceinline__ float4 ldg_stream(const float4* p) {
-  float4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+// 128-bit streaming load into integer registers. The words stay integers end to end:
+// routed through float registers, `bits ^ 0x80000000` may be folded into a float
+// negation, which is free to canonicalize NaN payloads (and int32 words that look
+// like NaNs), breaking both exact int32 keys and first-NaN-payload semantics.
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
 }
@@ -60,7 +64,7 @@ __device__ __forceinline__ void take(Acc& a, int slot, uint32_t bits, int64_t in
     a.u[slot] += bits;
   } else {
     const uint32_t k = (K == kBestMax) ? key_max(bits, FP) : key_min(bits, FP);
-    if (k > a.key) {  // strict: earlier indices win ties within a thread
+    if (k > a.key || a.idx == INT64_MAX) {  // strict: earlier indices win ties within a thread
       a.key = k;
       a.idx = index;
     }
@@ -68,7 +72,8 @@ __device__ __forceinline__ void take(Acc& a, int slot, uint32_t bits, int64_t in
 }
 
 __device__ __forceinline__ bool better(uint32_t ka, int64_t ia, uint32_t kb, int64_t ib) {
-  return ka > kb || (ka == kb && ia < ib);
+  // an empty slot (index INT64_MAX) never beats a real element
+  return ka > kb || (ka == kb && ia < ib) || (ib == INT64_MAX && ia != INT64_MAX);
 }
 
 // Folds (sum or key/index) across the CTA in a fixed order; result in thread 0.
@@ -123,29 +128,29 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
     const int tid = threadIdx.x;
     int64_t tail_begin = begin;
     if (VEC && end > begin) {
-      const float4* xv = reinterpret_cast<const float4*>(xr + begin);
+      const uint4* xv = reinterpret_cast<const uint4*>(xr + begin);
       const int64_t nvec = (end - begin) >> 2;
       int64_t i = tid;
       for (; i + (kUnroll - 1) * kStage1Threads < nvec; i += kUnroll * kStage1Threads) {
-        float4 v[kUnroll];
+        uint4 v[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) v[u] = ldg_stream(xv + i + u * kStage1Threads);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int64_t e = begin + 4 * (i + u * kStage1Threads) + index_base;
-          take<K, FP>(a, 4 * u + 0, __float_as_uint(v[u].x), e + 0);
-          take<K, FP>(a, 4 * u + 1, __float_as_uint(v[u].y), e + 1);
-          take<K, FP>(a, 4 * u + 2, __float_as_uint(v[u].z), e + 2);
-          take<K, FP>(a, 4 * u + 3, __float_as_uint(v[u].w), e + 3);
+          take<K, FP>(a, 4 * u + 0, v[u].x, e + 0);
+          take<K, FP>(a, 4 * u + 1, v[u].y, e + 1);
+          take<K, FP>(a, 4 * u + 2, v[u].z, e + 2);
+          take<K, FP>(a, 4 * u + 3, v[u].w, e + 3);
         }
       }
       for (; i < nvec; i += kStage1Threads) {
-        const float4 v = ldg_stream(xv + i);
+        const uint4 v = ldg_stream(xv + i);
         const int64_t e = begin + 4 * i + index_base;
-        take<K, FP>(a, 0, __float_as_uint(v.x), e + 0);
-        take<K, FP>(a, 1, __float_as_uint(v.y), e + 1);
-        take<K, FP>(a, 2, __float_as_uint(v.z), e + 2);
-        take<K, FP>(a, 3, __float_as_uint(v.w), e + 3);
+        take<K, FP>(a, 0, v.x, e + 0);
+        take<K, FP>(a, 1, v.y, e + 1);
+        take<K, FP>(a, 2, v.z, e + 2);
+        take<K, FP>(a, 3, v.w, e + 3);
       }
       tail_begin = begin + nvec * 4;
     }
@@ -422,6 +427,7 @@ void launch_stage1(cudaStream_t s, const uint32_t* x, int64_t rows, int64_t n, i
                    tcx_partial* parts, const Stage1Grid& g) {
   const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (n % 4 == 0 || rows == 1);
   dim3 grid(g.parts, g.rows_y);
+  TimedLaunch timer("reduce_stage1", s);
   if (vec) reduce_stage1<K, FP, true><<<grid, kStage1Threads, 0, s>>>(x, rows, n, g.chunk, index_base, parts);
   else reduce_stage1<K, FP, false><<<grid, kStage1Threads, 0, s>>>(x, rows, n, g.chunk, index_base, parts);
 }
@@ -437,6 +443,7 @@ int tree_reduce(cudaStream_t s, int op, int dtype, const void* input, int64_t ro
   const bool fp = dtype == TCX_FLOAT32;
   const int kind = kind_of(op, dtype);
   const int grid2 = static_cast<int>(std::min<int64_t>(rows, 65535));
+  TimedLaunch timer("reduce_tree", s);
   switch (kind) {
     case kSumF:
       launch_stage1<kSumF, true>(s, x, rows, n, index_base, parts, g);
@@ -521,6 +528,7 @@ int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* outp
         return tree_reduce(s, op, dtype, input, rows, reduce, 0, out_mode(op), output, ws, ws_bytes);
     }
     const int grid = static_cast<int>(std::min<int64_t>(ceil_div(rows, kRowsPerCta), 65535LL * 16));
+    TimedLaunch timer("rows_ordered", s);
     if (f32) {
       auto* x = static_cast<const float*>(input);
       auto* o = static_cast<float*>(output);
@@ -536,6 +544,7 @@ int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* outp
     return launch_status("ordered row reduction");
   }
   const int grid = grid_for(count, 256);
+  TimedLaunch timer("axis_strided", s);
   if (f32) {
     auto* x = static_cast<const float*>(input);
     auto* o = static_cast<float*>(output);
@@ -559,7 +568,11 @@ using namespace tcx;
 extern "C" {
 
 size_t tcx_sm100_reduce_workspace_bytes(int64_t count) {
-  return tree_workspace(1, std::max<int64_t>(count, 1));
+  // Upper bound of tree_workspace(rows, n) over every split rows * n == count that
+  // runs the tree (n >= 1024): fewer rows than the CTA target use at most that many
+  // records; more rows use one record per row.
+  const int64_t records = std::max<int64_t>(4LL * sm_count(), count / 1024 + 1);
+  return static_cast<size_t>(records) * sizeof(tcx_partial);
 }
 
 int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* input,
@@ -571,6 +584,7 @@ int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* inp
     if (op == TCX_OP_MAX || op == TCX_OP_MIN || op == TCX_OP_ARGMAX)
       return invalid("reduction requires a non-empty input");
     // sum of nothing is 0, mean of nothing is NaN (cpu_backend.cpp:1146-1147)
+    TimedLaunch timer("fill_word", reinterpret_cast<cudaStream_t>(stream));
     fill_word<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<uint32_t*>(output), op == TCX_OP_MEAN ? 0x7fc00000u : 0u);
     return launch_status("empty reduction");
@@ -597,6 +611,7 @@ int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype, const tcx_p
   if (nparts <= 0) return invalid("combine requires at least one record");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int mode = out_mode(op);
+  TimedLaunch timer("reduce_combine", s);
   switch (kind_of(op, dtype)) {
     case kSumF: combine_records<kSumF><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
     case kSumI: combine_records<kSumI><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
@@ -632,6 +647,7 @@ int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* in
   Meta meta;
   if (int st = load_meta(meta, index_metadata, rank)) return st;
   const int grid = grid_for(groups, 256);
+  TimedLaunch timer("reduce_axes_general", s);
   if (dtype == TCX_FLOAT32) {
     auto* x = static_cast<const float*>(input);
     auto* o = static_cast<float*>(output);
@@ -669,6 +685,7 @@ int tcx_sm100_min_argmax(tcx_stream_t stream, int op, int dtype, const void* inp
   Meta meta;
   if (int st = load_meta(meta, index_metadata, rank)) return st;
   const int grid = grid_for(groups, 256);
+  TimedLaunch timer("min_argmax_general", s);
   auto* x = static_cast<const uint32_t*>(input);
   auto* o = static_cast<uint32_t*>(output);
   if (op == TCX_OP_ARGMAX) {

@@ -319,6 +319,7 @@ template <int OP, int THREADS, int VPT>
 void launch_row(cudaStream_t s, const float* x, float* out, int64_t rows, int64_t n, float eps,
                 const float* w, const float* b, bool vec) {
   const int grid = static_cast<int>(std::min<int64_t>(rows, 1LL << 20));
+  TimedLaunch timer("row_kernel", s);
   if (vec) row_kernel<OP, THREADS, VPT, true><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
   else row_kernel<OP, THREADS, VPT, false><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
 }
@@ -330,7 +331,10 @@ int run_rows(cudaStream_t s, const float* x, float* out, int64_t outer, int64_t 
   if (inner != 1) {
     const int64_t count = outer * inner;
     const int grid = static_cast<int>(std::min<int64_t>(ceil_div(count, 256), 32LL * sm_count()));
-    row_strided<OP><<<grid, 256, 0, s>>>(x, out, outer, reduce, inner, eps, w, b);
+    {
+      TimedLaunch timer("row_strided", s);
+      row_strided<OP><<<grid, 256, 0, s>>>(x, out, outer, reduce, inner, eps, w, b);
+    }
     return launch_status("strided row op");
   }
   const int64_t n = reduce;
@@ -343,6 +347,7 @@ int run_rows(cudaStream_t s, const float* x, float* out, int64_t outer, int64_t 
   else if (n <= 32768) launch_row<OP, 1024, 8>(s, x, out, outer, n, eps, w, b, vec);
   else {
     const int grid = static_cast<int>(std::min<int64_t>(outer, 1LL << 20));
+    TimedLaunch timer("row_stream", s);
     row_stream<OP><<<grid, 1024, 0, s>>>(x, out, outer, n, eps, w, b);
   }
   return launch_status("row op");

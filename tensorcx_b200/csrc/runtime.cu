@@ -1,14 +1,28 @@
 // C-ABI runtime entry points: error reporting, device checks, the device error word.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 
 namespace tcx {
 namespace {
 thread_local std::string g_last_error;
+
+struct TimerRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+struct TimerState {
+  bool enabled = false;
+  std::vector<TimerRecord> records;
+};
+thread_local TimerState g_timer;
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
 std::once_flag g_sm_once[kMaxDevices];
@@ -31,6 +45,26 @@ int sm_count() {
     g_sm_count[dev] = n;
   });
   return g_sm_count[dev];
+}
+
+TimedLaunch::TimedLaunch(const char* name, cudaStream_t stream) : name_(name), stream_(stream) {
+  if (!g_timer.enabled) return;
+  if (cudaEventCreate(&start_) != cudaSuccess || cudaEventRecord(start_, stream_) != cudaSuccess) {
+    cudaGetLastError();
+    start_ = nullptr;
+  }
+}
+
+TimedLaunch::~TimedLaunch() {
+  if (!start_) return;
+  cudaEvent_t stop = nullptr;
+  if (cudaEventCreate(&stop) == cudaSuccess && cudaEventRecord(stop, stream_) == cudaSuccess) {
+    g_timer.records.push_back({name_, start_, stop});
+  } else {
+    cudaGetLastError();
+    cudaEventDestroy(start_);
+    if (stop) cudaEventDestroy(stop);
+  }
 }
 
 int* device_error_word() {
@@ -62,6 +96,50 @@ int tcx_sm100_device_supported(int device) {
     return TCX_UNAVAILABLE;
   }
   return TCX_OK;
+}
+
+int tcx_sm100_timer_enable(int enable) {
+  tcx::g_timer.enabled = enable != 0;
+  return TCX_OK;
+}
+
+int tcx_sm100_timer_read(char* names, size_t names_bytes, int64_t* launches, double* total_ms,
+                         int32_t capacity, int32_t* entries) {
+  tcx::clear_error();
+  std::vector<std::string> order;
+  std::map<std::string, std::pair<int64_t, double>> sums;
+  int status = TCX_OK;
+  for (auto& r : tcx::g_timer.records) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess) {
+      tcx::set_error("timer event failed");
+      status = TCX_INTERNAL;
+      cudaGetLastError();
+    }
+    if (!sums.count(r.name)) order.push_back(r.name);
+    auto& e = sums[r.name];
+    e.first += 1;
+    e.second += ms;
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  tcx::g_timer.records.clear();
+  int32_t n = 0;
+  size_t used = 0;
+  for (const auto& name : order) {
+    if (n >= capacity) break;
+    const size_t len = std::min<size_t>(name.size(), 63);
+    if (names && used + len + 1 <= names_bytes) {
+      std::memcpy(names + used, name.data(), len);
+      names[used + len] = '\0';
+      used += len + 1;
+    }
+    if (launches) launches[n] = sums[name].first;
+    if (total_ms) total_ms[n] = sums[name].second;
+    ++n;
+  }
+  if (entries) *entries = n;
+  return status;
 }
 
 int tcx_sm100_device_error(int device, int* code) {

@@ -12,6 +12,7 @@ allocator. Ops are asynchronous like torch ops; call torch.cuda.synchronize() (o
 """
 from __future__ import annotations
 
+import builtins
 import ctypes
 import math
 
@@ -75,8 +76,8 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
         _check_tensor(bias, "bias")
         if bias.shape != (p.n,) or bias.dtype != torch.float32:
             raise ValueError("bias must be float32 with shape (n,)")
-    nba = lhs.numel() // max(1, p.m * p.k) if p.m * p.k else 1
-    nbb = rhs.numel() // max(1, p.k * p.n) if p.k * p.n else 1
+    nba = lhs.numel() // builtins.max(1, p.m * p.k) if p.m * p.k else 1
+    nbb = rhs.numel() // builtins.max(1, p.k * p.n) if p.k * p.n else 1
     ws_bytes = lib().tcx_sm100_matmul_workspace_bytes(p.m, p.n, p.k, nba, nbb, MATMUL_PATH[path])
     keep, ws = _workspace(ws_bytes, lhs.device)
     batches = plan.numel(p.batch_shape) if out.numel() else 0

@@ -24,13 +24,42 @@ def close(a, b, tol):
     np.testing.assert_allclose(a, b, rtol=tol, atol=tol, equal_nan=True)
 
 
+def exact_row_op(op, x, axis, eps=1e-5):
+    """float64 evaluation of the reference formulas (cpu_backend.cpp:125-240)."""
+    x = x.astype(np.float64)
+    with np.errstate(all="ignore"):
+        if op == "softmax":
+            e = np.exp(x - np.max(x, axis=axis, keepdims=True))
+            return e / np.sum(e, axis=axis, keepdims=True)
+        if op == "rmsnorm":
+            return x / np.sqrt(np.mean(x * x, axis=axis, keepdims=True) + np.float32(eps))
+        mean = np.mean(x, axis=axis, keepdims=True)
+        return (x - mean) / np.sqrt(np.mean((x - mean) ** 2, axis=axis, keepdims=True) + np.float32(eps))
+
+
+def row_close(got, cpu, exact, tol=1e-5):
+    """Within the reference tolerance of the CPU result, or (elementwise) at least as
+    close to the float64 result as the CPU's own float32 result is. The CPU adds the
+    softmax denominator / norm statistics left to right in float32, so for wide rows
+    its own error can exceed 1e-5 (terms below half an ulp of the running sum are
+    dropped); a tree-ordered sum on the GPU is closer to exact there."""
+    got, cpu, exact = (np.asarray(v, np.float64) for v in (got, cpu, exact))
+    nan_ok = np.isnan(got) == np.isnan(cpu)
+    assert nan_ok.all(), "NaN placement differs"
+    fin = ~np.isnan(cpu)
+    near = np.abs(got - cpu) <= tol + tol * np.abs(cpu)
+    better = np.abs(got - exact) <= np.abs(cpu - exact) + 1e-7 * np.abs(exact)
+    bad = fin & ~(near | better)
+    assert not bad.any(), (got[bad][:5], cpu[bad][:5], exact[bad][:5])
+
+
 @pytest.mark.parametrize("op", ROW_OPS)
 @pytest.mark.parametrize("width", [1, 2, 7, 33, 255, 256, 257, 1023, 1024, 1025, 4095, 4096, 4097, 8192,
                                    12000, 16384, 32768, 40000])
 def test_row_ops_widths(tcx, oracle, op, width):
     rows = max(1, min(64, (1 << 20) // width))
     x = (np.random.default_rng(width).normal(size=(rows, width)) * 3).astype(np.float32)
-    close(host(getattr(tcx, op)(dev(x), axis=-1)), getattr(oracle, op)(x, -1), 1e-5)
+    row_close(host(getattr(tcx, op)(dev(x), axis=-1)), getattr(oracle, op)(x, -1), exact_row_op(op, x, -1))
 
 
 @pytest.mark.parametrize("op", ROW_OPS)

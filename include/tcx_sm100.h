@@ -152,6 +152,20 @@ int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* inp
                          int64_t count, void* output, void* workspace,
                          size_t workspace_bytes);
 
+/* tcx_sm100_reduce_all for callers that cannot allocate device memory (no
+ * counterpart in the reference). Some hosts own the whole device memory budget and
+ * forbid any other allocation, and some loops cannot pay the device-wide
+ * synchronization of cudaMalloc/cudaFree; this entry point needs no workspace. Its
+ * scratch is a fixed 16 KiB device array inside the library (1024 partial records),
+ * held on every device that loads the library until the process exits. The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress), so
+ * make that first call before any stream capture. Calls share the one array: two
+ * calls that overlap on the GPU (e.g. on different streams) race and must be
+ * serialized by the caller. Inputs whose stage-1 grid needs more than 1024 records
+ * are rejected with TCX_INVALID_ARGUMENT (never on GPUs with up to 256 SMs). */
+int tcx_sm100_reduce_all_noalloc(tcx_stream_t stream, int op, int dtype, const void* input,
+                                 int64_t count, void* output);
+
 /* Per-shard partial of a full-tensor reduction, for combining across GPUs. The
  * record is produced on the device; shards are combined in rank order by
  * tcx_sm100_reduce_combine, so the result does not depend on collective ordering.

@@ -46,6 +46,7 @@ SIGNATURES = {
                                             _vp, _sz]),
     "tcx_sm100_reduce_workspace_bytes": (_sz, [_i64]),
     "tcx_sm100_reduce_all": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _vp, _vp, _sz]),
+    "tcx_sm100_reduce_all_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _vp]),
     "tcx_sm100_reduce_partial": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _sz]),
     "tcx_sm100_reduce_combine": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i32, _i64, _vp]),
     "tcx_sm100_unary": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64]),

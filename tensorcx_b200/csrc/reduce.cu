@@ -19,6 +19,8 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
+#include <string>
 #include <type_traits>
 
 #include "common.cuh"
@@ -699,3 +701,58 @@ int tcx_sm100_min_argmax(tcx_stream_t stream, int op, int dtype, const void* inp
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Full-tensor reduction without any allocation (no counterpart in the reference).
+//
+// For callers that may not allocate device memory at all: hosts that hand the whole
+// GPU memory budget to their own allocator up front, or loops that cannot afford the
+// device-wide synchronization cudaMalloc/cudaFree imply. The stage-1 records live in
+// this fixed, file-scope device array instead of a caller-supplied workspace. Every
+// device that loads the library holds the array (16 KiB) until the process exits.
+namespace {
+constexpr int kNoAllocRecords = 1024;
+constexpr int kNoAllocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+void* g_noalloc_ptr[kNoAllocMaxDevices];
+cudaError_t g_noalloc_status[kNoAllocMaxDevices];
+}  // namespace
+
+static __device__ __align__(256) tcx_partial tcx_noalloc_records[kNoAllocRecords];
+
+extern "C" int tcx_sm100_reduce_all_noalloc(tcx_stream_t stream, int op, int dtype, const void* input,
+                                            int64_t count, void* output) {
+  clear_error();
+  if (!valid_reduce_op(op, dtype)) return invalid("unsupported full reduction op/dtype");
+  if (count < 0) return invalid("negative element count");
+  if (op == TCX_OP_ARGMAX && count > INT32_MAX) return invalid("argmax index range exceeds int32");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return launch_status("cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return invalid("device index beyond the no-allocation table");
+  // Once per device, with that device current: the host-side name of the array is
+  // only a stand-in, so the kernels get the device address looked up here.
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, tcx_noalloc_records);
+    g_noalloc_ptr[dev] = p;
+  });
+  if (g_noalloc_status[dev] != cudaSuccess) {
+    set_error(std::string("cudaGetSymbolAddress(no-allocation scratch): ") +
+              cudaGetErrorString(g_noalloc_status[dev]));
+    return TCX_INTERNAL;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (count == 0) {
+    if (op == TCX_OP_MAX || op == TCX_OP_MIN || op == TCX_OP_ARGMAX)
+      return invalid("reduction requires a non-empty input");
+    fill_word<<<1, 1, 0, s>>>(static_cast<uint32_t*>(output), op == TCX_OP_MEAN ? 0x7fc00000u : 0u);
+    return launch_status("empty reduction");
+  }
+  const size_t capacity = sizeof(tcx_partial) * kNoAllocRecords;
+  const size_t need = tree_workspace(1, count);
+  if (need > capacity)
+    return invalid("input needs more partial records than the fixed no-allocation scratch holds (1024)");
+  // Stage 1 writes every record stage 2 reads, so the previous call's contents never
+  // leak into a result and nothing has to be cleared first.
+  return tree_reduce(s, op, dtype, input, 1, count, 0, out_mode(op), output, g_noalloc_ptr[dev], capacity);
+}

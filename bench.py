@@ -42,7 +42,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SIZE = 8192
-METRIC = "fp32 matmul TFLOP/s (8192^3, 3xTF32 on tcgen05)"
+METRIC = "fp32 matmul TFLOP/s (M=N=K=8192)"
 
 
 def parse():
@@ -434,9 +434,10 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         del x, y
 
     # full reductions over 2^28 elements: shard + per-rank record + NCCL all-gather
+    from tensorcx_b200 import shard as sharding
     total = 1 << 28
-    shard = total // world
-    base = rank * shard
+    base, stop = sharding.shard_range(total, rank, world)
+    shard = stop - base
     xf = torch.randn(shard, device="cuda", generator=g)
     xi = torch.randint(-1000, 1001, (shard,), device="cuda", generator=g, dtype=torch.int32)
     gathered = torch.empty((world, 16), dtype=torch.uint8, device="cuda")

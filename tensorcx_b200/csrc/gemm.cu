@@ -169,51 +169,107 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-// A [nb][M][K] -> W [2*nb][M][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
-__global__ void split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows,
-                           int64_t k, int64_t kp, int* __restrict__ nonfinite) {
-  const int64_t total = nb * rows * kp;
+__device__ __forceinline__ void split_one(float x, float& hi, float& lo, bool& bad) {
+  bad |= !isfinite(x);
+  hi = tf32_rna(x);
+  lo = tf32_rna(__fsub_rn(x, hi));
+}
+
+__device__ __forceinline__ float4 ldg_f4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+// A [nb][rows][K] -> W [2*nb][rows][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
+// blockIdx.y walks rows, threads walk 4-wide K chunks: one 128-bit load and two
+// 128-bit stores per thread step when VEC (K % 4 == 0, 16-byte aligned A).
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows, int64_t k,
+           int64_t kp, int* __restrict__ nonfinite) {
   const int64_t plane = rows * kp;
+  const int64_t kq = kp >> 2;
   bool bad = false;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t b = i / plane, rem = i % plane, r = rem / kp, c = rem % kp;
-    const float x = c < k ? __ldg(a + (b * rows + r) * k + c) : 0.0f;
-    bad |= !isfinite(x);
-    const float hi = tf32_rna(x);
-    const float lo = tf32_rna(__fsub_rn(x, hi));
-    w[(2 * b) * plane + rem] = hi;
-    w[(2 * b + 1) * plane + rem] = lo;
+  for (int64_t row = blockIdx.y; row < nb * rows; row += gridDim.y) {
+    const int64_t b = row / rows, r = row - b * rows;
+    const float* src = a + row * k;
+    float* dhi = w + (2 * b) * plane + r * kp;
+    float* dlo = dhi + plane;
+    for (int64_t q = blockIdx.x * 256LL + threadIdx.x; q < kq; q += 256LL * gridDim.x) {
+      const int64_t c = q * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (VEC) {
+        if (c < k) x = ldg_f4(src + c);
+      } else {
+        if (c + 0 < k) x.x = __ldg(src + c + 0);
+        if (c + 1 < k) x.y = __ldg(src + c + 1);
+        if (c + 2 < k) x.z = __ldg(src + c + 2);
+        if (c + 3 < k) x.w = __ldg(src + c + 3);
+      }
+      float4 h, l;
+      split_one(x.x, h.x, l.x, bad);
+      split_one(x.y, h.y, l.y, bad);
+      split_one(x.z, h.z, l.z, bad);
+      split_one(x.w, h.w, l.w, bad);
+      *reinterpret_cast<float4*>(dhi + c) = h;
+      *reinterpret_cast<float4*>(dlo + c) = l;
+    }
   }
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
 }
 
-// B [nb][K][N] -> W [2*nb][N][Kp] (transposed, K-major), 32x32 tiles through smem.
-__global__ void split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k,
-                           int64_t n, int64_t kp, int* __restrict__ nonfinite) {
-  __shared__ float tile[32][33];
+// B [nb][K][N] -> W [2*nb][N][Kp] (transposed to K-major, zero padded in K).
+// A CTA moves a 32 (k) x 128 (n) tile: coalesced 128-bit loads along n (VEC: N % 4 == 0
+// and 16-byte aligned B), scalar shared-memory transpose (pitch 129: conflict-free
+// reads), 128-bit stores along k.
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k, int64_t n,
+           int64_t kp, int* __restrict__ nonfinite) {
+  __shared__ float tile[32][129];
   const int64_t plane = n * kp;
-  const int64_t tiles_n = (n + 31) / 32, tiles_k = kp / 32;
+  const int64_t tiles_n = (n + 127) / 128, tiles_k = kp / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   bool bad = false;
   for (int64_t t = blockIdx.x; t < nb * tiles_n * tiles_k; t += gridDim.x) {
     const int64_t b = t / (tiles_n * tiles_k), rem = t % (tiles_n * tiles_k);
-    const int64_t n0 = (rem % tiles_n) * 32, k0 = (rem / tiles_n) * 32;
-    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-      const int64_t kk = k0 + j, nn = n0 + threadIdx.x;
-      float x = 0.0f;
-      if (kk < k && nn < n) x = __ldg(bsrc + (b * k + kk) * n + nn);
-      bad |= !isfinite(x);
-      tile[j][threadIdx.x] = x;
+    const int64_t n0 = (rem % tiles_n) * 128, k0 = (rem / tiles_n) * 32;
+    const float* src = bsrc + b * k * n;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kk = warp * 4 + j;
+      const int64_t gk = k0 + kk, gn = n0 + lane * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gk < k) {
+        if (VEC) {
+          if (gn < n) x = ldg_f4(src + gk * n + gn);
+        } else {
+          const float* p = src + gk * n + gn;
+          if (gn + 0 < n) x.x = __ldg(p + 0);
+          if (gn + 1 < n) x.y = __ldg(p + 1);
+          if (gn + 2 < n) x.z = __ldg(p + 2);
+          if (gn + 3 < n) x.w = __ldg(p + 3);
+        }
+      }
+      tile[kk][lane * 4 + 0] = x.x;
+      tile[kk][lane * 4 + 1] = x.y;
+      tile[kk][lane * 4 + 2] = x.z;
+      tile[kk][lane * 4 + 3] = x.w;
     }
     __syncthreads();
-    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-      const int64_t nn = n0 + j, kk = k0 + threadIdx.x;
-      if (nn < n) {
-        const float x = tile[threadIdx.x][j];
-        const float hi = tf32_rna(x);
-        const float lo = tf32_rna(__fsub_rn(x, hi));
-        w[(2 * b) * plane + nn * kp + kk] = hi;
-        w[(2 * b + 1) * plane + nn * kp + kk] = lo;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int nn = (threadIdx.x >> 3) + 32 * j;
+      const int k4 = threadIdx.x & 7;
+      const int64_t gn = n0 + nn;
+      float4 h, l;
+      split_one(tile[4 * k4 + 0][nn], h.x, l.x, bad);
+      split_one(tile[4 * k4 + 1][nn], h.y, l.y, bad);
+      split_one(tile[4 * k4 + 2][nn], h.z, l.z, bad);
+      split_one(tile[4 * k4 + 3][nn], h.w, l.w, bad);
+      if (gn < n) {
+        float* dhi = w + (2 * b) * plane + gn * kp + k0 + 4 * k4;
+        *reinterpret_cast<float4*>(dhi) = h;
+        *reinterpret_cast<float4*>(dhi + plane) = l;
       }
     }
     __syncthreads();
@@ -640,17 +696,22 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
 
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
   {
-    const int64_t total = nba * m * lay.kp;
-    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 16LL * sms));
+    const bool vec_a = k % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0;
+    const int64_t kq = lay.kp / 4;
+    dim3 grid_a(static_cast<unsigned>(std::min<int64_t>(ceil_div(kq, 256), 64)),
+                static_cast<unsigned>(std::min<int64_t>(nba * m, 65535)));
     {
       TimedLaunch timer("split_rows", s);
-      split_rows<<<grid, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
+      if (vec_a) split_rows<true><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
+      else split_rows<false><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
     }
-    const int64_t tiles = nbb * ceil_div(n, 32) * (lay.kp / 32);
-    const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 32LL * sms));
+    const bool vec_b = n % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+    const int64_t tiles = nbb * ceil_div(n, 128) * (lay.kp / 32);
+    const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
     {
       TimedLaunch timer("split_cols", s);
-      split_cols<<<grid_b, dim3(32, 8), 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
+      if (vec_b) split_cols<true><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
+      else split_cols<false><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
     }
   }
   if (int st = launch_status("matmul split pre-pass")) return st;

@@ -58,6 +58,30 @@ struct Acc {
   int64_t idx;
 };
 
+// Per-thread best element, compared as values (a handful of instructions per
+// element); converted to an exact order key once per thread (key_max / key_min).
+// A thread visits its elements in increasing index order, so strict comparisons keep
+// the first of equal values (and -0 == +0 compares equal). Once a NaN is held,
+// `bv == bv` is false and nothing replaces it: the first NaN wins.
+struct Best {
+  uint32_t bits;  // value held (raw word)
+  int64_t idx;    // its index, INT64_MAX when the thread has seen no element
+};
+
+template <int K, bool FP>
+__device__ __forceinline__ void take_best(Best& b, uint32_t bits, int64_t index) {
+  bool take;
+  if (FP) {
+    const float v = __uint_as_float(bits), bv = __uint_as_float(b.bits);
+    const bool beats = (K == kBestMax) ? !(v <= bv) : !(v >= bv);  // true for a NaN v
+    take = (beats && bv == bv) || b.idx == INT64_MAX;
+  } else {
+    const int32_t v = static_cast<int32_t>(bits), bv = static_cast<int32_t>(b.bits);
+    take = ((K == kBestMax) ? v > bv : v < bv) || b.idx == INT64_MAX;
+  }
+  if (take) { b.bits = bits; b.idx = index; }
+}
+
 template <int K, bool FP>
 __device__ __forceinline__ void take(Acc& a, int slot, uint32_t bits, int64_t index) {
   if (K == kSumF) {
@@ -127,6 +151,8 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
 #pragma unroll
     for (int s = 0; s < 4 * kUnroll; ++s) { a.f[s] = 0.0f; a.u[s] = 0u; }
     a.key = 0; a.idx = INT64_MAX;
+    Best best{0u, INT64_MAX};
+    constexpr bool kBestKind = K == kBestMax || K == kBestMin;
     const int tid = threadIdx.x;
     int64_t tail_begin = begin;
     if (VEC && end > begin) {
@@ -140,27 +166,47 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int64_t e = begin + 4 * (i + u * kStage1Threads) + index_base;
-          take<K, FP>(a, 4 * u + 0, v[u].x, e + 0);
-          take<K, FP>(a, 4 * u + 1, v[u].y, e + 1);
-          take<K, FP>(a, 4 * u + 2, v[u].z, e + 2);
-          take<K, FP>(a, 4 * u + 3, v[u].w, e + 3);
+          if constexpr (kBestKind) {
+            take_best<K, FP>(best, v[u].x, e + 0);
+            take_best<K, FP>(best, v[u].y, e + 1);
+            take_best<K, FP>(best, v[u].z, e + 2);
+            take_best<K, FP>(best, v[u].w, e + 3);
+          } else {
+            take<K, FP>(a, 4 * u + 0, v[u].x, e + 0);
+            take<K, FP>(a, 4 * u + 1, v[u].y, e + 1);
+            take<K, FP>(a, 4 * u + 2, v[u].z, e + 2);
+            take<K, FP>(a, 4 * u + 3, v[u].w, e + 3);
+          }
         }
       }
       for (; i < nvec; i += kStage1Threads) {
         const uint4 v = ldg_stream(xv + i);
         const int64_t e = begin + 4 * i + index_base;
-        take<K, FP>(a, 0, v.x, e + 0);
-        take<K, FP>(a, 1, v.y, e + 1);
-        take<K, FP>(a, 2, v.z, e + 2);
-        take<K, FP>(a, 3, v.w, e + 3);
+        if constexpr (kBestKind) {
+          take_best<K, FP>(best, v.x, e + 0);
+          take_best<K, FP>(best, v.y, e + 1);
+          take_best<K, FP>(best, v.z, e + 2);
+          take_best<K, FP>(best, v.w, e + 3);
+        } else {
+          take<K, FP>(a, 0, v.x, e + 0);
+          take<K, FP>(a, 1, v.y, e + 1);
+          take<K, FP>(a, 2, v.z, e + 2);
+          take<K, FP>(a, 3, v.w, e + 3);
+        }
       }
       tail_begin = begin + nvec * 4;
     }
-    for (int64_t j = tail_begin + tid; j < end; j += kStage1Threads)
-      take<K, FP>(a, 0, __ldg(xr + j), j + index_base);
+    for (int64_t j = tail_begin + tid; j < end; j += kStage1Threads) {
+      if constexpr (kBestKind) take_best<K, FP>(best, __ldg(xr + j), j + index_base);
+      else take<K, FP>(a, 0, __ldg(xr + j), j + index_base);
+    }
 
     uint32_t bits = 0, key = a.key;
     int64_t idx = a.idx;
+    if constexpr (kBestKind) {
+      idx = best.idx;
+      key = idx == INT64_MAX ? 0u : ((K == kBestMax) ? key_max(best.bits, FP) : key_min(best.bits, FP));
+    }
     if (K == kSumF) {
       // fixed pairwise order over the 16 accumulators
       float t[4 * kUnroll];

@@ -25,6 +25,15 @@ namespace {
 
 enum RowOp { kSoftmax = 0, kRms = 1, kLayer = 2 };
 
+// e^x through the base-2 identity e^x = 2^(x * log2 e) and the hardware ex2.approx
+// instruction (relative error ~2^-22 on the ex2 step, plus |x| * 2^-24 from rounding
+// x * log2 e: < 2e-6 for the |x| <= 60 a softmax row can feed it before underflow).
+__device__ __forceinline__ float exp_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 1.4426950408889634f)));
+  return y;
+}
+
 __device__ __forceinline__ float nan_max(float a, float b) {
   if (a != a) return a;
   if (b != b) return b;
@@ -72,29 +81,32 @@ struct Block {
   }
 };
 
-// Per-row math on values held by the CTA's threads. E = elements per thread.
-template <int OP, int THREADS, int E>
-__device__ __forceinline__ void row_math(float (&v)[E], const bool (&valid)[E], int64_t n,
-                                         float first, float eps, float* smem) {
+// Per-row math on values held by the CTA's threads. E = elements per thread; element
+// q of a thread is valid when its column (given by col(q)) is < n.
+template <int OP, int THREADS, int E, typename Col>
+__device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, float first, float eps,
+                                         float* smem) {
   using B = Block<THREADS>;
   if (OP == kSoftmax) {
     float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (valid[i]) m = nan_max(m, v[i]);
+    for (int i = 0; i < E; ++i) if (col(i) < n) m = nan_max(m, v[i]);
     m = B::max(m, smem);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      v[i] = valid[i] ? expf(__fsub_rn(v[i], m)) : 0.0f;
+      v[i] = col(i) < n ? exp_ex2(__fsub_rn(v[i], m)) : 0.0f;
       s = __fadd_rn(s, v[i]);
     }
     s = B::sum(s, smem);
+    // one IEEE reciprocal per row, then a multiply per element (<= 1.5 ulp vs division)
+    const float inv = __frcp_rn(s);
 #pragma unroll
-    for (int i = 0; i < E; ++i) v[i] = __fdiv_rn(v[i], s);
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], inv);
   } else if (OP == kRms) {
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (valid[i]) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    for (int i = 0; i < E; ++i) if (col(i) < n) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
     ss = B::sum(ss, smem);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
 #pragma unroll
@@ -103,7 +115,7 @@ __device__ __forceinline__ void row_math(float (&v)[E], const bool (&valid)[E], 
     float s = 0.0f;
     bool eq = true;
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (valid[i]) { s = __fadd_rn(s, v[i]); eq = eq && (v[i] == first); }
+    for (int i = 0; i < E; ++i) if (col(i) < n) { s = __fadd_rn(s, v[i]); eq = eq && (v[i] == first); }
     s = B::sum(s, smem);
     eq = B::all(eq, smem);
     if (eq && isfinite(first)) {
@@ -116,7 +128,7 @@ __device__ __forceinline__ void row_math(float (&v)[E], const bool (&valid)[E], 
     float ssd = 0.0f;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      if (valid[i]) {
+      if (col(i) < n) {
         const float d = __fsub_rn(v[i], mean);
         ssd = __fadd_rn(ssd, __fmul_rn(d, d));
       }
@@ -142,7 +154,8 @@ __device__ __forceinline__ float affine(float y, const float* w, const float* b,
 
 // One CTA per row, the row held in registers. VEC: float4 accesses (row length % 4 == 0
 // and 16-byte aligned rows); otherwise scalar accesses, element tid + THREADS*q.
-template <int OP, int THREADS, int VPT, bool VEC>
+// FULL: n == THREADS * VPT * 4 exactly (every slot valid; no bounds checks).
+template <int OP, int THREADS, int VPT, bool VEC, bool FULL = false>
 __global__ void __launch_bounds__(THREADS)
 row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n,
            float eps, const float* __restrict__ w, const float* __restrict__ b) {
@@ -152,28 +165,29 @@ row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, i
     const float* xr = x + row * n;
     float* orow = out + row * n;
     float v[E];
-    bool valid[E];
     if (VEC) {
       const int64_t n4 = n >> 2;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int64_t i4 = threadIdx.x + static_cast<int64_t>(j) * THREADS;
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-        const bool ok = i4 < n4;
-        if (ok) t = __ldcs(reinterpret_cast<const float4*>(xr) + i4);
+        if (i4 < n4) t = __ldcs(reinterpret_cast<const float4*>(xr) + i4);
         v[4 * j + 0] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
-        valid[4 * j + 0] = valid[4 * j + 1] = valid[4 * j + 2] = valid[4 * j + 3] = ok;
       }
     } else {
 #pragma unroll
       for (int q = 0; q < E; ++q) {
         const int64_t i = threadIdx.x + static_cast<int64_t>(q) * THREADS;
-        valid[q] = i < n;
-        v[q] = valid[q] ? __ldcs(xr + i) : 0.0f;
+        v[q] = i < n ? __ldcs(xr + i) : 0.0f;
       }
     }
     const float first = OP == kLayer ? __ldg(xr) : 0.0f;
-    row_math<OP, THREADS, E>(v, valid, n, first, eps, smem);
+    auto col = [](int q) -> int64_t {
+      if (FULL) return 0;  // every element valid: col(q) < n always holds
+      return VEC ? 4 * (threadIdx.x + static_cast<int64_t>(q >> 2) * THREADS) + (q & 3)
+                 : threadIdx.x + static_cast<int64_t>(q) * THREADS;
+    };
+    row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
     if (VEC) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
@@ -212,9 +226,10 @@ row_stream(const float* __restrict__ x, float* __restrict__ out, int64_t rows, i
       for (int64_t i = threadIdx.x; i < n; i += 1024) m = nan_max(m, xr[i]);
       m = B::max(m, smem);
       float s = 0.0f;
-      for (int64_t i = threadIdx.x; i < n; i += 1024) s = __fadd_rn(s, expf(__fsub_rn(xr[i], m)));
+      for (int64_t i = threadIdx.x; i < n; i += 1024) s = __fadd_rn(s, exp_ex2(__fsub_rn(xr[i], m)));
       s = B::sum(s, smem);
-      for (int64_t i = threadIdx.x; i < n; i += 1024) orow[i] = __fdiv_rn(expf(__fsub_rn(xr[i], m)), s);
+      const float inv = __frcp_rn(s);
+      for (int64_t i = threadIdx.x; i < n; i += 1024) orow[i] = __fmul_rn(exp_ex2(__fsub_rn(xr[i], m)), inv);
     } else if (OP == kRms) {
       float ss = 0.0f;
       for (int64_t i = threadIdx.x; i < n; i += 1024) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
@@ -320,7 +335,9 @@ void launch_row(cudaStream_t s, const float* x, float* out, int64_t rows, int64_
                 const float* w, const float* b, bool vec) {
   const int grid = static_cast<int>(std::min<int64_t>(rows, 1LL << 20));
   TimedLaunch timer("row_kernel", s);
-  if (vec) row_kernel<OP, THREADS, VPT, true><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
+  if (vec && n == static_cast<int64_t>(THREADS) * VPT * 4)
+    row_kernel<OP, THREADS, VPT, true, true><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
+  else if (vec) row_kernel<OP, THREADS, VPT, true><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
   else row_kernel<OP, THREADS, VPT, false><<<grid, THREADS, 0, s>>>(x, out, rows, n, eps, w, b);
 }
 

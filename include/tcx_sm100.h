@@ -216,6 +216,10 @@ int tcx_sm100_clip(tcx_stream_t stream, int dtype, const void* input, const void
 int tcx_sm100_bias_act(tcx_stream_t stream, const float* input, const float* bias,
                        float* output, int64_t rows, int64_t cols, int act);
 
+/* Fills `count` 32-bit elements with the raw word `bits` (float32 or int32 value as
+ * stored). Replaces launch_fill (cuda_kernels.h:13-14). */
+int tcx_sm100_fill(tcx_stream_t stream, void* output, int64_t count, uint32_t bits);
+
 /* ------------------------------------------------------------------- matmul --- */
 
 /* Scratch for tcx_sm100_matmul: the tf32 hi/lo split of both operands (K-major).
@@ -241,6 +245,17 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
                      const int64_t* rhs_batch_strides, int32_t batch_rank,
                      const float* bias, int act, int path, void* workspace,
                      size_t workspace_bytes);
+
+/* linear(x, w, bias): out[r, o] = act(sum_k x[r, k] * w[o, k] + bias[o]) for x [rows, in],
+ * w [out_features, in] (the nn.Linear layout, i.e. K-major), bias [out_features] or
+ * NULL. One GEMM with the bias (and activation) in its epilogue; the weight is used
+ * in place, without the transpose copy of the reference's kLinear composite
+ * (core/inference.cpp:89-102: transpose, matmul, add). Same kernels, accuracy and
+ * workspace rules as tcx_sm100_matmul. */
+size_t tcx_sm100_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features, int path);
+int tcx_sm100_linear(tcx_stream_t stream, const float* x, const float* w, const float* bias, float* output,
+                     int64_t rows, int64_t in_features, int64_t out_features, int act, int path,
+                     void* workspace, size_t workspace_bytes);
 
 #ifdef __cplusplus
 }  /* extern "C" */

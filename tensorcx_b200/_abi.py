@@ -53,6 +53,10 @@ SIGNATURES = {
     "tcx_sm100_binary": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _i64, _i64p, _i32]),
     "tcx_sm100_clip": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64p, _i32]),
     "tcx_sm100_bias_act": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_int]),
+    "tcx_sm100_fill": (ctypes.c_int, [_vp, _vp, _i64, ctypes.c_uint32]),
+    "tcx_sm100_linear_workspace_bytes": (_sz, [_i64, _i64, _i64, ctypes.c_int]),
+    "tcx_sm100_linear": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int,
+                                        _vp, _sz]),
     "tcx_sm100_matmul_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int]),
     "tcx_sm100_matmul": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i32,
                                         _vp, ctypes.c_int, ctypes.c_int, _vp, _sz]),

@@ -1,0 +1,614 @@
+// CudaBackend::execute for the sm100 backend: validation and planning with the
+// unchanged tensor.cx core (validate_primitive_execution_contract, make_*_plan), then
+// one C-ABI call per primitive (include/tcx_sm100.h) on the device's stream, a
+// synchronize of that stream (the ABI stays synchronous, docs/BACKENDS.md:178-180)
+// and publication of the result slot only on success (cuda_backend.cpp:612-613 of the
+// reference). Validation messages follow the reference CUDA backend so the bindings
+// raise the same errors.
+#include "tensorcx/backends/cuda/cuda_backend.h"
+
+#include <cuda_runtime_api.h>
+
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <numeric>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "tcx_sm100.h"
+#include "tensorcx/backends/cuda/cuda_device.h"
+#include "tensorcx/backends/cuda/cuda_memory_pool.h"
+#include "tensorcx/core/math.h"
+#include "tensorcx/core/shape.h"
+
+namespace tensorcx::cuda {
+namespace {
+
+Status invalid(std::string message) { return {StatusCode::kInvalidArgument, std::move(message)}; }
+
+Status abi_status(int rc, const char* what) {
+  if (rc == TCX_OK) return Status::Ok();
+  const auto code = rc == TCX_INVALID_ARGUMENT ? StatusCode::kInvalidArgument
+                    : rc == TCX_UNAVAILABLE   ? StatusCode::kUnavailable
+                                              : StatusCode::kInternal;
+  return Status(code, std::string(what) + ": " + tcx_sm100_last_error());
+}
+
+Expected<std::size_t> byte_size(DType dtype, const Shape& shape) {
+  if (dtype != DType::kFloat32 && dtype != DType::kInt32 && dtype != DType::kBool)
+    return invalid("unsupported CUDA dtype");
+  const auto count = static_cast<std::uint64_t>(numel(shape));
+  if (count > std::numeric_limits<std::size_t>::max() / dtype_size(dtype)) return invalid("CUDA buffer size overflow");
+  return static_cast<std::size_t>(count) * dtype_size(dtype);
+}
+
+tcx_stream_t abi_stream(const DeviceScope& scope) { return reinterpret_cast<tcx_stream_t>(scope.stream()); }
+
+// Stream-ordered scratch for one call: from the thread's pool when one is entered,
+// otherwise from the device's default stream-ordered pool. Released (stream-ordered)
+// when the call's work is queued, so no explicit wait is needed.
+class Scratch {
+ public:
+  Scratch(std::size_t bytes, const DeviceScope& scope) : bytes_(bytes), stream_(scope.stream()) {
+    if (!bytes_) return;
+    const std::size_t padded = bytes_ + 1024;
+    pool_ = active_memory_pool();
+    if (pool_) {
+      auto p = pool_->allocate(padded);
+      if (!p) { status_ = p.status(); return; }
+      raw_ = p.value();
+    } else {
+      status_ = runtime_status(cudaMallocAsync(&raw_, padded, stream_), "CUDA workspace allocation");
+      if (!status_.ok()) return;
+    }
+    aligned_ = reinterpret_cast<void*>((reinterpret_cast<std::uintptr_t>(raw_) + 1023) & ~std::uintptr_t(1023));
+  }
+  ~Scratch() {
+    if (!raw_) return;
+    if (pool_) pool_->release(raw_, bytes_ + 1024, true);
+    else (void)cudaFreeAsync(raw_, stream_);
+  }
+  Scratch(const Scratch&) = delete;
+  Scratch& operator=(const Scratch&) = delete;
+  const Status& status() const { return status_; }
+  void* data() const { return aligned_; }
+  std::size_t bytes() const { return bytes_; }
+
+ private:
+  std::size_t bytes_;
+  cudaStream_t stream_;
+  std::shared_ptr<MemoryPool> pool_;
+  void* raw_{nullptr};
+  void* aligned_{nullptr};
+  Status status_;
+};
+
+struct Axis {
+  Shape reduced_shape;
+  std::int64_t outer{1}, reduce{1}, inner{1};
+};
+
+// One-axis view (cpu_backend.cpp:76-123 and cuda_backend.cpp:520-534 of the reference).
+Expected<Axis> axis_view(const Tensor& t, std::int64_t axis) {
+  Axis a;
+  const auto rank = static_cast<std::int64_t>(t.shape.size());
+  if (!rank) {
+    if (axis != 0 && axis != -1) return invalid("reduction axis is out of range");
+    return a;
+  }
+  if (axis < 0) axis += rank;
+  if (axis < 0 || axis >= rank) return invalid("reduction axis is out of range");
+  a.outer = numel(Shape(t.shape.begin(), t.shape.begin() + axis));
+  a.inner = t.strides[axis];
+  a.reduce = t.shape[axis];
+  a.reduced_shape = t.shape;
+  a.reduced_shape.erase(a.reduced_shape.begin() + axis);
+  return a;
+}
+
+Expected<float> checked_epsilon(double eps) {
+  if (!std::isfinite(eps) || eps < 0 || eps > std::numeric_limits<float>::max() ||
+      (eps > 0 && static_cast<float>(eps) == 0))
+    return invalid("epsilon must be finite and non-negative and representable as float32");
+  return static_cast<float>(eps);
+}
+
+bool is_binary(OpKind k) {
+  return k == OpKind::kAdd || k == OpKind::kSubtract || k == OpKind::kMultiply || k == OpKind::kDivide;
+}
+
+class Executor {
+ public:
+  Executor(const BackendExecution& e, std::vector<CudaTensor>& in, const DeviceScope& scope)
+      : e_(e), in_(in), scope_(scope) {}
+
+  Status run(Tensor& out) {
+    const auto kind = e_.op.kind;
+    if (kind == OpKind::kFill) return fill(out);
+    if (kind == OpKind::kMatmul) return matmul(out);
+    if (kind == OpKind::kLinear) return linear(out);
+    if (kind == OpKind::kSum || kind == OpKind::kMax || kind == OpKind::kMean) return reduction(out);
+    if (kind == OpKind::kSoftmax || kind == OpKind::kRmsNorm || kind == OpKind::kLayerNorm) return row_op(out);
+    if (kind == OpKind::kAffineRmsNorm || kind == OpKind::kAffineLayerNorm) return affine_norm(out);
+    if (kind == OpKind::kExp || kind == OpKind::kGelu || kind == OpKind::kSilu) return unary(out);
+    if (is_binary(kind)) return binary(out);
+    if (kind == OpKind::kMin || kind == OpKind::kArgmax || kind == OpKind::kClip) return math(out);
+    return {StatusCode::kUnavailable,
+            "operation is not on the sm100 hot path (served ops: fill, matmul, linear, sum, max, mean, min, "
+            "argmax, clip, softmax, rmsnorm, layernorm and their affine forms, exp, gelu, silu, add, subtract, "
+            "multiply, divide)"};
+  }
+
+ private:
+  const BackendExecution& e_;
+  std::vector<CudaTensor>& in_;
+  const DeviceScope& scope_;
+
+  void* ptr(std::size_t i) const { return in_[i].buffer()->data(); }
+
+  Expected<std::shared_ptr<CudaBuffer>> output(DType dtype, const Shape& shape) {
+    return CudaBuffer::create(dtype, shape, scope_.device());
+  }
+
+  Status publish(Tensor& out, DType dtype, const Shape& shape, std::shared_ptr<CudaBuffer> buffer) {
+    out = to_core_tensor(CudaTensor(dtype, shape, std::move(buffer)));
+    return Status::Ok();
+  }
+
+  Status require_float32() {
+    for (const auto& t : in_)
+      if (t.dtype() != DType::kFloat32) return invalid("CUDA operation only supports float32 for this dtype");
+    return Status::Ok();
+  }
+
+  Status fill(Tensor& out) {
+    const auto& desc = e_.outputs[0];
+    auto buffer = output(desc.dtype, desc.shape);
+    if (!buffer) return buffer.status();
+    const auto count = numel(desc.shape);
+    if (count) {
+      if (desc.dtype == DType::kBool) {
+        auto st = runtime_status(cudaMemsetAsync(buffer.value()->data(), e_.op.scalar_value != 0,
+                                                 buffer.value()->nbytes(), scope_.stream()),
+                                 "CUDA bool fill");
+        if (!st.ok()) return st;
+      } else {
+        std::uint32_t bits;
+        if (desc.dtype == DType::kInt32) {
+          if (!is_int32_representable(e_.op.scalar_value))
+            return invalid("fill/arithmetic scalar must be an integer in int32 range");
+          const auto v = static_cast<std::int32_t>(e_.op.scalar_value);
+          std::memcpy(&bits, &v, 4);
+        } else {
+          const auto v = static_cast<float>(e_.op.scalar_value);
+          std::memcpy(&bits, &v, 4);
+        }
+        auto st = abi_status(tcx_sm100_fill(abi_stream(scope_), buffer.value()->data(), count, bits), "CUDA fill");
+        if (!st.ok()) return st;
+      }
+    }
+    return publish(out, desc.dtype, desc.shape, buffer.move_value());
+  }
+
+  Status matmul(Tensor& out) {
+    if (e_.op.matmul_preference != MatmulPreference::kAuto && e_.op.matmul_preference != MatmulPreference::kCustom)
+      return invalid("CUDA matmul supports auto or custom");
+    if (auto st = require_float32(); !st.ok()) return st;
+    const auto plan = make_matmul_plan(in_[0].shape(), in_[1].shape());
+    auto buffer = output(DType::kFloat32, plan.output_shape);
+    if (!buffer) return buffer.status();
+    const auto count = numel(plan.output_shape);
+    if (count) {
+      const auto batches = count / plan.n / plan.m;
+      const auto nba = plan.m * plan.k != 0 ? numel(in_[0].shape()) / (plan.m * plan.k) : 1;
+      const auto nbb = plan.k * plan.n != 0 ? numel(in_[1].shape()) / (plan.k * plan.n) : 1;
+      Scratch ws(tcx_sm100_matmul_workspace_bytes(plan.m, plan.n, plan.k, nba, nbb, TCX_MATMUL_AUTO), scope_);
+      if (!ws.status().ok()) return ws.status();
+      auto st = abi_status(
+          tcx_sm100_matmul(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
+                           static_cast<float*>(buffer.value()->data()), plan.m, plan.n, plan.k, batches,
+                           plan.batch_shape.data(), plan.lhs_batch_strides.data(), plan.rhs_batch_strides.data(),
+                           static_cast<std::int32_t>(plan.batch_shape.size()), nullptr, TCX_ACT_NONE,
+                           TCX_MATMUL_AUTO, ws.data(), ws.bytes()),
+          "CUDA matmul");
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kFloat32, plan.output_shape, buffer.move_value());
+  }
+
+  // kLinear (core/inference.cpp:89-102) in one GEMM: weight read in place, bias fused.
+  Status linear(Tensor& out) {
+    if (in_.size() < 2 || in_.size() > 3) return invalid("linear requires input, weight and optional bias");
+    for (const auto& t : in_)
+      if (t.dtype() != DType::kFloat32) return invalid("inference values require float32 tensors");
+    const auto& x = in_[0].shape();
+    const auto& w = in_[1].shape();
+    if (x.empty() || w.size() != 2 || x.back() != w[1])
+      return invalid("linear requires (..., in_features) and (out_features, in_features)");
+    if (in_.size() == 3 && in_[2].shape() != Shape{w[0]}) return invalid("linear bias must have shape (out_features,)");
+    Shape shape = x;
+    shape.back() = w[0];
+    (void)numel(shape);
+    auto buffer = output(DType::kFloat32, shape);
+    if (!buffer) return buffer.status();
+    const auto rows = numel(Shape(x.begin(), x.end() - 1));
+    if (numel(shape)) {
+      Scratch ws(tcx_sm100_linear_workspace_bytes(rows, w[1], w[0], TCX_MATMUL_AUTO), scope_);
+      if (!ws.status().ok()) return ws.status();
+      auto st = abi_status(tcx_sm100_linear(abi_stream(scope_), static_cast<const float*>(ptr(0)),
+                                            static_cast<const float*>(ptr(1)),
+                                            in_.size() == 3 ? static_cast<const float*>(ptr(2)) : nullptr,
+                                            static_cast<float*>(buffer.value()->data()), rows, w[1], w[0],
+                                            TCX_ACT_NONE, TCX_MATMUL_AUTO, ws.data(), ws.bytes()),
+                           "CUDA linear");
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kFloat32, shape, buffer.move_value());
+  }
+
+  Status reduction(Tensor& out) {
+    const auto kind = e_.op.kind;
+    const auto& t = e_.inputs[0];
+    const auto dtype = t.dtype;
+    if (dtype != DType::kFloat32 && !(dtype == DType::kInt32 && kind != OpKind::kMean))
+      return invalid("CUDA operation only supports float32 for this dtype");
+    const int code = static_cast<int>(kind);
+    const int dt = dtype == DType::kFloat32 ? TCX_FLOAT32 : TCX_INT32;
+    if (e_.op.reduction_axes) {
+      const auto plan = make_reduction_plan(t.shape, *e_.op.reduction_axes);
+      if (kind == OpKind::kMax && plan.reduction_size == 0) return invalid("max reduction requires non-empty axes");
+      auto buffer = output(dtype, e_.op.reduction_axes->empty() ? t.shape : plan.output_shape);
+      if (!buffer) return buffer.status();
+      if (e_.op.reduction_axes->empty()) {  // no axes: an independent copy
+        auto st = runtime_status(cudaMemcpyAsync(buffer.value()->data(), ptr(0), in_[0].nbytes(),
+                                                 cudaMemcpyDeviceToDevice, scope_.stream()),
+                                 "CUDA copy");
+        if (!st.ok()) return st;
+        return publish(out, dtype, t.shape, buffer.move_value());
+      }
+      const auto groups = numel(plan.output_shape);
+      if (groups) {
+        Scratch ws(tcx_sm100_reduce_workspace_bytes(groups * plan.reduction_size), scope_);
+        if (!ws.status().ok()) return ws.status();
+        auto st = abi_status(
+            tcx_sm100_reduce_axes(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(), groups,
+                                  plan.reduction_size, plan.index_metadata.data(),
+                                  static_cast<std::int32_t>(plan.output_shape.size()),
+                                  static_cast<std::int32_t>(t.shape.size()), ws.data(), ws.bytes()),
+            "CUDA multi-axis reduction");
+        if (!st.ok()) return st;
+      }
+      return publish(out, dtype, plan.output_shape, buffer.move_value());
+    }
+    auto a = axis_view(t, e_.op.axis);
+    if (!a) return a.status();
+    if (kind == OpKind::kMax && !a.value().reduce) return invalid("max reduction requires a non-empty axis");
+    auto buffer = output(dtype, a.value().reduced_shape);
+    if (!buffer) return buffer.status();
+    if (a.value().outer * a.value().inner != 0) {
+      Scratch ws(tcx_sm100_axis_workspace_bytes(code, a.value().outer, a.value().reduce, a.value().inner), scope_);
+      if (!ws.status().ok()) return ws.status();
+      auto st = abi_status(tcx_sm100_axis(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(),
+                                          a.value().outer, a.value().reduce, a.value().inner, 0.0f, ws.data(),
+                                          ws.bytes()),
+                           "CUDA axis reduction");
+      if (!st.ok()) return st;
+    }
+    return publish(out, dtype, a.value().reduced_shape, buffer.move_value());
+  }
+
+  Status row_op(Tensor& out) {
+    if (auto st = require_float32(); !st.ok()) return st;
+    const auto& t = e_.inputs[0];
+    auto a = axis_view(t, e_.op.axis);
+    if (!a) return a.status();
+    float eps = 0.0f;
+    if (e_.op.kind != OpKind::kSoftmax) {
+      auto e = checked_epsilon(e_.op.epsilon);
+      if (!e) return e.status();
+      eps = e.value();
+    }
+    auto buffer = output(DType::kFloat32, t.shape);
+    if (!buffer) return buffer.status();
+    if (numel(t.shape)) {
+      auto st = abi_status(tcx_sm100_axis(abi_stream(scope_), static_cast<int>(e_.op.kind), TCX_FLOAT32, ptr(0),
+                                          buffer.value()->data(), a.value().outer, a.value().reduce,
+                                          a.value().inner, eps, nullptr, 0),
+                           "CUDA row operation");
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kFloat32, t.shape, buffer.move_value());
+  }
+
+  // kAffineRmsNorm / kAffineLayerNorm (core/inference.cpp:103-122) in one kernel.
+  Status affine_norm(Tensor& out) {
+    const auto& op = e_.op;
+    if (e_.inputs.size() != 1U + op.has_weight + op.has_bias || (op.kind == OpKind::kAffineRmsNorm && op.has_bias))
+      return invalid("invalid affine normalization parameters");
+    for (const auto& t : in_)
+      if (t.dtype() != DType::kFloat32) return invalid("inference values require float32 tensors");
+    const auto& x = e_.inputs[0];
+    auto a = axis_view(x, op.axis);
+    if (!a) return invalid("normalization axis out of range");
+    const Shape expected = x.shape.empty() ? Shape{} : Shape{a.value().reduce};
+    for (std::size_t i = 1; i < e_.inputs.size(); ++i)
+      if (e_.inputs[i].shape != expected) return invalid("affine parameters must match the normalized axis");
+    auto eps = checked_epsilon(op.epsilon);
+    if (!eps) return invalid("epsilon must be finite, non-negative and representable as float32");
+    auto buffer = output(DType::kFloat32, x.shape);
+    if (!buffer) return buffer.status();
+    if (numel(x.shape)) {
+      std::size_t next = 1;
+      const float* w = op.has_weight ? static_cast<const float*>(ptr(next++)) : nullptr;
+      const float* b = op.has_bias ? static_cast<const float*>(ptr(next)) : nullptr;
+      auto st = abi_status(
+          tcx_sm100_affine_norm(abi_stream(scope_), op.kind == OpKind::kAffineRmsNorm ? TCX_OP_RMSNORM : TCX_OP_LAYERNORM,
+                                static_cast<const float*>(ptr(0)), static_cast<float*>(buffer.value()->data()),
+                                a.value().outer, a.value().reduce, a.value().inner, eps.value(), w, b),
+          "CUDA affine normalization");
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kFloat32, x.shape, buffer.move_value());
+  }
+
+  Status unary(Tensor& out) {
+    if (auto st = require_float32(); !st.ok()) return st;
+    const auto& t = e_.inputs[0];
+    auto buffer = output(DType::kFloat32, t.shape);
+    if (!buffer) return buffer.status();
+    auto st = abi_status(tcx_sm100_unary(abi_stream(scope_), static_cast<int>(e_.op.kind),
+                                         static_cast<const float*>(ptr(0)),
+                                         static_cast<float*>(buffer.value()->data()), numel(t.shape)),
+                         "CUDA unary");
+    if (!st.ok()) return st;
+    return publish(out, DType::kFloat32, t.shape, buffer.move_value());
+  }
+
+  Status binary(Tensor& out) {
+    const auto kind = e_.op.kind;
+    const auto& l = e_.inputs[0];
+    const auto& r = e_.inputs[1];
+    if (l.dtype != r.dtype) return invalid("dtype mismatch for binary operation");
+    if (l.dtype != DType::kFloat32 && !(l.dtype == DType::kInt32 && kind != OpKind::kDivide))
+      return invalid("CUDA operation only supports float32 for this dtype");
+    Shape shape = l.shape;
+    Shape metadata;
+    if (l.shape != r.shape) {
+      const auto plan = make_broadcast_plan(l.shape, r.shape);
+      shape = plan.output_shape;
+      metadata = plan.output_shape;
+      metadata.insert(metadata.end(), plan.lhs_strides.begin(), plan.lhs_strides.end());
+      metadata.insert(metadata.end(), plan.rhs_strides.begin(), plan.rhs_strides.end());
+    }
+    auto buffer = output(l.dtype, shape);
+    if (!buffer) return buffer.status();
+    auto st = abi_status(tcx_sm100_binary(abi_stream(scope_), static_cast<int>(kind),
+                                          l.dtype == DType::kFloat32 ? TCX_FLOAT32 : TCX_INT32, ptr(0), ptr(1),
+                                          buffer.value()->data(), numel(shape),
+                                          metadata.empty() ? nullptr : metadata.data(),
+                                          metadata.empty() ? 0 : static_cast<std::int32_t>(shape.size())),
+                         "CUDA binary");
+    if (!st.ok()) return st;
+    return publish(out, l.dtype, shape, buffer.move_value());
+  }
+
+  // min / argmax / clip through make_math_plan (core/math.cpp:13-71).
+  Status math(Tensor& out) {
+    const auto plan = make_math_plan(e_.op, e_.inputs);
+    auto buffer = output(plan.dtype, plan.shape);
+    if (!buffer) return buffer.status();
+    const int dt = e_.inputs[0].dtype == DType::kFloat32 ? TCX_FLOAT32 : TCX_INT32;
+    if (plan.groups) {
+      Status st;
+      if (e_.op.kind == OpKind::kClip) {
+        st = abi_status(tcx_sm100_clip(abi_stream(scope_), dt, ptr(0), ptr(1), ptr(2), buffer.value()->data(),
+                                       plan.groups, plan.metadata.data(), static_cast<std::int32_t>(plan.rank)),
+                        "CUDA clip");
+      } else {
+        Scratch ws(tcx_sm100_reduce_workspace_bytes(plan.groups * plan.reduce), scope_);
+        if (!ws.status().ok()) return ws.status();
+        st = abi_status(tcx_sm100_min_argmax(abi_stream(scope_), static_cast<int>(e_.op.kind), dt, ptr(0),
+                                             buffer.value()->data(), plan.groups, plan.reduce,
+                                             plan.metadata.data(), static_cast<std::int32_t>(plan.rank),
+                                             ws.data(), ws.bytes()),
+                        "CUDA min/argmax");
+      }
+      if (!st.ok()) return st;
+    }
+    return publish(out, plan.dtype, plan.shape, buffer.move_value());
+  }
+};
+
+}  // namespace
+
+// ------------------------------------------------------------------ buffers
+Expected<std::shared_ptr<CudaBuffer>> CudaBuffer::create(DType dtype, const Shape& shape, int device) {
+  auto bytes = byte_size(dtype, shape);
+  if (!bytes) return bytes.status();
+  DeviceScope scope(device);
+  if (!scope.ready()) return scope.status();
+  auto buffer = std::make_shared<CudaBuffer>();
+  buffer->dtype_ = dtype;
+  buffer->bytes_ = bytes.value();
+  buffer->device_ = device;
+  if (buffer->bytes_) {
+    auto pool = active_memory_pool();
+    if (pool) {
+      auto p = pool->allocate(buffer->bytes_);
+      if (!p) return p.status();
+      buffer->data_ = p.value();
+      buffer->pool_ = std::move(pool);
+    } else {
+      auto st = runtime_status(cudaMallocAsync(&buffer->data_, buffer->bytes_, scope.stream()), "CUDA allocation");
+      if (!st.ok()) return st;
+    }
+  }
+  return buffer;
+}
+
+Expected<std::shared_ptr<CudaBuffer>> CudaBuffer::borrow(DType dtype, const Shape& shape, void* data,
+                                                        std::shared_ptr<void> owner, int device) {
+  auto bytes = byte_size(dtype, shape);
+  if (!bytes) return bytes.status();
+  if (bytes.value() && !data) return invalid("borrowed CUDA memory requires a pointer");
+  auto buffer = std::make_shared<CudaBuffer>();
+  buffer->dtype_ = dtype;
+  buffer->bytes_ = bytes.value();
+  buffer->device_ = device;
+  buffer->data_ = data;
+  buffer->external_owner_ = owner ? std::move(owner) : std::shared_ptr<void>(data, [](void*) {});
+  return buffer;
+}
+
+CudaBuffer::~CudaBuffer() {
+  if (external_owner_ || !data_) return;
+  DeviceScope scope(device_);
+  if (!scope.ready()) return;
+  if (pool_) pool_->release(data_, bytes_, !exported_.load(std::memory_order_relaxed));
+  else (void)cudaFreeAsync(data_, scope.stream());
+}
+
+StorageRelation CudaBuffer::storage_relation(const Buffer& other) const {
+  const auto* rhs = dynamic_cast<const CudaBuffer*>(&other);
+  if (!rhs) return Buffer::storage_relation(other);
+  if (device_ != rhs->device_) return StorageRelation::kDisjoint;
+  if (this == rhs) return StorageRelation::kSameRange;
+  if (!nbytes() || !rhs->nbytes()) return StorageRelation::kDisjoint;
+  const auto a = reinterpret_cast<std::uintptr_t>(data_), b = reinterpret_cast<std::uintptr_t>(rhs->data_);
+  if (a == b && nbytes() == rhs->nbytes()) return StorageRelation::kSameRange;
+  const bool overlap = a <= b ? b - a < nbytes() : a - b < rhs->nbytes();
+  return overlap ? StorageRelation::kPartialOverlap : StorageRelation::kDisjoint;
+}
+
+// ------------------------------------------------------------------ tensors
+CudaTensor::CudaTensor(DType dtype, Shape shape, std::shared_ptr<CudaBuffer> buffer)
+    : dtype_(dtype), shape_(std::move(shape)), strides_(contiguous_strides(shape_)), buffer_(std::move(buffer)) {}
+
+std::size_t CudaTensor::nbytes() const { return buffer_ ? buffer_->nbytes() : 0; }
+
+Tensor to_core_tensor(const CudaTensor& t) {
+  return Tensor{t.dtype(), t.shape(), t.strides(), Device{"cuda", t.buffer()->device()},
+                std::static_pointer_cast<Buffer>(t.buffer()), 0};
+}
+
+Expected<CudaTensor> from_core_tensor(const Tensor& t) {
+  try {
+    if (t.device.type != "cuda") return invalid("CUDA tensor metadata requires device='cuda'");
+    if (t.device.index < 0 || t.device.index >= device_count())
+      return invalid("CUDA tensor metadata requires an available device index");
+    if (t.offset != 0) return invalid("CUDA tensor metadata with non-zero offset is unsupported");
+    if (t.strides != contiguous_strides(t.shape)) return invalid("CUDA tensor metadata must be contiguous");
+    auto buffer = std::dynamic_pointer_cast<CudaBuffer>(t.buffer);
+    if (!buffer) return invalid("CUDA tensor metadata requires a CUDA buffer");
+    auto bytes = byte_size(t.dtype, t.shape);
+    if (!bytes) return bytes.status();
+    if (buffer->nbytes() != bytes.value() || buffer->dtype() != t.dtype)
+      return invalid("CUDA buffer does not match tensor metadata");
+    if (buffer->device() != t.device.index) return invalid("CUDA buffer device does not match tensor device");
+    return CudaTensor(t.dtype, t.shape, std::move(buffer));
+  } catch (const std::invalid_argument& e) {
+    return invalid(e.what());
+  }
+}
+
+// ------------------------------------------------------------------ device API
+bool available() { return device_count() > 0 && tcx_sm100_device_supported(0) == TCX_OK; }
+
+Expected<std::string> device_name() {
+  auto info = device_info();
+  if (!info) return info.status();
+  return info.value().name;
+}
+
+Expected<DeviceInfo> device_info() {
+  DeviceScope scope(0);
+  if (!scope.ready()) return scope.status();
+  cudaDeviceProp prop{};
+  auto st = runtime_status(cudaGetDeviceProperties(&prop, 0), "cudaGetDeviceProperties");
+  if (!st.ok()) return st;
+  DeviceInfo info;
+  info.name = prop.name;
+  info.major = prop.major;
+  info.minor = prop.minor;
+  (void)cudaRuntimeGetVersion(&info.runtime_version);
+  (void)cudaDriverGetVersion(&info.driver_version);
+  (void)cudaMemGetInfo(&info.free_bytes, &info.total_bytes);
+  cudaGetLastError();
+  return info;
+}
+
+Expected<CudaTensor> empty(Shape shape, DType dtype, int device) {
+  try {
+    (void)contiguous_strides(shape);
+    auto buffer = CudaBuffer::create(dtype, shape, device);
+    if (!buffer) return buffer.status();
+    return CudaTensor(dtype, std::move(shape), buffer.move_value());
+  } catch (const std::invalid_argument& e) {
+    return invalid(e.what());
+  }
+}
+
+Expected<CudaTensor> from_cpu(const cpu::CpuTensor& tensor, int device) {
+  auto buffer = CudaBuffer::create(tensor.dtype(), tensor.shape(), device);
+  if (!buffer) return buffer.status();
+  if (buffer.value()->nbytes()) {
+    DeviceScope scope(device);
+    if (!scope.ready()) return scope.status();
+    auto st = runtime_status(cudaMemcpyAsync(buffer.value()->data(), tensor.data(), buffer.value()->nbytes(),
+                                             cudaMemcpyHostToDevice, scope.stream()),
+                             "CUDA upload");
+    if (st.ok()) st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA upload synchronize");
+    if (!st.ok()) return st;
+  }
+  return CudaTensor(tensor.dtype(), tensor.shape(), buffer.move_value());
+}
+
+Expected<cpu::CpuTensor> to_cpu(const CudaTensor& tensor) {
+  cpu::CpuTensor result(tensor.dtype(), tensor.shape());
+  if (tensor.nbytes()) {
+    DeviceScope scope(tensor.buffer()->device());
+    if (!scope.ready()) return scope.status();
+    auto st = runtime_status(cudaMemcpyAsync(result.mutable_data(), tensor.buffer()->data(), tensor.nbytes(),
+                                             cudaMemcpyDeviceToHost, scope.stream()),
+                             "CUDA download");
+    if (st.ok()) st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA download synchronize");
+    if (!st.ok()) return st;
+  }
+  return result;
+}
+
+// ------------------------------------------------------------------ execute
+Status CudaBackend::execute(const BackendExecution& e) {
+  try {
+    if (e.op_class == BackendOpClass::kKernel)
+      return {StatusCode::kUnavailable, "the sm100 backend serves primitives; compiled kernels are not supported"};
+    if (auto st = validate_primitive_execution_contract(e, "cuda"); !st.ok()) return st;
+    std::vector<CudaTensor> in;
+    in.reserve(e.inputs.size());
+    for (const auto& t : e.inputs) {
+      auto c = from_core_tensor(t);
+      if (!c) return c.status();
+      in.push_back(c.move_value());
+    }
+    const int device = e.op.kind == OpKind::kFill ? e.outputs[0].device.index : in.empty() ? 0 : in[0].buffer()->device();
+    for (const auto& t : in)
+      if (t.buffer()->device() != device) return invalid("device mismatch between CUDA inputs");
+    DeviceScope scope(device);
+    if (!scope.ready()) return scope.status();
+    Tensor result;
+    Executor ex(e, in, scope);
+    if (auto st = ex.run(result); !st.ok()) return st;
+    if (auto st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA stream synchronize"); !st.ok())
+      return st;
+    e.outputs[0] = std::move(result);  // publish only on success
+    return Status::Ok();
+  } catch (const std::invalid_argument& err) {
+    return invalid(err.what());
+  } catch (const std::exception& err) {
+    return {StatusCode::kInternal, err.what()};
+  }
+}
+
+}  // namespace tensorcx::cuda

@@ -168,6 +168,18 @@ __global__ void bias_act_kernel(const float* __restrict__ x, const float* __rest
   }
 }
 
+__global__ void fill_kernel(uint32_t* __restrict__ out, int64_t n, uint32_t bits) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int64_t done = 0;
+  if (reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const uint4 v = make_uint4(bits, bits, bits, bits);
+    for (int64_t i = tid; i < (n >> 2); i += stride) reinterpret_cast<uint4*>(out)[i] = v;
+    done = (n >> 2) << 2;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) out[i] = bits;
+}
+
 int ew_grid(int64_t n) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256 * 4), 8LL * sm_count() * 4)));
 }
@@ -203,6 +215,16 @@ int collapse(const int64_t* shape, std::vector<std::vector<int64_t>>& strides, i
 using namespace tcx;
 
 extern "C" {
+
+int tcx_sm100_fill(tcx_stream_t stream, void* output, int64_t count, uint32_t bits) {
+  clear_error();
+  if (count < 0) return invalid("negative element count");
+  if (count == 0) return TCX_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  TimedLaunch timer("fill", s);
+  fill_kernel<<<ew_grid(count), 256, 0, s>>>(static_cast<uint32_t*>(output), count, bits);
+  return launch_status("fill");
+}
 
 int tcx_sm100_unary(tcx_stream_t stream, int op, const float* input, float* output, int64_t count) {
   clear_error();

@@ -494,7 +494,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 constexpr int kFM = 64, kFN = 64, kFK = 16;
 
 // mode 0: always compute; mode 1: only when *nonfinite is set (fallback behind the
-// tensor-core kernel).
+// tensor-core kernel). BT: B is stored transposed ([n][k], K-major), as a linear weight.
+template <bool BT>
 __global__ void __launch_bounds__(256)
 gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ c,
                  int64_t m, int64_t n, int64_t k, int64_t batches, BatchMap bm,
@@ -524,7 +525,14 @@ gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float
         as[cc][rr] = (gm < m && gk < k) ? __ldg(ab + gm * k + gk) : 0.0f;
         const int br = e / kFN, bc = e % kFN;
         const int64_t bk = k0 + br, bn = n0 + bc;
-        bs[br][bc] = (bk < k && bn < n) ? __ldg(bb + bk * n + bn) : 0.0f;
+        if (BT) {
+          // transposed B: consecutive threads walk k for one n (coalesced along k)
+          const int tk = e % kFK, tn = e / kFK;
+          const int64_t gk = k0 + tk, gn = n0 + tn;
+          bs[tk][tn] = (gk < k && gn < n) ? __ldg(bb + gn * k + gk) : 0.0f;
+        } else {
+          bs[br][bc] = (bk < k && bn < n) ? __ldg(bb + bk * n + bn) : 0.0f;
+        }
       }
       __syncthreads();
 #pragma unroll
@@ -657,10 +665,11 @@ size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t
   return tensor_layout(m, n, k, std::max<int64_t>(lhs_batches, 1), std::max<int64_t>(rhs_batches, 1)).total;
 }
 
-int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
-                     int64_t n, int64_t k, int64_t batches, const int64_t* batch_shape,
-                     const int64_t* lhs_batch_strides, const int64_t* rhs_batch_strides, int32_t batch_rank,
-                     const float* bias, int act, int path, void* workspace, size_t workspace_bytes) {
+static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
+                      int64_t n, int64_t k, int64_t batches, const int64_t* batch_shape,
+                      const int64_t* lhs_batch_strides, const int64_t* rhs_batch_strides, int32_t batch_rank,
+                      const float* bias, int act, int path, void* workspace, size_t workspace_bytes,
+                      bool rhs_kmajor) {
   clear_error();
   if (m < 0 || n < 0 || k < 0 || batches < 0 || batch_rank < 0) return invalid("negative matmul extents");
   if (act != TCX_ACT_NONE && act != TCX_ACT_SILU && act != TCX_ACT_RELU) return invalid("unsupported activation");
@@ -679,7 +688,8 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
     const int grid = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
     {
       TimedLaunch timer("gemm_ffma", s);
-      gemm_ffma_kernel<<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
+      if (rhs_kmajor) gemm_ffma_kernel<true><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
+      else gemm_ffma_kernel<false><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, nullptr, 0);
     }
     return launch_status("ffma matmul");
   }
@@ -705,10 +715,17 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
       if (vec_a) split_rows<true><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
       else split_rows<false><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
     }
-    const bool vec_b = n % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
-    const int64_t tiles = nbb * ceil_div(n, 128) * (lay.kp / 32);
-    const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
-    {
+    if (rhs_kmajor) {
+      // B already K-major ([n][k], a linear weight): the row split applies as is
+      const bool vec_w = k % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+      dim3 grid_w(grid_a.x, static_cast<unsigned>(std::min<int64_t>(nbb * n, 65535)));
+      TimedLaunch timer("split_rows", s);
+      if (vec_w) split_rows<true><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);
+      else split_rows<false><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);
+    } else {
+      const bool vec_b = n % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+      const int64_t tiles = nbb * ceil_div(n, 128) * (lay.kp / 32);
+      const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
       TimedLaunch timer("split_cols", s);
       if (vec_b) split_cols<true><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
       else split_cols<false><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
@@ -755,9 +772,29 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
   const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
   {
     TimedLaunch timer("gemm_ffma_fallback", s);
-    gemm_ffma_kernel<<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+    if (rhs_kmajor) gemm_ffma_kernel<true><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+    else gemm_ffma_kernel<false><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
   }
   return launch_status("matmul fallback");
 }
 
+}
+
+int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
+                     int64_t n, int64_t k, int64_t batches, const int64_t* batch_shape,
+                     const int64_t* lhs_batch_strides, const int64_t* rhs_batch_strides, int32_t batch_rank,
+                     const float* bias, int act, int path, void* workspace, size_t workspace_bytes) {
+  return run_matmul(stream, lhs, rhs, output, m, n, k, batches, batch_shape, lhs_batch_strides,
+                    rhs_batch_strides, batch_rank, bias, act, path, workspace, workspace_bytes, false);
+}
+
+size_t tcx_sm100_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features, int path) {
+  return tcx_sm100_matmul_workspace_bytes(rows, out_features, in_features, 1, 1, path);
+}
+
+int tcx_sm100_linear(tcx_stream_t stream, const float* x, const float* w, const float* bias, float* output,
+                     int64_t rows, int64_t in_features, int64_t out_features, int act, int path,
+                     void* workspace, size_t workspace_bytes) {
+  return run_matmul(stream, x, w, output, rows, out_features, in_features, 1, nullptr, nullptr, nullptr, 0, bias,
+                    act, path, workspace, workspace_bytes, true);
 }  // extern "C"

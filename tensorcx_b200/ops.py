@@ -90,15 +90,27 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-           act: str = "none") -> torch.Tensor:
-    """linear(x, w[out, in], b[out]) (core/inference.cpp:89-102) as one matmul with the
-    bias (and optional activation) fused into the epilogue."""
+           act: str = "none", path: str = "auto") -> torch.Tensor:
+    """linear(x[..., in], w[out, in], b[out]) (core/inference.cpp:89-102) as one GEMM:
+    the weight is read in place (K-major), the bias and optional activation run in the
+    epilogue; no transpose copy, no separate add."""
     _check_tensor(x, "x"), _check_tensor(weight, "weight")
+    if x.dtype != torch.float32 or weight.dtype != torch.float32:
+        raise ValueError("inference values require float32 tensors")
     if x.dim() == 0 or weight.dim() != 2 or x.shape[-1] != weight.shape[1]:
         raise ValueError("linear requires (..., in_features) and (out_features, in_features)")
-    if bias is not None and bias.shape != (weight.shape[0],):
-        raise ValueError("linear bias must have shape (out_features,)")
-    return matmul(x, weight.t().contiguous(), bias=bias, act=act)
+    if bias is not None:
+        _check_tensor(bias, "bias")
+        if tuple(bias.shape) != (weight.shape[0],):
+            raise ValueError("linear bias must have shape (out_features,)")
+    rows = x.numel() // x.shape[-1] if x.shape[-1] else plan.numel(x.shape[:-1])
+    out = torch.empty(tuple(x.shape[:-1]) + (weight.shape[0],), dtype=torch.float32, device=x.device)
+    ws_bytes = lib().tcx_sm100_linear_workspace_bytes(rows, weight.shape[1], weight.shape[0], MATMUL_PATH[path])
+    keep, ws = _workspace(ws_bytes, x.device)
+    check(lib().tcx_sm100_linear(_stream(), _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), rows, weight.shape[1],
+                                 weight.shape[0], ACT[act], MATMUL_PATH[path], ws, ws_bytes))
+    del keep
+    return out
 
 
 # ---------------------------------------------------------------- reductions

@@ -1,0 +1,298 @@
+// TEST INFRASTRUCTURE: contract test of the sm100 CudaBackend, in the style of the
+// reference's tests/cpp/test_cuda_backend_contract.cpp (returns 77 to skip without a
+// GPU). Every hot-path primitive runs through CudaBackend::execute on device tensors
+// and is compared with the reference CpuBackend on the same inputs; malformed
+// descriptors must fail with kInvalidArgument and leave result slots untouched; the
+// memory pool's OOM / free-failure accounting is driven by an injected PoolRuntime
+// (host fakes, no GPU memory exhausted).
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "tensorcx/backends/cpu/cpu_backend.h"
+#include "tensorcx/backends/cuda/cuda_backend.h"
+#include "tensorcx/backends/cuda/cuda_device.h"
+#include "tensorcx/backends/cuda/cuda_memory_pool.h"
+
+using namespace tensorcx;
+
+namespace {
+int failures = 0;
+void check(bool ok, const std::string& what) {
+  if (!ok) {
+    std::fprintf(stderr, "FAIL: %s\n", what.c_str());
+    ++failures;
+  }
+}
+
+cpu::CpuTensor randn(Shape shape, std::uint32_t seed, float scale = 1.0f) {
+  std::mt19937 gen(seed);
+  std::normal_distribution<float> dist(0.0f, scale);
+  std::vector<float> v(static_cast<std::size_t>(numel(shape)));
+  for (auto& x : v) x = dist(gen);
+  return cpu::CpuTensor(shape, std::move(v));
+}
+
+cpu::CpuTensor randi(Shape shape, std::uint32_t seed) {
+  std::mt19937 gen(seed);
+  std::uniform_int_distribution<std::int32_t> dist(-1000, 1000);
+  std::vector<std::int32_t> v(static_cast<std::size_t>(numel(shape)));
+  for (auto& x : v) x = dist(gen);
+  return cpu::CpuTensor(shape, std::move(v));
+}
+
+Tensor on_gpu(const cpu::CpuTensor& t, int device = 0) {
+  auto c = cuda::from_cpu(t, device);
+  if (!c) {
+    std::fprintf(stderr, "upload failed: %s\n", c.status().message().c_str());
+    std::exit(1);
+  }
+  return cuda::to_core_tensor(c.value());
+}
+
+Status run(Backend& backend, OpDesc op, std::vector<Tensor> inputs, Tensor& out) {
+  std::vector<Tensor> outputs(1);
+  BackendExecution e{BackendOpClass::kPrimitive, op, inputs, outputs, std::nullopt, std::nullopt, {}};
+  auto st = backend.execute(e);
+  if (st.ok()) out = outputs[0];
+  return st;
+}
+
+cpu::CpuTensor download(const Tensor& t) {
+  auto c = cuda::from_core_tensor(t);
+  if (!c) { std::fprintf(stderr, "bad result: %s\n", c.status().message().c_str()); std::exit(1); }
+  auto h = cuda::to_cpu(c.value());
+  if (!h) { std::fprintf(stderr, "download failed: %s\n", h.status().message().c_str()); std::exit(1); }
+  return h.move_value();
+}
+
+// |gpu - cpu| <= atol + rtol |cpu| elementwise (NaN == NaN), or exact for int32.
+bool close(const cpu::CpuTensor& a, const cpu::CpuTensor& b, double rtol, double atol) {
+  if (a.shape() != b.shape() || a.dtype() != b.dtype()) return false;
+  if (a.dtype() == DType::kInt32) {
+    return std::memcmp(a.data(), b.data(), static_cast<std::size_t>(a.size()) * 4) == 0;
+  }
+  auto x = a.float_data(), y = b.float_data();
+  for (std::size_t i = 0; i < x.size(); ++i) {
+    if (std::isnan(x[i]) || std::isnan(y[i])) {
+      if (std::isnan(x[i]) != std::isnan(y[i])) return false;
+      continue;
+    }
+    if (std::fabs(double(x[i]) - y[i]) > atol + rtol * std::fabs(double(y[i]))) return false;
+  }
+  return true;
+}
+
+struct Case {
+  std::string name;
+  OpDesc op;
+  std::vector<cpu::CpuTensor> inputs;
+  double rtol, atol;
+};
+
+void compare(Backend& gpu, Backend& ref, const Case& c, int device = 0) {
+  std::vector<Tensor> gin, cin;
+  for (const auto& t : c.inputs) {
+    gin.push_back(on_gpu(t, device));
+    cin.push_back(cpu::to_core_tensor(t));
+  }
+  Tensor g, r;
+  auto gs = run(gpu, c.op, gin, g);
+  auto rs = run(ref, c.op, cin, r);
+  if (!rs.ok()) {
+    check(!gs.ok() && gs.code() == rs.code(), c.name + ": CPU rejects (" + rs.message() + "), GPU must too");
+    return;
+  }
+  if (!gs.ok()) { check(false, c.name + ": " + gs.message()); return; }
+  check(g.device.type == "cuda" && g.device.index == device, c.name + ": result device");
+  check(close(download(g), cpu::from_core_tensor(r), c.rtol, c.atol), c.name + ": parity with CpuBackend");
+}
+
+OpDesc desc(OpKind k) { OpDesc op; op.kind = k; return op; }
+OpDesc axis_op(OpKind k, std::int64_t axis, double eps = 1e-5) { OpDesc op; op.kind = k; op.axis = axis; op.epsilon = eps; return op; }
+OpDesc axes_op(OpKind k, Shape axes) { OpDesc op; op.kind = k; op.reduction_axes = axes; return op; }
+
+// host fakes for the pool contract
+int fake_oom_left = 0;
+int fake_free_errors = 0;
+std::vector<void*> fake_blocks;
+cudaError_t fake_allocate(void** p, std::size_t bytes) {
+  if (fake_oom_left > 0) { --fake_oom_left; return cudaErrorMemoryAllocation; }
+  *p = std::malloc(bytes);
+  fake_blocks.push_back(*p);
+  return cudaSuccess;
+}
+cudaError_t fake_free(void* p) {
+  std::free(p);
+  if (fake_free_errors > 0) { --fake_free_errors; return cudaErrorInvalidValue; }
+  return cudaSuccess;
+}
+cudaError_t fake_clear() { return cudaSuccess; }
+
+void pool_contract() {
+  using cuda::MemoryPool;
+  using cuda::PoolRuntime;
+  auto pool = std::make_shared<MemoryPool>(1024, 4, PoolRuntime{fake_allocate, fake_free, fake_clear});
+  check(pool->enter().ok(), "pool enter");
+  check(!std::make_shared<MemoryPool>(1024, 4, PoolRuntime{fake_allocate, fake_free, fake_clear})->enter().ok(),
+        "nested pool rejected");
+  auto a = pool->allocate(128);
+  check(a.has_value(), "pool allocate");
+  void* address = a.value();
+  pool->release(address, 128, true);
+  auto b = pool->allocate(128);
+  check(b.has_value() && b.value() == address && pool->stats().hits == 1, "exact-size reuse");
+  pool->release(b.value(), 128, true);
+  fake_oom_left = 1;  // next miss runs out: the cache is drained and the allocation retried once
+  auto c = pool->allocate(256);
+  check(c.has_value() && pool->stats().oom_retries == 1 && pool->stats().free_calls == 1, "OOM drain and retry");
+  pool->release(c.value(), 256, false);
+  check(pool->stats().uncached_returns == 1, "non-reusable block returned, not cached");
+  fake_oom_left = 2;  // a retry that also fails is one allocation failure
+  auto d = pool->allocate(64);
+  check(!d.has_value() && pool->stats().allocation_failures == 1, "failed retry accounting (no cache: no retry)");
+  fake_oom_left = 0;
+  auto e = pool->allocate(32);
+  pool->release(e.value(), 32, true);
+  fake_free_errors = 1;
+  check(!pool->trim().ok() && pool->stats().free_failures == 1 && pool->stats().cached_bytes == 0,
+        "trim reports free failure and gives ownership up");
+  check(pool->exit().ok(), "pool exit");
+  check(!pool->enter().ok(), "pools are single-use");
+  check(pool->stats().in_use_bytes == 0, "nothing left in use");
+}
+
+void error_contract(Backend& gpu) {
+  auto a = on_gpu(randn({2, 3}, 1));
+  Tensor sentinel;
+  sentinel.device = Device{"sentinel", 7};
+  std::vector<Tensor> outputs{sentinel};
+  // matmul contracting mismatch
+  std::vector<Tensor> in{a, a};
+  BackendExecution e{BackendOpClass::kPrimitive, desc(OpKind::kMatmul), in, outputs, std::nullopt, std::nullopt, {}};
+  auto st = gpu.execute(e);
+  check(st.code() == StatusCode::kInvalidArgument, "matmul shape mismatch -> invalid argument");
+  check(outputs[0].device.type == "sentinel", "failed matmul leaves the result slot untouched");
+  // bad epsilon
+  std::vector<Tensor> one{a};
+  BackendExecution n{BackendOpClass::kPrimitive, axis_op(OpKind::kRmsNorm, -1, -1.0), one, outputs, std::nullopt,
+                     std::nullopt, {}};
+  st = gpu.execute(n);
+  check(st.code() == StatusCode::kInvalidArgument && st.message().find("epsilon") != std::string::npos,
+        "bad epsilon -> invalid argument");
+  check(outputs[0].device.type == "sentinel", "failed norm leaves the result slot untouched");
+  // axis out of range, wrong input count, CPU tensor handed to the CUDA backend
+  BackendExecution r{BackendOpClass::kPrimitive, axis_op(OpKind::kSum, 2), one, outputs, std::nullopt, std::nullopt, {}};
+  check(gpu.execute(r).code() == StatusCode::kInvalidArgument, "axis out of range");
+  BackendExecution wrong{BackendOpClass::kPrimitive, desc(OpKind::kAdd), one, outputs, std::nullopt, std::nullopt, {}};
+  check(gpu.execute(wrong).code() == StatusCode::kInvalidArgument, "input count mismatch");
+  std::vector<Tensor> host{cpu::to_core_tensor(randn({2, 3}, 2))};
+  BackendExecution h{BackendOpClass::kPrimitive, desc(OpKind::kExp), host, outputs, std::nullopt, std::nullopt, {}};
+  check(gpu.execute(h).code() == StatusCode::kInvalidArgument, "CPU tensor rejected");
+  check(outputs[0].device.type == "sentinel", "rejected calls leave the result slot untouched");
+}
+}  // namespace
+
+int main() {
+  if (!cuda::available()) {
+    std::printf("no sm_100 GPU: skipped\n");
+    return 77;
+  }
+  cuda::CudaBackend gpu;
+  cpu::CpuBackend ref;
+  check(gpu.name() == "cuda", "backend name");
+  std::vector<Case> cases;
+  // matmul: reference test shapes, batched broadcast, and sizes that take the tcgen05 path
+  for (auto [a, b] : std::vector<std::pair<Shape, Shape>>{
+           {{2, 3}, {3, 4}}, {{15, 17}, {17, 31}}, {{65, 129}, {129, 67}}, {{3}, {3}}, {{2, 3, 4}, {4}},
+           {{2, 1, 3, 4}, {1, 5, 4, 6}}, {{2, 17, 19}, {1, 19, 33}}, {{256, 512}, {512, 384}},
+           {{3, 200, 160}, {160, 300}}, {{0, 3}, {3, 4}}, {{3, 0}, {0, 4}}})
+    cases.push_back({"matmul", desc(OpKind::kMatmul), {randn(a, 11), randn(b, 12)}, 1e-4, 1e-4});
+  // reductions: one axis, multi-axis, full; float32 and int32
+  for (auto k : {OpKind::kSum, OpKind::kMax, OpKind::kMean}) {
+    for (std::int64_t ax : {0, 1, -1}) cases.push_back({"axis", axis_op(k, ax), {randn({7, 300}, 21)}, 1e-5, 1e-5});
+    cases.push_back({"row65536", axis_op(k, -1), {randn({2, 3, 65536}, 22)}, 0, 0});  // bit-exact order
+    cases.push_back({"axes", axes_op(k, {0, 2}), {randn({4, 5, 6}, 23)}, 1e-5, 1e-5});
+    cases.push_back({"full", axes_op(k, {0, 1}), {randn({512, 1025}, 24)}, 1e-5, 1e-5});
+    if (k != OpKind::kMean) {
+      cases.push_back({"i32 axis", axis_op(k, 1), {randi({9, 777}, 25)}, 0, 0});
+      cases.push_back({"i32 full", axes_op(k, {0, 1}), {randi({300, 1000}, 26)}, 0, 0});
+    }
+  }
+  cases.push_back({"mean int32 rejected", axis_op(OpKind::kMean, 0), {randi({4}, 27)}, 0, 0});
+  for (auto k : {OpKind::kMin, OpKind::kArgmax}) {
+    cases.push_back({"math axis", axes_op(k, {1}), {randn({5, 3000}, 31)}, 0, 0});
+    cases.push_back({"math full", axes_op(k, {0, 1}), {randn({64, 4100}, 32)}, 0, 0});
+    cases.push_back({"math i32", axes_op(k, {0}), {randi({6, 9}, 33)}, 0, 0});
+  }
+  {
+    OpDesc clip = desc(OpKind::kClip);
+    std::vector<float> lo{0.0f}, hi{INFINITY};
+    cases.push_back({"relu = clip(lower=0)", clip,
+                     {randn({33, 7}, 34), cpu::CpuTensor(Shape{}, lo), cpu::CpuTensor(Shape{}, hi)}, 0, 0});
+  }
+  for (auto k : {OpKind::kSoftmax, OpKind::kRmsNorm, OpKind::kLayerNorm}) {
+    for (auto s : std::vector<Shape>{{16, 4096}, {4, 300}, {3, 33}})
+      cases.push_back({"row op", axis_op(k, -1), {randn(s, 41, 3.0f)}, 1e-5, 1e-5});
+    cases.push_back({"row op axis 0", axis_op(k, 0), {randn({50, 3}, 42)}, 1e-5, 1e-5});
+  }
+  {
+    OpDesc aff = axis_op(OpKind::kAffineLayerNorm, -1);
+    aff.has_weight = aff.has_bias = true;
+    cases.push_back({"affine layernorm", aff, {randn({8, 1024}, 51, 3.0f), randn({1024}, 52), randn({1024}, 53)}, 1e-5, 1e-5});
+    OpDesc rms = axis_op(OpKind::kAffineRmsNorm, -1);
+    rms.has_weight = true;
+    cases.push_back({"affine rmsnorm", rms, {randn({8, 1024}, 54, 3.0f), randn({1024}, 55)}, 1e-5, 1e-5});
+  }
+  for (auto k : {OpKind::kExp, OpKind::kGelu, OpKind::kSilu})
+    cases.push_back({"unary", desc(k), {randn({1000}, 61, 3.0f)}, 1e-6, 1e-6});
+  for (auto k : {OpKind::kAdd, OpKind::kSubtract, OpKind::kMultiply, OpKind::kDivide}) {
+    cases.push_back({"binary bcast", desc(k), {randn({64, 37}, 71), randn({37}, 72)}, 0, 0});
+    cases.push_back({"binary same", desc(k), {randn({5, 6}, 73), randn({5, 6}, 74)}, 0, 0});
+  }
+  cases.push_back({"int add wrap", desc(OpKind::kAdd), {randi({100}, 75), randi({100}, 76)}, 0, 0});
+  cases.push_back({"linear", desc(OpKind::kLinear), {randn({256, 784}, 81), randn({512, 784}, 82, 0.03f), randn({512}, 83)},
+                   1e-4, 1e-4});
+  cases.push_back({"linear no bias", desc(OpKind::kLinear), {randn({3, 5}, 84), randn({7, 5}, 85)}, 1e-4, 1e-4});
+  for (const auto& c : cases) compare(gpu, ref, c);
+
+  // fill descriptor
+  {
+    OpDesc f = desc(OpKind::kFill);
+    f.scalar_value = 2.5;
+    Tensor d{DType::kFloat32, {3, 5}, contiguous_strides({3, 5}), Device{"cuda", 0}, nullptr, 0};
+    std::vector<Tensor> outputs{d};
+    BackendExecution e{BackendOpClass::kPrimitive, f, {}, outputs, std::nullopt, std::nullopt, {}};
+    auto st = gpu.execute(e);
+    check(st.ok(), "fill: " + st.message());
+    if (st.ok()) {
+      auto h = download(outputs[0]);
+      bool ok = true;
+      for (float v : h.float_data()) ok = ok && v == 2.5f;
+      check(ok, "fill values");
+    }
+  }
+  error_contract(gpu);
+  pool_contract();
+  // the same ops inside a real stream-ordered pool scope
+  {
+    auto pool = std::make_shared<cuda::MemoryPool>(1 << 28, 64);
+    check(pool->enter().ok(), "real pool enter");
+    for (int i = 0; i < 3; ++i)
+      compare(gpu, ref, {"matmul in pool", desc(OpKind::kMatmul), {randn({256, 300}, 91), randn({300, 260}, 92)}, 1e-4, 1e-4});
+    check(pool->stats().hits > 0, "pool reuses blocks across calls");
+    check(pool->exit().ok(), "real pool exit");
+  }
+  // multi-device: a second GPU when present
+  if (cuda::device_count() > 1) {
+    compare(gpu, ref, {"matmul dev1", desc(OpKind::kMatmul), {randn({256, 512}, 93), randn({512, 384}, 94)}, 1e-4, 1e-4}, 1);
+    compare(gpu, ref, {"sum dev1", axes_op(OpKind::kSum, {0, 1}), {randi({700, 999}, 95)}, 0, 0}, 1);
+  }
+  std::printf("%zu parity cases, %d failures\n", cases.size(), failures);
+  return failures ? 1 : 0;
+}

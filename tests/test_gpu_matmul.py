@@ -152,9 +152,16 @@ def test_broadcast_rhs_tensor_path(tcx, oracle):
     frob_ok(host(tcx.matmul(dev(a2), dev(b2), path="tensor")), oracle.matmul(a2, b2), 64)
 
 
-def test_linear_fused(tcx, oracle):
+@pytest.mark.parametrize("path", ["auto", "ffma", "tensor"])
+@pytest.mark.parametrize("shape", [(256, 784, 512), (256, 512, 10), (3, 7, 5), (2, 130, 300, 200)])
+def test_linear_fused(tcx, oracle, path, shape):
+    """linear reads the [out, in] weight in place (no transpose copy) with the bias in
+    the GEMM epilogue; equals the reference composite transpose -> matmul -> add."""
     rng = np.random.default_rng(8)
-    x = rng.normal(size=(256, 784)).astype(np.float32)
-    w = rng.uniform(-1 / 28, 1 / 28, (512, 784)).astype(np.float32)
-    b = rng.normal(size=512).astype(np.float32)
-    frob_ok(host(tcx.linear(dev(x), dev(w), dev(b))), oracle.linear(x, w, b), 784)
+    *lead, fin, fout = shape
+    x = rng.normal(size=(*lead, fin)).astype(np.float32)
+    w = rng.uniform(-1 / np.sqrt(fin), 1 / np.sqrt(fin), (fout, fin)).astype(np.float32)
+    b = rng.normal(size=fout).astype(np.float32)
+    got = host(tcx.linear(dev(x), dev(w), dev(b), path=path))
+    assert got.shape == (*lead, fout)
+    frob_ok(got, oracle.linear(x, w, b), fin)

@@ -17,8 +17,11 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <string>
 
 #include "common.cuh"
+#include "ptx.cuh"
+
 
 namespace tcx {
 namespace {
@@ -211,6 +214,92 @@ row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, i
   }
 }
 
+// Long rows (8192 < n <= 32768, n % 4 == 0, 16-byte aligned): a persistent kernel, one
+// 1024-thread CTA per SM. The CTA holds the current row in registers while the next
+// row streams into shared memory through one cp.async.bulk (TMA bulk) copy that
+// completes on an mbarrier, so the SM's HBM reads never pause for the row's
+// reductions, exponentials and stores.
+template <int OP, int VPT>
+__global__ void __launch_bounds__(1024, 1)
+row_staged_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n, float eps,
+                  const float* __restrict__ w, const float* __restrict__ b, int* err) {
+  constexpr int THREADS = 1024, E = VPT * 4;
+  extern __shared__ __align__(128) float stage[];  // one row (n floats)
+  __shared__ float smem[32];
+  __shared__ uint64_t bar;
+  const uint32_t bar_addr = ptx::smem_u32(&bar);
+  const uint32_t stage_addr = ptx::smem_u32(stage);
+  const uint32_t bytes = static_cast<uint32_t>(n * 4);
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar_addr, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int64_t row) {  // thread 0 only
+    ptx::mbar_expect_tx(bar_addr, bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     stage_addr),
+                 "l"(x + row * n), "r"(bytes), "r"(bar_addr)
+                 : "memory");
+  };
+  int64_t row = blockIdx.x;
+  if (threadIdx.x == 0 && row < rows) issue(row);
+  const int n4 = static_cast<int>(n >> 2);
+  for (uint32_t it = 0; row < rows; row += gridDim.x, ++it) {
+    ptx::wait_or_give_up(bar_addr, it & 1u, err, 0x301);
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int i4 = static_cast<int>(threadIdx.x) + j * THREADS;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i4 < n4) t = reinterpret_cast<const float4*>(stage)[i4];
+      v[4 * j + 0] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+    }
+    __syncthreads();  // the whole row is in registers: the stage may be refilled
+    if (threadIdx.x == 0 && row + gridDim.x < rows) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(row + gridDim.x);
+    }
+    const float first = OP == kLayer ? __ldg(x + row * n) : 0.0f;
+    auto col = [](int q) -> int64_t {
+      return 4 * (static_cast<int64_t>(threadIdx.x) + static_cast<int64_t>(q >> 2) * THREADS) + (q & 3);
+    };
+    row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
+    float* orow = out + row * n;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int i4 = static_cast<int>(threadIdx.x) + j * THREADS;
+      if (i4 < n4) {
+        float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (w || b) {
+          t.x = affine(t.x, w, b, 4LL * i4 + 0); t.y = affine(t.y, w, b, 4LL * i4 + 1);
+          t.z = affine(t.z, w, b, 4LL * i4 + 2); t.w = affine(t.w, w, b, 4LL * i4 + 3);
+        }
+        __stcs(reinterpret_cast<float4*>(orow) + i4, t);
+      }
+    }
+  }
+}
+
+template <int OP, int VPT>
+int launch_staged_row(cudaStream_t s, const float* x, float* out, int64_t rows, int64_t n, float eps,
+                      const float* w, const float* b) {
+  const int smem = static_cast<int>(n * 4);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(row_staged_kernel<OP, VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             4 * 32768) != cudaSuccess)
+      return launch_status("staged row smem attribute");
+    attr_done[dev] = true;
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(rows, sm_count()));
+  TimedLaunch timer("row_staged", s);
+  row_staged_kernel<OP, VPT><<<grid, 1024, smem, s>>>(x, out, rows, n, eps, w, b, device_error_word());
+  return launch_status("staged row op");
+}
+
 // Rows longer than the register-resident limit: CTA per row, streaming passes.
 template <int OP>
 __global__ void __launch_bounds__(1024)
@@ -360,6 +449,8 @@ int run_rows(cudaStream_t s, const float* x, float* out, int64_t outer, int64_t 
   if (n <= 1024) launch_row<OP, 128, 2>(s, x, out, outer, n, eps, w, b, vec);
   else if (n <= 4096) launch_row<OP, 256, 4>(s, x, out, outer, n, eps, w, b, vec);
   else if (n <= 8192) launch_row<OP, 512, 4>(s, x, out, outer, n, eps, w, b, vec);
+  else if (vec && n <= 16384) return launch_staged_row<OP, 4>(s, x, out, outer, n, eps, w, b);
+  else if (vec && n <= 32768) return launch_staged_row<OP, 8>(s, x, out, outer, n, eps, w, b);
   else if (n <= 16384) launch_row<OP, 512, 8>(s, x, out, outer, n, eps, w, b, vec);
   else if (n <= 32768) launch_row<OP, 1024, 8>(s, x, out, outer, n, eps, w, b, vec);
   else {

@@ -83,10 +83,24 @@ def test_row_special_values(tcx, oracle, op, row):
 @pytest.mark.parametrize("op", ["rmsnorm", "layernorm"])
 @pytest.mark.parametrize("eps", [0.0, 1e-45, 1e-5, 1e30])
 @pytest.mark.parametrize("value", [0.0, 0.3, 1e38])
-@pytest.mark.parametrize("width", [33, 257, 4096])
+@pytest.mark.parametrize("width", [33, 257, 4096, 16384, 32768])
 def test_constant_rows(tcx, oracle, op, eps, value, width):
     a = np.full((3, width), value, dtype=np.float32)
-    close(host(getattr(tcx, op)(dev(a), axis=-1, eps=eps)), getattr(oracle, op)(a, -1, eps), 1e-5)
+    row_close(host(getattr(tcx, op)(dev(a), axis=-1, eps=eps)), getattr(oracle, op)(a, -1, eps),
+              exact_row_op(op, a, -1, eps))
+
+
+@pytest.mark.parametrize("op", ROW_OPS)
+@pytest.mark.parametrize("width", [12000, 16384, 30000, 32768])
+def test_mixed_constant_and_random_rows(tcx, oracle, op, width):
+    """Rows that take different branches inside one launch (a constant layernorm row
+    skips the variance exchange of the cluster kernels), interleaved with NaN rows."""
+    rng = np.random.default_rng(width)
+    x = (rng.normal(size=(9, width)) * 3).astype(np.float32)
+    x[1] = 0.25
+    x[4] = -7.0
+    x[6, width // 2] = np.nan
+    row_close(host(getattr(tcx, op)(dev(x), axis=-1)), getattr(oracle, op)(x, -1), exact_row_op(op, x, -1))
 
 
 @pytest.mark.parametrize("op", ["rmsnorm", "layernorm"])

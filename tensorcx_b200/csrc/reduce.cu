@@ -58,29 +58,65 @@ struct Acc {
   int64_t idx;
 };
 
-// Per-thread best element, compared as values (a handful of instructions per
-// element); converted to an exact order key once per thread (key_max / key_min).
-// A thread visits its elements in increasing index order, so strict comparisons keep
-// the first of equal values (and -0 == +0 compares equal). Once a NaN is held,
-// `bv == bv` is false and nothing replaces it: the first NaN wins.
-struct Best {
-  uint32_t bits;  // value held (raw word)
-  int64_t idx;    // its index, INT64_MAX when the thread has seen no element
-};
-
+// Per-thread best element for max / min / argmax, tracked as a value plus a 32-bit
+// offset from the chunk start: one compare and two selects per element. A thread
+// visits its elements in increasing index order, so the strict compare keeps the
+// first of equal values (and -0 == +0 compare equal). NaN is handled apart: the first
+// NaN wins outright, and one check per four elements (their sum is NaN if any is NaN,
+// or for +inf + -inf, which the exact slow path then rules out) keeps it off the
+// common path. The exact order key (key_max / key_min) is formed once per thread.
 template <int K, bool FP>
-__device__ __forceinline__ void take_best(Best& b, uint32_t bits, int64_t index) {
-  bool take;
-  if (FP) {
-    const float v = __uint_as_float(bits), bv = __uint_as_float(b.bits);
-    const bool beats = (K == kBestMax) ? !(v <= bv) : !(v >= bv);  // true for a NaN v
-    take = (beats && bv == bv) || b.idx == INT64_MAX;
-  } else {
-    const int32_t v = static_cast<int32_t>(bits), bv = static_cast<int32_t>(b.bits);
-    take = ((K == kBestMax) ? v > bv : v < bv) || b.idx == INT64_MAX;
+struct BestRun {
+  using V = typename std::conditional<FP, float, int32_t>::type;
+  V bv;
+  int32_t bi = -1;          // offset of bv, -1 while nothing beat the identity
+  int32_t first = -1;       // offset of the first element this thread saw
+  int32_t nan_at = -1;      // offset of the first NaN, -1 if none
+  __device__ BestRun() {
+    if constexpr (FP) bv = (K == kBestMax) ? -INFINITY : INFINITY;
+    else bv = (K == kBestMax) ? INT32_MIN : INT32_MAX;
   }
-  if (take) { b.bits = bits; b.idx = index; }
-}
+  __device__ __forceinline__ void one(uint32_t bits, int32_t off) {
+    V v;
+    if constexpr (FP) v = __uint_as_float(bits);
+    else v = static_cast<int32_t>(bits);
+    const bool better = (K == kBestMax) ? (v > bv) : (v < bv);
+    bv = better ? v : bv;
+    bi = better ? off : bi;
+  }
+  __device__ __forceinline__ void four(uint4 w, int32_t off) {
+    if (first < 0) first = off;
+    one(w.x, off + 0);
+    one(w.y, off + 1);
+    one(w.z, off + 2);
+    one(w.w, off + 3);
+    if constexpr (FP) {
+      const float s = __fadd_rn(__fadd_rn(__uint_as_float(w.x), __uint_as_float(w.y)),
+                                __fadd_rn(__uint_as_float(w.z), __uint_as_float(w.w)));
+      if (s != s && nan_at < 0) {
+        if (is_nan_bits(w.x)) nan_at = off;
+        else if (is_nan_bits(w.y)) nan_at = off + 1;
+        else if (is_nan_bits(w.z)) nan_at = off + 2;
+        else if (is_nan_bits(w.w)) nan_at = off + 3;
+      }
+    }
+  }
+  __device__ __forceinline__ void single(uint32_t bits, int32_t off) {
+    if (first < 0) first = off;
+    one(bits, off);
+    if constexpr (FP) {
+      if (nan_at < 0 && is_nan_bits(bits)) nan_at = off;
+    }
+  }
+  // (key, global index) of this thread's best; key 0 / INT64_MAX when it saw nothing.
+  __device__ __forceinline__ void result(const uint32_t* chunk, int64_t base, uint32_t& key, int64_t& idx) const {
+    int32_t at = nan_at >= 0 ? nan_at : (bi >= 0 ? bi : first);
+    if (at < 0) { key = 0; idx = INT64_MAX; return; }
+    const uint32_t bits = chunk[at];
+    key = (K == kBestMax) ? key_max(bits, FP) : key_min(bits, FP);
+    idx = base + at;
+  }
+};
 
 template <int K, bool FP>
 __device__ __forceinline__ void take(Acc& a, int slot, uint32_t bits, int64_t index) {
@@ -151,7 +187,7 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
 #pragma unroll
     for (int s = 0; s < 4 * kUnroll; ++s) { a.f[s] = 0.0f; a.u[s] = 0u; }
     a.key = 0; a.idx = INT64_MAX;
-    Best best{0u, INT64_MAX};
+    BestRun<K, FP> best;
     constexpr bool kBestKind = K == kBestMax || K == kBestMin;
     const int tid = threadIdx.x;
     int64_t tail_begin = begin;
@@ -167,10 +203,7 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
         for (int u = 0; u < kUnroll; ++u) {
           const int64_t e = begin + 4 * (i + u * kStage1Threads) + index_base;
           if constexpr (kBestKind) {
-            take_best<K, FP>(best, v[u].x, e + 0);
-            take_best<K, FP>(best, v[u].y, e + 1);
-            take_best<K, FP>(best, v[u].z, e + 2);
-            take_best<K, FP>(best, v[u].w, e + 3);
+            best.four(v[u], static_cast<int32_t>(4 * (i + u * kStage1Threads)));
           } else {
             take<K, FP>(a, 4 * u + 0, v[u].x, e + 0);
             take<K, FP>(a, 4 * u + 1, v[u].y, e + 1);
@@ -183,10 +216,7 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
         const uint4 v = ldg_stream(xv + i);
         const int64_t e = begin + 4 * i + index_base;
         if constexpr (kBestKind) {
-          take_best<K, FP>(best, v.x, e + 0);
-          take_best<K, FP>(best, v.y, e + 1);
-          take_best<K, FP>(best, v.z, e + 2);
-          take_best<K, FP>(best, v.w, e + 3);
+          best.four(v, static_cast<int32_t>(4 * i));
         } else {
           take<K, FP>(a, 0, v.x, e + 0);
           take<K, FP>(a, 1, v.y, e + 1);
@@ -197,16 +227,13 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
       tail_begin = begin + nvec * 4;
     }
     for (int64_t j = tail_begin + tid; j < end; j += kStage1Threads) {
-      if constexpr (kBestKind) take_best<K, FP>(best, __ldg(xr + j), j + index_base);
+      if constexpr (kBestKind) best.single(__ldg(xr + j), static_cast<int32_t>(j - begin));
       else take<K, FP>(a, 0, __ldg(xr + j), j + index_base);
     }
 
     uint32_t bits = 0, key = a.key;
     int64_t idx = a.idx;
-    if constexpr (kBestKind) {
-      idx = best.idx;
-      key = idx == INT64_MAX ? 0u : ((K == kBestMax) ? key_max(best.bits, FP) : key_min(best.bits, FP));
-    }
+    if constexpr (kBestKind) best.result(xr + begin, begin + index_base, key, idx);
     if (K == kSumF) {
       // fixed pairwise order over the 16 accumulators
       float t[4 * kUnroll];
@@ -486,6 +513,7 @@ int tree_reduce(cudaStream_t s, int op, int dtype, const void* input, int64_t ro
   const Stage1Grid g = stage1_grid(rows, n);
   const size_t need = static_cast<size_t>(rows) * g.parts * sizeof(tcx_partial);
   if (!ws || ws_bytes < need) return invalid("reduction workspace is missing or too small");
+  if (g.chunk > INT32_MAX) return invalid("reduction chunk exceeds 2^31 elements");
   auto* parts = static_cast<tcx_partial*>(ws);
   const auto* x = static_cast<const uint32_t*>(input);
   const bool fp = dtype == TCX_FLOAT32;

@@ -73,6 +73,26 @@ struct Block {
     for (int off = 16; off > 0; off >>= 1) t = nan_max(t, __shfl_xor_sync(0xffffffffu, t, off));
     return t;
   }
+  // Sums two values in one pass (one pair of barriers instead of two).
+  __device__ static float2 sum2(float a, float b, float* smem) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+      b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, off));
+    }
+    if (kWarps == 1) return make_float2(a, b);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) { smem[warp] = a; smem[32 + warp] = b; }
+    __syncthreads();
+    float ta = lane < kWarps ? smem[lane] : 0.0f, tb = lane < kWarps ? smem[32 + lane] : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      ta = __fadd_rn(ta, __shfl_xor_sync(0xffffffffu, ta, off));
+      tb = __fadd_rn(tb, __shfl_xor_sync(0xffffffffu, tb, off));
+    }
+    return make_float2(ta, tb);
+  }
   __device__ static bool all(bool v, float* smem) {
     v = __all_sync(0xffffffffu, v);
     if (kWarps == 1) return v;
@@ -115,12 +135,12 @@ __device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, floa
 #pragma unroll
     for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], scale);
   } else {
-    float s = 0.0f;
-    bool eq = true;
+    float s = 0.0f, neq = 0.0f;  // neq counts elements != first (exact below 2^24 per thread)
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (col(i) < n) { s = __fadd_rn(s, v[i]); eq = eq && (v[i] == first); }
-    s = B::sum(s, smem);
-    eq = B::all(eq, smem);
+    for (int i = 0; i < E; ++i) if (col(i) < n) { s = __fadd_rn(s, v[i]); neq += (v[i] == first) ? 0.0f : 1.0f; }
+    const float2 r = B::sum2(s, neq, smem);
+    s = r.x;
+    const bool eq = r.y == 0.0f;
     if (eq && isfinite(first)) {
       const float value = eps == 0.0f ? __int_as_float(0x7fc00000) : 0.0f;
 #pragma unroll
@@ -163,7 +183,7 @@ __global__ void __launch_bounds__(THREADS)
 row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n,
            float eps, const float* __restrict__ w, const float* __restrict__ b) {
   constexpr int E = VPT * 4;
-  __shared__ float smem[32];
+  __shared__ float smem[64];
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* xr = x + row * n;
     float* orow = out + row * n;
@@ -225,7 +245,7 @@ row_staged_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t 
                   const float* __restrict__ w, const float* __restrict__ b, int* err) {
   constexpr int THREADS = 1024, E = VPT * 4;
   extern __shared__ __align__(128) float stage[];  // one row (n floats)
-  __shared__ float smem[32];
+  __shared__ float smem[64];
   __shared__ uint64_t bar;
   const uint32_t bar_addr = ptx::smem_u32(&bar);
   const uint32_t stage_addr = ptx::smem_u32(stage);

@@ -246,6 +246,19 @@ int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, fl
                      const float* bias, int act, int path, void* workspace,
                      size_t workspace_bytes);
 
+/* C = A @ B for HOST buffers A [m, k], B [k, n], C [m, n] (row-major float32), the
+ * transfer-inclusive form of tcx_sm100_matmul. B is uploaded once; A and C move in
+ * row chunks through three streams (upload, compute, download) so copies in both
+ * directions overlap the GEMMs of neighbouring chunks. Synchronous: returns when C is
+ * complete in host memory. Host buffers should be page-locked (cudaHostAlloc or
+ * cudaHostRegister); pageable buffers still work, without overlap. `workspace` is
+ * device memory of at least tcx_sm100_matmul_host_workspace_bytes(m, n, k). Uses the
+ * current device. (The reference's equivalent is from_cpu, matmul and to_cpu in
+ * sequence, cuda_backend.cpp:215-264.) */
+size_t tcx_sm100_matmul_host_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_host, int64_t m, int64_t n,
+                          int64_t k, void* workspace, size_t workspace_bytes);
+
 /* linear(x, w, bias): out[r, o] = act(sum_k x[r, k] * w[o, k] + bias[o]) for x [rows, in],
  * w [out_features, in] (the nn.Linear layout, i.e. K-major), bias [out_features] or
  * NULL. One GEMM with the bias (and activation) in its epilogue; the weight is used

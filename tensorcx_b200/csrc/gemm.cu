@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -778,8 +779,6 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   return launch_status("matmul fallback");
 }
 
-}
-
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
                      int64_t n, int64_t k, int64_t batches, const int64_t* batch_shape,
                      const int64_t* lhs_batch_strides, const int64_t* rhs_batch_strides, int32_t batch_rank,
@@ -797,4 +796,126 @@ int tcx_sm100_linear(tcx_stream_t stream, const float* x, const float* w, const 
                      void* workspace, size_t workspace_bytes) {
   return run_matmul(stream, x, w, output, rows, out_features, in_features, 1, nullptr, nullptr, nullptr, 0, bias,
                     act, path, workspace, workspace_bytes, true);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ host-buffer matmul
+namespace {
+struct HostPlan {
+  int64_t chunk_m, chunks;
+  size_t off_b, off_a[2], off_c[2], off_ws, ws_bytes, total;
+};
+
+HostPlan host_plan(int64_t m, int64_t n, int64_t k) {
+  HostPlan p;
+  p.chunks = m >= 1024 ? 4 : 1;
+  p.chunk_m = (m + p.chunks - 1) / p.chunks;
+  p.chunk_m = (p.chunk_m + kBM - 1) / kBM * kBM;
+  p.chunks = (m + p.chunk_m - 1) / p.chunk_m;
+  size_t off = 0;
+  p.off_b = off;
+  off = align_up(off + static_cast<size_t>(k * n) * 4, 1024);
+  for (int s = 0; s < 2; ++s) {
+    p.off_a[s] = off;
+    off = align_up(off + static_cast<size_t>(p.chunk_m * k) * 4, 1024);
+    p.off_c[s] = off;
+    off = align_up(off + static_cast<size_t>(p.chunk_m * n) * 4, 1024);
+  }
+  p.off_ws = off;
+  p.ws_bytes = tcx_sm100_matmul_workspace_bytes(p.chunk_m, n, k, 1, 1, TCX_MATMUL_AUTO);
+  p.total = align_up(off + p.ws_bytes, 1024);
+  return p;
+}
+
+struct Streams {
+  cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
+  cudaEvent_t b_ready = nullptr, a_ready = nullptr, c_ready = nullptr, a_free[2] = {nullptr, nullptr},
+              c_free[2] = {nullptr, nullptr};
+  cudaError_t create() {
+    cudaError_t e = cudaSuccess;
+    for (cudaStream_t* st : {&in, &comp, &out})
+      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(st, cudaStreamNonBlocking);
+    for (cudaEvent_t* ev : {&b_ready, &a_ready, &c_ready, &a_free[0], &a_free[1], &c_free[0], &c_free[1]})
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    return e;
+  }
+  ~Streams() {
+    for (cudaEvent_t ev : {b_ready, a_ready, c_ready, a_free[0], a_free[1], c_free[0], c_free[1]})
+      if (ev) cudaEventDestroy(ev);
+    for (cudaStream_t st : {in, comp, out})
+      if (st) cudaStreamDestroy(st);
+  }
+};
+}  // namespace
+
+extern "C" {
+
+size_t tcx_sm100_matmul_host_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k < 0) return 0;
+  return host_plan(m, n, k).total;
+}
+
+int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_host, int64_t m, int64_t n,
+                          int64_t k, void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (m < 0 || n < 0 || k < 0) return invalid("negative matmul extents");
+  if (m == 0 || n == 0) return TCX_OK;
+  if (!c_host || (k > 0 && (!a_host || !b_host))) return invalid("missing host buffer");
+  const HostPlan p = host_plan(m, n, k);
+  if (!workspace || workspace_bytes < p.total) return invalid("matmul workspace is missing or too small");
+  if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("matmul workspace must be 1024-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* b_dev = reinterpret_cast<float*>(ws + p.off_b);
+  Streams st;
+  if (cudaError_t e = st.create(); e != cudaSuccess) {
+    set_error(std::string("matmul_host streams: ") + cudaGetErrorString(e));
+    return TCX_INTERNAL;
+  }
+  auto fail = [](cudaError_t e, const char* what) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return TCX_INTERNAL;
+  };
+  if (k > 0) {
+    if (cudaError_t e = cudaMemcpyAsync(b_dev, b_host, static_cast<size_t>(k * n) * 4, cudaMemcpyHostToDevice, st.in);
+        e != cudaSuccess)
+      return fail(e, "matmul_host B upload");
+  }
+  cudaEventRecord(st.b_ready, st.in);
+  cudaStreamWaitEvent(st.comp, st.b_ready, 0);
+  for (int64_t i = 0; i < p.chunks; ++i) {
+    const int slot = static_cast<int>(i & 1);
+    const int64_t r0 = i * p.chunk_m;
+    const int64_t rows = std::min<int64_t>(p.chunk_m, m - r0);
+    float* a_dev = reinterpret_cast<float*>(ws + p.off_a[slot]);
+    float* c_dev = reinterpret_cast<float*>(ws + p.off_c[slot]);
+    // upload A chunk once the GEMM two chunks back has finished reading this slot
+    if (i >= 2) cudaStreamWaitEvent(st.in, st.a_free[slot], 0);
+    if (k > 0) {
+      if (cudaError_t e = cudaMemcpyAsync(a_dev, a_host + r0 * k, static_cast<size_t>(rows * k) * 4,
+                                          cudaMemcpyHostToDevice, st.in);
+          e != cudaSuccess)
+        return fail(e, "matmul_host A upload");
+    }
+    cudaEventRecord(st.a_ready, st.in);
+    cudaStreamWaitEvent(st.comp, st.a_ready, 0);
+    if (i >= 2) cudaStreamWaitEvent(st.comp, st.c_free[slot], 0);  // C slot downloaded
+    const int rc = run_matmul(reinterpret_cast<tcx_stream_t>(st.comp), a_dev, b_dev, c_dev, rows, n, k, 1, nullptr,
+                              nullptr, nullptr, 0, nullptr, TCX_ACT_NONE, TCX_MATMUL_AUTO, ws + p.off_ws, p.ws_bytes,
+                              false);
+    if (rc != TCX_OK) return rc;
+    cudaEventRecord(st.a_free[slot], st.comp);
+    cudaEventRecord(st.c_ready, st.comp);
+    cudaStreamWaitEvent(st.out, st.c_ready, 0);
+    if (cudaError_t e = cudaMemcpyAsync(c_host + r0 * n, c_dev, static_cast<size_t>(rows * n) * 4,
+                                        cudaMemcpyDeviceToHost, st.out);
+        e != cudaSuccess)
+      return fail(e, "matmul_host C download");
+    cudaEventRecord(st.c_free[slot], st.out);
+  }
+  if (cudaError_t e = cudaStreamSynchronize(st.out); e != cudaSuccess) return fail(e, "matmul_host synchronize");
+  if (cudaError_t e = cudaStreamSynchronize(st.comp); e != cudaSuccess) return fail(e, "matmul_host synchronize");
+  return launch_status("matmul_host");
+}
+
 }  // extern "C"

@@ -89,6 +89,32 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
     return out
 
 
+def matmul_host(a_host: torch.Tensor, b_host: torch.Tensor, c_host: torch.Tensor | None = None,
+                device: int | None = None) -> torch.Tensor:
+    """C = A @ B for 2-D float32 HOST tensors (pinned for copy/compute overlap):
+    tcx_sm100_matmul_host pipelines the uploads, GEMMs and downloads in row chunks.
+    Returns the host tensor C (synchronous)."""
+    for t, name in ((a_host, "lhs"), (b_host, "rhs")):
+        if not isinstance(t, torch.Tensor) or t.is_cuda or t.dtype != torch.float32 or t.dim() != 2:
+            raise ValueError(f"{name} must be a 2-D float32 host tensor")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    m, k = a_host.shape
+    if b_host.shape[0] != k:
+        raise ValueError("matmul shape mismatch: contracting dimensions differ")
+    n = b_host.shape[1]
+    if c_host is None:
+        c_host = torch.empty((m, n), dtype=torch.float32, pin_memory=a_host.is_pinned())
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        ws_bytes = lib().tcx_sm100_matmul_host_workspace_bytes(m, n, k)
+        keep, ws = _workspace(ws_bytes, dev)
+        torch.cuda.current_stream().synchronize()  # workspace allocation is stream-ordered
+        check(lib().tcx_sm100_matmul_host(_ptr(a_host), _ptr(b_host), _ptr(c_host), m, n, k, ws, ws_bytes))
+    del keep
+    return c_host
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            act: str = "none", path: str = "auto") -> torch.Tensor:
     """linear(x[..., in], w[out, in], b[out]) (core/inference.cpp:89-102) as one GEMM:

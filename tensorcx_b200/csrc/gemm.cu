@@ -181,38 +181,53 @@ __device__ __forceinline__ float4 ldg_f4(const float* p) {
 }
 
 // A [nb][rows][K] -> W [2*nb][rows][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
-// blockIdx.y walks rows, threads walk 4-wide K chunks: one 128-bit load and two
-// 128-bit stores per thread step when VEC (K % 4 == 0, 16-byte aligned A).
+// A flat grid-stride walk over 4-wide K chunks of all rows; each thread issues 4
+// independent 128-bit loads before converting (VEC: K % 4 == 0, 16-byte aligned A),
+// so enough bytes are in flight per SM to run at HBM speed.
 template <bool VEC>
 __global__ void __launch_bounds__(256)
 split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows, int64_t k,
            int64_t kp, int* __restrict__ nonfinite) {
+  constexpr int U = 4;
   const int64_t plane = rows * kp;
-  const int64_t kq = kp >> 2;
+  const int64_t kq = kp >> 2;                // 4-wide chunks per row
+  const int64_t total = nb * rows * kq;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   bool bad = false;
-  for (int64_t row = blockIdx.y; row < nb * rows; row += gridDim.y) {
-    const int64_t b = row / rows, r = row - b * rows;
-    const float* src = a + row * k;
-    float* dhi = w + (2 * b) * plane + r * kp;
-    float* dlo = dhi + plane;
-    for (int64_t q = blockIdx.x * 256LL + threadIdx.x; q < kq; q += 256LL * gridDim.x) {
-      const int64_t c = q * 4;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (VEC) {
-        if (c < k) x = ldg_f4(src + c);
-      } else {
-        if (c + 0 < k) x.x = __ldg(src + c + 0);
-        if (c + 1 < k) x.y = __ldg(src + c + 1);
-        if (c + 2 < k) x.z = __ldg(src + c + 2);
-        if (c + 3 < k) x.w = __ldg(src + c + 3);
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * U) {
+    float4 x[U];
+    int64_t row[U], c[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t q = base + u * stride;
+      x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      row[u] = q / kq;
+      c[u] = (q - row[u] * kq) * 4;
+      if (q < total) {
+        const float* src = a + row[u] * k;
+        if (VEC) {
+          if (c[u] < k) x[u] = ldg_f4(src + c[u]);
+        } else {
+          if (c[u] + 0 < k) x[u].x = __ldg(src + c[u] + 0);
+          if (c[u] + 1 < k) x[u].y = __ldg(src + c[u] + 1);
+          if (c[u] + 2 < k) x[u].z = __ldg(src + c[u] + 2);
+          if (c[u] + 3 < k) x[u].w = __ldg(src + c[u] + 3);
+        }
       }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (base + u * stride >= total) continue;
+      const int64_t b = row[u] / rows, r = row[u] - b * rows;
       float4 h, l;
-      split_one(x.x, h.x, l.x, bad);
-      split_one(x.y, h.y, l.y, bad);
-      split_one(x.z, h.z, l.z, bad);
-      split_one(x.w, h.w, l.w, bad);
-      *reinterpret_cast<float4*>(dhi + c) = h;
-      *reinterpret_cast<float4*>(dlo + c) = l;
+      split_one(x[u].x, h.x, l.x, bad);
+      split_one(x[u].y, h.y, l.y, bad);
+      split_one(x[u].z, h.z, l.z, bad);
+      split_one(x[u].w, h.w, l.w, bad);
+      float* dhi = w + (2 * b) * plane + r * kp + c[u];
+      *reinterpret_cast<float4*>(dhi) = h;
+      *reinterpret_cast<float4*>(dhi + plane) = l;
     }
   }
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
@@ -708,9 +723,7 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
   {
     const bool vec_a = k % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0;
-    const int64_t kq = lay.kp / 4;
-    dim3 grid_a(static_cast<unsigned>(std::min<int64_t>(ceil_div(kq, 256), 64)),
-                static_cast<unsigned>(std::min<int64_t>(nba * m, 65535)));
+    const int grid_a = static_cast<int>(std::min<int64_t>(ceil_div(nba * m * (lay.kp / 4), 256 * 4), 16LL * sms));
     {
       TimedLaunch timer("split_rows", s);
       if (vec_a) split_rows<true><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
@@ -719,7 +732,7 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
     if (rhs_kmajor) {
       // B already K-major ([n][k], a linear weight): the row split applies as is
       const bool vec_w = k % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
-      dim3 grid_w(grid_a.x, static_cast<unsigned>(std::min<int64_t>(nbb * n, 65535)));
+      const int grid_w = static_cast<int>(std::min<int64_t>(ceil_div(nbb * n * (lay.kp / 4), 256 * 4), 16LL * sms));
       TimedLaunch timer("split_rows", s);
       if (vec_w) split_rows<true><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);
       else split_rows<false><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);

@@ -380,7 +380,11 @@ def gpu_arm(args):
                        "per_gpu": f"{size}^3", "parallelism": f"independent products, {world} GPU(s)",
                        "l2": "inputs (256 MiB each) larger than the 126 MB L2; no flush"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
-                         "frac": achieved / peak_3x, "traffic": None,
+                         "frac": achieved / peak_3x,
+                         # DRAM bytes read + written by one gemm_tf32x3 launch at 8192^3 in one
+                         # ncu capture (profiles/gemm_tf32x3_matmul_8192_traffic.md)
+                         "traffic": 6142193408 if size == 8192 else None,
+                         "traffic_unit": "B per launch",
                          "kernel": "gemm_tf32x3 (tcgen05.mma kind::tf32 x3 per k-step)",
                          "kernel_ms": gemm_avg_ms,
                          "peak_note": f"cuBLAS TF32 GEMM {size}^3 measured in this run = {tf32_tflops:.1f} TFLOP/s, "

@@ -15,7 +15,9 @@ from __future__ import annotations
 import builtins
 import ctypes
 import math
+import operator
 
+import numpy as np
 import torch
 
 from . import plan
@@ -140,23 +142,62 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 
 # ---------------------------------------------------------------- reductions
-def _axes_sequence(axis, rank):
-    values = tuple(axis) if isinstance(axis, (tuple, list)) else (axis,)
-    scalar = rank == 0 and len(values) == 1 and values[0] in (0, -1)
-    if scalar:
-        return (), True
-    out = []
-    for v in values:
-        if not -rank <= v < rank:
-            raise ValueError("reduction axis is out of range")
-        out.append(v % rank)
-    return tuple(out), False
+def _normalize_axis(axis) -> int:
+    """tensor.py:422-431: an operator.index integer, never a bool."""
+    if isinstance(axis, (bool, np.bool_)):
+        raise ValueError("axis must be an integer")
+    try:
+        value = operator.index(axis)
+    except TypeError:
+        raise ValueError("axis must be an integer") from None
+    if value < -(2**63) or value > 2**63 - 1:
+        raise ValueError("axis is out of range")
+    return int(value)
 
 
-def _reduce(name: str, x: torch.Tensor, axis) -> torch.Tensor:
-    """tensor.py:_reduce: a single axis uses the one-axis primitive, otherwise the
-    multi-axis plan (every axis when axis is None)."""
+def _axis_sequence(axes) -> tuple[tuple[int, ...], bool]:
+    """tensor.py:279-292: integer axes and whether the argument was one integer."""
+    if isinstance(axes, (bool, np.bool_, str, bytes)):
+        raise ValueError("axis must be an integer or iterable of integers")
+    try:
+        value = operator.index(axes)
+    except TypeError:
+        try:
+            values = tuple(axes)
+        except TypeError:
+            raise ValueError("axis must be an integer or iterable of integers") from None
+        return tuple(_normalize_axis(v) for v in values), False
+    return (_normalize_axis(value),), True
+
+
+def _axes_in_rank(axes, rank: int, label: str = "reduction axis") -> tuple[int, ...]:
+    """tensor.py:295-301: in range after wrapping negatives, no repeats."""
+    normalized = tuple(a + rank if a < 0 else a for a in axes)
+    if builtins.any(a < 0 or a >= rank for a in normalized):
+        raise ValueError(f"{label} is out of range")
+    if len(set(normalized)) != len(normalized):
+        raise ValueError("axes must not repeat")
+    return normalized
+
+
+def _check_keepdims(keepdims) -> None:
+    if not isinstance(keepdims, (bool, np.bool_)):
+        raise TypeError("keepdims must be a boolean")
+
+
+def _keep(result: torch.Tensor, x: torch.Tensor, axes, keepdims) -> torch.Tensor:
+    """tensor.py:526-529: reduced axes come back as extent 1 (a view, no copy)."""
+    if keepdims and x.dim():
+        selected = set(axes)
+        return result.reshape(tuple(1 if i in selected else n for i, n in enumerate(x.shape)))
+    return result
+
+
+def _reduce(name: str, x: torch.Tensor, axis, keepdims=False) -> torch.Tensor:
+    """tensor.py:508-529: a single axis (or a scalar's 0/-1) uses the one-axis
+    primitive, every other selection (None = all axes) the multi-axis plan."""
     _check_tensor(x)
+    _check_keepdims(keepdims)
     dt = _dtype(x)
     if name == "mean" and dt != FLOAT32:
         raise ValueError("mean only supports float32 tensors")
@@ -164,7 +205,9 @@ def _reduce(name: str, x: torch.Tensor, axis) -> torch.Tensor:
     if axis is None:
         axes, scalar = tuple(range(rank)), rank == 0
     else:
-        axes, scalar = _axes_sequence(axis, rank)
+        values, single = _axis_sequence(axis)
+        scalar = rank == 0 and single and values[0] in (0, -1)
+        axes = () if scalar else _axes_in_rank(values, rank)
     if scalar or len(axes) == 1:
         shape, outer, reduce, inner = plan.axis(list(x.shape), axes[0] if axes else 0)
         if name == "max" and reduce == 0:
@@ -174,7 +217,7 @@ def _reduce(name: str, x: torch.Tensor, axis) -> torch.Tensor:
         keep, ws = _workspace(ws_bytes, x.device)
         check(lib().tcx_sm100_axis(_stream(), OP[name], dt, _ptr(x), _ptr(out), outer, reduce, inner,
                                    0.0, ws, ws_bytes))
-        return out
+        return _keep(out, x, axes, keepdims)
     p = plan.reduction(list(x.shape), axes)
     if name == "max" and p.reduction_size == 0:
         raise ValueError("max reduction requires non-empty axes")
@@ -187,38 +230,43 @@ def _reduce(name: str, x: torch.Tensor, axis) -> torch.Tensor:
     check(lib().tcx_sm100_reduce_axes(_stream(), OP[name], dt, _ptr(x), _ptr(out), groups,
                                       p.reduction_size, i64_array(p.index_metadata),
                                       len(p.output_shape), x.dim(), ws, ws_bytes))
-    return out
+    return _keep(out, x, axes, keepdims)
 
 
-def sum(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001 - tensor.cx name
-    return _reduce("sum", x, axis)
+def sum(x: torch.Tensor, axis=None, keepdims=False) -> torch.Tensor:  # noqa: A001 - tensor.cx name
+    return _reduce("sum", x, axis, keepdims)
 
 
-def max(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001
-    return _reduce("max", x, axis)
+def max(x: torch.Tensor, axis=None, keepdims=False) -> torch.Tensor:  # noqa: A001
+    return _reduce("max", x, axis, keepdims)
 
 
-def mean(x: torch.Tensor, axis=None) -> torch.Tensor:
-    return _reduce("mean", x, axis)
+def mean(x: torch.Tensor, axis=None, keepdims=False) -> torch.Tensor:
+    return _reduce("mean", x, axis, keepdims)
 
 
-def _min_argmax(name: str, x: torch.Tensor, axis) -> torch.Tensor:
-    """make_math_plan (core/math.cpp:39-56) then the C ABI."""
+def _min_argmax(name: str, x: torch.Tensor, axis, keepdims=False) -> torch.Tensor:
+    """tensor.py:834-855 (min takes any axis selection, argmax one axis or None),
+    make_math_plan (core/math.cpp:39-56), then the C ABI."""
     _check_tensor(x)
+    _check_keepdims(keepdims)
     dt = _dtype(x)
     rank = x.dim()
     if axis is None:
-        axes = list(range(rank))
+        axes = tuple(range(rank))
+    elif name == "argmax":
+        value = _normalize_axis(axis)
+        axes = () if rank == 0 and value in (0, -1) else _axes_in_rank((value,), rank, "axis")
     else:
-        vals = list(axis) if isinstance(axis, (tuple, list)) else [axis]
-        axes = [] if (rank == 0 and len(vals) == 1 and vals[0] in (0, -1)) else vals
+        values, single = _axis_sequence(axis)
+        scalar = rank == 0 and single and values[0] in (0, -1)
+        axes = () if scalar else _axes_in_rank(values, rank)
     p = plan.reduction(list(x.shape), axes)
     if not p.reduction_size:
         raise ValueError("min/argmax require a non-empty reduction")
     if name == "argmax":
         extent = 1
         for a in axes:
-            a = a + rank if a < 0 else a
             if x.shape[a] > (2**31 - 1) // extent:
                 raise ValueError("argmax index range exceeds int32")
             extent *= x.shape[a]
@@ -229,15 +277,15 @@ def _min_argmax(name: str, x: torch.Tensor, axis) -> torch.Tensor:
     check(lib().tcx_sm100_min_argmax(_stream(), OP[name], dt, _ptr(x), _ptr(out), groups,
                                      p.reduction_size, i64_array(p.index_metadata), x.dim(), ws,
                                      ws_bytes))
-    return out
+    return _keep(out, x, axes, keepdims)
 
 
-def min(x: torch.Tensor, axis=None) -> torch.Tensor:  # noqa: A001
-    return _min_argmax("min", x, axis)
+def min(x: torch.Tensor, axis=None, keepdims=False) -> torch.Tensor:  # noqa: A001
+    return _min_argmax("min", x, axis, keepdims)
 
 
-def argmax(x: torch.Tensor, axis=None) -> torch.Tensor:
-    return _min_argmax("argmax", x, axis)
+def argmax(x: torch.Tensor, axis=None, keepdims=False) -> torch.Tensor:
+    return _min_argmax("argmax", x, axis, keepdims)
 
 
 def reduce_partial(x: torch.Tensor, op: str, index_base: int = 0) -> torch.Tensor:

@@ -16,7 +16,7 @@ PATHS = ["ffma", "tensor"]
 
 
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return torch.from_numpy(np.array(a, order="C")).cuda()  # keeps 0-d arrays 0-d
 
 
 def host(t):

@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 
 
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return torch.from_numpy(np.array(a, order="C")).cuda()  # keeps 0-d arrays 0-d
 
 
 def host(t):

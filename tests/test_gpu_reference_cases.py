@@ -1,0 +1,310 @@
+"""The reference's own device acceptance cases, run through this backend.
+
+Each test restates a case of the reference's Python suite on the same inputs and checks
+it the way that test does (NumPy expectation, tolerance, error type), plus the CPU oracle
+bit for bit where the reduction order is the sequential one:
+  tests/python/test_multi_axis_reductions.py:19-140 (sum/max/mean over axis selections)
+  tests/python/test_int32_primitives.py:23-130 (int32 wraparound: binary, reductions)
+  tests/python/test_inference_ops.py:51-100 (linear, affine rmsnorm/layernorm)
+"""
+import gc
+import operator
+import warnings
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    return torch.from_numpy(np.array(a, order="C")).cuda()  # keeps 0-d arrays 0-d
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def same_bits(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    if a.dtype == np.float32:
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    else:
+        np.testing.assert_array_equal(a, b)
+
+
+def same_bits_or_nan(a, b):
+    """Bit-exact except that NaNs match NaNs: a NaN that arithmetic creates (inf - inf)
+    carries the platform's default pattern (0xFFC00000 from x86 SSE, 0x7FFFFFFF from
+    the GPU); stored NaN payloads are checked bit for bit where they are copied."""
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape and np.array_equal(np.isnan(a), np.isnan(b))
+    keep = ~np.isnan(a)
+    same_bits(a[keep], b[keep])
+
+
+# ------------------------------------------------------ multi-axis reductions
+CASES = [
+    ((2, 3, 4), None), ((2, 3, 4), ()), ((2, 3, 4), (0, 2)),
+    ((2, 3, 4), (2, 0)), ((2, 3, 4), (-1, 0)), ((2, 3, 4), (0, 1, 2)),
+    ((2, 3, 4), (0, 1)), ((2, 3, 4), (1, 2)), ((2, 3, 4), (1,)),
+    ((2, 3, 4), -1), ((1, 1, 1), (0, 2)), ((257, 2, 3), (1, 2)),
+    ((2, 3, 257), (0, 2)), ((0, 2, 3), (1, 2)), ((2, 0, 3), (0, 2)),
+    ((2, 0, 3), (1, 2)), ((2, 0, 3), None), ((2, 0, 3), ()),
+    ((0, 2, 0), (0, 2)), ((0,), None), ((), None), ((), ()), ((), 0), ((), -1),
+]
+
+
+@pytest.mark.parametrize("name", ["sum", "max", "mean"])
+@pytest.mark.parametrize("dtype", [np.float32, np.int32])
+@pytest.mark.parametrize("shape,axis", CASES)
+def test_multi_axis_numpy_parity(tcx, oracle, name, dtype, shape, axis):
+    """test_multi_axis_reductions.py:31-60."""
+    values = np.resize(np.array([-5, -1, 0, 2, 7], dtype=dtype), shape)
+    x = dev(values)
+    if dtype == np.int32 and name == "mean":
+        for keepdims in (False, True):
+            with pytest.raises(ValueError, match="float32"):
+                getattr(tcx, name)(x, axis, keepdims=keepdims)
+        return
+    reference_axis = None if not shape and axis in (0, -1) else axis
+    for keepdims in (False, True):
+        kwargs = {"axis": reference_axis, "keepdims": keepdims}
+        if name == "sum":
+            kwargs["dtype"] = dtype  # int32 sums keep int32 and wrap
+        try:
+            with warnings.catch_warnings(), np.errstate(all="ignore"):
+                warnings.simplefilter("ignore", RuntimeWarning)
+                expected = getattr(np, name)(values, **kwargs)
+        except ValueError:
+            with pytest.raises(ValueError):
+                getattr(tcx, name)(x, axis, keepdims=keepdims)
+            continue
+        for y in (getattr(tcx, name)(x, axis, keepdims=keepdims),
+                  getattr(tcx, name)(x, axis=axis, keepdims=np.bool_(keepdims))):
+            assert tuple(y.shape) == expected.shape and y.dtype == x.dtype and y.is_cuda
+            assert y.data_ptr() != x.data_ptr() or x.numel() == 0
+            got = host(y)
+            np.testing.assert_allclose(got, expected, rtol=1e-5, atol=1e-5, equal_nan=True)
+            same_bits_or_nan(got.reshape(-1), getattr(oracle, name)(values, axis).reshape(-1))
+    same_bits(host(x), values)
+
+
+@pytest.mark.parametrize("name", ["sum", "max", "mean"])
+def test_multi_axis_default_and_sequence_protocol(tcx, name):
+    """test_multi_axis_reductions.py:64-75: None, iterables and __index__ axes."""
+    class Axis:
+        def __index__(self):
+            return 0
+    x = dev(np.arange(24, dtype=np.float32).reshape(2, 3, 4))
+    fn = getattr(tcx, name)
+    same_bits(host(fn(x)), host(fn(x, None)))
+    expected = host(fn(x, (0, 2)))
+    for axes in ([Axis(), np.int32(2)], iter([2, 0]), np.array([0, 2])):
+        same_bits(host(fn(x, axes)), expected)
+    same_bits(host(fn(x, Axis())), host(fn(x, 0)))
+
+
+@pytest.mark.parametrize("name", ["sum", "max", "mean"])
+def test_multi_axis_validation_even_for_empty_inputs(tcx, name):
+    """test_multi_axis_reductions.py:78-98."""
+    fn = getattr(tcx, name)
+    for shape in ((2, 3, 4), (2, 0, 4)):
+        x = torch.empty(shape, dtype=torch.float32, device="cuda")
+        for axes in (True, np.bool_(True), 0.5, "0", b"0", (0, 0), (0, -3),
+                     (3,), (-4,), (0, True), (0, 2.0), (2**64,), (-(2**64),)):
+            with pytest.raises(ValueError):
+                fn(x, axes)
+        for keepdims in (1, None, "yes", []):
+            with pytest.raises(TypeError, match="keepdims"):
+                fn(x, (0, 2), keepdims=keepdims)
+    scalar = dev(np.array(1.0, np.float32))
+    for axes in ((0,), (-1,), 1, -2):
+        with pytest.raises(ValueError):
+            fn(scalar, axes)
+    with pytest.raises(TypeError):
+        fn([1.0], None)
+
+
+@pytest.mark.parametrize("name", ["sum", "max", "mean"])
+def test_multi_axis_empty_selection_copies_stored_bits(tcx, name):
+    """test_multi_axis_reductions.py:101-111: axis=() returns a copy of the stored
+    bits (signed zero, NaN payload, subnormal, inf) that outlives the input."""
+    bits = np.array([0x80000000, 0x7FC12345, 1, 0x7F800000], dtype=np.uint32)
+    x = dev(bits.view(np.float32))
+    y = getattr(tcx, name)(x, ())
+    assert y.data_ptr() != x.data_ptr()
+    del x
+    gc.collect()
+    np.testing.assert_array_equal(host(y).view(np.uint32), bits)
+
+
+@pytest.mark.parametrize("name", ["sum", "max", "mean"])
+def test_multi_axis_special_values_and_canonical_order(tcx, oracle, name):
+    """test_multi_axis_reductions.py:114-131: every axis spelling equals the one-pass
+    row-major reduction of the flattened tensor, signed zeros included."""
+    for values in ([[0., -0.], [-0., 0.]], [[np.inf, 2], [-np.inf, 4]],
+                   [[1, np.nan], [3, 4]], [[3e38, 3e38], [-3e38, -3e38]],
+                   [[1e20, 1], [-1e20, 3]]):
+        data = np.array(values, dtype=np.float32)
+        expected = getattr(oracle, name)(data.reshape(-1), 0)
+        x = dev(data)
+        for axes in (None, (0, 1), (1, 0), (-1, -2)):
+            actual = host(getattr(tcx, name)(x, axes))
+            np.testing.assert_allclose(actual, expected, equal_nan=True)
+            same_bits_or_nan(actual, expected)
+            if expected == 0:
+                assert np.signbit(actual) == np.signbit(expected)
+    if name == "mean":
+        # One sum then one division gives +inf where sequential means would give NaN.
+        assert np.isposinf(host(tcx.mean(dev(np.array([[3e38, 3e38], [-3e38, -3e38]], np.float32)),
+                                         (0, 1))))
+
+
+def test_multi_axis_int32_wrap_and_dtype_rejection(tcx):
+    """test_multi_axis_reductions.py:134-141."""
+    data = np.array([[2**31 - 1, 2**31 - 1], [-2**31, -17]], dtype=np.int32)
+    x = dev(data)
+    for axes in (None, (), (0, 1)):
+        np.testing.assert_array_equal(host(tcx.sum(x, axes)), data.sum(axis=axes, dtype=np.int32))
+        np.testing.assert_array_equal(host(tcx.max(x, axes)), data.max(axis=axes))
+        with pytest.raises(ValueError, match="float32"):
+            tcx.mean(x, axes)
+
+
+# --------------------------------------------------------------- int32 exact
+EDGES = np.array([-2**31, 2**31 - 1, -16777217, 16777217, -1, 0, 1, 65537], dtype=np.int32)
+SHAPES = [(), (0,), (2, 0, 3), (1,), (255,), (256,), (257,), (3, 257), (2, 3, 5)]
+OPS = [("add", operator.add), ("subtract", operator.sub), ("multiply", operator.mul)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("op", OPS, ids=lambda o: o[0])
+def test_int32_binary_exact_wrap(tcx, shape, op):
+    """test_int32_primitives.py:44-54."""
+    a, b = np.resize(EDGES, shape), np.resize(EDGES[::-1], shape)
+    with np.errstate(over="ignore"):
+        expected = op[1](a, b)
+    x, y = dev(a), dev(b)
+    out = getattr(tcx, op[0])(x, y)
+    assert out.dtype == torch.int32 and tuple(out.shape) == expected.shape
+    np.testing.assert_array_equal(host(out), expected)
+    np.testing.assert_array_equal(host(x), a)
+    np.testing.assert_array_equal(host(y), b)
+
+
+@pytest.mark.parametrize("op", OPS, ids=lambda o: o[0])
+@pytest.mark.parametrize("shapes", [((2, 1, 257), (3, 1)), ((257,), ()), ((), (257,)),
+                                    ((2, 0, 3), (1, 3)), ((0, 3), (1, 3))])
+def test_int32_broadcast_exact_wrap(tcx, op, shapes):
+    """test_int32_primitives.py:80-90."""
+    a, b = (np.resize(EDGES, s) for s in shapes)
+    with np.errstate(over="ignore"):
+        expected = op[1](a, b)
+    np.testing.assert_array_equal(host(getattr(tcx, op[0])(dev(a), dev(b))), expected)
+
+
+REDUCTIONS = [((2, 3, 257), 0), ((2, 3, 257), 1), ((3, 257), -1),
+              ((2, 3, 257), (0, 2)), ((2, 3, 257), (2, 0)), ((3, 257), None),
+              ((2, 3), ()), ((2, 0, 3), 1), ((0, 2, 3), (1, 2)),
+              ((0, 2, 3), (0, 2)), ((2, 0, 3), None), ((), 0), ((), -1), ((), None)]
+
+
+@pytest.mark.parametrize("shape,axes", REDUCTIONS)
+@pytest.mark.parametrize("name", ["sum", "max"])
+@pytest.mark.parametrize("keepdims", [False, True])
+def test_int32_reductions_exact_wrap(tcx, shape, axes, name, keepdims):
+    """test_int32_primitives.py:100-116."""
+    a = np.resize(EDGES, shape)
+    x = dev(a)
+    kwargs = dict(axis=None if not shape and axes in (0, -1) else axes, keepdims=keepdims)
+    if name == "sum":
+        kwargs["dtype"] = np.int32
+    try:
+        expected = getattr(np, name)(a, **kwargs)
+    except ValueError:
+        with pytest.raises(ValueError, match="non-empty"):
+            getattr(tcx, name)(x, axes, keepdims=keepdims)
+    else:
+        out = getattr(tcx, name)(x, axes, keepdims=keepdims)
+        assert out.dtype == torch.int32 and tuple(out.shape) == np.shape(expected)
+        np.testing.assert_array_equal(host(out), expected)
+    np.testing.assert_array_equal(host(x), a)
+
+
+@pytest.mark.parametrize("op", OPS, ids=lambda o: o[0])
+def test_int32_random_bits_and_signed_max(tcx, op):
+    """test_int32_primitives.py:119-130."""
+    rng = np.random.default_rng(4401)
+    a, b = (rng.integers(0, 2**32, size=(7, 1027), dtype=np.uint32).view(np.int32) for _ in range(2))
+    x, y = dev(a), dev(b)
+    with np.errstate(over="ignore"):
+        expected = op[1](a, b)
+    np.testing.assert_array_equal(host(getattr(tcx, op[0])(x, y)), expected)
+    np.testing.assert_array_equal(host(tcx.sum(x, (0, 1))), a.sum(dtype=np.int32))
+    np.testing.assert_array_equal(host(tcx.max(x, 1)), a.max(axis=1))
+    negatives = np.array([[-2**31, -7, -16777217]], dtype=np.int32)
+    np.testing.assert_array_equal(host(tcx.max(dev(negatives), 1)), negatives.max(axis=1))
+
+
+# ------------------------------------------------------------ inference ops
+def f32(shape, seed=0):
+    return np.random.default_rng(seed).standard_normal(shape).astype(np.float32)
+
+
+@pytest.mark.parametrize("shape,out", [((3,), 4), ((2, 3), 5), ((2, 1, 4, 3), 2),
+                                       ((0, 3), 2), ((2, 0), 3), ((2, 3), 0), ((0,), 2)])
+@pytest.mark.parametrize("bias", [False, True])
+@pytest.mark.parametrize("path", ["auto", "ffma"])
+def test_linear_parity(tcx, oracle, shape, out, bias, path):
+    """test_inference_ops.py:51-65: x @ w.T + b for 1-d, batched and empty inputs."""
+    a, w, b = f32(shape), f32((out, shape[-1]), 4), f32((out,), 9)
+    expected = a @ w.T + (b if bias else 0)
+    x, weight, offset = dev(a), dev(w), dev(b)
+    y = tcx.linear(x, weight, offset if bias else None, path=path)
+    got = host(y)
+    assert got.shape == expected.shape
+    np.testing.assert_allclose(got, expected, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(got, oracle.linear(a, w, b if bias else None), rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(host(x), a)
+    np.testing.assert_array_equal(host(weight), w)
+
+
+@pytest.mark.parametrize("shape,axis", [((2, 3, 4), -1), ((2, 3, 4), 1), ((2, 3, 4), 0),
+                                        ((3,), -1), ((), 0), ((), -1), ((0, 3), 1), ((2, 0, 3), 1)])
+@pytest.mark.parametrize("kind,params", [("rmsnorm", "weight"), ("layernorm", "weight"),
+                                         ("layernorm", "both"), ("layernorm", "bias")])
+def test_affine_norm_parity(tcx, shape, axis, kind, params):
+    """test_inference_ops.py:68-100: normalized, then * weight, then + bias, along
+    any axis, for scalars and empty tensors too."""
+    a = f32(shape)
+    pshape = (shape[axis],) if shape else ()
+    w, b = f32(pshape, 5), f32(pshape, 6)
+    kwargs = {}
+    if params in ("weight", "both"):
+        kwargs["weight"] = dev(w)
+    if params in ("bias", "both"):
+        kwargs["bias"] = dev(b)
+    with np.errstate(all="ignore"):
+        if a.size or not shape:
+            red = axis if shape else None
+            base = a if kind == "rmsnorm" else a - np.mean(a, axis=red, keepdims=True)
+            expected = base / np.sqrt(np.mean(base * base, axis=red, keepdims=True) + np.float32(1e-5))
+        else:
+            expected = np.empty(shape, np.float32)
+        pview = [1] * len(shape)
+        if shape:
+            pview[axis] = shape[axis]
+        if "weight" in kwargs:
+            expected = expected * w.reshape(pview)
+        if "bias" in kwargs:
+            expected = expected + b.reshape(pview)
+    x = dev(a)
+    got = host(getattr(tcx, kind)(x, axis, **kwargs))
+    assert got.shape == np.shape(expected)
+    np.testing.assert_allclose(got, expected, rtol=1e-5, atol=1e-5, equal_nan=True)
+    # weight=None is the unweighted op
+    same_bits(host(getattr(tcx, kind)(x, axis, weight=None)), host(getattr(tcx, kind)(x, axis)))

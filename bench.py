@@ -505,6 +505,58 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                      "peak": peak_3x, "unit": "TFLOP/s",
                      "frac": (fl / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
                      "kernel": "gemm_tf32x3", "kernel_ms": k_avg}}
+
+    # attention, [32 heads, 2048 queries, 2048 keys, 128 features]: heads sharded
+    heads = max(1, 32 // world)
+    q = torch.randn(heads, 2048, 128, device="cuda", generator=g)
+    k = torch.randn(heads, 2048, 128, device="cuda", generator=g)
+    v = torch.randn(heads, 2048, 128, device="cuda", generator=g)
+
+    def st():
+        return ops.attention(q, k, v, is_causal=True)
+    st()
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    n_att = max(3, steps // 2)
+    ms = timer.run(st, n_att, 1, sampler) / n_att
+    lib.tcx_sm100_timer_enable(0)
+    kern = read_timer(lib)
+    fl = 4.0 * heads * 2048 * 2048 * 128
+    k_launches, k_ms = kern.get("gemm_tf32x3", (0, 0.0))
+    k_avg = timer.max_over_ranks(k_ms / max(k_launches, 1))
+    out["attention_causal_32x2048x2048x128"] = {
+        "value": world * fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+        "config": f"q,k,v [32,2048,128] float32, causal, heads sharded {world} way(s); "
+                  "4*H*L*S*D flops (both GEMMs, masked half counted)",
+        "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()},
+        "roofline": {"bound": "tensor", "achieved": (fl / 2) / (k_avg * 1e-3) / 1e12 if k_avg else None,
+                     "peak": peak_3x, "unit": "TFLOP/s",
+                     "frac": ((fl / 2) / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
+                     "kernel": "gemm_tf32x3", "kernel_ms": k_avg}}
+    del q, k, v
+
+    # MLP latency (configs[0]: x[256,784] -> linear 512 + ReLU -> linear 10 -> softmax)
+    x = torch.randn(256, 784, device="cuda", generator=g)
+    w1 = (torch.rand(784, 512, device="cuda", generator=g) * 2 - 1) / 784 ** 0.5
+    w2 = (torch.rand(512, 10, device="cuda", generator=g) * 2 - 1) / 512 ** 0.5
+    b1 = torch.zeros(512, device="cuda")
+    b2 = torch.zeros(10, device="cuda")
+
+    def mlp():
+        h = ops.matmul(x, w1, bias=b1, act="relu")
+        return ops.softmax(ops.matmul(h, w2, bias=b2), axis=-1)
+    mlp()
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    ms = timer.run(mlp, 50, 1, sampler) / 50
+    lib.tcx_sm100_timer_enable(0)
+    kern = read_timer(lib)
+    out["mlp_256x784x512x10_latency"] = {
+        "value": ms, "unit": "ms", "higher_is_better": False, "ms_per_step": ms,
+        "config": "x[256,784] @ W1[784,512] + b1 -> ReLU (fused epilogue) -> @ W2[512,10] + b2 -> softmax; "
+                  "per-rank replica, stream-ordered launches, no host sync inside",
+        "gpu_launches_per_step": sum(c for c, _ in kern.values()) / 50,
+        "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()}}
     return out
 
 

@@ -270,6 +270,39 @@ int tcx_sm100_linear(tcx_stream_t stream, const float* x, const float* w, const 
                      int64_t rows, int64_t in_features, int64_t out_features, int act, int path,
                      void* workspace, size_t workspace_bytes);
 
+/* Masked, scaled row softmax of attention scores (kAttentionSoftmax; plan
+ * make_attention_softmax_plan, core/inference.cpp:56-83; CPU semantics
+ * cpu_inference.cpp:22-45; replaces launch_attention_softmax, kernels/inference.cu:53).
+ * The target is `shape` [..., queries, keys] (rank 2..32), output contiguous. `scores`
+ * and `mask` are read through broadcast strides over that shape (0 = broadcast; the
+ * last-axis stride must be 0 or 1). mask_kind: 0 none, 1 bool (one byte per element,
+ * nonzero = allowed), 2 float32 added to the scaled score. Per row: score = -inf where
+ * causal and key > query, where a bool mask is false or a float mask is -inf; otherwise
+ * scores * scale + mask. A row whose maximum is -inf is all zeros; a NaN makes the row
+ * NaN; else exp(score - max) / sum. `scale` must be finite. */
+int tcx_sm100_attention_softmax(tcx_stream_t stream, const float* scores, const void* mask, int32_t mask_kind,
+                                float* output, const int64_t* shape, const int64_t* score_strides,
+                                const int64_t* mask_strides, int32_t rank, float scale, int32_t causal);
+
+/* Scaled dot-product attention (kAttention, core/inference.cpp:123-160): out =
+ * attention_softmax(Q·Kᵀ, mask, scale, causal) · V for q [batch..., queries, features],
+ * k [batch..., keys, features], v [batch..., keys, value_features], each batch-broadcast
+ * to `batch_shape` through its batch strides (element units, 0 = broadcast, as
+ * tcx_sm100_matmul). mask_strides: batch_rank + 2 strides of the mask over
+ * [batch..., queries, keys] (ignored when mask_kind is 0). The keys are read K-major by
+ * the GEMM (no transpose copy); the scores live in the workspace. Output contiguous
+ * [batch..., queries, value_features]. q/k/v_batches = the number of distinct batch
+ * matrices of each operand (the product of its own batch extents). */
+size_t tcx_sm100_attention_workspace_bytes(int64_t batches, int64_t queries, int64_t keys, int64_t features,
+                                           int64_t value_features, int64_t q_batches, int64_t k_batches,
+                                           int64_t v_batches);
+int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, const float* v, const void* mask,
+                        int32_t mask_kind, float* output, int64_t queries, int64_t keys, int64_t features,
+                        int64_t value_features, const int64_t* batch_shape, const int64_t* q_batch_strides,
+                        const int64_t* k_batch_strides, const int64_t* v_batch_strides, int32_t batch_rank,
+                        const int64_t* mask_strides, float scale, int32_t causal, void* workspace,
+                        size_t workspace_bytes);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

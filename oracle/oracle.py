@@ -189,6 +189,40 @@ def broadcast_plan(lhs, rhs):
     return out, ls, rs
 
 
+def checked_scale(scale: float) -> float:
+    """checked_scale, core/inference.cpp:15-20: finite, representable as float32, and
+    not flushed to zero."""
+    narrowed = float(np.float32(scale)) if math.isfinite(scale) and abs(scale) <= 3.4028234663852886e38 else math.inf
+    if not math.isfinite(scale) or not math.isfinite(narrowed) or (scale != 0 and narrowed == 0):
+        raise ValueError("attention scale must be finite and representable as float32")
+    return narrowed
+
+
+def attention_batch(qs, ks, vs):
+    """The batch shape and feature count of the attention composite
+    (core/inference.cpp:128-148)."""
+    for s in (qs, ks, vs):
+        if len(s) < 2:
+            raise ValueError("attention tensors require rank >= 2")
+    features = qs[-1]
+    if features <= 0 or features != ks[-1] or ks[-2] != vs[-2]:
+        raise ValueError("attention query/key features and key/value sequence sizes must match; "
+                         "features must be positive")
+    batch = []
+    for s in (qs, ks, vs):
+        inp = list(s[:-2])
+        rank = max(len(batch), len(inp))
+        merged = []
+        for a in range(rank):
+            left = 1 if a < rank - len(batch) else batch[a - (rank - len(batch))]
+            right = 1 if a < rank - len(inp) else inp[a - (rank - len(inp))]
+            if left != right and left != 1 and right != 1:
+                raise ValueError("attention batch dimensions cannot broadcast")
+            merged.append(right if left == 1 else left)
+        batch = merged
+    return batch, features
+
+
 def axis_dims(shape, axis):
     """reduction_dims of cpu_backend.cpp:76-123: (output shape, outer, reduce, inner)."""
     rank = len(shape)
@@ -469,6 +503,48 @@ class Oracle(_Lib):
         y = self.matmul(x, np.ascontiguousarray(np.swapaxes(w, -1, -2)))
         return self.add(y, b) if b is not None else y
 
+    # ---------------------------------------------------------------- attention
+    def attention_softmax(self, scores, shape, mask=None, causal=False, scale=1.0):
+        """kAttentionSoftmax: cpu_inference.cpp:22-45, with the checks of
+        make_attention_softmax_plan (core/inference.cpp:56-83)."""
+        scores = np.array(scores, dtype=np.float32, order="C")
+        shape = [int(d) for d in shape]
+        if scores.ndim < 2 or len(shape) < 2:
+            raise ValueError("attention scores must have rank >= 2")
+        out_s, sstr, _ = broadcast_plan(list(scores.shape), shape)
+        if out_s != shape:
+            raise ValueError("attention scores cannot broadcast to target")
+        kind, mstr, m = 0, [0] * len(shape), None
+        if mask is not None:
+            m = np.array(mask, order="C")
+            if m.dtype == np.bool_:
+                kind, m = 1, m.view(np.uint8)
+            elif m.dtype == np.float32:
+                kind = 2
+            else:
+                raise ValueError("attention mask must be bool or float32")
+            out_m, mstr, _ = broadcast_plan(list(m.shape), shape)
+            if out_m != shape:
+                raise ValueError("attention mask cannot broadcast to scores")
+        scale = checked_scale(scale)
+        out = np.empty(shape, np.float32)
+        if out.size:
+            self.lib.tcxo_attention_softmax(_ptr(scores), None if m is None else _ptr(m), kind, _ptr(out),
+                                            _i64(shape), _i64(sstr), _i64(mstr), len(shape),
+                                            ctypes.c_float(scale), int(bool(causal)))
+        return out
+
+    def attention(self, q, k, v, mask=None, causal=False, scale=None):
+        """kAttention composite (core/inference.cpp:123-160): matmul(q, transpose(k)),
+        the attention softmax over the broadcast batch, then matmul with v."""
+        q, k, v = (np.array(t, dtype=np.float32, order="C") for t in (q, k, v))
+        batch, features = attention_batch(q.shape, k.shape, v.shape)
+        scores = list(batch) + [q.shape[-2], k.shape[-2]]
+        scale = checked_scale(1.0 / math.sqrt(features) if scale is None else scale)
+        product = self.matmul(q, np.ascontiguousarray(np.swapaxes(k, -1, -2)))
+        probabilities = self.attention_softmax(product, scores, mask, causal, scale)
+        return self.matmul(probabilities, v)
+
 
 class Reference(_Lib):
     """The reference's own CPU backend (oracle/_ref/libtcx_ref.so)."""
@@ -643,3 +719,47 @@ class Reference(_Lib):
                                     ctypes.c_int64(out.size))
         self._check(rc)
         return out[:numel(shape)].reshape(shape)
+
+    def attention(self, q, k, v, mask=None, causal=False, scale=None):
+        q, k, v = (np.array(t, dtype=np.float32, order="C") for t in (q, k, v))
+        kind, m = 0, None
+        if mask is not None:
+            m = np.array(mask, order="C")
+            kind = 1 if m.dtype == np.bool_ else 2
+            if kind == 1:
+                m = m.view(np.uint8)
+        try:
+            batch = np.broadcast_shapes(q.shape[:-2], k.shape[:-2], v.shape[:-2])
+            cap = max(1, int(np.prod(batch, dtype=np.int64)) * q.shape[-2] * v.shape[-1])
+        except ValueError:
+            cap = 1
+        out = np.empty(cap, np.float32)
+        oshape = (ctypes.c_int64 * 64)()
+        orank = ctypes.c_int(0)
+        rc = self.lib.tcxref_attention(_ptr(q), _i64(q.shape), q.ndim, _ptr(k), _i64(k.shape), k.ndim,
+                                       _ptr(v), _i64(v.shape), v.ndim, None if m is None else _ptr(m), kind,
+                                       _i64([] if m is None else m.shape), 0 if m is None else m.ndim,
+                                       int(bool(causal)), int(scale is not None),
+                                       ctypes.c_double(0.0 if scale is None else scale), _ptr(out),
+                                       ctypes.c_int64(cap), oshape, ctypes.byref(orank))
+        self._check(rc)
+        shape = [oshape[i] for i in range(orank.value)]
+        return out[:numel(shape)].reshape(shape)
+
+    def attention_softmax(self, scores, shape, mask=None, causal=False, scale=1.0):
+        scores = np.array(scores, dtype=np.float32, order="C")
+        kind, m = 0, None
+        if mask is not None:
+            m = np.array(mask, order="C")
+            kind = 1 if m.dtype == np.bool_ else 2
+            if kind == 1:
+                m = m.view(np.uint8)
+        cap = max(1, numel(list(shape)))
+        out = np.empty(cap, np.float32)
+        rc = self.lib.tcxref_attention_softmax(_ptr(scores), _i64(scores.shape), scores.ndim,
+                                               None if m is None else _ptr(m), kind,
+                                               _i64([] if m is None else m.shape), 0 if m is None else m.ndim,
+                                               _i64(list(shape)), len(shape), int(bool(causal)),
+                                               ctypes.c_double(scale), _ptr(out), ctypes.c_int64(cap))
+        self._check(rc)
+        return out[:numel(list(shape))].reshape(list(shape))

@@ -33,6 +33,11 @@ Tensor make_tensor(int dtype, const void* data, const std::int64_t* dims, int ra
     if (n) std::memcpy(v.data(), data, n * 4);
     return cpu::to_core_tensor(cpu::CpuTensor(shape, std::move(v)));
   }
+  if (dtype == 2) {  // bool, one byte per element
+    std::vector<std::uint8_t> v(n);
+    if (n) std::memcpy(v.data(), data, n);
+    return cpu::to_core_tensor(cpu::CpuTensor(shape, std::move(v)));
+  }
   std::vector<std::int32_t> v(n);
   if (n) std::memcpy(v.data(), data, n * 4);
   return cpu::to_core_tensor(cpu::CpuTensor(shape, std::move(v)));
@@ -151,6 +156,41 @@ int tcxref_linear(const float* x, const std::int64_t* xd, int xr, const float* w
     std::vector<Tensor> inputs{make_tensor(0, x, xd, xr), make_tensor(0, w, wd, 2)};
     std::int64_t bd[1] = {wd[0]};
     if (bias) inputs.push_back(make_tensor(0, bias, bd, 1));
+    return run(op, inputs, out, capacity, nullptr, nullptr);
+  });
+}
+
+// Attention composite (cpp/tensorcx/core/inference.cpp:123-160): query, key, value and
+// an optional mask (mask_kind 0 none, 1 bool, 2 float32).
+// has_scale = 0 uses the default 1/sqrt(features).
+int tcxref_attention(const float* q, const std::int64_t* qd, int qr, const float* k, const std::int64_t* kd,
+                     int kr, const float* v, const std::int64_t* vd, int vr, const void* mask,
+                     int mask_kind, const std::int64_t* md, int mr, int causal, int has_scale, double scale,
+                     float* out, std::int64_t capacity, std::int64_t* out_shape, int* out_rank) {
+  return guarded([&] {
+    OpDesc op{OpKind::kAttention};
+    op.causal = causal != 0;
+    if (has_scale) op.attention_scale = scale;
+    std::vector<Tensor> inputs{make_tensor(0, q, qd, qr), make_tensor(0, k, kd, kr), make_tensor(0, v, vd, vr)};
+    if (mask_kind == 1) inputs.push_back(make_tensor(2, mask, md, mr));
+    if (mask_kind == 2) inputs.push_back(make_tensor(0, mask, md, mr));
+    return run(op, inputs, out, capacity, out_shape, out_rank);
+  });
+}
+
+// Attention softmax primitive (kAttentionSoftmax, cpu_inference.cpp:22-45) of scores
+// broadcast to the target shape td, with an optional mask (mask_kind 1 bool, 2 float).
+int tcxref_attention_softmax(const float* scores, const std::int64_t* sd, int sr, const void* mask,
+                             int mask_kind, const std::int64_t* md, int mr, const std::int64_t* td, int tr,
+                             int causal, double scale, float* out, std::int64_t capacity) {
+  return guarded([&] {
+    OpDesc op{OpKind::kAttentionSoftmax};
+    op.causal = causal != 0;
+    op.attention_scale = scale;
+    op.attention_shape = Shape(td, td + tr);
+    std::vector<Tensor> inputs{make_tensor(0, scores, sd, sr)};
+    if (mask_kind == 1) inputs.push_back(make_tensor(2, mask, md, mr));
+    if (mask_kind == 2) inputs.push_back(make_tensor(0, mask, md, mr));
     return run(op, inputs, out, capacity, nullptr, nullptr);
   });
 }

@@ -326,6 +326,59 @@ void tcxo_matmul_rows(const float* a, const float* b, float* out, int64_t m, int
 
 /* Exact (float64) sum, used as a secondary accuracy reference for the
  * full-tensor float32 sum (not a reference function). */
+/* Masked, scaled attention softmax over the target `shape` [..., queries, keys]:
+ * execute_inference_primitive, cpu_inference.cpp:22-45 (plan: core/inference.cpp:56-83).
+ * scores / mask are read through broadcast strides (sstr / mstr, element units);
+ * mask_kind 0 none, 1 bool bytes, 2 float32. Output contiguous. */
+static int64_t attn_offset(int64_t i, const int64_t* shape, const int64_t* strides, int rank) {
+  int64_t off = 0;
+  for (int a = rank - 1; a >= 0; --a) {
+    off += (i % shape[a]) * strides[a];
+    i /= shape[a];
+  }
+  return off;
+}
+
+static float attn_score(const float* scores, const void* mask, int mask_kind, const int64_t* shape,
+                        const int64_t* sstr, const int64_t* mstr, int rank, int64_t i, int64_t col,
+                        int64_t query, float scale, int causal) {
+  if (causal && col > query) return -INFINITY;
+  if (mask_kind == 1 && !((const unsigned char*)mask)[attn_offset(i, shape, mstr, rank)]) return -INFINITY;
+  const float bias = mask_kind == 2 ? ((const float*)mask)[attn_offset(i, shape, mstr, rank)] : 0.0f;
+  if (bias == -INFINITY) return bias;
+  return scores[attn_offset(i, shape, sstr, rank)] * scale + bias;
+}
+
+void tcxo_attention_softmax(const float* scores, const void* mask, int mask_kind, float* out,
+                            const int64_t* shape, const int64_t* sstr, const int64_t* mstr, int rank,
+                            float scale, int causal) {
+  int64_t count = 1;
+  for (int a = 0; a < rank; ++a) count *= shape[a];
+  const int64_t columns = shape[rank - 1];
+  const int64_t rows = columns ? count / columns : 0;
+  for (int64_t row = 0; row < rows; ++row) {
+    const int64_t query = row % shape[rank - 2];
+    float maximum = -INFINITY;
+    for (int64_t col = 0; col < columns; ++col) {
+      const float v = attn_score(scores, mask, mask_kind, shape, sstr, mstr, rank, row * columns + col, col,
+                                 query, scale, causal);
+      if (isnan(v)) { maximum = v; break; }
+      maximum = (maximum < v) ? v : maximum;
+    }
+    if (maximum == -INFINITY) {
+      for (int64_t col = 0; col < columns; ++col) out[row * columns + col] = 0.0f;
+      continue;
+    }
+    float total = 0.0f;
+    for (int64_t col = 0; col < columns; ++col)
+      total += expf(attn_score(scores, mask, mask_kind, shape, sstr, mstr, rank, row * columns + col, col, query,
+                               scale, causal) - maximum);
+    for (int64_t col = 0; col < columns; ++col)
+      out[row * columns + col] = expf(attn_score(scores, mask, mask_kind, shape, sstr, mstr, rank,
+                                                 row * columns + col, col, query, scale, causal) - maximum) / total;
+  }
+}
+
 double tcxo_sum_f64(const float* x, int64_t count) {
   double s = 0.0;
   for (int64_t i = 0; i < count; ++i) s += (double)x[i];

@@ -9,6 +9,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -20,6 +21,7 @@
 #include "tcx_sm100.h"
 #include "tensorcx/backends/cuda/cuda_device.h"
 #include "tensorcx/backends/cuda/cuda_memory_pool.h"
+#include "tensorcx/core/inference.h"
 #include "tensorcx/core/math.h"
 #include "tensorcx/core/shape.h"
 
@@ -135,10 +137,12 @@ class Executor {
     if (kind == OpKind::kExp || kind == OpKind::kGelu || kind == OpKind::kSilu) return unary(out);
     if (is_binary(kind)) return binary(out);
     if (kind == OpKind::kMin || kind == OpKind::kArgmax || kind == OpKind::kClip) return math(out);
+    if (kind == OpKind::kAttentionSoftmax) return attention_softmax(out);
+    if (kind == OpKind::kAttention) return attention(out);
     return {StatusCode::kUnavailable,
             "operation is not on the sm100 hot path (served ops: fill, matmul, linear, sum, max, mean, min, "
             "argmax, clip, softmax, rmsnorm, layernorm and their affine forms, exp, gelu, silu, add, subtract, "
-            "multiply, divide)"};
+            "multiply, divide, attention, attention softmax)"};
   }
 
  private:
@@ -245,6 +249,108 @@ class Executor {
                            "CUDA linear");
       if (!st.ok()) return st;
     }
+    return publish(out, DType::kFloat32, shape, buffer.move_value());
+  }
+
+  // kAttentionSoftmax (plan core/inference.cpp:56-83): one masked-softmax kernel reading
+  // the scores and mask through the plan's broadcast strides.
+  Status attention_softmax(Tensor& out) {
+    const auto plan = make_attention_softmax_plan(e_.op, e_.inputs);
+    auto buffer = output(DType::kFloat32, plan.shape);
+    if (!buffer) return buffer.status();
+    const auto rank = plan.shape.size();
+    if (numel(plan.shape)) {
+      auto st = abi_status(
+          tcx_sm100_attention_softmax(abi_stream(scope_), static_cast<const float*>(ptr(0)),
+                                      plan.mask_kind ? ptr(1) : nullptr, static_cast<std::int32_t>(plan.mask_kind),
+                                      static_cast<float*>(buffer.value()->data()), plan.shape.data(),
+                                      plan.metadata.data() + rank,
+                                      plan.mask_kind ? plan.metadata.data() + 2 * rank : nullptr,
+                                      static_cast<std::int32_t>(rank), plan.scale, e_.op.causal ? 1 : 0),
+          "CUDA attention softmax");
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kFloat32, plan.shape, buffer.move_value());
+  }
+
+  // kAttention (core/inference.cpp:123-160) as one C-ABI call: the two GEMMs read the
+  // keys K-major (no transpose launch) and the scores stay in stream-ordered scratch.
+  Status attention(Tensor& out) {
+    if (in_.size() < 3 || in_.size() > 4) return invalid("attention requires query, key, value and optional mask");
+    for (std::size_t i = 0; i < 3; ++i) {
+      if (in_[i].dtype() != DType::kFloat32) return invalid("inference values require float32 tensors");
+      if (in_[i].shape().size() < 2) return invalid("attention tensors require rank >= 2");
+    }
+    const auto& q = in_[0].shape();
+    const auto& k = in_[1].shape();
+    const auto& v = in_[2].shape();
+    const Dim features = q.back(), queries = q[q.size() - 2], keys = k[k.size() - 2];
+    if (features <= 0 || features != k.back() || keys != v[v.size() - 2])
+      return invalid("attention query/key features and key/value sequence sizes must match; features must be positive");
+    Shape batch;
+    for (const auto* s : {&q, &k, &v}) {
+      const std::size_t own = s->size() - 2;
+      const std::size_t rank = std::max(batch.size(), own);
+      Shape merged(rank, 1);
+      for (std::size_t a = 0; a < rank; ++a) {
+        const Dim left = a < rank - batch.size() ? 1 : batch[a - (rank - batch.size())];
+        const Dim right = a < rank - own ? 1 : (*s)[a - (rank - own)];
+        if (left != right && left != 1 && right != 1) return invalid("attention batch dimensions cannot broadcast");
+        merged[a] = left == 1 ? right : left;
+      }
+      batch = std::move(merged);
+    }
+    Shape scores = batch;
+    scores.push_back(queries);
+    scores.push_back(keys);
+    Shape shape = batch;
+    shape.push_back(queries);
+    shape.push_back(v.back());
+    (void)numel(scores), (void)contiguous_strides(scores), (void)numel(shape), (void)contiguous_strides(shape);
+    const double requested = e_.op.attention_scale.value_or(1.0 / std::sqrt(static_cast<double>(features)));
+    const float scale = static_cast<float>(requested);
+    if (!std::isfinite(requested) || !std::isfinite(scale) || (requested != 0 && scale == 0))
+      return invalid("attention scale must be finite and representable as float32");
+    // mask dtype / broadcast checks of the softmax plan, before any allocation
+    OpDesc softmax{OpKind::kAttentionSoftmax};
+    softmax.attention_shape = scores;
+    softmax.causal = e_.op.causal;
+    softmax.attention_scale = scale;
+    Tensor descriptor = e_.inputs[0];
+    descriptor.shape = scores;
+    descriptor.strides = contiguous_strides(scores);
+    std::vector<Tensor> preview{descriptor};
+    if (in_.size() == 4) preview.push_back(e_.inputs[3]);
+    const auto plan = make_attention_softmax_plan(softmax, preview);
+    auto buffer = output(DType::kFloat32, shape);
+    if (!buffer) return buffer.status();
+    if (!numel(shape)) return publish(out, DType::kFloat32, shape, buffer.move_value());
+    const std::size_t rank = batch.size();
+    auto batch_strides = [&](const Shape& s) {
+      const auto own = contiguous_strides(s);
+      const std::size_t r = s.size() - 2;
+      Shape st(rank, 0);
+      for (std::size_t a = rank - r; a < rank; ++a)
+        if (s[a - (rank - r)] != 1) st[a] = own[a - (rank - r)];
+      return st;
+    };
+    const Shape qs = batch_strides(q), ks = batch_strides(k), vs = batch_strides(v);
+    const Dim nb = numel(batch);
+    const Dim qn = numel(Shape(q.begin(), q.end() - 2)), kn = numel(Shape(k.begin(), k.end() - 2)),
+              vn = numel(Shape(v.begin(), v.end() - 2));
+    Scratch ws(tcx_sm100_attention_workspace_bytes(nb, queries, keys, features, v.back(), qn, kn, vn), scope_);
+    if (!ws.status().ok()) return ws.status();
+    const auto srank = scores.size();
+    auto st = abi_status(
+        tcx_sm100_attention(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
+                            static_cast<const float*>(ptr(2)), plan.mask_kind ? ptr(3) : nullptr,
+                            static_cast<std::int32_t>(plan.mask_kind), static_cast<float*>(buffer.value()->data()),
+                            queries, keys, features, v.back(), batch.data(), qs.data(), ks.data(), vs.data(),
+                            static_cast<std::int32_t>(rank),
+                            plan.mask_kind ? plan.metadata.data() + 2 * srank : nullptr, scale,
+                            e_.op.causal ? 1 : 0, ws.data(), ws.bytes()),
+        "CUDA attention");
+    if (!st.ok()) return st;
     return publish(out, DType::kFloat32, shape, buffer.move_value());
   }
 

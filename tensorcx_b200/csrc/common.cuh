@@ -91,4 +91,11 @@ int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* outp
                 int64_t outer, int64_t reduce, int64_t inner, void* ws, size_t ws_bytes);
 size_t axis_reduce_workspace(int64_t outer, int64_t reduce, int64_t inner);
 
+// Batched matmul of tcx_sm100_matmul (gemm.cu) for composites; rhs_kmajor reads the
+// right operand as [batch..., n, k]. Workspace as tcx_sm100_matmul_workspace_bytes.
+int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* output, int64_t m, int64_t n,
+               int64_t k, int64_t batches, const int64_t* batch_shape, const int64_t* lhs_batch_strides,
+               const int64_t* rhs_batch_strides, int32_t batch_rank, bool rhs_kmajor, void* workspace,
+               size_t workspace_bytes);
+
 }  // namespace tcx

@@ -932,3 +932,16 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
 }
 
 }  // extern "C"
+
+namespace tcx {
+// In-library entry for composites (attention.cu): the matmul of tcx_sm100_matmul with
+// the right operand optionally K-major ([batch..., n, k], the layout of a key matrix).
+int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* output, int64_t m, int64_t n,
+               int64_t k, int64_t batches, const int64_t* batch_shape, const int64_t* lhs_batch_strides,
+               const int64_t* rhs_batch_strides, int32_t batch_rank, bool rhs_kmajor, void* workspace,
+               size_t workspace_bytes) {
+  return run_matmul(reinterpret_cast<tcx_stream_t>(stream), lhs, rhs, output, m, n, k, batches, batch_shape,
+                    lhs_batch_strides, rhs_batch_strides, batch_rank, nullptr, TCX_ACT_NONE, TCX_MATMUL_AUTO,
+                    workspace, workspace_bytes, rhs_kmajor);
+}
+}  // namespace tcx

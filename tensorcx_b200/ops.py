@@ -25,7 +25,8 @@ from ._abi import ACT, FLOAT32, INT32, MATMUL_PATH, OP, Partial, check, i64_arra
 
 __all__ = ["matmul", "sum", "max", "mean", "min", "argmax", "softmax", "rmsnorm", "layernorm",
            "exp", "gelu", "silu", "add", "subtract", "multiply", "divide", "clip", "relu",
-           "bias_act", "linear", "reduce_partial", "reduce_combine", "Partial"]
+           "bias_act", "linear", "attention", "scaled_dot_product_attention", "attention_softmax",
+           "reduce_partial", "reduce_combine", "Partial"]
 
 
 def _dtype(t: torch.Tensor) -> int:
@@ -442,3 +443,154 @@ def bias_act(x: torch.Tensor, bias: torch.Tensor | None, act: str = "silu") -> t
     rows = x.numel() // cols if cols else 0
     check(lib().tcx_sm100_bias_act(_stream(), _ptr(x), _ptr(bias), _ptr(out), rows, cols, ACT[act]))
     return out
+
+
+# ---------------------------------------------------------------- attention
+def _checked_scale(scale: float) -> float:
+    """checked_scale (core/inference.cpp:15-20): finite, representable as float32 and
+    not flushed to zero."""
+    finite = math.isfinite(scale)
+    narrowed = float(np.float32(scale)) if finite and abs(scale) <= 3.4028234663852886e38 else math.inf
+    if not finite or not math.isfinite(narrowed) or (scale != 0 and narrowed == 0):
+        raise ValueError("attention scale must be finite and representable as float32")
+    return narrowed
+
+
+def _broadcast_strides(shape, target):
+    """Element strides of a contiguous `shape` read as broadcast to `target` (0 on
+    broadcast axes), or None when it does not broadcast (shape.cpp:78-104)."""
+    rank, own = len(target), len(shape)
+    if own > rank:
+        return None
+    contiguous = plan.strides(list(shape))
+    out = [0] * rank
+    for a in range(rank):
+        if a < rank - own:
+            continue
+        d = shape[a - (rank - own)]
+        if d != target[a] and d != 1:
+            return None
+        if d != 1:
+            out[a] = contiguous[a - (rank - own)]
+    return out
+
+
+def _mask_kind(mask: torch.Tensor) -> int:
+    if mask.dtype == torch.bool:
+        return 1
+    if mask.dtype == torch.float32:
+        return 2
+    raise ValueError("attention mask must be bool or float32")
+
+
+def attention_softmax(scores: torch.Tensor, shape=None, mask: torch.Tensor | None = None, *, scale: float = 1.0,
+                      is_causal: bool = False) -> torch.Tensor:
+    """The kAttentionSoftmax primitive (core/inference.cpp:56-83): softmax over the
+    last axis of scale * scores + mask, scores and mask broadcast to `shape`
+    (default: the scores' shape), masked entries -inf, fully masked rows zero."""
+    _check_tensor(scores, "scores")
+    if scores.dtype != torch.float32:
+        raise ValueError("inference values require float32 tensors")
+    target = list(scores.shape) if shape is None else [int(d) for d in shape]
+    if scores.dim() < 2 or len(target) < 2:
+        raise ValueError("attention scores must have rank >= 2")
+    sstr = _broadcast_strides(list(scores.shape), target)
+    if sstr is None:
+        raise ValueError("attention scores cannot broadcast to target")
+    kind, mstr = 0, None
+    if mask is not None:
+        _check_tensor(mask, "mask")
+        kind = _mask_kind(mask)
+        mstr = _broadcast_strides(list(mask.shape), target)
+        if mstr is None:
+            raise ValueError("attention mask cannot broadcast to scores")
+    s = _checked_scale(float(scale))
+    plan.numel(target)
+    out = torch.empty(target, dtype=torch.float32, device=scores.device)
+    check(lib().tcx_sm100_attention_softmax(_stream(), _ptr(scores), _ptr(mask), kind, _ptr(out),
+                                            i64_array(target), i64_array(sstr),
+                                            i64_array(mstr) if mstr is not None else None, len(target), s,
+                                            int(bool(is_causal))))
+    return out
+
+
+def scaled_dot_product_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                                 attn_mask: torch.Tensor | None = None, *, is_causal=False,
+                                 scale=None) -> torch.Tensor:
+    """tensor.py:924-946 and the kAttention composite (core/inference.cpp:123-160):
+    softmax(scale * query·keyᵀ + mask) · value over broadcast batch dimensions; True
+    mask entries are allowed, causal is upper-left, the default scale 1/sqrt(features).
+    Runs as one C-ABI call: two tcgen05 GEMMs (keys read K-major, no transpose copy)
+    around the masked softmax, scores kept in a stream-ordered workspace."""
+    tensors = (query, key, value) + (() if attn_mask is None else (attn_mask,))
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError("attention expects Tensor arguments")
+    if builtins.any(t.device != query.device for t in tensors):
+        raise ValueError("device mismatch: attention tensors must share one device")
+    if not isinstance(is_causal, (bool, np.bool_)):
+        raise TypeError("is_causal must be a boolean")
+    if scale is not None:
+        if isinstance(scale, (bool, np.bool_)) or not isinstance(scale, (int, float, np.integer, np.floating)):
+            raise TypeError("attention scale must be a real scalar")
+        try:
+            scale = float(scale)
+        except OverflowError:
+            raise ValueError("attention scale is out of range") from None
+    for t in (query, key, value):
+        _check_tensor(t)
+        if t.dtype != torch.float32:
+            raise ValueError("inference values require float32 tensors")
+        if t.dim() < 2:
+            raise ValueError("attention tensors require rank >= 2")
+    features, queries, keys = query.shape[-1], query.shape[-2], key.shape[-2]
+    if features <= 0 or features != key.shape[-1] or keys != value.shape[-2]:
+        raise ValueError("attention query/key features and key/value sequence sizes must match; "
+                         "features must be positive")
+    batch = []
+    for t in (query, key, value):
+        own = list(t.shape[:-2])
+        rank = builtins.max(len(batch), len(own))
+        merged = []
+        for a in range(rank):
+            left = 1 if a < rank - len(batch) else batch[a - (rank - len(batch))]
+            right = 1 if a < rank - len(own) else own[a - (rank - len(own))]
+            if left != right and left != 1 and right != 1:
+                raise ValueError("attention batch dimensions cannot broadcast")
+            merged.append(right if left == 1 else left)
+        batch = merged
+    scores_shape = batch + [queries, keys]
+    out_shape = batch + [queries, value.shape[-1]]
+    plan.numel(scores_shape), plan.numel(out_shape)
+    s = _checked_scale(1.0 / math.sqrt(features) if scale is None else scale)
+    kind, mstr = 0, None
+    if attn_mask is not None:
+        _check_tensor(attn_mask, "mask")
+        kind = _mask_kind(attn_mask)
+        mstr = _broadcast_strides(list(attn_mask.shape), scores_shape)
+        if mstr is None:
+            raise ValueError("attention mask cannot broadcast to scores")
+    out = torch.empty(out_shape, dtype=torch.float32, device=query.device)
+    if out.numel() == 0:
+        return out
+    rank = len(batch)
+
+    def batch_strides(t):
+        st = _broadcast_strides(list(t.shape), batch + list(t.shape[-2:]))
+        return st[:rank]
+    qs, ks, vs = batch_strides(query), batch_strides(key), batch_strides(value)
+    nb = plan.numel(batch)
+    ws_bytes = lib().tcx_sm100_attention_workspace_bytes(
+        nb, queries, keys, features, value.shape[-1], plan.numel(list(query.shape[:-2])),
+        plan.numel(list(key.shape[:-2])), plan.numel(list(value.shape[:-2])))
+    keep, ws = _workspace(ws_bytes, query.device)
+    check(lib().tcx_sm100_attention(_stream(), _ptr(query), _ptr(key), _ptr(value), _ptr(attn_mask), kind,
+                                    _ptr(out), queries, keys, features, value.shape[-1], i64_array(batch),
+                                    i64_array(qs), i64_array(ks), i64_array(vs), rank,
+                                    i64_array(mstr) if mstr is not None else None, s, int(bool(is_causal)),
+                                    ws, ws_bytes))
+    del keep
+    return out
+
+
+attention = scaled_dot_product_attention

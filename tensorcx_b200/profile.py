@@ -5,6 +5,7 @@ timing. Prints the mean device time per call (CUDA events).
     python -m tensorcx_b200.profile bmm --batch 64 --size 2048
     python -m tensorcx_b200.profile softmax|rmsnorm|layernorm --rows 16384 --cols 4096
     python -m tensorcx_b200.profile sum|max|min|argmax|mean --n 268435456 [--int32]
+    python -m tensorcx_b200.profile attention --batch 32 --rows 2048 --cols 2048 --size 128 [--causal]
 """
 from __future__ import annotations
 
@@ -26,6 +27,7 @@ def main():
     p.add_argument("--int32", action="store_true")
     p.add_argument("--path", default="auto")
     p.add_argument("--repeat", type=int, default=3)
+    p.add_argument("--causal", action="store_true")
     a = p.parse_args()
     torch.cuda.set_device(0)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -50,6 +52,11 @@ def main():
             x = torch.randn(a.n, device="cuda", generator=g)
         f = getattr(ops, w)
         fn = lambda: f(x)  # noqa: E731
+    elif w == "attention":  # batch = heads, rows = queries, cols = keys, size = features
+        q = torch.randn(a.batch, a.rows, a.size, device="cuda", generator=g)
+        k = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)
+        v = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)
+        fn = lambda: ops.attention(q, k, v, is_causal=a.causal)  # noqa: E731
     else:
         raise SystemExit(f"unknown workload {w}")
     fn()

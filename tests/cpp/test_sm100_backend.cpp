@@ -46,6 +46,13 @@ cpu::CpuTensor randi(Shape shape, std::uint32_t seed) {
   return cpu::CpuTensor(shape, std::move(v));
 }
 
+cpu::CpuTensor randb(Shape shape, std::uint32_t seed) {
+  std::mt19937 g(seed);
+  std::vector<std::uint8_t> v(static_cast<std::size_t>(numel(shape)));
+  for (auto& x : v) x = (g() % 10) < 7;
+  return cpu::CpuTensor(shape, std::move(v));
+}
+
 Tensor on_gpu(const cpu::CpuTensor& t, int device = 0) {
   auto c = cuda::from_cpu(t, device);
   if (!c) {
@@ -275,6 +282,32 @@ int main() {
   cases.push_back({"linear", desc(OpKind::kLinear), {randn({256, 784}, 81), randn({512, 784}, 82, 0.03f), randn({512}, 83)},
                    1e-4, 1e-4});
   cases.push_back({"linear no bias", desc(OpKind::kLinear), {randn({3, 5}, 84), randn({7, 5}, 85)}, 1e-4, 1e-4});
+  // attention composite and its softmax primitive (core/inference.cpp:56-160)
+  {
+    OpDesc att = desc(OpKind::kAttention);
+    cases.push_back({"attention", att, {randn({2, 64, 32}, 101), randn({2, 300, 32}, 102), randn({2, 300, 16}, 103)},
+                     2e-4, 2e-5});
+    cases.push_back({"attention tensor path", att,
+                     {randn({4, 256, 64}, 104), randn({4, 1024, 64}, 105), randn({4, 1024, 64}, 106)}, 2e-4, 2e-5});
+    OpDesc causal = att;
+    causal.causal = true;
+    cases.push_back({"attention causal bool mask", causal,
+                     {randn({2, 40, 16}, 107), randn({1, 50, 16}, 108), randn({2, 50, 8}, 109), randb({40, 50}, 110)},
+                     2e-4, 2e-5});
+    OpDesc scaled = att;
+    scaled.attention_scale = 0.3;
+    cases.push_back({"attention additive mask", scaled,
+                     {randn({2, 1, 3, 4}, 111), randn({1, 3, 5, 4}, 112), randn({2, 3, 5, 2}, 113), randn({3, 5}, 114)},
+                     2e-4, 2e-5});
+    cases.push_back({"attention empty keys", att, {randn({3, 4}, 115), randn({0, 4}, 116), randn({0, 2}, 117)}, 0, 0});
+    OpDesc sm = desc(OpKind::kAttentionSoftmax);
+    sm.attention_shape = Shape{2, 5, 600};
+    sm.attention_scale = 0.7;
+    sm.causal = true;
+    cases.push_back({"attention softmax", sm, {randn({2, 5, 600}, 118, 4.0f), randn({600}, 119)}, 1e-5, 1e-7});
+    OpDesc bad = att;
+    cases.push_back({"attention feature mismatch", bad, {randn({3, 4}, 120), randn({5, 3}, 121), randn({5, 2}, 122)}, 0, 0});
+  }
   for (const auto& c : cases) compare(gpu, ref, c);
 
   // fill descriptor

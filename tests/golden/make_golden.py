@@ -84,10 +84,43 @@ def cases():
                                                         b=rng.uniform(-1, 1, sb).astype(np.float32)), {}))
     a = np.array([[[np.nan, 1]], [[np.inf, 1]], [[-np.inf, -1]], [[-0., 0.]]], np.float32)
     out.append(("matmul_special", "matmul", dict(a=a, b=np.array([[1.], [2.]], np.float32)), {}))
+    # attention composite and primitive (test_inference_ops.py:27-164 shapes and masks)
+    g = np.random.default_rng(20260102)
+    n = lambda *s: g.normal(size=s).astype(np.float32)  # noqa: E731
+    for sq, sk, sv in [((3, 4), (5, 4), (5, 2)), ((2, 3, 4), (2, 5, 4), (2, 5, 6)),
+                       ((2, 1, 3, 4), (1, 3, 5, 4), (2, 3, 5, 2)), ((3, 4), (5, 4), (2, 1, 5, 2)),
+                       ((0, 4), (5, 4), (5, 2)), ((3, 4), (0, 4), (0, 2)), ((3, 4), (5, 4), (5, 0))]:
+        lq, lk = sq[-2], sk[-2]
+        bool_mask = g.random((lq, lk)) > 0.4
+        if lq:
+            bool_mask[0] = False
+        add_mask = n(lq, lk)
+        add_mask[g.random((lq, lk)) < 0.3] = -np.inf
+        for mname, mask in (("none", None), ("bool", bool_mask), ("add", add_mask), ("false", np.array(False))):
+            for causal in (False, True):
+                ins = dict(q=n(*sq), k=n(*sk), v=n(*sv))
+                if mask is not None:
+                    ins["mask"] = mask
+                out.append((f"attention_{sq}_{sk}_{mname}_{causal}", "attention", ins, dict(causal=causal)))
+    for scale in (0.0, -0.5, 2.0, 1e-40):
+        out.append((f"attention_scale_{scale}", "attention",
+                    dict(q=n(2, 3, 4), k=n(5, 4), v=n(5, 3), mask=g.random((2, 1, 5)) > 0.3), dict(scale=scale)))
+    k = np.ones((2, 2), np.float32)
+    k[0] = np.nan
+    out.append(("attention_nan_key", "attention", dict(q=np.ones((1, 2), np.float32), k=k, v=n(2, 3)), {}))
+    for shape, sshape, mshape, causal in [((2, 3, 7), (3, 7), (2, 1, 7), True), ((4, 9), (4, 1), (9,), False)]:
+        mask = n(*mshape)
+        mask[g.random(mshape) < 0.3] = -np.inf
+        out.append((f"attention_softmax_{shape}", "attention_softmax", dict(scores=n(*sshape), mask=mask),
+                    dict(shape=shape, causal=causal, scale=0.7)))
     return out
 
 
 def run(ref, op, inputs, kw):
+    if op == "attention":
+        return ref.attention(inputs["q"], inputs["k"], inputs["v"], inputs.get("mask"), **kw)
+    if op == "attention_softmax":
+        return ref.attention_softmax(inputs["scores"], kw["shape"], inputs.get("mask"), kw["causal"], kw["scale"])
     if op in ("add", "subtract", "multiply", "divide", "matmul"):
         return getattr(ref, op)(inputs["a"], inputs["b"])
     return getattr(ref, op)(inputs["x"], **kw)

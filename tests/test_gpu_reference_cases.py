@@ -308,3 +308,203 @@ def test_affine_norm_parity(tcx, shape, axis, kind, params):
     np.testing.assert_allclose(got, expected, rtol=1e-5, atol=1e-5, equal_nan=True)
     # weight=None is the unweighted op
     same_bits(host(getattr(tcx, kind)(x, axis, weight=None)), host(getattr(tcx, kind)(x, axis)))
+
+
+# ------------------------------------------------------------------ attention
+def numpy_attention(q, k, v, mask=None, causal=False, scale=None):
+    """Float64-free NumPy statement of the kAttention contract (scale * q·kᵀ, then a
+    bool mask selects, a float mask adds and -inf in it selects, causal keeps
+    key <= query, fully masked rows give zeros)."""
+    batch = np.broadcast_shapes(q.shape[:-2], k.shape[:-2], v.shape[:-2])
+    lq, lk = q.shape[-2], k.shape[-2]
+    s = np.float32(1 / np.sqrt(q.shape[-1]) if scale is None else scale)
+    logits = np.broadcast_to(np.matmul(q, np.swapaxes(k, -1, -2)), batch + (lq, lk)) * s
+    keep = np.ones(batch + (lq, lk), bool)
+    if causal:
+        keep = keep & np.tri(lq, lk, dtype=bool)
+    if mask is not None:
+        if mask.dtype == np.bool_:
+            keep = keep & mask
+        else:
+            keep = keep & (mask != -np.inf)
+            logits = logits + mask
+    logits = np.where(keep, logits, -np.inf).astype(np.float32)
+    if lk == 0:
+        return np.zeros(batch + (lq, v.shape[-1]), np.float32)
+    with np.errstate(all="ignore"):
+        top = logits.max(axis=-1, keepdims=True)
+        e = np.exp(logits - top)
+        p = np.where(top == -np.inf, np.float32(0), e / e.sum(axis=-1, keepdims=True))
+        return (p @ v).astype(np.float32)
+
+
+def attn_check(got, expected):
+    assert got.shape == expected.shape, (got.shape, expected.shape)
+    np.testing.assert_allclose(got, expected, rtol=2e-4, atol=2e-5, equal_nan=True)
+
+
+def gauss(shape, seed=31):
+    return np.random.default_rng(seed).normal(size=shape).astype(np.float32)
+
+
+ATTN_SHAPES = [((3, 4), (5, 4), (5, 2)), ((2, 3, 4), (2, 5, 4), (2, 5, 6)),
+               ((2, 1, 3, 4), (1, 3, 5, 4), (2, 3, 5, 2)), ((3, 4), (5, 4), (2, 1, 5, 2)),
+               ((0, 4), (5, 4), (5, 2)), ((3, 4), (0, 4), (0, 2)),
+               ((0, 3, 4), (1, 5, 4), (1, 5, 2)), ((3, 4), (5, 4), (5, 0))]
+
+
+def attn_mask(kind, mshape):
+    rng = np.random.default_rng(41)
+    if kind == "bool":
+        m = rng.random(mshape) > 0.4
+        if m.shape[0]:
+            m[0] = False
+        return m
+    if kind == "additive":
+        m = gauss(mshape)
+        m[rng.random(mshape) < 0.3] = -np.inf
+        if m.shape[0]:
+            m[0] = -np.inf
+        return m
+    if kind == "scalar_false":
+        return np.array(False)
+    return None
+
+
+@pytest.mark.parametrize("shapes", ATTN_SHAPES)
+@pytest.mark.parametrize("mask_kind", ["none", "bool", "additive", "scalar_false"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_parity(tcx, oracle, shapes, mask_kind, causal):
+    """test_inference_ops.py:136-155: broadcast batches, empty extents, every mask
+    kind, causal or not; the oracle is the reference composite restated."""
+    q, k, v = [gauss(s, i + 10) for i, s in enumerate(shapes)]
+    mask = attn_mask(mask_kind, (q.shape[-2], k.shape[-2]))
+    got = host(tcx.attention(dev(q), dev(k), dev(v), None if mask is None else dev(mask), is_causal=causal))
+    attn_check(got, numpy_attention(q, k, v, mask, causal))
+    attn_check(got, oracle.attention(q, k, v, mask, causal))
+
+
+@pytest.mark.parametrize("scale", [0, -0.5, 2, np.float32(0.3)])
+def test_attention_scale_and_batched_mask(tcx, scale):
+    """test_inference_ops.py:158-164."""
+    q, k, v = gauss((2, 3, 4)), gauss((5, 4), 2), gauss((5, 3), 3)
+    mask = np.random.default_rng(4).random((2, 1, 5)) > 0.3
+    got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask), scale=scale))
+    attn_check(got, numpy_attention(q, k, v, mask, scale=scale))
+
+
+def test_attention_causality(tcx):
+    """test_inference_ops.py:167-174: causal rows never see later keys or values."""
+    q, k, v = gauss((5, 4)), gauss((5, 4), 2), gauss((5, 3), 3)
+    before = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=True))
+    k[3:] += 100
+    v[3:] -= 500
+    after = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=True))
+    np.testing.assert_array_equal(before[:3], after[:3])
+
+
+@pytest.mark.parametrize("exceptional", [np.nan, np.inf, -np.inf])
+@pytest.mark.parametrize("masked", [False, True])
+def test_attention_nonfinite_scores(tcx, oracle, exceptional, masked):
+    """test_inference_ops.py:177-184: inf/NaN keys, masked or not."""
+    q, k, v = np.ones((1, 2), np.float32), np.ones((2, 2), np.float32), gauss((2, 3))
+    k[0] = exceptional
+    mask = np.array([[not masked, True]])
+    got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask)))
+    with np.errstate(all="ignore"):
+        attn_check(got, numpy_attention(q, k, v, mask))
+        attn_check(got, oracle.attention(q, k, v, mask))
+
+
+@pytest.mark.parametrize("scale", [np.nan, np.inf, -np.inf, 1e300, 1e-300, 10**400])
+def test_attention_invalid_scale_even_empty(tcx, scale):
+    """test_inference_ops.py:187-190."""
+    q, k, v = (torch.zeros(s, device="cuda") for s in ((0, 2), (3, 2), (3, 1)))
+    with pytest.raises(ValueError):
+        tcx.attention(q, k, v, scale=scale)
+
+
+@pytest.mark.parametrize("scale", [True, "2", 1j, [1]])
+def test_attention_invalid_scale_type(tcx, scale):
+    """test_inference_ops.py:193-196."""
+    x = torch.ones((2, 2), device="cuda")
+    with pytest.raises(TypeError):
+        tcx.attention(x, x, x, scale=scale)
+
+
+@pytest.mark.parametrize("case", ["rank", "features", "zero_features", "sequence", "batch", "mask_int",
+                                  "mask_shape", "mask_rank", "int"])
+def test_attention_invalid_contract(tcx, case):
+    """test_inference_ops.py:213-238, the attention rows."""
+    def t(shape, dtype=torch.float32):
+        return torch.zeros(shape, dtype=dtype, device="cuda")
+    calls = {
+        "rank": lambda: tcx.attention(t((3,)), t((2, 3)), t((2, 3))),
+        "features": lambda: tcx.attention(t((0, 3)), t((2, 4)), t((2, 3))),
+        "zero_features": lambda: tcx.attention(t((0, 0)), t((2, 0)), t((2, 3))),
+        "sequence": lambda: tcx.attention(t((0, 3)), t((2, 3)), t((3, 3))),
+        "batch": lambda: tcx.attention(t((2, 0, 3)), t((3, 2, 3)), t((3, 2, 3))),
+        "mask_int": lambda: tcx.attention(t((0, 3)), t((2, 3)), t((2, 3)), t((0, 2), torch.int32)),
+        "mask_shape": lambda: tcx.attention(t((0, 3)), t((2, 3)), t((2, 3)), t((0, 3), torch.bool)),
+        "mask_rank": lambda: tcx.attention(t((0, 3)), t((2, 3)), t((2, 3)), t((1, 0, 2), torch.bool)),
+        "int": lambda: tcx.attention(t((0, 3), torch.int32), t((2, 3)), t((2, 3))),
+    }
+    with pytest.raises(ValueError):
+        calls[case]()
+
+
+@pytest.mark.parametrize("scale", [1e-39, -1e-39, 1e-40, -1e-40])
+def test_attention_subnormal_scale(tcx, scale):
+    """test_inference_ops.py:283-287: subnormal scales survive the float32 narrowing."""
+    q, k, v = np.array([[1]], np.float32), np.array([[0], [1e38]], np.float32), np.array([[0], [1]], np.float32)
+    got = host(tcx.attention(dev(q), dev(k), dev(v), scale=scale))
+    attn_check(got, numpy_attention(q, k, v, scale=scale))
+
+
+def test_attention_huge_empty_batch(tcx):
+    """test_inference_ops.py:290-294, with 2**40 for the reference's 2**62 (a torch
+    tensor's strides overflow at 2**62 even when it is empty)."""
+    q = torch.empty((0, 2**40, 4, 0, 2), device="cuda")
+    v = torch.empty((0, 2**40, 4, 0, 3), device="cuda")
+    out = tcx.attention(q, q, v)
+    assert tuple(out.shape) == tuple(v.shape)
+
+
+def test_attention_high_rank_metadata(tcx):
+    """test_inference_ops.py:297-302: 17 batch axes."""
+    shape = (1,) * 17
+    q, k, v = gauss(shape + (3, 4)), gauss(shape + (2, 4), 2), gauss(shape + (2, 3), 3)
+    attn_check(host(tcx.attention(dev(q), dev(k), dev(v))), numpy_attention(q, k, v))
+
+
+@pytest.mark.parametrize("lq,lk,d,dv", [(64, 300, 32, 16), (256, 1024, 64, 64), (128, 2048, 128, 128),
+                                        (200, 4096, 64, 80), (64, 8192, 64, 64), (16, 20000, 32, 32)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_sizes_through_every_softmax_width(tcx, oracle, lq, lk, d, dv, causal):
+    """Sizes that reach the tcgen05 GEMMs and each register / streaming softmax shape,
+    against the restated reference composite."""
+    q, k, v = gauss((2, lq, d), 1), gauss((2, lk, d), 2), gauss((2, lk, dv), 3)
+    mask = np.random.default_rng(5).random((lq, lk)) > 0.2
+    got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask), is_causal=causal))
+    attn_check(got, oracle.attention(q, k, v, mask, causal))
+
+
+@pytest.mark.parametrize("shape,sshape,mshape,kind", [
+    ((4, 7), (4, 7), None, None), ((2, 3, 130), (3, 130), (2, 1, 130), "bool"),
+    ((2, 5, 600), (2, 5, 600), (600,), "float"), ((3, 2100), (1, 2100), (3, 1), "bool"),
+    ((2, 9000), (2, 9000), (2, 9000), "float"), ((2, 3, 4), (2, 3, 1), (3, 4), "float")])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_softmax_primitive(tcx, oracle, shape, sshape, mshape, kind, causal):
+    """kAttentionSoftmax with broadcast scores and masks (core/inference.cpp:56-83)."""
+    scores = gauss(sshape, 8) * 4
+    mask = None
+    if kind == "bool":
+        mask = np.random.default_rng(9).random(mshape) > 0.3
+    elif kind == "float":
+        mask = gauss(mshape, 10)
+        mask[np.random.default_rng(11).random(mshape) < 0.2] = -np.inf
+    got = host(tcx.attention_softmax(dev(scores), shape, None if mask is None else dev(mask), scale=0.7,
+                                     is_causal=causal))
+    want = oracle.attention_softmax(scores, shape, mask, causal, 0.7)
+    assert got.shape == want.shape
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-7, equal_nan=True)

@@ -22,6 +22,10 @@ def bits(a):
 
 
 def run(impl, op, inputs, kw):
+    if op == "attention":
+        return impl.attention(inputs["q"], inputs["k"], inputs["v"], inputs.get("mask"), **kw)
+    if op == "attention_softmax":
+        return impl.attention_softmax(inputs["scores"], kw["shape"], inputs.get("mask"), kw["causal"], kw["scale"])
     if op in ("add", "subtract", "multiply", "divide", "matmul"):
         return getattr(impl, op)(inputs["a"], inputs["b"])
     return getattr(impl, op)(inputs["x"], **kw)
@@ -67,6 +71,8 @@ def _random_cases(seed):
     yield "matmul", dict(a=rng.uniform(-1, 1, (3, 17, 9)).astype(np.float32),
                          b=rng.uniform(-1, 1, (9, 5)).astype(np.float32)), {}
     yield "add", dict(a=rng.normal(size=(7, 6)).astype(np.float32), b=rng.normal(size=(6,)).astype(np.float32)), {}
+    q, k, v = (rng.normal(size=s).astype(np.float32) for s in ((2, 5, 8), (1, 7, 8), (2, 7, 3)))
+    yield "attention", dict(q=q, k=k, v=v, mask=rng.random((5, 7)) > 0.3), dict(causal=bool(seed % 2))
 
 
 @pytest.mark.parametrize("seed", [1, 2, 3])

@@ -481,6 +481,25 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                              f"{'NCCL all_gather' if world > 1 else 'the combine kernel'} in rank order"})
     del xf, xi
 
+    # strided and multi-axis reductions (1 GiB each): axis 0 of [65536, 4096], and
+    # axes (0, 2) of [64, 4096, 1024]; outer rows sharded
+    for name, shape, axis in [("sum_axis0_65536x4096", (65536 // world, 4096), 0),
+                              ("sum_axes02_64x4096x1024", (64 // world, 4096, 1024), (0, 2))]:
+        x = torch.randn(*shape, device="cuda", generator=g)
+
+        def st(x=x, axis=axis):
+            return ops.sum(x, axis=axis)
+        st()
+        read_timer(lib)
+        lib.tcx_sm100_timer_enable(1)
+        ms = timer.run(st, steps, 2, sampler) / steps
+        lib.tcx_sm100_timer_enable(0)
+        kern = read_timer(lib)
+        hbm_entry(name, 4.0 * x.numel(), ms, "axis_chunks" if axis == 0 else "axes_chunks", kern,
+                  {"config": f"float32 {list(shape)} sum over axis {axis} per rank (leading axis sharded "
+                             f"{world} way(s)), 4 B/element; partials per rank are not combined across ranks"})
+        del x
+
     # batched matmul + fused bias + SiLU: [64, 2048, 2048]^2, batch sharded
     nb = 64 // world
     a = torch.rand(nb, 2048, 2048, device="cuda", generator=g) * 2 - 1

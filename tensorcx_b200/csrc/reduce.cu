@@ -416,6 +416,200 @@ __device__ __forceinline__ int64_t meta_offset(int64_t index, const Meta& m, int
   return value;
 }
 
+// ------------------------------------------------------ chunked strided axis
+// [outer, reduce, inner] with few (outer, inner) outputs: the reduce axis is cut into
+// `nchunks` pieces; one thread per (outer, piece, inner) folds its piece in index order
+// (coalesced along inner), then one thread per output folds the pieces in order with
+// the same rule. Exact for int32 and for max (the first NaN and the first of equal
+// values survive both folds); float sums are regrouped into pieces (deterministic).
+template <typename T, int OP>  // OP: 0 sum, 1 max, 2 mean
+__device__ __forceinline__ bool fold_one(T& acc, T v) {
+  if (OP == 1) {
+    if constexpr (std::is_same<T, float>::value) {
+      if (isnan(v)) { acc = v; return true; }
+    }
+    acc = (acc < v) ? v : acc;
+  } else {
+    if constexpr (std::is_same<T, float>::value) acc = __fadd_rn(acc, v);
+    else acc = static_cast<T>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(v));
+  }
+  return false;
+}
+
+template <typename T, int OP, int W>  // W adjacent inner columns per thread (1 or 4)
+__global__ void __launch_bounds__(256)
+axis_chunks(const T* __restrict__ x, T* __restrict__ part, int64_t outer, int64_t reduce, int64_t inner,
+            int64_t nchunks, int64_t chunk) {
+  constexpr int kU = 8;  // rows in flight per thread
+  const int64_t cols = inner / W;
+  const int64_t items = outer * nchunks * cols;
+  for (int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; id < items;
+       id += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t jw = id % cols, t = id / cols;
+    const int64_t c = t % nchunks, o = t / nchunks;
+    const int64_t r0 = c * chunk, r1 = min(r0 + chunk, reduce);
+    const T* xp = x + (o * reduce + r0) * inner + jw * W;
+    T acc[W];
+    bool done[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      acc[w] = OP == 1 ? max_identity<T>() : static_cast<T>(0);
+      done[w] = false;
+    }
+    for (int64_t r = r0; r < r1; r += kU) {
+      T v[kU][W];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (r + u < r1) {
+          if constexpr (W == 4) {
+            const auto q = *reinterpret_cast<const typename std::conditional<std::is_same<T, float>::value, float4, int4>::type*>(xp + u * inner);
+            v[u][0] = q.x; v[u][1] = q.y; v[u][2] = q.z; v[u][3] = q.w;
+          } else {
+            v[u][0] = xp[u * inner];
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (r + u < r1) {
+#pragma unroll
+          for (int w = 0; w < W; ++w)
+            if (!done[w]) done[w] = fold_one<T, OP>(acc[w], v[u][w]);
+        }
+      }
+      xp += kU * inner;
+    }
+#pragma unroll
+    for (int w = 0; w < W; ++w) part[(o * nchunks + c) * inner + jw * W + w] = acc[w];
+  }
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(256)
+axis_chunks_fold(const T* __restrict__ part, T* __restrict__ out, int64_t outer, int64_t reduce,
+                 int64_t inner, int64_t nchunks) {
+  const int64_t count = outer * inner;
+  for (int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; id < count;
+       id += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = id / inner, j = id % inner;
+    T acc;
+    acc = OP == 1 ? max_identity<T>() : static_cast<T>(0);
+    for (int64_t c = 0; c < nchunks; ++c)
+      if (fold_one<T, OP>(acc, part[(o * nchunks + c) * inner + j])) break;
+    if constexpr (std::is_same<T, float>::value) {
+      if (OP == 2) acc = reduce ? __fdiv_rn(acc, static_cast<float>(reduce)) : __int_as_float(0x7fc00000);
+    }
+    out[id] = acc;
+  }
+}
+
+// ------------------------------------------------------ chunked multi-axis
+// General selections with long reductions: one warp per (group, piece of `chunk`
+// reduction indices). Lanes take indices r = r0 + lane + 32 i; the innermost reduced
+// axis is walked incrementally (coalesced when it is contiguous) and the other reduced
+// axes are re-derived only when that axis wraps. Each warp leaves one 16-byte record
+// (sum bits, or order key + index + bits), folded per group in piece order: exact for
+// int32 and max (key order = the reference's first-NaN / first-of-equals rule), float
+// sums regrouped (deterministic).
+template <int K, bool FP, int V>  // V consecutive elements per lane and load (1, or 4 as a uint4)
+__global__ void __launch_bounds__(256)
+axes_chunks(const uint32_t* __restrict__ x, tcx_partial* __restrict__ part, int64_t groups, int64_t size,
+            int64_t nchunks, int64_t chunk, Meta meta, int outer_rank) {
+  const int lane = threadIdx.x & 31;
+  const int64_t items = groups * nchunks;
+  const int last = meta.rank - 1;
+  const int64_t e_in = meta.v[2 * last], s_in = meta.v[2 * last + 1];
+  constexpr int64_t kStep = 32 * V;
+  for (int64_t item = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; item < items;
+       item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t g = item / nchunks, c = item % nchunks;
+    const int64_t base = meta_offset(g, meta, 0, outer_rank);
+    const int64_t r0 = c * chunk, r1 = min(r0 + chunk, size);
+    uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0, best = 0;
+    int64_t idx = INT64_MAX;
+    auto fold = [&](uint32_t w, int64_t at) {
+      if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(w)));
+      else if (K == kSumI) bits += w;
+      else {
+        const uint32_t k = key_max(w, FP);
+        if (k > key || idx == INT64_MAX) { key = k; idx = at; best = w; }
+      }
+    };
+    int64_t r = r0 + V * lane;
+    if (r < r1) {
+      int64_t q = r / e_in, p = r % e_in;
+      int64_t run = base + meta_offset(q, meta, outer_rank, last);
+      for (; r < r1; r += 4 * kStep) {
+        // four addresses from the index walk, four loads in flight, then the folds
+        uint32_t w[4][V];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (r + kStep * u < r1) {
+            if constexpr (V == 4) {
+              const uint4 t = *reinterpret_cast<const uint4*>(x + run + p);
+              w[u][0] = t.x; w[u][1] = t.y; w[u][2] = t.z; w[u][3] = t.w;
+            } else {
+              w[u][0] = __ldg(x + run + p * s_in);
+            }
+          }
+          p += kStep;
+          if (p >= e_in) {
+            q += p / e_in;
+            p %= e_in;
+            run = base + meta_offset(q, meta, outer_rank, last);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t ru = r + kStep * u;
+          if (ru >= r1) break;
+#pragma unroll
+          for (int e = 0; e < V; ++e) fold(w[u][e], ru + e);
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {  // fixed tree order across lanes
+      const uint32_t ob = __shfl_xor_sync(0xffffffffu, bits, off);
+      const uint32_t ok = __shfl_xor_sync(0xffffffffu, key, off);
+      const uint32_t ow = __shfl_xor_sync(0xffffffffu, best, off);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, off);
+      if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(ob)));
+      else if (K == kSumI) bits += ob;
+      else if (better(ok, oi, key, idx)) { key = ok; idx = oi; best = ow; }
+    }
+    if (lane == 0) {
+      tcx_partial rec;
+      rec.key = key;
+      rec.bits = K <= kSumI ? bits : best;
+      rec.index = idx;
+      part[item] = rec;
+    }
+  }
+}
+
+template <int K>
+__global__ void __launch_bounds__(256)
+axes_chunks_fold(const tcx_partial* __restrict__ part, uint32_t* __restrict__ out, int64_t groups,
+                 int64_t nchunks, int64_t size, int mean) {
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0, best = 0;
+    int64_t idx = INT64_MAX;
+    for (int64_t c = 0; c < nchunks; ++c) {
+      const tcx_partial p = part[g * nchunks + c];
+      if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(p.bits)));
+      else if (K == kSumI) bits += p.bits;
+      else if (better(p.key, p.index, key, idx)) { key = p.key; idx = p.index; best = p.bits; }
+    }
+    if (K <= kSumI) {
+      out[g] = mean ? __float_as_uint(__fdiv_rn(__uint_as_float(bits), static_cast<float>(size))) : bits;
+    } else {
+      out[g] = best;
+    }
+  }
+}
+
 // General multi-axis sum/max/mean, one thread per output (cpu_backend.cpp:1123-1152).
 template <typename T, int OP>
 __global__ void reduce_axes_general(const T* __restrict__ x, T* __restrict__ out,
@@ -583,8 +777,21 @@ int load_meta(Meta& m, const int64_t* meta, int rank) {
 
 }  // namespace
 
+// Pieces of a strided-axis reduction (1 = one thread per output): only when the
+// outputs alone leave most of the GPU idle and each output has real work.
+int64_t strided_chunks(int64_t outer, int64_t reduce, int64_t inner) {
+  const int64_t count = outer * inner;
+  if (inner <= 1 || count <= 0 || count >= 32768 || reduce < 256) return 1;
+  const int64_t target = 2048LL * sm_count();  // one wave of resident threads
+  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(reduce, 64), ceil_div(target, count)));
+}
+
 size_t axis_reduce_workspace(int64_t outer, int64_t reduce, int64_t inner) {
-  if (inner != 1 || reduce <= 65536 || outer >= 4096 || outer <= 0) return 0;
+  if (inner != 1) {
+    const int64_t pieces = strided_chunks(outer, reduce, inner);
+    return pieces > 1 ? static_cast<size_t>(outer * pieces * inner) * 4 : 0;
+  }
+  if (reduce <= 65536 || outer >= 4096 || outer <= 0) return 0;
   return tree_workspace(outer, reduce);
 }
 
@@ -619,6 +826,33 @@ int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* outp
     }
     return launch_status("ordered row reduction");
   }
+  const int64_t pieces = strided_chunks(outer, reduce, inner);
+  if (pieces > 1 && ws && ws_bytes >= static_cast<size_t>(outer * pieces * inner) * 4) {
+    const int64_t chunk = ceil_div(reduce, pieces);
+    const bool vec = inner % 4 == 0 && reinterpret_cast<uintptr_t>(input) % 16 == 0;
+    const int grid1 = grid_for(outer * pieces * (vec ? inner / 4 : inner), 256), grid2 = grid_for(count, 256);
+    TimedLaunch timer("axis_chunks", s);
+    auto run = [&](auto zero, auto op_tag) {
+      using T = decltype(zero);
+      constexpr int OP = decltype(op_tag)::value;
+      constexpr int FOLD = OP;
+      const T* x = static_cast<const T*>(input);
+      T* part = static_cast<T*>(ws);
+      T* o = static_cast<T*>(output);
+      if (vec) axis_chunks<T, OP == 2 ? 0 : OP, 4><<<grid1, 256, 0, s>>>(x, part, outer, reduce, inner, pieces, chunk);
+      else axis_chunks<T, OP == 2 ? 0 : OP, 1><<<grid1, 256, 0, s>>>(x, part, outer, reduce, inner, pieces, chunk);
+      axis_chunks_fold<T, FOLD><<<grid2, 256, 0, s>>>(part, o, outer, reduce, inner, pieces);
+    };
+    if (f32) {
+      if (op == TCX_OP_MAX) run(0.0f, std::integral_constant<int, 1>());
+      else if (op == TCX_OP_SUM) run(0.0f, std::integral_constant<int, 0>());
+      else run(0.0f, std::integral_constant<int, 2>());
+    } else {
+      if (op == TCX_OP_MAX) run(int32_t(0), std::integral_constant<int, 1>());
+      else run(int32_t(0), std::integral_constant<int, 0>());
+    }
+    return launch_status("chunked strided axis reduction");
+  }
   const int grid = grid_for(count, 256);
   TimedLaunch timer("axis_strided", s);
   if (f32) {
@@ -647,7 +881,9 @@ size_t tcx_sm100_reduce_workspace_bytes(int64_t count) {
   // Upper bound of tree_workspace(rows, n) over every split rows * n == count that
   // runs the tree (n >= 1024): fewer rows than the CTA target use at most that many
   // records; more rows use one record per row.
-  const int64_t records = std::max<int64_t>(4LL * sm_count(), count / 1024 + 1);
+  // (chunked multi-axis selections need at most count / 1024 + groups records, with
+  // groups <= count / 2048: covered by 2 * count / 1024.)
+  const int64_t records = std::max<int64_t>(4LL * sm_count(), 2 * (count / 1024) + 1);
   return static_cast<size_t>(records) * sizeof(tcx_partial);
 }
 
@@ -722,6 +958,46 @@ int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* in
   }
   Meta meta;
   if (int st = load_meta(meta, index_metadata, rank)) return st;
+  // long reductions over few groups: warps per (group, piece), records folded in order
+  if (reduction_size >= 2048 && groups < 65536 && outer_rank < rank) {
+    const int64_t target = 64LL * sm_count();  // warps: 8 per CTA, 8 CTAs per SM
+    const int64_t pieces = std::max<int64_t>(1, std::min<int64_t>(ceil_div(reduction_size, 1024),
+                                                                  ceil_div(target, groups)));
+    const int last = rank - 1;
+    // 16-byte loads when the innermost reduced axis is the contiguous last axis with an
+    // extent divisible by 4 (every other stride is then a multiple of 4 as well)
+    const bool vec = index_metadata[2 * last + 1] == 1 && index_metadata[2 * last] % 4 == 0 &&
+                     reinterpret_cast<uintptr_t>(input) % 16 == 0;
+    const int64_t chunk = vec ? ceil_div(ceil_div(reduction_size, pieces), 4) * 4 : ceil_div(reduction_size, pieces);
+    const int64_t npieces = ceil_div(reduction_size, chunk);
+    const size_t need = static_cast<size_t>(groups * npieces) * sizeof(tcx_partial);
+    if (npieces > 1 && workspace && workspace_bytes >= need) {
+      auto* part = static_cast<tcx_partial*>(workspace);
+      const auto* x = static_cast<const uint32_t*>(input);
+      auto* o = static_cast<uint32_t*>(output);
+      const int grid1 = grid_for(groups * npieces * 32, 256), grid2 = grid_for(groups, 256);
+      const bool fp = dtype == TCX_FLOAT32;
+      TimedLaunch timer("axes_chunks", s);
+      auto run = [&](auto kind_tag, auto fp_tag) {
+        constexpr int K = decltype(kind_tag)::value;
+        constexpr bool FP = decltype(fp_tag)::value;
+        if (vec) axes_chunks<K, FP, 4><<<grid1, 256, 0, s>>>(x, part, groups, reduction_size, npieces, chunk, meta, outer_rank);
+        else axes_chunks<K, FP, 1><<<grid1, 256, 0, s>>>(x, part, groups, reduction_size, npieces, chunk, meta, outer_rank);
+        axes_chunks_fold<K><<<grid2, 256, 0, s>>>(part, o, groups, npieces, reduction_size, op == TCX_OP_MEAN);
+      };
+      using T0 = std::integral_constant<bool, false>;
+      using T1 = std::integral_constant<bool, true>;
+      if (op == TCX_OP_MAX) {
+        if (fp) run(std::integral_constant<int, kBestMax>(), T1());
+        else run(std::integral_constant<int, kBestMax>(), T0());
+      } else if (fp) {
+        run(std::integral_constant<int, kSumF>(), T1());
+      } else {
+        run(std::integral_constant<int, kSumI>(), T0());
+      }
+      return launch_status("chunked multi-axis reduction");
+    }
+  }
   const int grid = grid_for(groups, 256);
   TimedLaunch timer("reduce_axes_general", s);
   if (dtype == TCX_FLOAT32) {

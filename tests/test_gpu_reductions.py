@@ -175,3 +175,51 @@ def test_partial_records_combine_in_rank_order(tcx, oracle):
             assert sum_close(float(got), float(expect), exact), (op, got, expect, exact)
         else:
             same_bits(got, expect)
+
+
+def sums_close(got, cpu, exact, mass):
+    """Elementwise float32 sum/mean criterion for regrouped (parallel) reductions:
+    within 1e-5 relative of the CPU's sequential result, or at least as close to the
+    exact float64 value as the CPU is, or within 1e-6 of the absolute mass sum |x|
+    (sums that cancel to near zero)."""
+    got, cpu, exact, mass = (np.asarray(a, np.float64) for a in (got, cpu, exact, mass))
+    ok = (np.abs(got - cpu) <= 1e-5 * np.abs(cpu)) | (np.abs(got - exact) <= np.abs(cpu - exact)) | \
+         (np.abs(got - exact) <= 1e-6 * mass)
+    return bool(ok.all())
+
+
+STRIDED = [((4096, 3), 0), ((100000, 7), 0), ((8, 5000, 64), 1), ((2, 70000, 3), 1), ((3000, 2, 5), 0)]
+MULTI = [((64, 100, 1024), (0, 2)), ((300, 17, 40), (0, 2)), ((3, 4096, 5), (0, 1)), ((50, 3, 2000), (2, 0)),
+         ((2, 3, 4, 5000), (0, 1, 3))]
+
+
+@pytest.mark.parametrize("shape,axis", STRIDED + MULTI)
+def test_parallel_strided_and_multi_axis_exact_kinds(tcx, oracle, shape, axis):
+    """Strided single axes and general selections with few outputs run in pieces:
+    int32 sums and every max stay bit-exact (first NaN, first of equal values)."""
+    rng = np.random.default_rng(len(shape) * 7 + shape[0])
+    xi = rng.integers(-1000, 1000, shape).astype(np.int32)
+    xi.flat[::101] = 2**31 - 1  # wraparound
+    for op in ("sum", "max"):
+        same_bits(host(getattr(tcx, op)(dev(xi), axis=axis)), getattr(oracle, op)(xi, axis))
+    xf = rng.normal(size=shape).astype(np.float32)
+    flat = xf.reshape(-1)
+    flat[rng.integers(0, flat.size, 50)] = np.float32(xf.max())  # ties across pieces
+    flat[rng.integers(0, flat.size, 20)] = -0.0
+    same_bits(host(tcx.max(dev(xf), axis=axis)), oracle.max(xf, axis))
+    flat[rng.integers(0, flat.size, 3)] = np.nan
+    flat[rng.integers(0, flat.size, 1)] = np.frombuffer(np.uint32(0x7fc0abcd).tobytes(), np.float32)[0]
+    same_bits(host(tcx.max(dev(xf), axis=axis)), oracle.max(xf, axis))
+
+
+@pytest.mark.parametrize("shape,axis", STRIDED + MULTI)
+@pytest.mark.parametrize("op", ["sum", "mean"])
+def test_parallel_strided_and_multi_axis_float_sums(tcx, oracle, shape, axis, op):
+    x = np.random.default_rng(shape[-1]).normal(size=shape).astype(np.float32)
+    got = host(getattr(tcx, op)(dev(x), axis=axis))
+    cpu = getattr(oracle, op)(x, axis)
+    x64 = x.astype(np.float64)
+    exact = x64.sum(axis=axis) if op == "sum" else x64.mean(axis=axis)
+    mass = np.abs(x64).sum(axis=axis) / (1 if op == "sum" else x64.size / np.asarray(exact).size)
+    assert got.shape == cpu.shape
+    assert sums_close(got, cpu, exact, mass)

@@ -500,6 +500,37 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                              f"{world} way(s)), 4 B/element; partials per rank are not combined across ranks"})
         del x
 
+    # host <-> device transfers of 1 GiB pageable host memory (from_cpu / to_cpu): the
+    # pinned two-slot staging of tcx_sm100_copy_to_* against the driver's pageable path
+    import numpy as np
+    nbytes = 1 << 30
+    host_buf = np.ones(nbytes // 4, np.float32)
+    back_buf = np.empty_like(host_buf)
+    dev_buf = torch.empty(nbytes // 4, device="cuda")
+    cs = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    hp, bp, dp = (ctypes.c_void_p(host_buf.ctypes.data), ctypes.c_void_p(back_buf.ctypes.data),
+                  ctypes.c_void_p(dev_buf.data_ptr()))
+
+    def wall(fn, reps=3):
+        fn()
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        return nbytes / best / 1e9
+    host_t, back_t = torch.from_numpy(host_buf), torch.from_numpy(back_buf)
+    out["transfer_pageable_1GiB"] = {
+        "value": wall(lambda: lib.tcx_sm100_copy_to_device(cs, dp, hp, nbytes)), "unit": "GB/s",
+        "d2h_gbs": wall(lambda: lib.tcx_sm100_copy_to_host(cs, bp, dp, nbytes)),
+        "driver_pageable_h2d_gbs": wall(lambda: dev_buf.copy_(host_t)),
+        "driver_pageable_d2h_gbs": wall(lambda: back_t.copy_(dev_buf)),
+        "config": "1 GiB pageable numpy buffer <-> device, synchronous, wall clock (best of 3); value = "
+                  "host-to-device through tcx_sm100_copy_to_device"}
+    del host_buf, back_buf, dev_buf, host_t, back_t
+
     # batched matmul + fused bias + SiLU: [64, 2048, 2048]^2, batch sharded
     nb = 64 // world
     a = torch.rand(nb, 2048, 2048, device="cuda", generator=g) * 2 - 1

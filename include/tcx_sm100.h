@@ -303,6 +303,15 @@ int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, con
                         const int64_t* mask_strides, float scale, int32_t causal, void* workspace,
                         size_t workspace_bytes);
 
+/* Synchronous copies between host and device memory of the current device (the
+ * transfers of from_cpu / to_cpu, cuda_backend.cpp:215-264 of the reference). Pageable
+ * host buffers of 4 MiB and more are staged through two page-locked 32 MiB slots per
+ * device, with several host threads copying one slot while the DMA engine moves the
+ * other; page-locked buffers and small copies use one cudaMemcpyAsync. `stream` orders
+ * the copy after earlier work on it; the call returns when the copy is complete. */
+int tcx_sm100_copy_to_device(tcx_stream_t stream, void* dst, const void* src, size_t bytes);
+int tcx_sm100_copy_to_host(tcx_stream_t stream, void* dst, const void* src, size_t bytes);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -64,6 +64,8 @@ SIGNATURES = {
     "tcx_sm100_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
     "tcx_sm100_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64p,
                                            _i64p, _i64p, _i64p, _i32, _i64p, _f32, _i32, _vp, _sz]),
+    "tcx_sm100_copy_to_device": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
+    "tcx_sm100_copy_to_host": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
     "tcx_sm100_matmul_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int]),
     "tcx_sm100_matmul": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i32,
                                         _vp, ctypes.c_int, ctypes.c_int, _vp, _sz]),

@@ -662,10 +662,10 @@ Expected<CudaTensor> from_cpu(const cpu::CpuTensor& tensor, int device) {
   if (buffer.value()->nbytes()) {
     DeviceScope scope(device);
     if (!scope.ready()) return scope.status();
-    auto st = runtime_status(cudaMemcpyAsync(buffer.value()->data(), tensor.data(), buffer.value()->nbytes(),
-                                             cudaMemcpyHostToDevice, scope.stream()),
-                             "CUDA upload");
-    if (st.ok()) st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA upload synchronize");
+    // pinned staging with parallel host copies for large pageable tensors (synchronous)
+    auto st = abi_status(tcx_sm100_copy_to_device(abi_stream(scope), buffer.value()->data(), tensor.data(),
+                                                  buffer.value()->nbytes()),
+                         "CUDA upload");
     if (!st.ok()) return st;
   }
   return CudaTensor(tensor.dtype(), tensor.shape(), buffer.move_value());
@@ -676,10 +676,9 @@ Expected<cpu::CpuTensor> to_cpu(const CudaTensor& tensor) {
   if (tensor.nbytes()) {
     DeviceScope scope(tensor.buffer()->device());
     if (!scope.ready()) return scope.status();
-    auto st = runtime_status(cudaMemcpyAsync(result.mutable_data(), tensor.buffer()->data(), tensor.nbytes(),
-                                             cudaMemcpyDeviceToHost, scope.stream()),
-                             "CUDA download");
-    if (st.ok()) st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA download synchronize");
+    auto st = abi_status(tcx_sm100_copy_to_host(abi_stream(scope), result.mutable_data(), tensor.buffer()->data(),
+                                                tensor.nbytes()),
+                         "CUDA download");
     if (!st.ok()) return st;
   }
   return result;

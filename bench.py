@@ -327,6 +327,30 @@ def gpu_arm(args):
     e2e_ws = ctypes.c_void_p((e2e_buf.data_ptr() + 1023) // 1024 * 1024)
     torch.cuda.synchronize()
 
+    # the transfer floor of one step: A and B uploaded over PCIe from page-locked memory
+    # while C comes back on another stream (full duplex; the download slows the uploads)
+    up = e2e_buf[:3 * size * size * 4].view(torch.float32)
+    s_up, s_down = torch.cuda.Stream(), torch.cuda.Stream()
+    h2d_s = duplex_s = float("inf")
+    for duplex in (False, True):
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            with torch.cuda.stream(s_up):
+                up[:size * size].copy_(a_host.view(-1), non_blocking=True)
+                up[size * size:2 * size * size].copy_(b_host.view(-1), non_blocking=True)
+            if duplex:
+                with torch.cuda.stream(s_down):
+                    c_host.view(-1).copy_(up[2 * size * size:], non_blocking=True)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t1
+            if duplex:
+                duplex_s = min(duplex_s, dt)
+            else:
+                h2d_s = min(h2d_s, dt)
+    h2d_gbs = 2 * size * size * 4 / h2d_s / 1e9
+    del up
+
     def e2e_step():
         _abi.check(lib.tcx_sm100_matmul_host(ctypes.c_void_p(a_host.data_ptr()), ctypes.c_void_p(b_host.data_ptr()),
                                              ctypes.c_void_p(c_host.data_ptr()), size, size, size, e2e_ws,
@@ -395,7 +419,10 @@ def gpu_arm(args):
                         / max(args.steps, 1)},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * size * size * 4,
                     "d2h_bytes_per_step": size * size * 4, "ms_per_step": e2e_ms,
-                    "api": "tcx_sm100_matmul_host (pinned host A, B in; C out; synchronous)"},
+                    "api": "tcx_sm100_matmul_host (pinned host A, B in; C out; synchronous)",
+                    "pcie_h2d_gbs": h2d_gbs, "upload_floor_ms": h2d_s * 1e3,
+                    "transfer_floor_ms": duplex_s * 1e3,
+                    "frac_of_transfer_floor": duplex_s * 1e3 / e2e_ms},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "kernels_in_timed_region": {k: {"launches": v[0], "total_ms": v[1]} for k, v in kernels.items()},

@@ -671,6 +671,88 @@ int64_t distinct_batches(const BatchMap& bm, bool lhs, int64_t per) {
   for (int a = 0; a < bm.rank; ++a) max_off += (bm.shape[a] - 1) * (lhs ? bm.lhs[a] : bm.rhs[a]);
   return max_off / per + 1;
 }
+
+// ------------------------------------------------------------ tensor-path phases
+// Split pre-pass of the left operand: nba matrices [m, k] -> hi/lo planes
+// [2 * nba, m, kp] (K-major); raises *flag on inf / NaN.
+void split_a(cudaStream_t s, const float* lhs, float* wa, int64_t nba, int64_t m, int64_t k, int64_t kp,
+             int* flag, int sms) {
+  const bool vec_a = k % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0;
+  const int grid_a = static_cast<int>(std::min<int64_t>(ceil_div(nba * m * (kp / 4), 256 * 4), 16LL * sms));
+  TimedLaunch timer("split_rows", s);
+  if (vec_a) split_rows<true><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, kp, flag);
+  else split_rows<false><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, kp, flag);
+}
+
+// Split pre-pass of the right operand into K-major planes [2 * nbb, n, kp]: a row split
+// when it is already K-major ([n][k], a linear weight or key matrix), else a transpose.
+void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n, int64_t k, int64_t kp, int* flag,
+             bool kmajor, int sms) {
+  if (kmajor) {
+    const bool vec_w = k % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+    const int grid_w = static_cast<int>(std::min<int64_t>(ceil_div(nbb * n * (kp / 4), 256 * 4), 16LL * sms));
+    TimedLaunch timer("split_rows", s);
+    if (vec_w) split_rows<true><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, kp, flag);
+    else split_rows<false><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, kp, flag);
+  } else {
+    const bool vec_b = n % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+    const int64_t tiles = nbb * ceil_div(n, 128) * (kp / 32);
+    const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
+    TimedLaunch timer("split_cols", s);
+    if (vec_b) split_cols<true><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, kp, flag);
+    else split_cols<false><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, kp, flag);
+  }
+}
+
+// The tcgen05 GEMM over split planes, then the IEEE FFMA fallback that runs only when
+// the pre-pass raised *flag (reading the original lhs / rhs).
+int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
+                int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
+                const float* lhs, const float* rhs, bool rhs_kmajor, int sms) {
+  alignas(64) CUtensorMap map_a, map_b;
+  if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, kBN))
+    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
+        cudaSuccess)
+      return launch_status("gemm smem attribute");
+    attr_done[dev] = true;
+  }
+  GemmArgs g;
+  g.c = output;
+  g.bias = bias;
+  g.nonfinite = flag;
+  g.err = device_error_word();
+  g.m = m; g.n = n; g.k_elems = k;
+  g.lhs_mk = m * k; g.rhs_kn = k * n;
+  g.num_kb = static_cast<int32_t>(kp / kBK);
+  g.tiles_m = static_cast<int32_t>(ceil_div(m, kBM));
+  g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
+  g.act = act;
+  g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
+  g.batches = batches;
+  g.bm = bm;
+  const int64_t tiles = batches * g.tiles_m * g.tiles_n;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  {
+    TimedLaunch timer("gemm_tf32x3", s);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
+  }
+  if (int st = launch_status("tcgen05 matmul")) return st;
+  // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
+  const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
+  const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
+  {
+    TimedLaunch timer("gemm_ffma_fallback", s);
+    if (rhs_kmajor) gemm_ffma_kernel<true><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+    else gemm_ffma_kernel<false><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+  }
+  return launch_status("matmul fallback");
+}
 }  // namespace
 
 extern "C" {
@@ -721,75 +803,11 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   if (2 * std::max(nba, nbb) > INT32_MAX) return invalid("too many operand batches for the tensor path");
 
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
-  {
-    const bool vec_a = k % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0;
-    const int grid_a = static_cast<int>(std::min<int64_t>(ceil_div(nba * m * (lay.kp / 4), 256 * 4), 16LL * sms));
-    {
-      TimedLaunch timer("split_rows", s);
-      if (vec_a) split_rows<true><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
-      else split_rows<false><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, lay.kp, flag);
-    }
-    if (rhs_kmajor) {
-      // B already K-major ([n][k], a linear weight): the row split applies as is
-      const bool vec_w = k % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
-      const int grid_w = static_cast<int>(std::min<int64_t>(ceil_div(nbb * n * (lay.kp / 4), 256 * 4), 16LL * sms));
-      TimedLaunch timer("split_rows", s);
-      if (vec_w) split_rows<true><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);
-      else split_rows<false><<<grid_w, 256, 0, s>>>(rhs, wb, nbb, n, k, lay.kp, flag);
-    } else {
-      const bool vec_b = n % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
-      const int64_t tiles = nbb * ceil_div(n, 128) * (lay.kp / 32);
-      const int grid_b = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
-      TimedLaunch timer("split_cols", s);
-      if (vec_b) split_cols<true><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
-      else split_cols<false><<<grid_b, 256, 0, s>>>(rhs, wb, nbb, k, n, lay.kp, flag);
-    }
-  }
+  split_a(s, lhs, wa, nba, m, k, lay.kp, flag, sms);
+  split_b(s, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
   if (int st = launch_status("matmul split pre-pass")) return st;
-
-  alignas(64) CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, wa, 2 * nba, m, lay.kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, lay.kp, kBN))
-    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
-
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
-        cudaSuccess)
-      return launch_status("gemm smem attribute");
-    attr_done[dev] = true;
-  }
-  GemmArgs g;
-  g.c = output;
-  g.bias = bias;
-  g.nonfinite = flag;
-  g.err = device_error_word();
-  g.m = m; g.n = n; g.k_elems = k;
-  g.lhs_mk = m * k; g.rhs_kn = k * n;
-  g.num_kb = static_cast<int32_t>(lay.kp / kBK);
-  g.tiles_m = static_cast<int32_t>(ceil_div(m, kBM));
-  g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
-  g.act = act;
-  g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
-  g.batches = batches;
-  g.bm = bm;
-  const int64_t tiles = batches * g.tiles_m * g.tiles_n;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
-  {
-    TimedLaunch timer("gemm_tf32x3", s);
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
-  }
-  if (int st = launch_status("tcgen05 matmul")) return st;
-  // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
-  const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
-  const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
-  {
-    TimedLaunch timer("gemm_ffma_fallback", s);
-    if (rhs_kmajor) gemm_ffma_kernel<true><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
-    else gemm_ffma_kernel<false><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
-  }
-  return launch_status("matmul fallback");
+  return gemm_planes(s, wa, wb, nba, nbb, m, n, k, lay.kp, batches, bm, output, bias, act, flag, lhs, rhs,
+                     rhs_kmajor, sms);
 }
 
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
@@ -815,47 +833,75 @@ int tcx_sm100_linear(tcx_stream_t stream, const float* x, const float* w, const 
 
 // ------------------------------------------------------------ host-buffer matmul
 namespace {
+constexpr int kHostSlots = 3;
+
 struct HostPlan {
-  int64_t chunk_m, chunks;
-  size_t off_b, off_a[2], off_c[2], off_ws, ws_bytes, total;
+  int64_t chunk_m, chunks, kp;
+  bool tensor;  // chunks run the tcgen05 path with B split once; else run_matmul per chunk
+  size_t off_b, off_bp, off_bflag, off_a[kHostSlots], off_ap[kHostSlots], off_c[kHostSlots],
+      off_flag[kHostSlots], off_ws, ws_bytes, total;
 };
 
+// Row chunks of A (and C). The PCIe uploads are the floor of the whole call; chunks
+// of 512 rows keep each chunk's GEMM (B split once) about as long as the next chunk's
+// upload, and keep the tail that nothing overlaps (the last GEMM and download) short.
+// Measured at 8192^3: 512-row chunks 11.6 ms per call, 1024 rows 12.1, 2048 rows 13.3.
 HostPlan host_plan(int64_t m, int64_t n, int64_t k) {
   HostPlan p;
-  p.chunks = m >= 1024 ? 4 : 1;
-  p.chunk_m = (m + p.chunks - 1) / p.chunks;
-  p.chunk_m = (p.chunk_m + kBM - 1) / kBM * kBM;
+  p.chunk_m = m >= 2048 ? 512 : m;
   p.chunks = (m + p.chunk_m - 1) / p.chunk_m;
+  p.kp = (k + kBK - 1) / kBK * kBK;
+  p.tensor = use_tensor(p.chunk_m, n, k, TCX_MATMUL_AUTO);
   size_t off = 0;
   p.off_b = off;
   off = align_up(off + static_cast<size_t>(k * n) * 4, 1024);
-  for (int s = 0; s < 2; ++s) {
+  p.off_bp = p.off_bflag = off;
+  if (p.tensor) {
+    off = align_up(off + static_cast<size_t>(2 * n * p.kp) * 4, 1024);
+    p.off_bflag = off;
+    off += 1024;
+  }
+  for (int s = 0; s < kHostSlots; ++s) {
     p.off_a[s] = off;
     off = align_up(off + static_cast<size_t>(p.chunk_m * k) * 4, 1024);
     p.off_c[s] = off;
     off = align_up(off + static_cast<size_t>(p.chunk_m * n) * 4, 1024);
+    p.off_ap[s] = p.off_flag[s] = off;
+    if (p.tensor) {
+      off = align_up(off + static_cast<size_t>(2 * p.chunk_m * p.kp) * 4, 1024);
+      p.off_flag[s] = off;
+      off += 1024;
+    }
   }
   p.off_ws = off;
-  p.ws_bytes = tcx_sm100_matmul_workspace_bytes(p.chunk_m, n, k, 1, 1, TCX_MATMUL_AUTO);
+  p.ws_bytes = p.tensor ? 0 : tcx_sm100_matmul_workspace_bytes(p.chunk_m, n, k, 1, 1, TCX_MATMUL_AUTO);
   p.total = align_up(off + p.ws_bytes, 1024);
   return p;
 }
 
 struct Streams {
   cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
-  cudaEvent_t b_ready = nullptr, a_ready = nullptr, c_ready = nullptr, a_free[2] = {nullptr, nullptr},
-              c_free[2] = {nullptr, nullptr};
+  cudaEvent_t b_ready = nullptr, a_ready = nullptr, c_ready = nullptr, a_free[kHostSlots] = {},
+              c_free[kHostSlots] = {};
   cudaError_t create() {
     cudaError_t e = cudaSuccess;
     for (cudaStream_t* st : {&in, &comp, &out})
       if (e == cudaSuccess) e = cudaStreamCreateWithFlags(st, cudaStreamNonBlocking);
-    for (cudaEvent_t* ev : {&b_ready, &a_ready, &c_ready, &a_free[0], &a_free[1], &c_free[0], &c_free[1]})
+    for (cudaEvent_t* ev : {&b_ready, &a_ready, &c_ready})
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    for (int i = 0; i < kHostSlots; ++i) {
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a_free[i], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c_free[i], cudaEventDisableTiming);
+    }
     return e;
   }
   ~Streams() {
-    for (cudaEvent_t ev : {b_ready, a_ready, c_ready, a_free[0], a_free[1], c_free[0], c_free[1]})
+    for (cudaEvent_t ev : {b_ready, a_ready, c_ready})
       if (ev) cudaEventDestroy(ev);
+    for (int i = 0; i < kHostSlots; ++i) {
+      if (a_free[i]) cudaEventDestroy(a_free[i]);
+      if (c_free[i]) cudaEventDestroy(c_free[i]);
+    }
     for (cudaStream_t st : {in, comp, out})
       if (st) cudaStreamDestroy(st);
   }
@@ -896,14 +942,25 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
   }
   cudaEventRecord(st.b_ready, st.in);
   cudaStreamWaitEvent(st.comp, st.b_ready, 0);
+  cudaStream_t comp = st.comp;
+  const int sms = sm_count();
+  float* b_planes = reinterpret_cast<float*>(ws + p.off_bp);
+  int* b_flag = reinterpret_cast<int*>(ws + p.off_bflag);
+  if (p.tensor) {  // B's split pre-pass once, shared by every chunk
+    if (cudaError_t e = cudaMemsetAsync(b_flag, 0, sizeof(int), comp); e != cudaSuccess)
+      return fail(e, "matmul_host flag reset");
+    split_b(comp, b_dev, b_planes, 1, n, k, p.kp, b_flag, false, sms);
+  }
+  BatchMap one;
+  one.rank = 0;
   for (int64_t i = 0; i < p.chunks; ++i) {
-    const int slot = static_cast<int>(i & 1);
+    const int slot = static_cast<int>(i % kHostSlots);
     const int64_t r0 = i * p.chunk_m;
     const int64_t rows = std::min<int64_t>(p.chunk_m, m - r0);
     float* a_dev = reinterpret_cast<float*>(ws + p.off_a[slot]);
     float* c_dev = reinterpret_cast<float*>(ws + p.off_c[slot]);
-    // upload A chunk once the GEMM two chunks back has finished reading this slot
-    if (i >= 2) cudaStreamWaitEvent(st.in, st.a_free[slot], 0);
+    // upload A chunk once the GEMM that last used this slot has finished with it
+    if (i >= kHostSlots) cudaStreamWaitEvent(st.in, st.a_free[slot], 0);
     if (k > 0) {
       if (cudaError_t e = cudaMemcpyAsync(a_dev, a_host + r0 * k, static_cast<size_t>(rows * k) * 4,
                                           cudaMemcpyHostToDevice, st.in);
@@ -911,14 +968,27 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
         return fail(e, "matmul_host A upload");
     }
     cudaEventRecord(st.a_ready, st.in);
-    cudaStreamWaitEvent(st.comp, st.a_ready, 0);
-    if (i >= 2) cudaStreamWaitEvent(st.comp, st.c_free[slot], 0);  // C slot downloaded
-    const int rc = run_matmul(reinterpret_cast<tcx_stream_t>(st.comp), a_dev, b_dev, c_dev, rows, n, k, 1, nullptr,
-                              nullptr, nullptr, 0, nullptr, TCX_ACT_NONE, TCX_MATMUL_AUTO, ws + p.off_ws, p.ws_bytes,
-                              false);
-    if (rc != TCX_OK) return rc;
-    cudaEventRecord(st.a_free[slot], st.comp);
-    cudaEventRecord(st.c_ready, st.comp);
+    cudaStreamWaitEvent(comp, st.a_ready, 0);
+    if (i >= kHostSlots) cudaStreamWaitEvent(comp, st.c_free[slot], 0);  // C slot downloaded
+    if (p.tensor) {
+      // the chunk's flag starts as B's (inf / NaN anywhere in B), then A's split adds to it
+      float* a_planes = reinterpret_cast<float*>(ws + p.off_ap[slot]);
+      int* flag = reinterpret_cast<int*>(ws + p.off_flag[slot]);
+      if (cudaError_t e = cudaMemcpyAsync(flag, b_flag, sizeof(int), cudaMemcpyDeviceToDevice, comp); e != cudaSuccess)
+        return fail(e, "matmul_host flag copy");
+      split_a(comp, a_dev, a_planes, 1, rows, k, p.kp, flag, sms);
+      if (int rc = launch_status("matmul_host split pre-pass")) return rc;
+      if (int rc = gemm_planes(comp, a_planes, b_planes, 1, 1, rows, n, k, p.kp, 1, one, c_dev, nullptr,
+                               TCX_ACT_NONE, flag, a_dev, b_dev, false, sms))
+        return rc;
+    } else {
+      const int rc = run_matmul(reinterpret_cast<tcx_stream_t>(comp), a_dev, b_dev, c_dev, rows, n, k, 1, nullptr,
+                                nullptr, nullptr, 0, nullptr, TCX_ACT_NONE, TCX_MATMUL_AUTO, ws + p.off_ws, p.ws_bytes,
+                                false);
+      if (rc != TCX_OK) return rc;
+    }
+    cudaEventRecord(st.a_free[slot], comp);
+    cudaEventRecord(st.c_ready, comp);
     cudaStreamWaitEvent(st.out, st.c_ready, 0);
     if (cudaError_t e = cudaMemcpyAsync(c_host + r0 * n, c_dev, static_cast<size_t>(rows * n) * 4,
                                         cudaMemcpyDeviceToHost, st.out);

@@ -285,7 +285,12 @@ int tcx_sm100_attention_softmax(tcx_stream_t stream, const float* scores, const 
                                 const int64_t* mask_strides, int32_t rank, float scale, int32_t causal);
 
 /* Scaled dot-product attention (kAttention, core/inference.cpp:123-160): out =
- * attention_softmax(Q·Kᵀ, mask, scale, causal) · V for q [batch..., queries, features],
+ * attention_softmax(Q·Kᵀ, mask, scale, causal) · V. Without a mask, with features and
+ * value_features multiples of 32 up to 128 and a 16-byte aligned output, one fused
+ * tcgen05 kernel computes it (scores and probabilities stay in TMEM; the workspace holds
+ * only the 3xTF32 split planes of q, k and v); otherwise the composite below runs. Inputs
+ * holding inf / NaN are computed by an IEEE row kernel (decided on the device).
+ * q [batch..., queries, features],
  * k [batch..., keys, features], v [batch..., keys, value_features], each batch-broadcast
  * to `batch_shape` through its batch strides (element units, 0 = broadcast, as
  * tcx_sm100_matmul). mask_strides: batch_rank + 2 strides of the mask over
@@ -295,7 +300,7 @@ int tcx_sm100_attention_softmax(tcx_stream_t stream, const float* scores, const 
  * matrices of each operand (the product of its own batch extents). */
 size_t tcx_sm100_attention_workspace_bytes(int64_t batches, int64_t queries, int64_t keys, int64_t features,
                                            int64_t value_features, int64_t q_batches, int64_t k_batches,
-                                           int64_t v_batches);
+                                           int64_t v_batches, int32_t mask_kind);
 int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, const float* v, const void* mask,
                         int32_t mask_kind, float* output, int64_t queries, int64_t keys, int64_t features,
                         int64_t value_features, const int64_t* batch_shape, const int64_t* q_batch_strides,

@@ -61,7 +61,7 @@ SIGNATURES = {
     "tcx_sm100_matmul_host": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz]),
     "tcx_sm100_attention_softmax": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _i64p, _i64p, _i64p, _i32, _f32,
                                                    _i32]),
-    "tcx_sm100_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "tcx_sm100_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32]),
     "tcx_sm100_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64p,
                                            _i64p, _i64p, _i64p, _i32, _i64p, _f32, _i32, _vp, _sz]),
     "tcx_sm100_copy_to_device": (ctypes.c_int, [_vp, _vp, _vp, _sz]),

@@ -338,7 +338,9 @@ class Executor {
     const Dim nb = numel(batch);
     const Dim qn = numel(Shape(q.begin(), q.end() - 2)), kn = numel(Shape(k.begin(), k.end() - 2)),
               vn = numel(Shape(v.begin(), v.end() - 2));
-    Scratch ws(tcx_sm100_attention_workspace_bytes(nb, queries, keys, features, v.back(), qn, kn, vn), scope_);
+    Scratch ws(tcx_sm100_attention_workspace_bytes(nb, queries, keys, features, v.back(), qn, kn, vn,
+                                                   static_cast<std::int32_t>(plan.mask_kind)),
+               scope_);
     if (!ws.status().ok()) return ws.status();
     const auto srank = scores.size();
     auto st = abi_status(

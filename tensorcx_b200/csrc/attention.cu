@@ -462,8 +462,10 @@ int tcx_sm100_attention_softmax(tcx_stream_t stream, const float* scores, const 
 
 size_t tcx_sm100_attention_workspace_bytes(int64_t batches, int64_t queries, int64_t keys, int64_t features,
                                            int64_t value_features, int64_t q_batches, int64_t k_batches,
-                                           int64_t v_batches) {
+                                           int64_t v_batches, int32_t mask_kind) {
   if (batches < 0 || queries < 0 || keys < 0 || features < 0 || value_features < 0) return 0;
+  if (flash_eligible(queries, keys, features, value_features, mask_kind, 0))
+    return flash_workspace_bytes(queries, keys, features, value_features, q_batches, k_batches, v_batches);
   const size_t scores = round_up(static_cast<size_t>(batches) * queries * keys * sizeof(float), 1024);
   const size_t g1 = tcx_sm100_matmul_workspace_bytes(queries, keys, features, q_batches, k_batches, TCX_MATMUL_AUTO);
   const size_t g2 = tcx_sm100_matmul_workspace_bytes(queries, value_features, keys, batches, v_batches,
@@ -510,7 +512,17 @@ int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, con
     if (k_batch_strides[a]) kn *= batch_shape[a];
     if (v_batch_strides[a]) vn *= batch_shape[a];
   }
-  const size_t need = tcx_sm100_attention_workspace_bytes(batches, queries, keys, features, value_features, qn, kn, vn);
+  if (flash_eligible(queries, keys, features, value_features, mask_kind, batch_rank) &&
+      reinterpret_cast<uintptr_t>(output) % 16 == 0) {
+    const size_t need = flash_workspace_bytes(queries, keys, features, value_features, qn, kn, vn);
+    if (!workspace || workspace_bytes < need) return invalid("attention workspace is missing or too small");
+    if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("attention workspace must be 1024-byte aligned");
+    return attention_fused(s, q, k, v, output, queries, keys, features, value_features, batches, batch_shape,
+                           q_batch_strides, k_batch_strides, v_batch_strides, batch_rank, scale, causal != 0,
+                           workspace, workspace_bytes);
+  }
+  const size_t need = tcx_sm100_attention_workspace_bytes(batches, queries, keys, features, value_features, qn, kn, vn,
+                                                          mask_kind);
   if (need && (!workspace || workspace_bytes < need)) return invalid("attention workspace is missing or too small");
   if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("attention workspace must be 1024-byte aligned");
   float* scores = static_cast<float*>(workspace);

@@ -98,4 +98,24 @@ int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* o
                const int64_t* rhs_batch_strides, int32_t batch_rank, bool rhs_kmajor, void* workspace,
                size_t workspace_bytes);
 
+// Split pre-pass of the 3xTF32 tensor path (gemm.cu): nb matrices [rows, k] -> K-major
+// hi/lo planes [2 * nb, rows, kp]; the column form transposes nb matrices [k, n] into
+// [2 * nb, n, kp]. Both raise *flag on inf / NaN. encode_planes_map builds the TMA map
+// (box {32, box_rows, 1}, 128-byte swizzle) over such planes; `map` is a CUtensorMap*.
+void split_rows_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t rows, int64_t k,
+                       int64_t kp, int* flag);
+void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t k, int64_t n,
+                       int64_t kp, int* flag);
+bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows);
+
+// Fused attention (flash.cu): eligibility, workspace and launch.
+bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t value_features, int mask_kind,
+                    int batch_rank);
+size_t flash_workspace_bytes(int64_t queries, int64_t keys, int64_t features, int64_t value_features,
+                             int64_t q_batches, int64_t k_batches, int64_t v_batches);
+int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, float* out, int64_t L,
+                    int64_t S, int64_t d, int64_t dv, int64_t batches, const int64_t* batch_shape,
+                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int32_t rank,
+                    float scale, int causal, void* workspace, size_t workspace_bytes);
+
 }  // namespace tcx

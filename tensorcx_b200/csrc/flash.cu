@@ -1,0 +1,551 @@
+// Fused attention on sm_100a: O = softmax(scale * Q·Kᵀ) · V in one persistent,
+// warp-specialized kernel, the scores and probabilities never leaving the SM.
+//
+// Operands are the 3xTF32 split planes (hi = rna_tf32(x), lo = rna_tf32(x - hi)) of
+// Q [L, D], K [S, D] and Vᵀ [Dv, S], all K-major, made by the matmul pre-pass. One work
+// item is 128 queries of one batch; key blocks of 128 are visited in order:
+//   warp 0      TMA producer: per key block, D/32 stages of {Q hi/lo 128x32, K hi/lo
+//               128x32} into a 2-deep ring, then four {Vᵀ hi/lo Dv x 32} into another.
+//   warp 1      MMA issuer: S = Q·Kᵀ into TMEM (three tcgen05.mma.kind::tf32 per 8-wide
+//               k step: lo·hi, hi·lo, hi·hi); after the softmax warps publish P, O += P·V
+//               with P read straight from TMEM as the A operand (P_hi overwrites S in
+//               place, P_lo beside it), again as three products.
+//   warps 2-5   softmax, one thread per query row (its TMEM lane): row maximum of the
+//               scaled, causally masked scores (log2 domain), p = 2^(t - m), the row sum,
+//               and the hi/lo split of p written back to TMEM with tcgen05.st. The
+//               running maximum is raised only when a block's maximum exceeds it by more
+//               than 8 (p stays <= 256), and only then is O (in TMEM) rescaled; at the end
+//               O / sum is stored to HBM.
+// TMEM (512 columns): S / P_hi [0, 128), P_lo [128, 256), O [256, 256 + Dv).
+// Every wait is bounded (4 s of %globaltimer), with the same abort / drain / TMEM
+// release discipline as the GEMM. No TMA multicast.
+//
+// Non-finite inputs (flagged by the split pre-pass) make the kernel exit at once; a
+// row-wise IEEE kernel queued behind it (idle otherwise) computes the result the way
+// the reference composite does (core/inference.cpp:123-160).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "rowmath.cuh"
+
+namespace tcx {
+namespace {
+
+using namespace ptx;
+
+constexpr int kFQ = 128;     // queries per work item (MMA M)
+constexpr int kFK = 128;     // keys per block (S tile N, P·V contraction per block)
+constexpr int kFC = 32;      // one 128-byte swizzle row of float32: the TMA box width
+constexpr int kQKStages = 2;
+constexpr int kVStages = 2;
+constexpr int kMaxDv = 128;
+constexpr int kQTile = kFQ * kFC * 4;        // 16 KB
+constexpr int kKTile = kFK * kFC * 4;        // 16 KB
+constexpr int kQKStage = 2 * kQTile + 2 * kKTile;  // 64 KB
+constexpr int kVTileMax = kMaxDv * kFC * 4;  // 16 KB at Dv = 128
+constexpr int kVStage = 2 * kVTileMax;       // 32 KB
+constexpr int kFlashSmem = kQKStages * kQKStage + kVStages * kVStage + 1024 + 256;
+constexpr int kFlashThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColP = 0, kColPlo = 128, kColO = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+constexpr int kMaxFlashBatchRank = 30;  // the attention ABI's own batch-rank limit
+
+struct FlashArgs {
+  int64_t L, S;
+  int32_t dp, dv;          // features (multiple of 32, <= 128) and value features (idem)
+  int64_t batches;
+  int32_t rank;            // merged batch rank; strides in matrix units (0 = broadcast)
+  int64_t shape[kMaxFlashBatchRank], qs[kMaxFlashBatchRank], ks[kMaxFlashBatchRank], vs[kMaxFlashBatchRank];
+  int32_t q_tiles, kv_blocks;
+  float scale_log2;        // scale * log2(e)
+  int32_t causal;
+  float* out;              // [batches, L, dv]
+  const int* nonfinite;
+  int* err;
+};
+
+__device__ __forceinline__ void batch_planes(const FlashArgs& a, int64_t b, int64_t& pq, int64_t& pk, int64_t& pv) {
+  pq = pk = pv = 0;
+  for (int d = a.rank - 1; d >= 0; --d) {
+    const int64_t i = b % a.shape[d];
+    b /= a.shape[d];
+    pq += i * a.qs[d];
+    pk += i * a.ks[d];
+    pv += i * a.vs[d];
+  }
+}
+
+// Work item w -> (batch, query tile); the longest causal items first.
+__device__ __forceinline__ void item_coords(const FlashArgs& a, int64_t w, int64_t& b, int& qt, int& nkb) {
+  qt = a.q_tiles - 1 - static_cast<int>(w / a.batches);
+  b = w % a.batches;
+  nkb = a.causal ? min(a.kv_blocks, qt + 1) : a.kv_blocks;
+}
+
+__global__ void __launch_bounds__(kFlashThreads, 1)
+flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v, const FlashArgs a) {
+  if (*a.nonfinite) return;  // the IEEE row kernel queued behind this one does the work
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qk_ring = smem;
+  uint8_t* v_ring = smem + kQKStages * kQKStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kVStages * kVStage);
+  uint64_t* qk_full = bars;                      // [kQKStages]
+  uint64_t* qk_empty = bars + kQKStages;         // [kQKStages]
+  uint64_t* v_full = bars + 2 * kQKStages;       // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;         // [kVStages]
+  uint64_t* s_full = v_empty + kVStages;         // S of the block is in TMEM
+  uint64_t* p_full = s_full + 1;                 // P (and the rescaled O) are in TMEM
+  uint64_t* pv_done = p_full + 1;                // P·V of the block has completed
+  uint64_t* o_free = pv_done + 1;                // the item's O has been read out
+  uint64_t* drain = o_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dchunks = a.dp / kFC;
+  const uint32_t v_tile = static_cast<uint32_t>(a.dv) * kFC * 4;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQKStages; ++s) { mbar_init(smem_u32(&qk_full[s]), 1); mbar_init(smem_u32(&qk_empty[s]), 1); }
+    for (int s = 0; s < kVStages; ++s) { mbar_init(smem_u32(&v_full[s]), 1); mbar_init(smem_u32(&v_empty[s]), 1); }
+    mbar_init(smem_u32(s_full), 1);
+    mbar_init(smem_u32(p_full), 4);
+    mbar_init(smem_u32(pv_done), 1);
+    mbar_init(smem_u32(o_free), 4);
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int64_t items = a.batches * a.q_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int64_t qk_n = 0, v_n = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        int64_t b; int qt, nkb;
+        item_coords(a, w, b, qt, nkb);
+        int64_t pq, pk, pv;
+        batch_planes(a, b, pq, pk, pv);
+        for (int j = 0; j < nkb && ok; ++j) {
+          for (int c = 0; c < dchunks; ++c, ++qk_n) {
+            const int s = static_cast<int>(qk_n % kQKStages);
+            const uint32_t ph = static_cast<uint32_t>((qk_n / kQKStages) & 1);
+            if (!wait_bounded(smem_u32(&qk_empty[s]), ph ^ 1u, abort_flag, a.err, 0x401)) { ok = false; break; }
+            uint8_t* st = qk_ring + s * kQKStage;
+            const uint32_t fb = smem_u32(&qk_full[s]);
+            mbar_expect_tx(fb, kQKStage);
+            tma_load_3d(smem_u32(st), &map_q, fb, c * kFC, qt * kFQ, static_cast<int>(2 * pq));
+            tma_load_3d(smem_u32(st + kQTile), &map_q, fb, c * kFC, qt * kFQ, static_cast<int>(2 * pq + 1));
+            tma_load_3d(smem_u32(st + 2 * kQTile), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk));
+            tma_load_3d(smem_u32(st + 2 * kQTile + kKTile), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk + 1));
+          }
+          for (int c = 0; c < kFK / kFC && ok; ++c, ++v_n) {
+            const int s = static_cast<int>(v_n % kVStages);
+            const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
+            if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x402)) { ok = false; break; }
+            uint8_t* st = v_ring + s * kVStage;
+            const uint32_t fb = smem_u32(&v_full[s]);
+            mbar_expect_tx(fb, 2 * v_tile);
+            tma_load_3d(smem_u32(st), &map_v, fb, j * kFK + c * kFC, 0, static_cast<int>(2 * pv));
+            tma_load_3d(smem_u32(st + kVTileMax), &map_v, fb, j * kFK + c * kFC, 0, static_cast<int>(2 * pv + 1));
+          }
+        }
+      }
+      if (!ok) {  // every fill this thread issued must land before the CTA exits
+        for (int s = 0; s < kQKStages; ++s) {
+          const int64_t fills = qk_n > s ? (qk_n - s + kQKStages - 1) / kQKStages : 0;
+          if (!fills) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(smem_u32(&qk_full[s]), static_cast<uint32_t>((fills - 1) & 1)))
+            if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4f1); break; }
+        }
+        for (int s = 0; s < kVStages; ++s) {
+          const int64_t fills = v_n > s ? (v_n - s + kVStages - 1) / kVStages : 0;
+          if (!fills) continue;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(smem_u32(&v_full[s]), static_cast<uint32_t>((fills - 1) & 1)))
+            if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4f2); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // -------------------------------------------------------------- MMA issuer
+      const uint32_t id_s = idesc_tf32(kFQ, kFK);
+      const uint32_t id_o = idesc_tf32(kFQ, a.dv);
+      const uint32_t d_s = tmem + kColP, d_o = tmem + kColO;
+      int64_t qk_n = 0, v_n = 0, blk = 0, local = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x, ++local) {
+        int64_t b; int qt, nkb;
+        item_coords(a, w, b, qt, nkb);
+        // O of the previous item must have been read out before it is overwritten
+        if (!wait_bounded(smem_u32(o_free), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x411)) break;
+        for (int j = 0; j < nkb && ok; ++j, ++blk) {
+          if (j > 0) {  // S overwrites P of the previous block: its P·V must be complete
+            if (!wait_bounded(smem_u32(pv_done), static_cast<uint32_t>((blk - 1) & 1), abort_flag, a.err, 0x412)) { ok = false; break; }
+          }
+          tc_fence_after();
+          for (int c = 0; c < dchunks; ++c, ++qk_n) {
+            const int s = static_cast<int>(qk_n % kQKStages);
+            const uint32_t ph = static_cast<uint32_t>((qk_n / kQKStages) & 1);
+            if (!wait_bounded(smem_u32(&qk_full[s]), ph, abort_flag, a.err, 0x413)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t q_hi = smem_u32(qk_ring + s * kQKStage), q_lo = q_hi + kQTile;
+            const uint32_t k_hi = q_hi + 2 * kQTile, k_lo = k_hi + kKTile;
+#pragma unroll
+            for (int kk = 0; kk < kFC / 8; ++kk) {
+              const uint32_t off = kk * 32;
+              const uint32_t acc = (c == 0 && kk == 0) ? 0u : 1u;
+              mma_tf32(d_s, smem_desc_sw128(q_lo + off), smem_desc_sw128(k_hi + off), id_s, acc);
+              mma_tf32(d_s, smem_desc_sw128(q_hi + off), smem_desc_sw128(k_lo + off), id_s, 1u);
+              mma_tf32(d_s, smem_desc_sw128(q_hi + off), smem_desc_sw128(k_hi + off), id_s, 1u);
+            }
+            mma_commit(smem_u32(&qk_empty[s]));
+          }
+          if (!ok) break;
+          mma_commit(smem_u32(s_full));
+          if (!wait_bounded(smem_u32(p_full), static_cast<uint32_t>(blk & 1), abort_flag, a.err, 0x414)) { ok = false; break; }
+          tc_fence_after();
+          for (int c = 0; c < kFK / kFC; ++c, ++v_n) {
+            const int s = static_cast<int>(v_n % kVStages);
+            const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
+            if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x415)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t v_hi = smem_u32(v_ring + s * kVStage), v_lo = v_hi + kVTileMax;
+#pragma unroll
+            for (int kk = 0; kk < kFC / 8; ++kk) {
+              const uint32_t off = kk * 32;
+              const uint32_t col = static_cast<uint32_t>(c * kFC + kk * 8);
+              const uint32_t acc = (j == 0 && c == 0 && kk == 0) ? 0u : 1u;
+              mma_tf32_ta(d_o, tmem + kColPlo + col, smem_desc_sw128(v_hi + off), id_o, acc);
+              mma_tf32_ta(d_o, tmem + kColP + col, smem_desc_sw128(v_lo + off), id_o, 1u);
+              mma_tf32_ta(d_o, tmem + kColP + col, smem_desc_sw128(v_hi + off), id_o, 1u);
+            }
+            mma_commit(smem_u32(&v_empty[s]));
+          }
+          if (!ok) break;
+          mma_commit(smem_u32(pv_done));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int row_in_tile = quarter * 32 + lane;
+    int64_t blk = 0;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+      int64_t b; int qt, nkb;
+      item_coords(a, w, b, qt, nkb);
+      const int64_t query = static_cast<int64_t>(qt) * kFQ + row_in_tile;
+      float m_use = -INFINITY, l = 0.0f;
+      bool aborted = false;
+      for (int j = 0; j < nkb; ++j, ++blk) {
+        if (!wait_bounded(smem_u32(s_full), static_cast<uint32_t>(blk & 1), abort_flag, a.err, 0x421)) { aborted = true; break; }
+        tc_fence_after();
+        const int64_t key0 = static_cast<int64_t>(j) * kFK;
+        // keys allowed for this row in this block: [0, lim)
+        int64_t lim = a.S - key0;
+        if (a.causal) lim = min(lim, query - key0 + 1);
+        lim = lim < 0 ? 0 : (lim > kFK ? kFK : lim);
+        // pass 1: the block's row maximum (log2 domain)
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int cc = 0; cc < kFK; cc += 32) {
+          uint32_t r[32];
+          TCX_LD32(r, tmem + lane_base + kColP + cc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float t = __fmul_rn(__uint_as_float(r[e]), a.scale_log2);
+            if (cc + e < lim) mx = fmaxf(mx, t);
+          }
+        }
+        // raise the running maximum only when p would exceed 2^8; rescale O then
+        const bool need = mx > m_use + 8.0f;
+        float alpha = 1.0f;
+        if (need) {
+          alpha = j == 0 ? 0.0f : exp2f(m_use - mx);
+          m_use = mx;
+        }
+        l = __fmul_rn(l, alpha);
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int cc = 0; cc < a.dv; cc += 32) {
+            uint32_t r[32];
+            TCX_LD32(r, tmem + lane_base + kColO + cc);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[e]), alpha));
+            TCX_ST32(tmem + lane_base + kColO + cc, r);
+          }
+        }
+        // pass 2: p = 2^(t - m), the row sum, P_hi over S and P_lo beside it
+#pragma unroll 1
+        for (int cc = 0; cc < kFK; cc += 32) {
+          uint32_t r[32], lo[32];
+          TCX_LD32(r, tmem + lane_base + kColP + cc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float t = __fmul_rn(__uint_as_float(r[e]), a.scale_log2);
+            float p = 0.0f;
+            if (cc + e < lim) {
+              asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(t, m_use)));
+            }
+            l = __fadd_rn(l, p);
+            const float hi = tf32_rna(p);
+            r[e] = __float_as_uint(hi);
+            lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
+          }
+          TCX_ST32(tmem + lane_base + kColP + cc, r);
+          TCX_ST32(tmem + lane_base + kColPlo + cc, lo);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(p_full));
+      }
+      if (aborted) break;
+      // the item's last P·V, then O / l to HBM
+      if (!wait_bounded(smem_u32(pv_done), static_cast<uint32_t>((blk - 1) & 1), abort_flag, a.err, 0x422)) break;
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      float* orow = a.out + (b * a.L + query) * a.dv;
+      const bool row_ok = query < a.L;
+#pragma unroll 1
+      for (int cc = 0; cc < a.dv; cc += 32) {
+        uint32_t r[32];
+        TCX_LD32(r, tmem + lane_base + kColO + cc);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v;
+            v.x = __fmul_rn(__uint_as_float(r[e + 0]), inv);
+            v.y = __fmul_rn(__uint_as_float(r[e + 1]), inv);
+            v.z = __fmul_rn(__uint_as_float(r[e + 2]), inv);
+            v.w = __fmul_rn(__uint_as_float(r[e + 3]), inv);
+            *reinterpret_cast<float4*>(orow + cc + e) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(o_free));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) {
+      mma_commit(smem_u32(drain));  // every issued MMA completes before TMEM is released
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(smem_u32(drain), 0))
+        if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4fe); break; }
+    }
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// IEEE fallback, used only when the pre-pass saw inf / NaN: one CTA per (batch, query)
+// row computes the scores as float32 dot products in feature order (as the reference
+// matmul), the masked softmax of core/inference.cpp / cpu_inference.cpp, and P·V summed
+// over keys in order, recomputing the dot products per pass instead of storing them.
+constexpr int kRowThreads = 128;
+
+__global__ void __launch_bounds__(kRowThreads)
+flash_rows_fallback(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                    FlashArgs a, int64_t d, float scale, const int* __restrict__ flag) {
+  if (!*flag) return;
+  __shared__ float qrow[kMaxDv];
+  __shared__ float p_chunk[kRowThreads];
+  __shared__ float red[64];
+  using B = rowmath::Block<kRowThreads>;
+  const int64_t rows = a.batches * a.L;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t b = row / a.L, query = row % a.L;
+    int64_t pq, pk, pv;
+    batch_planes(a, b, pq, pk, pv);
+    const float* qr = q + (pq * a.L + query) * d;
+    const float* kb = k + pk * a.S * d;
+    const float* vb = v + pv * a.S * a.dv;
+    __syncthreads();
+    for (int i = threadIdx.x; i < d; i += kRowThreads) qrow[i] = qr[i];
+    __syncthreads();
+    const int64_t keys = a.causal ? (query + 1 < a.S ? query + 1 : a.S) : a.S;
+    auto score = [&](int64_t key) {
+      float acc = 0.0f;
+      const float* kr = kb + key * d;
+      for (int64_t i = 0; i < d; ++i) acc = __fadd_rn(acc, __fmul_rn(qrow[i], kr[i]));
+      return __fmul_rn(acc, scale);
+    };
+    float mx = -INFINITY;
+    bool nan = false;
+    for (int64_t key = threadIdx.x; key < keys; key += kRowThreads) {
+      const float s = score(key);
+      nan |= s != s;
+      mx = fmaxf(mx, s);
+    }
+    if (nan) mx = __int_as_float(0x7fc00000);
+    mx = B::max(mx, red);
+    float* orow = a.out + row * a.dv;
+    if (mx == -INFINITY) {  // every score -inf: the reference's all-zero row
+      for (int c = threadIdx.x; c < a.dv; c += kRowThreads) orow[c] = 0.0f;
+      continue;
+    }
+    float total = 0.0f;
+    for (int64_t key = threadIdx.x; key < keys; key += kRowThreads) total = __fadd_rn(total, expf(score(key) - mx));
+    total = B::sum(total, red);
+    // P·V over every key, masked ones with p = 0 (as the reference's dense product, so a
+    // non-finite value under a masked key still propagates)
+    float acc[kMaxDv / kRowThreads + 1] = {0.0f};
+    for (int64_t k0 = 0; k0 < a.S; k0 += kRowThreads) {
+      __syncthreads();
+      const int64_t key = k0 + threadIdx.x;
+      p_chunk[threadIdx.x] = key < keys ? __fdiv_rn(expf(score(key) - mx), total) : 0.0f;
+      __syncthreads();
+      const int64_t n = a.S - k0 < kRowThreads ? a.S - k0 : kRowThreads;
+      for (int c = threadIdx.x, slot = 0; c < a.dv; c += kRowThreads, ++slot)
+        for (int64_t i = 0; i < n; ++i) acc[slot] = __fadd_rn(acc[slot], __fmul_rn(p_chunk[i], vb[(k0 + i) * a.dv + c]));
+    }
+    for (int c = threadIdx.x, slot = 0; c < a.dv; c += kRowThreads, ++slot) orow[c] = acc[slot];
+  }
+}
+
+size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
+
+struct FlashLayout {
+  size_t off_flag, off_q, off_k, off_v, total;
+  int64_t sp;
+};
+
+FlashLayout flash_layout(int64_t L, int64_t S, int64_t d, int64_t dv, int64_t nq, int64_t nk, int64_t nv) {
+  FlashLayout f;
+  f.sp = (S + kFC - 1) / kFC * kFC;
+  f.off_flag = 0;
+  f.off_q = 1024;
+  f.off_k = round_up(f.off_q + static_cast<size_t>(2 * nq * L * d) * 4, 1024);
+  f.off_v = round_up(f.off_k + static_cast<size_t>(2 * nk * S * d) * 4, 1024);
+  f.total = round_up(f.off_v + static_cast<size_t>(2 * nv * dv * f.sp) * 4, 1024);
+  return f;
+}
+
+}  // namespace
+
+bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t value_features, int mask_kind,
+                    int batch_rank) {
+  return mask_kind == 0 && queries > 0 && keys > 0 && features % kFC == 0 && features <= 128 &&
+         value_features % kFC == 0 && value_features > 0 && value_features <= kMaxDv &&
+         batch_rank <= kMaxFlashBatchRank && queries <= INT32_MAX / 2 && keys <= INT32_MAX / 2;
+}
+
+size_t flash_workspace_bytes(int64_t queries, int64_t keys, int64_t features, int64_t value_features,
+                             int64_t q_batches, int64_t k_batches, int64_t v_batches) {
+  return flash_layout(queries, keys, features, value_features, q_batches, k_batches, v_batches).total;
+}
+
+int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, float* out, int64_t L,
+                    int64_t S, int64_t d, int64_t dv, int64_t batches, const int64_t* batch_shape,
+                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int32_t rank,
+                    float scale, int causal, void* workspace, size_t workspace_bytes) {
+  FlashArgs fa{};
+  fa.L = L; fa.S = S; fa.dp = static_cast<int32_t>(d); fa.dv = static_cast<int32_t>(dv);
+  fa.batches = batches;
+  // batch strides in matrix units; collapse extent-1 axes
+  int64_t nq = 1, nk = 1, nv = 1;
+  fa.rank = 0;
+  for (int i = 0; i < rank; ++i) {
+    if (batch_shape[i] == 1) continue;
+    if (fa.rank == kMaxFlashBatchRank) return invalid("attention batch rank exceeds 30");
+    fa.shape[fa.rank] = batch_shape[i];
+    fa.qs[fa.rank] = q_strides[i] / (L * d);
+    fa.ks[fa.rank] = k_strides[i] / (S * d);
+    fa.vs[fa.rank] = v_strides[i] / (S * dv);
+    if (q_strides[i]) nq *= batch_shape[i];
+    if (k_strides[i]) nk *= batch_shape[i];
+    if (v_strides[i]) nv *= batch_shape[i];
+    ++fa.rank;
+  }
+  const FlashLayout lay = flash_layout(L, S, d, dv, nq, nk, nv);
+  if (!workspace || workspace_bytes < lay.total) return invalid("attention workspace is missing or too small");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* flag = reinterpret_cast<int*>(ws + lay.off_flag);
+  float* wq = reinterpret_cast<float*>(ws + lay.off_q);
+  float* wk = reinterpret_cast<float*>(ws + lay.off_k);
+  float* wv = reinterpret_cast<float*>(ws + lay.off_v);
+  if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("attention flag reset");
+  // K-major split planes: Q [2nq][L][d], K [2nk][S][d] (rows already K-major), Vᵀ [2nv][dv][Sp]
+  split_rows_planes(s, q, wq, nq, L, d, d, flag);
+  split_rows_planes(s, k, wk, nk, S, d, d, flag);
+  split_cols_planes(s, v, wv, nv, S, dv, lay.sp, flag);
+  if (int st = launch_status("attention split pre-pass")) return st;
+
+  alignas(64) CUtensorMap map_q, map_k, map_v;
+  if (!encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) || !encode_planes_map(&map_k, wk, 2 * nk, S, d, kFK) ||
+      !encode_planes_map(&map_v, wv, 2 * nv, dv, lay.sp, static_cast<int>(dv)))
+    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(flash_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
+        cudaSuccess)
+      return launch_status("flash smem attribute");
+    attr_done[dev] = true;
+  }
+  fa.q_tiles = static_cast<int32_t>(ceil_div(L, kFQ));
+  fa.kv_blocks = static_cast<int32_t>(ceil_div(S, kFK));
+  fa.scale_log2 = scale * kLog2e;
+  fa.causal = causal;
+  fa.out = out;
+  fa.nonfinite = flag;
+  fa.err = device_error_word();
+  const int64_t items = batches * fa.q_tiles;
+  const int sms = sm_count();
+  {
+    TimedLaunch timer("flash_tf32x3", s);
+    flash_tf32x3_kernel<<<static_cast<int>(std::min<int64_t>(items, sms)), kFlashThreads, kFlashSmem, s>>>(
+        map_q, map_k, map_v, fa);
+  }
+  if (int st = launch_status("fused attention")) return st;
+  {
+    TimedLaunch timer("flash_rows_fallback", s);
+    const int grid = static_cast<int>(std::min<int64_t>(batches * L, 8LL * sms));
+    flash_rows_fallback<<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
+  }
+  return launch_status("attention fallback");
+}
+
+}  // namespace tcx

@@ -34,6 +34,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace tcx {
 namespace {
@@ -56,100 +57,8 @@ __device__ __forceinline__ int64_t batch_off(int64_t b, const int64_t* shape, co
   return off;
 }
 
-// ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legal wait
-
-// Bounded wait: false when the CTA is aborting or the limit passed (then it records
-// `site` in the device error word and raises the CTA abort flag).
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                             int* err, int site) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag) return false;
-    if (globaltimer() - start > kWaitLimitNs) {
-      *abort_flag = 1;
-      record_device_error(err, site);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, 128-byte-swizzled operand tile: rows of 128 bytes, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);        // start address
-  d |= static_cast<uint64_t>(1) << 16;                       // leading byte offset (unused)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;               // stride byte offset
-  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version
-  d |= static_cast<uint64_t>(2) << 61;                       // SWIZZLE_128B
-  return d;
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-
-#define TCX_LD32(r, taddr)                                                                          \
-  asm volatile(                                                                                     \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"               \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),               \
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),               \
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                \
-      : "r"(taddr))
+// PTX helpers (mbarriers, bounded waits, TMA, tcgen05): ptx.cuh
+using namespace ptx;
 
 __device__ __forceinline__ float silu_e(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
 __device__ __forceinline__ float relu_e(float v) {
@@ -164,11 +73,6 @@ __device__ __forceinline__ float epilogue_op(float v, const float* bias, int64_t
 }
 
 // ------------------------------------------------------------------- pre-pass
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 
 __device__ __forceinline__ void split_one(float x, float& hi, float& lo, bool& bad) {
   bad |= !isfinite(x);
@@ -1013,5 +917,19 @@ int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* o
   return run_matmul(reinterpret_cast<tcx_stream_t>(stream), lhs, rhs, output, m, n, k, batches, batch_shape,
                     lhs_batch_strides, rhs_batch_strides, batch_rank, nullptr, TCX_ACT_NONE, TCX_MATMUL_AUTO,
                     workspace, workspace_bytes, rhs_kmajor);
+}
+}  // namespace tcx
+
+namespace tcx {
+void split_rows_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t rows, int64_t k,
+                       int64_t kp, int* flag) {
+  split_a(s, x, planes, nb, rows, k, kp, flag, sm_count());
+}
+void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t k, int64_t n,
+                       int64_t kp, int* flag) {
+  split_b(s, x, planes, nb, n, k, kp, flag, false, sm_count());
+}
+bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows) {
+  return make_map(static_cast<CUtensorMap*>(map), base, planes, rows, kp, box_rows);
 }
 }  // namespace tcx

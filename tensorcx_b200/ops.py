@@ -520,8 +520,9 @@ def scaled_dot_product_attention(query: torch.Tensor, key: torch.Tensor, value: 
     """tensor.py:924-946 and the kAttention composite (core/inference.cpp:123-160):
     softmax(scale * query·keyᵀ + mask) · value over broadcast batch dimensions; True
     mask entries are allowed, causal is upper-left, the default scale 1/sqrt(features).
-    Runs as one C-ABI call: two tcgen05 GEMMs (keys read K-major, no transpose copy)
-    around the masked softmax, scores kept in a stream-ordered workspace."""
+    Runs as one C-ABI call: without a mask (and with feature sizes that are multiples of
+    32 up to 128) one fused tcgen05 kernel, otherwise two tcgen05 GEMMs (keys read
+    K-major, no transpose copy) around the masked softmax."""
     tensors = (query, key, value) + (() if attn_mask is None else (attn_mask,))
     for t in tensors:
         if not isinstance(t, torch.Tensor):
@@ -582,7 +583,7 @@ def scaled_dot_product_attention(query: torch.Tensor, key: torch.Tensor, value: 
     nb = plan.numel(batch)
     ws_bytes = lib().tcx_sm100_attention_workspace_bytes(
         nb, queries, keys, features, value.shape[-1], plan.numel(list(query.shape[:-2])),
-        plan.numel(list(key.shape[:-2])), plan.numel(list(value.shape[:-2])))
+        plan.numel(list(key.shape[:-2])), plan.numel(list(value.shape[:-2])), kind)
     keep, ws = _workspace(ws_bytes, query.device)
     check(lib().tcx_sm100_attention(_stream(), _ptr(query), _ptr(key), _ptr(value), _ptr(attn_mask), kind,
                                     _ptr(out), queries, keys, features, value.shape[-1], i64_array(batch),

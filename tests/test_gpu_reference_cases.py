@@ -508,3 +508,37 @@ def test_attention_softmax_primitive(tcx, oracle, shape, sshape, mshape, kind, c
     want = oracle.attention_softmax(scores, shape, mask, causal, 0.7)
     assert got.shape == want.shape
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-7, equal_nan=True)
+
+
+@pytest.mark.parametrize("lq,lk,d,dv", [(128, 128, 32, 32), (200, 300, 64, 64), (1, 5, 32, 64), (300, 77, 96, 32),
+                                        (256, 1000, 128, 128), (130, 2049, 64, 96), (2048, 2048, 128, 128)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_attention(tcx, oracle, lq, lk, d, dv, causal):
+    """No mask and feature sizes that are multiples of 32: the fused tcgen05 kernel
+    (scores and probabilities in TMEM), against the restated reference composite."""
+    q, k, v = gauss((2, lq, d), 1), gauss((2, lk, d), 2), gauss((2, lk, dv), 3)
+    got = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=causal))
+    if lq * lk > 500_000:  # the CPU composite is slow here: check the first rows only
+        attn_check(got[:, :64], oracle.attention(q[:, :64], k, v, None, causal))
+    else:
+        attn_check(got, oracle.attention(q, k, v, None, causal))
+
+
+@pytest.mark.parametrize("scale", [None, 0.0, -0.3, 3.0])
+def test_fused_attention_broadcast_and_scale(tcx, oracle, scale):
+    q, k, v = gauss((3, 2, 100, 64), 4), gauss((1, 2, 260, 64), 5), gauss((3, 1, 260, 32), 6)
+    got = host(tcx.attention(dev(q), dev(k), dev(v), scale=scale, is_causal=True))
+    attn_check(got, oracle.attention(q, k, v, None, True, scale))
+
+
+@pytest.mark.parametrize("where", ["q", "k", "v"])
+@pytest.mark.parametrize("value", [np.inf, -np.inf, np.nan])
+def test_fused_attention_nonfinite_inputs(tcx, oracle, where, value):
+    """inf / NaN anywhere sends the work to the IEEE row kernel, which follows the
+    reference composite (masked keys included in P·V, as its dense product does)."""
+    q, k, v = gauss((1, 70, 32), 7), gauss((1, 90, 32), 8), gauss((1, 90, 32), 9)
+    {"q": q, "k": k, "v": v}[where][0, 3, 5] = value
+    for causal in (False, True):
+        got = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=causal))
+        with np.errstate(all="ignore"):
+            attn_check(got, oracle.attention(q, k, v, None, causal))

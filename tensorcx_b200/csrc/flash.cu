@@ -3,20 +3,25 @@
 //
 // Operands are the 3xTF32 split planes (hi = rna_tf32(x), lo = rna_tf32(x - hi)) of
 // Q [L, D], K [S, D] and Vᵀ [Dv, S], all K-major, made by the matmul pre-pass. One work
-// item is 128 queries of one batch; key blocks of 128 are visited in order:
-//   warp 0      TMA producer: per key block, D/32 stages of {Q hi/lo 128x32, K hi/lo
-//               128x32} into a 2-deep ring, then four {Vᵀ hi/lo Dv x 32} into another.
-//   warp 1      MMA issuer: S = Q·Kᵀ into TMEM (three tcgen05.mma.kind::tf32 per 8-wide
-//               k step: lo·hi, hi·lo, hi·hi); after the softmax warps publish P, O += P·V
-//               with P read straight from TMEM as the A operand (P_hi overwrites S in
-//               place, P_lo beside it), again as three products.
+// item is 128 queries of one batch, whose Q hi/lo stays in shared memory; key blocks of
+// 64 are visited in order:
+//   warp 0      TMA producer: the item's Q (D/32 pairs of 128x32 hi/lo tiles), then per
+//               key block D/32 K hi/lo chunks (64x32) into a 2-deep ring and two Vᵀ
+//               hi/lo chunks (Dv x 32) into another.
+//   warp 1      MMA issuer, one block ahead of the softmax: S_j = Q·K_jᵀ into TMEM buffer
+//               j % 3 (three tcgen05.mma.kind::tf32 per 8-wide k step: lo·hi, hi·lo,
+//               hi·hi), then O += P_{j-1}·V_{j-1} with P read straight from TMEM as the A
+//               operand, again as three products. The softmax of block j overlaps the
+//               MMAs of block j+1.
 //   warps 2-5   softmax, one thread per query row (its TMEM lane): row maximum of the
 //               scaled, causally masked scores (log2 domain), p = 2^(t - m), the row sum,
-//               and the hi/lo split of p written back to TMEM with tcgen05.st. The
+//               and the hi/lo split of p written back over S with tcgen05.st. The
 //               running maximum is raised only when a block's maximum exceeds it by more
 //               than 8 (p stays <= 256), and only then is O (in TMEM) rescaled; at the end
 //               O / sum is stored to HBM.
-// TMEM (512 columns): S / P_hi [0, 128), P_lo [128, 256), O [256, 256 + Dv).
+// TMEM (512 columns): buffer b in {0, 1, 2}: S / P_hi [128 b, 128 b + 64), P_lo
+// [128 b + 64, 128 b + 128); O [384, 384 + Dv). Three buffers let S_{j+2} start while
+// P_{j-1} is still being read, so the MMA issuer never drains the tensor pipe.
 // Every wait is bounded (4 s of %globaltimer), with the same abort / drain / TMEM
 // release discipline as the GEMM. No TMA multicast.
 //
@@ -40,20 +45,23 @@ namespace {
 using namespace ptx;
 
 constexpr int kFQ = 128;     // queries per work item (MMA M)
-constexpr int kFK = 128;     // keys per block (S tile N, P·V contraction per block)
+constexpr int kFK = 64;      // keys per block (S tile N, P·V contraction per block)
 constexpr int kFC = 32;      // one 128-byte swizzle row of float32: the TMA box width
-constexpr int kQKStages = 2;
+constexpr int kKStages = 2;
 constexpr int kVStages = 2;
+constexpr int kMaxD = 128;
 constexpr int kMaxDv = 128;
-constexpr int kQTile = kFQ * kFC * 4;        // 16 KB
-constexpr int kKTile = kFK * kFC * 4;        // 16 KB
-constexpr int kQKStage = 2 * kQTile + 2 * kKTile;  // 64 KB
+constexpr int kQTile = kFQ * kFC * 4;        // 16 KB: one 32-wide chunk of Q, hi or lo
+constexpr int kQBytes = 2 * (kMaxD / kFC) * kQTile;  // 128 KB: all of Q hi/lo
+constexpr int kKTile = kFK * kFC * 4;        // 8 KB
+constexpr int kKStage = 2 * kKTile;          // 16 KB
 constexpr int kVTileMax = kMaxDv * kFC * 4;  // 16 KB at Dv = 128
 constexpr int kVStage = 2 * kVTileMax;       // 32 KB
-constexpr int kFlashSmem = kQKStages * kQKStage + kVStages * kVStage + 1024 + 256;
+constexpr int kFlashSmem = kQBytes + kKStages * kKStage + kVStages * kVStage + 1024 + 256;
 constexpr int kFlashThreads = 192;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColP = 0, kColPlo = 128, kColO = 256;
+constexpr int kSBufs = 3;
+constexpr uint32_t kColO = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
@@ -88,11 +96,22 @@ __device__ __forceinline__ void batch_planes(const FlashArgs& a, int64_t b, int6
   }
 }
 
+// Item of round r for this CTA: rounds alternate direction over the grid (a snake), so
+// with items ordered longest first each CTA's total stays near the mean (causal items
+// shrink with the query tile: round-robin leaves the busiest CTA 1.3x the mean on a
+// 32 x 16-tile grid, the snake 1.05x). -1 when this CTA has no item in round r.
+__device__ __forceinline__ int64_t snake_item(int64_t r, int64_t items) {
+  const int64_t g = gridDim.x;
+  const int64_t w = r * g + ((r & 1) ? g - 1 - blockIdx.x : blockIdx.x);
+  return w < items ? w : -1;
+}
+
 // Work item w -> (batch, query tile); the longest causal items first.
 __device__ __forceinline__ void item_coords(const FlashArgs& a, int64_t w, int64_t& b, int& qt, int& nkb) {
   qt = a.q_tiles - 1 - static_cast<int>(w / a.batches);
   b = w % a.batches;
-  nkb = a.causal ? min(a.kv_blocks, qt + 1) : a.kv_blocks;
+  // causal: keys up to the tile's last query, (qt + 1) * 128 - 1
+  nkb = a.causal ? min(a.kv_blocks, (qt + 1) * (kFQ / kFK)) : a.kv_blocks;
 }
 
 __global__ void __launch_bounds__(kFlashThreads, 1)
@@ -101,17 +120,20 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   if (*a.nonfinite) return;  // the IEEE row kernel queued behind this one does the work
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qk_ring = smem;
-  uint8_t* v_ring = smem + kQKStages * kQKStage;
+  uint8_t* q_res = smem;                                   // chunk c: hi at 2c, lo at 2c + 1
+  uint8_t* k_ring = smem + kQBytes;
+  uint8_t* v_ring = k_ring + kKStages * kKStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kVStages * kVStage);
-  uint64_t* qk_full = bars;                      // [kQKStages]
-  uint64_t* qk_empty = bars + kQKStages;         // [kQKStages]
-  uint64_t* v_full = bars + 2 * kQKStages;       // [kVStages]
+  uint64_t* k_full = bars;                       // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;         // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;         // [kVStages]
   uint64_t* v_empty = v_full + kVStages;         // [kVStages]
-  uint64_t* s_full = v_empty + kVStages;         // S of the block is in TMEM
-  uint64_t* p_full = s_full + 1;                 // P (and the rescaled O) are in TMEM
-  uint64_t* pv_done = p_full + 1;                // P·V of the block has completed
-  uint64_t* o_free = pv_done + 1;                // the item's O has been read out
+  uint64_t* s_full = v_empty + kVStages;         // [kSBufs] S of the block is in its TMEM buffer
+  uint64_t* p_full = s_full + kSBufs;            // [kSBufs] P (and the rescaled O) are in TMEM
+  uint64_t* pv_done = p_full + kSBufs;           // [kSBufs] P·V of the buffer's block has completed
+  uint64_t* q_full = pv_done + kSBufs;           // the item's Q has landed
+  uint64_t* q_empty = q_full + 1;                // the item's last S has read Q
+  uint64_t* o_free = q_empty + 1;                // the item's O has been read out
   uint64_t* drain = o_free + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -120,11 +142,15 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   const int dchunks = a.dp / kFC;
   const uint32_t v_tile = static_cast<uint32_t>(a.dv) * kFC * 4;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kQKStages; ++s) { mbar_init(smem_u32(&qk_full[s]), 1); mbar_init(smem_u32(&qk_empty[s]), 1); }
+    for (int s = 0; s < kKStages; ++s) { mbar_init(smem_u32(&k_full[s]), 1); mbar_init(smem_u32(&k_empty[s]), 1); }
     for (int s = 0; s < kVStages; ++s) { mbar_init(smem_u32(&v_full[s]), 1); mbar_init(smem_u32(&v_empty[s]), 1); }
-    mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(p_full), 4);
-    mbar_init(smem_u32(pv_done), 1);
+    for (int b = 0; b < kSBufs; ++b) {
+      mbar_init(smem_u32(&s_full[b]), 1);
+      mbar_init(smem_u32(&p_full[b]), 4);
+      mbar_init(smem_u32(&pv_done[b]), 1);
+    }
+    mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_empty), 1);
     mbar_init(smem_u32(o_free), 4);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -146,53 +172,73 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer
-      int64_t qk_n = 0, v_n = 0;
+      int64_t k_n = 0, v_n = 0, local = 0;
       bool ok = true;
-      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      for (int64_t r = 0; r * gridDim.x < items && ok; ++r) {
+        const int64_t w = snake_item(r, items);
+        if (w < 0) continue;
         int64_t b; int qt, nkb;
         item_coords(a, w, b, qt, nkb);
         int64_t pq, pk, pv;
         batch_planes(a, b, pq, pk, pv);
-        for (int j = 0; j < nkb && ok; ++j) {
-          for (int c = 0; c < dchunks; ++c, ++qk_n) {
-            const int s = static_cast<int>(qk_n % kQKStages);
-            const uint32_t ph = static_cast<uint32_t>((qk_n / kQKStages) & 1);
-            if (!wait_bounded(smem_u32(&qk_empty[s]), ph ^ 1u, abort_flag, a.err, 0x401)) { ok = false; break; }
-            uint8_t* st = qk_ring + s * kQKStage;
-            const uint32_t fb = smem_u32(&qk_full[s]);
-            mbar_expect_tx(fb, kQKStage);
-            tma_load_3d(smem_u32(st), &map_q, fb, c * kFC, qt * kFQ, static_cast<int>(2 * pq));
-            tma_load_3d(smem_u32(st + kQTile), &map_q, fb, c * kFC, qt * kFQ, static_cast<int>(2 * pq + 1));
-            tma_load_3d(smem_u32(st + 2 * kQTile), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk));
-            tma_load_3d(smem_u32(st + 2 * kQTile + kKTile), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk + 1));
+        // Q of this item, once the previous item's S products have read the old one
+        if (!wait_bounded(smem_u32(q_empty), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x400)) break;
+        ++local;
+        {
+          const uint32_t fb = smem_u32(q_full);
+          mbar_expect_tx(fb, static_cast<uint32_t>(2 * dchunks * kQTile));
+          for (int c = 0; c < dchunks; ++c) {
+            tma_load_3d(smem_u32(q_res + (2 * c) * kQTile), &map_q, fb, c * kFC, qt * kFQ, static_cast<int>(2 * pq));
+            tma_load_3d(smem_u32(q_res + (2 * c + 1) * kQTile), &map_q, fb, c * kFC, qt * kFQ,
+                        static_cast<int>(2 * pq + 1));
           }
-          for (int c = 0; c < kFK / kFC && ok; ++c, ++v_n) {
+        }
+        // the MMA issuer's order: K_j, then V_{j-1} (its P·V follows S_j), V_last at the end
+        auto load_k = [&](int j) {
+          for (int c = 0; c < dchunks; ++c, ++k_n) {
+            const int s = static_cast<int>(k_n % kKStages);
+            const uint32_t ph = static_cast<uint32_t>((k_n / kKStages) & 1);
+            if (!wait_bounded(smem_u32(&k_empty[s]), ph ^ 1u, abort_flag, a.err, 0x401)) return false;
+            uint8_t* st = k_ring + s * kKStage;
+            const uint32_t fb = smem_u32(&k_full[s]);
+            mbar_expect_tx(fb, kKStage);
+            tma_load_3d(smem_u32(st), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk));
+            tma_load_3d(smem_u32(st + kKTile), &map_k, fb, c * kFC, j * kFK, static_cast<int>(2 * pk + 1));
+          }
+          return true;
+        };
+        auto load_v = [&](int j) {
+          for (int c = 0; c < kFK / kFC; ++c, ++v_n) {
             const int s = static_cast<int>(v_n % kVStages);
             const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
-            if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x402)) { ok = false; break; }
+            if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x402)) return false;
             uint8_t* st = v_ring + s * kVStage;
             const uint32_t fb = smem_u32(&v_full[s]);
             mbar_expect_tx(fb, 2 * v_tile);
             tma_load_3d(smem_u32(st), &map_v, fb, j * kFK + c * kFC, 0, static_cast<int>(2 * pv));
             tma_load_3d(smem_u32(st + kVTileMax), &map_v, fb, j * kFK + c * kFC, 0, static_cast<int>(2 * pv + 1));
           }
+          return true;
+        };
+        for (int j = 0; j < nkb && ok; ++j) {
+          ok = load_k(j);
+          if (ok && j >= 1) ok = load_v(j - 1);
         }
+        if (ok && nkb >= 1) ok = load_v(nkb - 1);
       }
-      if (!ok) {  // every fill this thread issued must land before the CTA exits
-        for (int s = 0; s < kQKStages; ++s) {
-          const int64_t fills = qk_n > s ? (qk_n - s + kQKStages - 1) / kQKStages : 0;
-          if (!fills) continue;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(smem_u32(&qk_full[s]), static_cast<uint32_t>((fills - 1) & 1)))
-            if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4f1); break; }
-        }
-        for (int s = 0; s < kVStages; ++s) {
-          const int64_t fills = v_n > s ? (v_n - s + kVStages - 1) / kVStages : 0;
-          if (!fills) continue;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(smem_u32(&v_full[s]), static_cast<uint32_t>((fills - 1) & 1)))
-            if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4f2); break; }
-        }
+      if (!ok || *abort_flag) {  // every fill this thread issued must land before the CTA exits
+        auto settle = [&](uint64_t* full, int stages, int64_t n, int site) {
+          for (int s = 0; s < stages; ++s) {
+            const int64_t fills = n > s ? (n - s + stages - 1) / stages : 0;
+            if (!fills) continue;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(smem_u32(&full[s]), static_cast<uint32_t>((fills - 1) & 1)))
+              if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, site); break; }
+          }
+        };
+        settle(k_full, kKStages, k_n, 0x4f1);
+        settle(v_full, kVStages, v_n, 0x4f2);
+        settle(q_full, 1, local, 0x4f3);
       }
     }
   } else if (warp == 1) {
@@ -200,60 +246,82 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       // -------------------------------------------------------------- MMA issuer
       const uint32_t id_s = idesc_tf32(kFQ, kFK);
       const uint32_t id_o = idesc_tf32(kFQ, a.dv);
-      const uint32_t d_s = tmem + kColP, d_o = tmem + kColO;
-      int64_t qk_n = 0, v_n = 0, blk = 0, local = 0;
+      const uint32_t d_o = tmem + kColO;
+      int64_t k_n = 0, v_n = 0, g = 0, local = 0;  // g: blocks issued by this CTA so far
       bool ok = true;
-      for (int64_t w = blockIdx.x; w < items && ok; w += gridDim.x, ++local) {
+      // O += P·V of global block `gb` (buffer gb % 3); `first` starts the accumulator
+      int64_t item = 0;
+      auto issue_pv = [&](int64_t gb, bool first) -> bool {
+        const int buf = static_cast<int>(gb % kSBufs);
+        if (!wait_bounded(smem_u32(&p_full[buf]), static_cast<uint32_t>((gb / kSBufs) & 1), abort_flag, a.err, 0x414))
+          return false;
+        // the item's first P·V overwrites O: the previous item's O must have been read out
+        if (first && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x411))
+          return false;
+        tc_fence_after();
+        const uint32_t p_hi = tmem + static_cast<uint32_t>(buf * 128), p_lo = p_hi + kFK;
+        for (int c = 0; c < kFK / kFC; ++c, ++v_n) {
+          const int s = static_cast<int>(v_n % kVStages);
+          const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
+          if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x415)) return false;
+          tc_fence_after();
+          // descriptors built once per chunk; a k step adds 32 bytes (2 in the >> 4 field)
+          const uint64_t dv_hi = smem_desc_sw128(smem_u32(v_ring + s * kVStage));
+          const uint64_t dv_lo = smem_desc_sw128(smem_u32(v_ring + s * kVStage + kVTileMax));
+#pragma unroll
+          for (int kk = 0; kk < kFC / 8; ++kk) {
+            const uint32_t col = static_cast<uint32_t>(c * kFC + kk * 8);
+            const uint32_t acc = (first && c == 0 && kk == 0) ? 0u : 1u;
+            mma_tf32_ta(d_o, p_lo + col, dv_hi + 2 * kk, id_o, acc);
+            mma_tf32_ta(d_o, p_hi + col, dv_lo + 2 * kk, id_o, 1u);
+            mma_tf32_ta(d_o, p_hi + col, dv_hi + 2 * kk, id_o, 1u);
+          }
+          mma_commit(smem_u32(&v_empty[s]));
+        }
+        mma_commit(smem_u32(&pv_done[buf]));
+        return true;
+      };
+      for (int64_t r = 0; r * gridDim.x < items && ok; ++r) {
+        const int64_t w = snake_item(r, items);
+        if (w < 0) continue;
         int64_t b; int qt, nkb;
         item_coords(a, w, b, qt, nkb);
-        // O of the previous item must have been read out before it is overwritten
-        if (!wait_bounded(smem_u32(o_free), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x411)) break;
-        for (int j = 0; j < nkb && ok; ++j, ++blk) {
-          if (j > 0) {  // S overwrites P of the previous block: its P·V must be complete
-            if (!wait_bounded(smem_u32(pv_done), static_cast<uint32_t>((blk - 1) & 1), abort_flag, a.err, 0x412)) { ok = false; break; }
-          }
-          tc_fence_after();
-          for (int c = 0; c < dchunks; ++c, ++qk_n) {
-            const int s = static_cast<int>(qk_n % kQKStages);
-            const uint32_t ph = static_cast<uint32_t>((qk_n / kQKStages) & 1);
-            if (!wait_bounded(smem_u32(&qk_full[s]), ph, abort_flag, a.err, 0x413)) { ok = false; break; }
+        if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x410)) break;
+        item = local++;
+        tc_fence_after();
+        const int64_t g0 = g;
+        for (int j = 0; j < nkb && ok; ++j, ++g) {
+          const int buf = static_cast<int>(g % kSBufs);
+          if (g >= kSBufs) {  // S overwrites the buffer's previous P: that block's P·V must be done
+            if (!wait_bounded(smem_u32(&pv_done[buf]), static_cast<uint32_t>(((g - kSBufs) / kSBufs) & 1), abort_flag, a.err,
+                              0x412)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t q_hi = smem_u32(qk_ring + s * kQKStage), q_lo = q_hi + kQTile;
-            const uint32_t k_hi = q_hi + 2 * kQTile, k_lo = k_hi + kKTile;
+          }
+          const uint32_t d_s = tmem + static_cast<uint32_t>(buf * 128);
+          for (int c = 0; c < dchunks; ++c, ++k_n) {
+            const int s = static_cast<int>(k_n % kKStages);
+            const uint32_t ph = static_cast<uint32_t>((k_n / kKStages) & 1);
+            if (!wait_bounded(smem_u32(&k_full[s]), ph, abort_flag, a.err, 0x413)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t dq_hi = smem_desc_sw128(smem_u32(q_res + (2 * c) * kQTile));
+            const uint64_t dq_lo = smem_desc_sw128(smem_u32(q_res + (2 * c + 1) * kQTile));
+            const uint64_t dk_hi = smem_desc_sw128(smem_u32(k_ring + s * kKStage));
+            const uint64_t dk_lo = smem_desc_sw128(smem_u32(k_ring + s * kKStage + kKTile));
 #pragma unroll
             for (int kk = 0; kk < kFC / 8; ++kk) {
-              const uint32_t off = kk * 32;
               const uint32_t acc = (c == 0 && kk == 0) ? 0u : 1u;
-              mma_tf32(d_s, smem_desc_sw128(q_lo + off), smem_desc_sw128(k_hi + off), id_s, acc);
-              mma_tf32(d_s, smem_desc_sw128(q_hi + off), smem_desc_sw128(k_lo + off), id_s, 1u);
-              mma_tf32(d_s, smem_desc_sw128(q_hi + off), smem_desc_sw128(k_hi + off), id_s, 1u);
+              mma_tf32(d_s, dq_lo + 2 * kk, dk_hi + 2 * kk, id_s, acc);
+              mma_tf32(d_s, dq_hi + 2 * kk, dk_lo + 2 * kk, id_s, 1u);
+              mma_tf32(d_s, dq_hi + 2 * kk, dk_hi + 2 * kk, id_s, 1u);
             }
-            mma_commit(smem_u32(&qk_empty[s]));
+            mma_commit(smem_u32(&k_empty[s]));
           }
           if (!ok) break;
-          mma_commit(smem_u32(s_full));
-          if (!wait_bounded(smem_u32(p_full), static_cast<uint32_t>(blk & 1), abort_flag, a.err, 0x414)) { ok = false; break; }
-          tc_fence_after();
-          for (int c = 0; c < kFK / kFC; ++c, ++v_n) {
-            const int s = static_cast<int>(v_n % kVStages);
-            const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
-            if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x415)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t v_hi = smem_u32(v_ring + s * kVStage), v_lo = v_hi + kVTileMax;
-#pragma unroll
-            for (int kk = 0; kk < kFC / 8; ++kk) {
-              const uint32_t off = kk * 32;
-              const uint32_t col = static_cast<uint32_t>(c * kFC + kk * 8);
-              const uint32_t acc = (j == 0 && c == 0 && kk == 0) ? 0u : 1u;
-              mma_tf32_ta(d_o, tmem + kColPlo + col, smem_desc_sw128(v_hi + off), id_o, acc);
-              mma_tf32_ta(d_o, tmem + kColP + col, smem_desc_sw128(v_lo + off), id_o, 1u);
-              mma_tf32_ta(d_o, tmem + kColP + col, smem_desc_sw128(v_hi + off), id_o, 1u);
-            }
-            mma_commit(smem_u32(&v_empty[s]));
-          }
-          if (!ok) break;
-          mma_commit(smem_u32(pv_done));
+          mma_commit(smem_u32(&s_full[buf]));
+          if (j == nkb - 1) mma_commit(smem_u32(q_empty));  // the item's Q is no longer read
+          if (j >= 1 && !issue_pv(g - 1, j == 1)) { ok = false; break; }
         }
+        if (ok && nkb >= 1 && !issue_pv(g0 + nkb - 1, nkb == 1)) ok = false;
       }
     }
   } else {
@@ -261,15 +329,22 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int row_in_tile = quarter * 32 + lane;
-    int64_t blk = 0;
-    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    int64_t g = 0;
+    for (int64_t r = 0; r * gridDim.x < items; ++r) {
+      const int64_t w = snake_item(r, items);
+      if (w < 0) continue;
       int64_t b; int qt, nkb;
       item_coords(a, w, b, qt, nkb);
       const int64_t query = static_cast<int64_t>(qt) * kFQ + row_in_tile;
       float m_use = -INFINITY, l = 0.0f;
       bool aborted = false;
-      for (int j = 0; j < nkb; ++j, ++blk) {
-        if (!wait_bounded(smem_u32(s_full), static_cast<uint32_t>(blk & 1), abort_flag, a.err, 0x421)) { aborted = true; break; }
+      for (int j = 0; j < nkb; ++j, ++g) {
+        const int buf = static_cast<int>(g % kSBufs);
+        const uint32_t col_s = static_cast<uint32_t>(buf * 128), col_lo = col_s + kFK;
+        if (!wait_bounded(smem_u32(&s_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x421)) {
+          aborted = true;
+          break;
+        }
         tc_fence_after();
         const int64_t key0 = static_cast<int64_t>(j) * kFK;
         // keys allowed for this row in this block: [0, lim)
@@ -280,12 +355,12 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         float mx = -INFINITY;
 #pragma unroll 1
         for (int cc = 0; cc < kFK; cc += 32) {
-          uint32_t r[32];
-          TCX_LD32(r, tmem + lane_base + kColP + cc);
+          uint32_t rr[32];
+          TCX_LD32(rr, tmem + lane_base + col_s + cc);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float t = __fmul_rn(__uint_as_float(r[e]), a.scale_log2);
+            const float t = __fmul_rn(__uint_as_float(rr[e]), a.scale_log2);
             if (cc + e < lim) mx = fmaxf(mx, t);
           }
         }
@@ -298,62 +373,72 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         }
         l = __fmul_rn(l, alpha);
         if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // O holds blocks < j only once the previous block's P·V has completed
+          const int64_t gp = g - 1;
+          if (!wait_bounded(smem_u32(&pv_done[gp % kSBufs]), static_cast<uint32_t>((gp / kSBufs) & 1), abort_flag, a.err,
+                            0x423)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int cc = 0; cc < a.dv; cc += 32) {
-            uint32_t r[32];
-            TCX_LD32(r, tmem + lane_base + kColO + cc);
+            uint32_t rr[32];
+            TCX_LD32(rr, tmem + lane_base + kColO + cc);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__fmul_rn(__uint_as_float(r[e]), alpha));
-            TCX_ST32(tmem + lane_base + kColO + cc, r);
+            for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__fmul_rn(__uint_as_float(rr[e]), alpha));
+            TCX_ST32(tmem + lane_base + kColO + cc, rr);
           }
         }
         // pass 2: p = 2^(t - m), the row sum, P_hi over S and P_lo beside it
 #pragma unroll 1
         for (int cc = 0; cc < kFK; cc += 32) {
-          uint32_t r[32], lo[32];
-          TCX_LD32(r, tmem + lane_base + kColP + cc);
+          uint32_t rr[32], lo[32];
+          TCX_LD32(rr, tmem + lane_base + col_s + cc);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float t = __fmul_rn(__uint_as_float(r[e]), a.scale_log2);
+            const float t = __fmul_rn(__uint_as_float(rr[e]), a.scale_log2);
             float p = 0.0f;
             if (cc + e < lim) {
               asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(t, m_use)));
             }
             l = __fadd_rn(l, p);
             const float hi = tf32_rna(p);
-            r[e] = __float_as_uint(hi);
+            rr[e] = __float_as_uint(hi);
             lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
           }
-          TCX_ST32(tmem + lane_base + kColP + cc, r);
-          TCX_ST32(tmem + lane_base + kColPlo + cc, lo);
+          TCX_ST32(tmem + lane_base + col_s + cc, rr);
+          TCX_ST32(tmem + lane_base + col_lo + cc, lo);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(p_full));
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[buf]));
       }
       if (aborted) break;
       // the item's last P·V, then O / l to HBM
-      if (!wait_bounded(smem_u32(pv_done), static_cast<uint32_t>((blk - 1) & 1), abort_flag, a.err, 0x422)) break;
+      const int64_t gl = g - 1;
+      if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err, 0x422))
+        break;
       tc_fence_after();
       const float inv = 1.0f / l;
       float* orow = a.out + (b * a.L + query) * a.dv;
       const bool row_ok = query < a.L;
 #pragma unroll 1
       for (int cc = 0; cc < a.dv; cc += 32) {
-        uint32_t r[32];
-        TCX_LD32(r, tmem + lane_base + kColO + cc);
+        uint32_t rr[32];
+        TCX_LD32(rr, tmem + lane_base + kColO + cc);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (row_ok) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             float4 v;
-            v.x = __fmul_rn(__uint_as_float(r[e + 0]), inv);
-            v.y = __fmul_rn(__uint_as_float(r[e + 1]), inv);
-            v.z = __fmul_rn(__uint_as_float(r[e + 2]), inv);
-            v.w = __fmul_rn(__uint_as_float(r[e + 3]), inv);
+            v.x = __fmul_rn(__uint_as_float(rr[e + 0]), inv);
+            v.y = __fmul_rn(__uint_as_float(rr[e + 1]), inv);
+            v.z = __fmul_rn(__uint_as_float(rr[e + 2]), inv);
+            v.w = __fmul_rn(__uint_as_float(rr[e + 3]), inv);
             *reinterpret_cast<float4*>(orow + cc + e) = v;
           }
         }

@@ -6,6 +6,8 @@ timing. Prints the mean device time per call (CUDA events).
     python -m tensorcx_b200.profile softmax|rmsnorm|layernorm --rows 16384 --cols 4096
     python -m tensorcx_b200.profile sum|max|min|argmax|mean --n 268435456 [--int32]
     python -m tensorcx_b200.profile attention --batch 32 --rows 2048 --cols 2048 --size 128 [--causal]
+    python -m tensorcx_b200.profile sum_axis0 --rows 65536 --cols 4096
+    python -m tensorcx_b200.profile sum_axes02 --batch 64 --rows 4096 --cols 1024
 """
 from __future__ import annotations
 
@@ -52,6 +54,12 @@ def main():
             x = torch.randn(a.n, device="cuda", generator=g)
         f = getattr(ops, w)
         fn = lambda: f(x)  # noqa: E731
+    elif w == "sum_axis0":
+        x = torch.randn(a.rows, a.cols, device="cuda", generator=g)
+        fn = lambda: ops.sum(x, axis=0)  # noqa: E731
+    elif w == "sum_axes02":
+        x = torch.randn(a.batch, a.rows, a.cols, device="cuda", generator=g)
+        fn = lambda: ops.sum(x, axis=(0, 2))  # noqa: E731
     elif w == "attention":  # batch = heads, rows = queries, cols = keys, size = features
         q = torch.randn(a.batch, a.rows, a.size, device="cuda", generator=g)
         k = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)

@@ -410,6 +410,259 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   }
 }
 
+// ------------------------------------------------------- 2-SM (CTA pair) GEMM
+// The same 3xTF32 product on 256 x 256 tiles computed by a cluster of two CTAs on two
+// SMs with tcgen05.mma.cta_group::2 (M = 256): CTA r of the pair holds rows
+// [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile (its
+// half of N) in its own shared memory, at the same offsets; the leader CTA (rank 0)
+// issues every MMA, each SM's TMEM receives its 128 rows of the 256 x 256 accumulator.
+// Per SM and k step the tensor core reads 24 KB of operands instead of 36 KB, and the
+// stages shrink to 64 KB, so three fit: the single-SM kernel's shared-memory traffic
+// (operand reads plus TMA writes, ~150 B/clock against 128) drops to ~100 B/clock.
+// Both CTAs' TMA loads complete on the leader's full barrier (which expects both
+// halves); the leader's commits arrive on both CTAs' barriers (one commit per CTA, no
+// multicast); the peer's epilogue warps arrive on the leader's accumulator-empty
+// barrier remotely. No TMA multicast.
+constexpr int kStages2 = 3;
+constexpr int kHalf = 128;                                  // rows of A and of B per CTA
+constexpr int kTile2 = kHalf * kBK * 4;                     // 16 KB
+constexpr int kStage2Bytes = 4 * kTile2;                    // A hi/lo, B hi/lo: 64 KB
+constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256;
+constexpr uint32_t kIdesc2 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
+                             (static_cast<uint32_t>(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_index() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on the mbarrier at shared::cluster address `bar` once the pair's MMAs issued
+// so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Tile load into this CTA's shared memory whose completion is counted on the mbarrier
+// at shared::cluster address `bar` (the leader's).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                                 int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const GemmArgs g) {
+  // g.tiles_m counts 256-row tiles here; both CTAs of a pair return together
+  if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2Bytes);
+  uint64_t* full = bars;                          // [kStages2] (the leader's are used)
+  uint64_t* empty = bars + kStages2;              // [kStages2]
+  uint64_t* acc_full = bars + 2 * kStages2;       // [2]
+  uint64_t* acc_empty = bars + 2 * kStages2 + 2;  // [2] (the leader's, 8 warps arrive)
+  uint64_t* drain = bars + 2 * kStages2 + 4;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 8); }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive or load
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t total_tiles = g.batches * g.tiles_m * g.tiles_n;
+  const int64_t cid = cluster_index(), ncl = cluster_count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer (both CTAs)
+      int64_t kb_global = 0;
+      bool ok = true;
+      for (int64_t t = cid; t < total_tiles && ok; t += ncl) {
+        int64_t batch; int mt, nt;
+        tile_coords(t, g, batch, mt, nt);
+        const int64_t pa = batch_off(batch, g.bm.shape, g.bm.lhs, g.bm.rank) / (g.lhs_mk > 0 ? g.lhs_mk : 1);
+        const int64_t pb = batch_off(batch, g.bm.shape, g.bm.rhs, g.bm.rank) / (g.rhs_kn > 0 ? g.rhs_kn : 1);
+        const int row_a = mt * 2 * kHalf + static_cast<int>(rank) * kHalf;
+        const int row_b = nt * 2 * kHalf + static_cast<int>(rank) * kHalf;
+        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+          const int s = static_cast<int>(kb_global % kStages2);
+          const uint32_t phase = static_cast<uint32_t>((kb_global / kStages2) & 1);
+          if (!wait_bounded(smem_u32(&empty[s]), phase ^ 1u, abort_flag, g.err, 0x201)) { ok = false; break; }
+          uint8_t* st = smem + s * kStage2Bytes;
+          const uint32_t fb_local = smem_u32(&full[s]);
+          if (leader) mbar_expect_tx(fb_local, 2 * kStage2Bytes);  // both CTAs' halves
+          const uint32_t fb = map_rank(fb_local, 0);
+          const int kc = kb * kBK;
+          tma_load_3d_pair(smem_u32(st), &map_a, fb, kc, row_a, static_cast<int>(2 * pa));
+          tma_load_3d_pair(smem_u32(st + kTile2), &map_a, fb, kc, row_a, static_cast<int>(2 * pa + 1));
+          tma_load_3d_pair(smem_u32(st + 2 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb));
+          tma_load_3d_pair(smem_u32(st + 3 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb + 1));
+        }
+      }
+      if (!ok && leader) {  // the leader's fills must land before the CTA exits
+        for (int s = 0; s < kStages2; ++s) {
+          const int64_t fills = kb_global > s ? (kb_global - s + kStages2 - 1) / kStages2 : 0;
+          if (fills == 0) continue;
+          const uint32_t parity = static_cast<uint32_t>((fills - 1) & 1);
+          const uint64_t start = globaltimer();
+          while (!mbar_try_wait(smem_u32(&full[s]), parity))
+            if (globaltimer() - start > kWaitLimitNs) { record_device_error(g.err, 0x2ff); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------ MMA issuer (leader only)
+      int64_t kb_global = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = cid; t < total_tiles && ok; t += ncl, ++local) {
+        const int acc = static_cast<int>(local & 1);
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_flag, g.err, 0x202)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+          const int s = static_cast<int>(kb_global % kStages2);
+          const uint32_t phase = static_cast<uint32_t>((kb_global / kStages2) & 1);
+          if (!wait_bounded(smem_u32(&full[s]), phase, abort_flag, g.err, 0x203)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a_hi = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes));
+          const uint64_t a_lo = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + kTile2));
+          const uint64_t b_hi = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + 2 * kTile2));
+          const uint64_t b_lo = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + 3 * kTile2));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {  // 8 tf32 = 32 bytes = 2 in the >> 4 address field
+            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            mma_tf32_pair(d_tmem, a_lo + 2 * kk, b_hi + 2 * kk, kIdesc2, first);
+            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_lo + 2 * kk, kIdesc2, 1u);
+            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_hi + 2 * kk, kIdesc2, 1u);
+          }
+          const uint32_t e = smem_u32(&empty[s]);
+          mma_commit_pair(e);               // both CTAs' stages are free once these MMAs
+          mma_commit_pair(map_rank(e, 1));  // have read them
+        }
+        const uint32_t af = smem_u32(&acc_full[acc]);
+        mma_commit_pair(af);
+        mma_commit_pair(map_rank(af, 1));
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int64_t local = 0;
+    for (int64_t t = cid; t < total_tiles; t += ncl, ++local) {
+      const int acc = static_cast<int>(local & 1);
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!wait_bounded(smem_u32(&acc_full[acc]), acc_phase, abort_flag, g.err, 0x204)) break;
+      tc_fence_after();
+      int64_t batch; int mt, nt;
+      tile_coords(t, g, batch, mt, nt);
+      const int64_t row = static_cast<int64_t>(mt) * 2 * kHalf + static_cast<int64_t>(rank) * kHalf + q * 32 + lane;
+      const int64_t col0 = static_cast<int64_t>(nt) * kBN;
+      float* crow = g.c + (batch * g.m + row) * g.n;
+      const bool row_ok = row < g.m;
+      const bool vec = g.vec_store != 0;
+#pragma unroll 1
+      for (int cc = 0; cc < kBN; cc += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN + cc);
+        TCX_LD32(r, taddr);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (cc + 32 >= kBN) {
+          // all TMEM reads of this accumulator are done: tell the leader's MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&acc_empty[acc]), 0));
+        }
+        if (row_ok && !*abort_flag) {
+          const int64_t c = col0 + cc;
+          if (vec && c + 32 <= g.n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v;
+              v.x = epilogue_op(__uint_as_float(r[j + 0]), g.bias, c + j + 0, g.act);
+              v.y = epilogue_op(__uint_as_float(r[j + 1]), g.bias, c + j + 1, g.act);
+              v.z = epilogue_op(__uint_as_float(r[j + 2]), g.bias, c + j + 2, g.act);
+              v.w = epilogue_op(__uint_as_float(r[j + 3]), g.bias, c + j + 3, g.act);
+              *reinterpret_cast<float4*>(crow + c + j) = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), g.bias, c + j, g.act);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) {
+      // every MMA of the pair must complete before either CTA releases its TMEM
+      if (leader) {
+        mma_commit_pair(smem_u32(drain));
+        mma_commit_pair(map_rank(smem_u32(drain), 1));
+      }
+      const uint64_t start = globaltimer();
+      while (!mbar_try_wait(smem_u32(drain), 0))
+        if (globaltimer() - start > kWaitLimitNs) { record_device_error(g.err, 0x2fe); break; }
+    }
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+  cluster_sync_all();  // neither CTA leaves while the other may still touch its barriers
+}
+
 // --------------------------------------------------------------- FFMA GEMM
 constexpr int kFM = 64, kFN = 64, kFK = 16;
 
@@ -613,8 +866,11 @@ void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n
 int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
                 const float* lhs, const float* rhs, bool rhs_kmajor, int sms) {
+  // CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) once the tiles fill every pair of SMs
+  const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
+  const bool pair = m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 2;
   alignas(64) CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, kBN))
+  if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
     return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
 
   static bool attr_done[64] = {false};
@@ -622,7 +878,9 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemm2Smem) !=
+            cudaSuccess)
       return launch_status("gemm smem attribute");
     attr_done[dev] = true;
   }
@@ -640,9 +898,26 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
   g.batches = batches;
   g.bm = bm;
-  const int64_t tiles = batches * g.tiles_m * g.tiles_n;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
-  {
+  if (pair) {
+    g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
+    const int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kGemm2Smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TimedLaunch timer("gemm_tf32x3", s);
+    cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, g);
+  } else {
+    const int64_t tiles = batches * g.tiles_m * g.tiles_n;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
     TimedLaunch timer("gemm_tf32x3", s);
     gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
   }

@@ -866,9 +866,10 @@ void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n
 int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
                 const float* lhs, const float* rhs, bool rhs_kmajor, int sms) {
-  // CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) once the tiles fill every pair of SMs
+  // CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) once the tiles keep at least half
+  // of the SM pairs busy (a pair tile takes no longer than a single-SM 128 x 256 tile)
   const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
-  const bool pair = m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 2;
+  const bool pair = m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 4;
   alignas(64) CUtensorMap map_a, map_b;
   if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
     return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);

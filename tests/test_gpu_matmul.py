@@ -183,3 +183,35 @@ def test_matmul_host_pipeline(tcx, oracle, m, n, k):
         frob_ok(c[rows], ref, k)
     dev = host(tcx.matmul(a.cuda(), b.cuda()))
     np.testing.assert_array_equal(c, dev)  # identical kernels and order
+
+
+@pytest.mark.parametrize("lhs,rhs", [((2050, 130), (130, 2100)), ((1280, 1100), (1100, 2000)),
+                                     ((3, 700, 900), (900, 1100)), ((2, 1, 600, 96), (1, 3, 96, 1000))])
+def test_cta_pair_tiles_ragged_and_batched(tcx, oracle, lhs, rhs):
+    """Products large enough for the CTA-pair kernel (256 x 256 tiles on two SMs), with
+    ragged M and N edges and broadcast batches."""
+    rng = np.random.default_rng(lhs[-1] + rhs[-1])
+    a = rng.uniform(-1, 1, lhs).astype(np.float32)
+    b = rng.uniform(-1, 1, rhs).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), path="tensor"))
+    m = lhs[-2]
+    if a.ndim == 2:
+        ref = oracle.matmul(a, b, rows=slice(m - 300, m), batches=[0])[0]
+        frob_ok(got[m - 300:], ref, lhs[-1])
+    else:
+        frob_ok(got, oracle.matmul(a, b), lhs[-1])
+
+
+def test_cta_pair_epilogue_and_linear(tcx, oracle):
+    rng = np.random.default_rng(12)
+    a = rng.uniform(-1, 1, (4, 520, 384)).astype(np.float32)
+    b = rng.uniform(-1, 1, (4, 384, 1030)).astype(np.float32)
+    bias = rng.normal(size=1030).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), bias=dev(bias), act="relu", path="tensor"))
+    frob_ok(got, oracle.relu(oracle.add(oracle.matmul(a, b), bias)), 384)
+    x = rng.uniform(-1, 1, (2000, 512)).astype(np.float32)
+    w = rng.uniform(-1, 1, (1100, 512)).astype(np.float32)
+    wb = rng.normal(size=1100).astype(np.float32)
+    got = host(tcx.linear(dev(x), dev(w), dev(wb), path="tensor"))
+    ref = oracle.linear(x[:256], w, wb)
+    frob_ok(got[:256], ref, 512)

@@ -19,7 +19,9 @@
 #include <vector>
 
 #include "tcx_sm100.h"
+#include "tensorcx/backends/cuda/cuda_context.h"
 #include "tensorcx/backends/cuda/cuda_device.h"
+#include "tensorcx/backends/cuda/cuda_external_storage.h"
 #include "tensorcx/backends/cuda/cuda_memory_pool.h"
 #include "tensorcx/core/inference.h"
 #include "tensorcx/core/math.h"
@@ -570,6 +572,46 @@ Expected<std::shared_ptr<CudaBuffer>> CudaBuffer::borrow(DType dtype, const Shap
   return buffer;
 }
 
+Expected<std::shared_ptr<CudaBuffer>> CudaBuffer::borrow(DType dtype, const Shape& shape, void* data,
+                                                        std::shared_ptr<void> owner,
+                                                        std::shared_ptr<ExternalStorage> storage) {
+  int device = 0;
+  if (data) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, data) == cudaSuccess && attr.type == cudaMemoryTypeDevice) device = attr.device;
+    else cudaGetLastError();
+  }
+  auto bytes = byte_size(dtype, shape);
+  if (!bytes) return bytes.status();
+  if (storage) {
+    if (auto st = storage->validate_range(data, dtype, bytes.value()); !st.ok()) return st;
+  }
+  auto buffer = borrow(dtype, shape, data, std::move(owner), device);
+  if (!buffer) return buffer.status();
+  buffer.value()->external_storage_ = std::move(storage);
+  return buffer;
+}
+
+StorageIdentity CudaBuffer::storage_identity() const {
+  if (external_storage_) return external_storage_->identity(data_, bytes_);
+  return {this, 0, bytes_};
+}
+
+std::shared_ptr<StorageAccess> CudaBuffer::access() const {
+  return external_storage_ ? external_storage_->access() : nullptr;
+}
+
+const std::shared_ptr<PrimaryContext>& CudaBuffer::context() const {
+  if (!context_) {
+    DeviceScope scope(device_);
+    if (scope.ready()) {
+      auto ctx = PrimaryContext::acquire();
+      if (ctx) context_ = ctx.move_value();
+    }
+  }
+  return context_;
+}
+
 CudaBuffer::~CudaBuffer() {
   if (external_owner_ || !data_) return;
   DeviceScope scope(device_);
@@ -580,7 +622,7 @@ CudaBuffer::~CudaBuffer() {
 
 StorageRelation CudaBuffer::storage_relation(const Buffer& other) const {
   const auto* rhs = dynamic_cast<const CudaBuffer*>(&other);
-  if (!rhs) return Buffer::storage_relation(other);
+  if (!rhs || external_storage_ || rhs->external_storage_) return Buffer::storage_relation(other);
   if (device_ != rhs->device_) return StorageRelation::kDisjoint;
   if (this == rhs) return StorageRelation::kSameRange;
   if (!nbytes() || !rhs->nbytes()) return StorageRelation::kDisjoint;

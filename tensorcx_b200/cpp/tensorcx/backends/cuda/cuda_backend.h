@@ -17,17 +17,29 @@
 namespace tensorcx::cuda {
 
 class MemoryPool;
+class ExternalStorage;
+class PrimaryContext;
 
 // Device memory of one tensor: owned (stream-ordered pool or the device's default
-// stream-ordered pool) or borrowed from an external owner.
+// stream-ordered pool) or borrowed from an external owner (a DLPack producer, or a
+// registered ExternalStorage whose storage identity and lock it then reports).
 class CudaBuffer final : public Buffer {
  public:
   static Expected<std::shared_ptr<CudaBuffer>> create(DType dtype, const Shape& shape, int device = 0);
   static Expected<std::shared_ptr<CudaBuffer>> borrow(DType dtype, const Shape& shape, void* data,
                                                      std::shared_ptr<void> owner, int device = 0);
+  // The reference's form (cuda_buffer.h:22-45): the device is the one the pointer lives on.
+  static Expected<std::shared_ptr<CudaBuffer>> borrow(DType dtype, const Shape& shape, void* data,
+                                                     std::shared_ptr<void> owner,
+                                                     std::shared_ptr<ExternalStorage> storage);
   ~CudaBuffer() override;
   std::size_t nbytes() const override { return bytes_; }
   StorageRelation storage_relation(const Buffer& other) const override;
+  StorageIdentity storage_identity() const override;
+  std::shared_ptr<StorageAccess> access() const override;
+  const std::shared_ptr<ExternalStorage>& external_storage() const { return external_storage_; }
+  // The retained primary context of the buffer's device (acquired on first use).
+  const std::shared_ptr<PrimaryContext>& context() const;
   DType dtype() const { return dtype_; }
   void* data() const { return data_; }
   int device() const { return device_; }
@@ -43,6 +55,8 @@ class CudaBuffer final : public Buffer {
   std::atomic<bool> exported_{false};
   std::shared_ptr<MemoryPool> pool_;
   std::shared_ptr<void> external_owner_;
+  std::shared_ptr<ExternalStorage> external_storage_;
+  mutable std::shared_ptr<PrimaryContext> context_;
 };
 
 class CudaTensor {

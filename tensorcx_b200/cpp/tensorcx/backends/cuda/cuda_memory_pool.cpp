@@ -103,7 +103,7 @@ cudaError_t MemoryPool::free_locked(void* pointer, std::size_t bytes) {
   return error;
 }
 
-void MemoryPool::release(void* pointer, std::size_t bytes, bool reusable) noexcept {
+void MemoryPool::release(void* pointer, std::size_t bytes, bool reusable, bool /*context_ready*/) noexcept {
   try {
     std::lock_guard lock(mutex_);
     stats_.in_use_bytes -= bytes;

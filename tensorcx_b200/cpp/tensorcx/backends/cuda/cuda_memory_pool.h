@@ -46,7 +46,9 @@ class MemoryPool : public std::enable_shared_from_this<MemoryPool> {
   Status trim();
   PoolStats stats() const;
   Expected<void*> allocate(std::size_t bytes);
-  void release(void* pointer, std::size_t bytes, bool reusable) noexcept;
+  // context_ready: the reference's flag that the pool's context is current (always true
+  // here: blocks are freed stream-ordered on the backend's per-device stream).
+  void release(void* pointer, std::size_t bytes, bool reusable, bool context_ready = true) noexcept;
   void close_noexcept() noexcept;
 
  private:

@@ -16,6 +16,9 @@
 
 #include "tensorcx/backends/cpu/cpu_backend.h"
 #include "tensorcx/backends/cuda/cuda_backend.h"
+#include "tensorcx/backends/cuda/cuda_context.h"
+#include "tensorcx/backends/cuda/cuda_external_storage.h"
+#include "tensorcx/backends/cuda/cuda_kernel.h"
 #include "tensorcx/backends/cuda/cuda_device.h"
 #include "tensorcx/backends/cuda/cuda_memory_pool.h"
 
@@ -219,6 +222,86 @@ void error_contract(Backend& gpu) {
   check(gpu.execute(h).code() == StatusCode::kInvalidArgument, "CPU tensor rejected");
   check(outputs[0].device.type == "sentinel", "rejected calls leave the result slot untouched");
 }
+
+// The rest of the reference's backend surface: driver contexts, compiled kernels
+// (unavailable by design) and the external-storage registry and lease.
+struct FakeAccess final : StorageAccess {
+  Status validate() const override { return Status::Ok(); }
+};
+struct FakeStorage final : cuda::ExternalStorage {
+  void* base{};
+  std::size_t size{};
+  int completions{};
+  std::shared_ptr<StorageAccess> lock = std::make_shared<FakeAccess>();
+  std::shared_ptr<StorageAccess> access() override { return lock; }
+  std::uintptr_t begin() const override { return reinterpret_cast<std::uintptr_t>(base); }
+  std::size_t bytes() const override { return size; }
+  std::size_t mapped_bytes() const override { return size; }
+  Status validate_range(void* data, DType, std::size_t n) const override {
+    const auto a = reinterpret_cast<std::uintptr_t>(data);
+    return a >= begin() && a + n <= begin() + size ? Status::Ok()
+                                                   : Status(StatusCode::kInvalidArgument, "outside the storage");
+  }
+  StorageIdentity identity(void* data, std::size_t n) const override {
+    return {this, reinterpret_cast<std::uintptr_t>(data) - begin(), n};
+  }
+  Status complete_cuda() override {
+    ++completions;
+    return Status::Ok();
+  }
+  void poison() noexcept override {}
+};
+
+void surface_contract() {
+  check(cuda::compiled_kernel_support().code() == StatusCode::kUnavailable, "compiled kernels: unavailable");
+  auto module = cuda::CudaKernelModule::load(".version 8.7", "entry", cuda::KernelSignature{"ff", 1, 0});
+  check(!module && module.status().code() == StatusCode::kUnavailable, "kernel module load: unavailable");
+  check(!cuda::kernel_manifest(cuda::KernelSignature{"ff", 1, 0}).empty(), "kernel manifest text");
+  check(cuda::current_process(), "current process");
+  auto ctx = cuda::PrimaryContext::acquire();
+  check(ctx.has_value() && ctx.value()->get() != nullptr, "primary context retained");
+  if (ctx) {
+    cuda::ContextScope scope(ctx.value());
+    check(scope.ready(), "context scope pushes the primary context");
+  }
+  // external storage: registry lookups, borrowed buffers that report its identity and
+  // lock, and a lease that completes its CUDA work
+  auto fake = std::make_shared<FakeStorage>();
+  fake->size = 1 << 16;
+  auto backing = cuda::empty({static_cast<Dim>(fake->size / 4)}, DType::kFloat32);  // device memory to "own"
+  if (!backing) { check(false, "device memory for the external storage"); return; }
+  fake->base = backing.value().buffer()->data();
+  cuda::register_external_storage(fake);
+  auto hit = cuda::find_external_storage(static_cast<char*>(fake->base) + 256, 1024);
+  check(hit.has_value() && hit.value().get() == fake.get(), "registry finds the owner of a range");
+  auto miss = cuda::find_external_storage(static_cast<char*>(fake->base) + fake->size - 4, 64);
+  check(!miss && miss.status().code() == StatusCode::kInvalidArgument, "registry rejects a range past the end");
+  auto buf = cuda::CudaBuffer::borrow(DType::kFloat32, {16}, static_cast<char*>(fake->base) + 512, nullptr,
+                                      std::shared_ptr<cuda::ExternalStorage>(fake));
+  check(buf.has_value(), "borrow from external storage");
+  if (buf) {
+    const auto id = buf.value()->storage_identity();
+    check(id.token == fake.get() && id.offset == 512 && id.bytes == 64, "borrowed buffer reports the storage identity");
+    check(buf.value()->access() == fake->lock, "borrowed buffer reports the storage lock");
+    check(buf.value()->context() != nullptr, "buffer context");
+    Tensor t{DType::kFloat32, {16}, contiguous_strides({16}), Device{"cuda", 0}, buf.value(), 0};
+    std::vector<Tensor> ins{t}, outs(1);
+    BackendExecution e{BackendOpClass::kPrimitive, desc(OpKind::kExp), ins, outs, std::nullopt, std::nullopt, {}};
+    auto owners = cuda::external_owners(e);
+    check(owners.size() == 1 && owners[0].get() == fake.get(), "external owners of an execution");
+    {
+      cuda::ExternalLease lease(owners);
+      check(lease.status().ok(), "lease taken");
+      check(lease.finish().ok() && fake->completions == 1, "lease completes the owner's CUDA work");
+    }
+    check(fake->completions == 1, "a finished lease does not complete twice");
+  }
+  auto bad = cuda::CudaBuffer::borrow(DType::kFloat32, {1 << 20}, fake->base, nullptr,
+                                      std::shared_ptr<cuda::ExternalStorage>(fake));
+  check(!bad, "borrow beyond the storage is rejected");
+  cuda::unregister_external_storage(fake->begin(), fake.get());
+  check(!cuda::find_external_storage(fake->base, 4), "unregistered storage is no longer found");
+}
 }  // namespace
 
 int main() {
@@ -328,6 +411,7 @@ int main() {
   }
   error_contract(gpu);
   pool_contract();
+  surface_contract();
   // the same ops inside a real stream-ordered pool scope
   {
     auto pool = std::make_shared<cuda::MemoryPool>(1 << 28, 64);

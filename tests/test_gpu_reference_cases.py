@@ -542,3 +542,130 @@ def test_fused_attention_nonfinite_inputs(tcx, oracle, where, value):
         got = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=causal))
         with np.errstate(all="ignore"):
             attn_check(got, oracle.attention(q, k, v, None, causal))
+
+
+# ------------------------------------------------------------ min / argmax / clip
+MIN_CASES = [((), None), ((), 0), ((), -1), ((), ()), ((2, 3, 4), None), ((2, 3, 4), 0), ((2, 3, 4), -1),
+             ((2, 3, 4), (0, 2)), ((2, 3, 4), (-1, 0)), ((2, 3, 4), ()), ((0, 3), 1), ((2, 0, 3), 0)]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32])
+@pytest.mark.parametrize("shape,axis", MIN_CASES)
+@pytest.mark.parametrize("keepdims", [False, True])
+def test_min_parity(tcx, dtype, shape, axis, keepdims):
+    """test_math_ops.py:62-72."""
+    a = np.random.default_rng(42).integers(-500, 500, shape).astype(dtype)
+    x = dev(a)
+    try:
+        expected = np.min(a, axis=axis, keepdims=keepdims)
+    except ValueError:
+        with pytest.raises(ValueError):
+            tcx.min(x, axis, keepdims=keepdims)
+        return
+    got = host(tcx.min(x, axis, keepdims=keepdims))
+    assert got.shape == np.shape(expected)
+    np.testing.assert_array_equal(got, expected)
+
+
+ARGMAX_CASES = [((), None), ((), 0), ((), -1), ((2, 3, 4), None), ((2, 3, 4), 0), ((2, 3, 4), 1),
+                ((2, 3, 4), -1), ((0, 3), 1), ((2, 0, 3), 0)]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32])
+@pytest.mark.parametrize("shape,axis", ARGMAX_CASES)
+@pytest.mark.parametrize("keepdims", [False, True])
+def test_argmax_parity(tcx, dtype, shape, axis, keepdims):
+    """test_math_ops.py:75-83: first maximum, int32 indices."""
+    a = np.random.default_rng(73).integers(-3, 4, shape).astype(dtype)
+    x = dev(a)
+    try:
+        expected = np.asarray(np.argmax(a, axis=axis, keepdims=keepdims), dtype=np.int32)
+    except ValueError:
+        with pytest.raises(ValueError):
+            tcx.argmax(x, axis, keepdims=keepdims)
+        return
+    got = host(tcx.argmax(x, axis, keepdims=keepdims))
+    assert got.dtype == np.int32 and got.shape == expected.shape
+    np.testing.assert_array_equal(got, expected)
+
+
+@pytest.mark.parametrize("axis", [None, 0, 1, -1])
+def test_min_argmax_ieee_ties(tcx, axis):
+    """test_math_ops.py:86-91: NaN wins, both zeros equal, the lowest index on ties."""
+    a = np.array([[0., -0., 1e-40, -1e-40, np.inf], [np.nan, 2., np.nan, -np.inf, 2.]], np.float32)
+    x = dev(a)
+    np.testing.assert_array_equal(host(tcx.min(x, axis)), np.min(a, axis=axis))
+    np.testing.assert_array_equal(host(tcx.argmax(x, axis)), np.asarray(np.argmax(a, axis=axis), np.int32))
+
+
+def test_min_signed_zero_first_value(tcx):
+    """test_math_ops.py:226-233: among equal zeros the first one's bits are returned."""
+    bits = np.array([[0, 0x80000000], [0x80000000, 0]], np.uint32)
+    x = dev(bits.view(np.float32))
+    np.testing.assert_array_equal(host(tcx.min(x, 1)).view(np.uint32), bits[:, 0])
+    np.testing.assert_array_equal(host(tcx.argmax(x, 1)), [0, 0])
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32])
+@pytest.mark.parametrize("bounds", [(-2, 3), (None, 3), (-2, None), (4, -4), (0, 0)])
+@pytest.mark.parametrize("shape", [(), (0,), (2, 3, 4)])
+def test_clip_scalar_parity(tcx, dtype, bounds, shape):
+    """test_math_ops.py:94-102."""
+    a = np.random.default_rng(75).integers(-10, 10, shape).astype(dtype)
+    got = host(tcx.clip(dev(a), *bounds))
+    expected = np.asarray(np.clip(a, *bounds), dtype=dtype)
+    assert got.shape == expected.shape
+    np.testing.assert_array_equal(got, expected)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.int32])
+def test_clip_broadcast_bounds(tcx, dtype):
+    """test_math_ops.py:105-113: bounds broadcast the output beyond the input's shape."""
+    a = np.array([[[-4], [1], [9]]], dtype=dtype)
+    lo = np.array([[-1, 2, 7, 8]], dtype=dtype)
+    hi = np.array([[[3]], [[10]]], dtype=dtype)
+    got = host(tcx.clip(dev(a), dev(lo), dev(hi)))
+    np.testing.assert_array_equal(got, np.clip(a, lo, hi))
+
+
+def test_clip_ieee(tcx):
+    """test_math_ops.py:116-122: NaN in the input or a bound propagates; signed zeros and
+    subnormals keep their bits."""
+    a = np.array([np.nan, -0., 0., 1e-40, -1e-40, np.inf, -np.inf, 1., 2.], np.float32)
+    lo = np.array([-1., 0., -0., -2e-40, -2e-40, -1., -1., np.nan, -1.], np.float32)
+    hi = np.array([1., 0., -0., 2e-40, 2e-40, 1., 1., 2., np.nan], np.float32)
+    got = host(tcx.clip(dev(a), dev(lo), dev(hi)))
+    np.testing.assert_array_equal(got, np.clip(a, lo, hi))
+    np.testing.assert_array_equal(got[1:7].view(np.uint32), np.clip(a, lo, hi)[1:7].view(np.uint32))
+
+
+def test_clip_empty_broadcast(tcx):
+    """test_math_ops.py:237-241: an empty input broadcast against a bound."""
+    for dtype in (np.float32, np.int32):
+        x = dev(np.empty((0, 2, 1), dtype=dtype))
+        got = host(tcx.clip(x, dev(np.zeros((1, 3), dtype=dtype)), 4))
+        assert got.shape == (0, 2, 3) and got.dtype == dtype
+
+
+def test_math_errors(tcx):
+    """test_math_ops.py:191-223, the min / argmax / clip rows."""
+    x = dev(np.array([[1., 2.]], np.float32))
+    for shape in [(2, 0), (0, 0)]:
+        empty = torch.empty(shape, device="cuda")
+        for name in ("min", "argmax"):
+            with pytest.raises(ValueError):
+                getattr(tcx, name)(empty, axis=1)
+    for axis in [2, -3, (0, 1), True, 1.5]:
+        with pytest.raises((ValueError, TypeError)):
+            tcx.argmax(x, axis)
+    with pytest.raises(ValueError):
+        tcx.clip(x)
+    with pytest.raises(ValueError):
+        tcx.clip(x, dev(np.array(1, np.int32)), 2)
+    with pytest.raises(ValueError):
+        tcx.clip(x, torch.ones((3,), device="cuda"), 2)
+    for name in ("min", "argmax"):
+        with pytest.raises(TypeError):
+            getattr(tcx, name)(x, keepdims=1)
+    with pytest.raises(ValueError):
+        tcx.min(x, (0, 0))

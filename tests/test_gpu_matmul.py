@@ -215,3 +215,31 @@ def test_cta_pair_epilogue_and_linear(tcx, oracle):
     got = host(tcx.linear(dev(x), dev(w), dev(wb), path="tensor"))
     ref = oracle.linear(x[:256], w, wb)
     frob_ok(got[:256], ref, 512)
+
+
+@pytest.mark.parametrize("shapes", [((), (2, 2)), ((2, 2), ()), ((3,), (4,)), ((2, 3, 4), (3, 4, 5)),
+                                    ((2, 3, 4), (2, 5, 6)), ((0, 3, 4), (2, 4, 5)), ((0, 3, 4), (1, 5, 6))])
+def test_batched_matmul_invalid_shapes(tcx, shapes):
+    """test_batched_matmul.py:53-62."""
+    a, b = (torch.empty(s, device="cuda") for s in shapes)
+    with pytest.raises(ValueError):
+        tcx.matmul(a, b)
+
+
+def test_batched_matmul_rejects_dtype_even_empty(tcx):
+    """test_batched_matmul.py:65-73 (int32 operands; torch bool is no CUDA operand here)."""
+    for shape in [(2, 3, 3), (0, 3, 3)]:
+        a = torch.ones(shape, dtype=torch.int32, device="cuda")
+        b = torch.ones(shape, dtype=torch.float32, device="cuda")
+        for left, right in [(a, a), (a, b), (b, a)]:
+            with pytest.raises(ValueError):
+                tcx.matmul(left, right)
+
+
+def test_batched_matmul_rank_limit(tcx):
+    """test_batched_matmul.py:119-129: 2^15 batches over 15 axes of extent 2."""
+    a = torch.ones((2,) * 15 + (1, 1), device="cuda")
+    b = torch.ones((1, 1), device="cuda")
+    r = tcx.matmul(a, b)
+    assert tuple(r.shape) == tuple(a.shape)
+    np.testing.assert_array_equal(host(r).reshape(-1), np.ones(2**15, np.float32))

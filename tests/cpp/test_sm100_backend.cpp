@@ -13,6 +13,8 @@
 #include <random>
 #include <string>
 #include <vector>
+#include <thread>
+#include <atomic>
 
 #include "tensorcx/backends/cpu/cpu_backend.h"
 #include "tensorcx/backends/cuda/cuda_backend.h"
@@ -302,6 +304,30 @@ void surface_contract() {
   cuda::unregister_external_storage(fake->begin(), fake.get());
   check(!cuda::find_external_storage(fake->base, 4), "unregistered storage is no longer found");
 }
+
+// Calls arrive concurrently from many threads (the bindings release the GIL around
+// execute): four threads each run matmul -> softmax chains and check their results.
+void concurrency_contract(Backend& gpu, Backend& ref) {
+  const auto a = randn({64, 96}, 131), b = randn({96, 80}, 132);
+  Tensor rm, rs;
+  check(run(ref, desc(OpKind::kMatmul), {cpu::to_core_tensor(a), cpu::to_core_tensor(b)}, rm).ok(), "reference matmul");
+  check(run(ref, axis_op(OpKind::kSoftmax, -1), {rm}, rs).ok(), "reference softmax");
+  const auto expected = cpu::from_core_tensor(rs);
+  std::atomic<int> bad{0};
+  std::vector<std::thread> threads;
+  for (int t = 0; t < 4; ++t) {
+    threads.emplace_back([&] {
+      for (int i = 0; i < 8; ++i) {
+        Tensor m, s;
+        if (!run(gpu, desc(OpKind::kMatmul), {on_gpu(a), on_gpu(b)}, m).ok() ||
+            !run(gpu, axis_op(OpKind::kSoftmax, -1), {m}, s).ok() || !close(download(s), expected, 1e-4, 1e-5))
+          ++bad;
+      }
+    });
+  }
+  for (auto& th : threads) th.join();
+  check(bad.load() == 0, "concurrent executes from four threads");
+}
 }  // namespace
 
 int main() {
@@ -412,6 +438,7 @@ int main() {
   error_contract(gpu);
   pool_contract();
   surface_contract();
+  concurrency_contract(gpu, ref);
   // the same ops inside a real stream-ordered pool scope
   {
     auto pool = std::make_shared<cuda::MemoryPool>(1 << 28, 64);

@@ -669,3 +669,26 @@ def test_math_errors(tcx):
             getattr(tcx, name)(x, keepdims=1)
     with pytest.raises(ValueError):
         tcx.min(x, (0, 0))
+
+
+def test_concurrent_inference_chain(tcx, oracle):
+    """test_cuda_primitives.py:90-101: the same chain from four threads at once
+    (softmax(matmul(gelu(layernorm(matmul(x, w1))), w2))), each result checked."""
+    from concurrent.futures import ThreadPoolExecutor
+    rng = np.random.default_rng(19)
+    x = rng.normal(size=(7, 17)).astype(np.float32)
+    w1 = rng.normal(size=(17, 31)).astype(np.float32)
+    w2 = rng.normal(size=(31, 5)).astype(np.float32)
+    expected = oracle.softmax(oracle.matmul(oracle.gelu(oracle.layernorm(oracle.matmul(x, w1), -1)), w2), -1)
+    gx, g1, g2 = dev(x), dev(w1), dev(w2)
+
+    def forward():
+        torch.cuda.set_device(0)
+        y = tcx.softmax(tcx.matmul(tcx.gelu(tcx.layernorm(tcx.matmul(gx, g1), -1)), g2), -1)
+        torch.cuda.current_stream().synchronize()
+        return y.cpu().numpy()
+
+    with ThreadPoolExecutor(max_workers=4) as pool:
+        results = [f.result() for f in [pool.submit(forward) for _ in range(12)]]
+    for r in results:
+        np.testing.assert_allclose(r, expected, rtol=1e-4, atol=1e-5)

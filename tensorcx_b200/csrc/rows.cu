@@ -33,21 +33,26 @@ using rowmath::Block;
 using rowmath::exp_ex2;
 using rowmath::nan_max;
 
-// Per-row math on values held by the CTA's threads. E = elements per thread; element
-// q of a thread is valid when its column (given by col(q)) is < n.
-template <int OP, int THREADS, int E, typename Col>
-__device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, float first, float eps,
+// Per-row math on values held by the CTA's threads. E = elements per thread; valid(q)
+// tells whether slot q of this thread holds an element of the row. Callers fill the
+// other slots with the padding pad_value<OP>() gives (-inf for softmax, 0 for the norms),
+// which leaves every max and sum unchanged, so only layernorm's equality count and
+// deviation sum test valid(q).
+template <int OP, int THREADS, int E, typename Valid>
+__device__ __forceinline__ void row_math(float (&v)[E], Valid valid, int64_t n, float first, float eps,
                                          float* smem) {
   using B = Block<THREADS>;
   if (OP == kSoftmax) {
+    // fmaxf skips NaN elements; a NaN still makes the whole row NaN, as the reference
+    // does, because its exponential enters the row sum that divides every element.
     float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (col(i) < n) m = nan_max(m, v[i]);
+    for (int i = 0; i < E; ++i) m = fmaxf(m, v[i]);
     m = B::max(m, smem);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      v[i] = col(i) < n ? exp_ex2(__fsub_rn(v[i], m)) : 0.0f;
+      v[i] = exp_ex2(__fsub_rn(v[i], m));
       s = __fadd_rn(s, v[i]);
     }
     s = B::sum(s, smem);
@@ -58,7 +63,7 @@ __device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, floa
   } else if (OP == kRms) {
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (col(i) < n) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
     ss = B::sum(ss, smem);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
 #pragma unroll
@@ -66,7 +71,10 @@ __device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, floa
   } else {
     float s = 0.0f, neq = 0.0f;  // neq counts elements != first (exact below 2^24 per thread)
 #pragma unroll
-    for (int i = 0; i < E; ++i) if (col(i) < n) { s = __fadd_rn(s, v[i]); neq += (v[i] == first) ? 0.0f : 1.0f; }
+    for (int i = 0; i < E; ++i) {
+      s = __fadd_rn(s, v[i]);
+      if (valid(i)) neq += (v[i] == first) ? 0.0f : 1.0f;
+    }
     const float2 r = B::sum2(s, neq, smem);
     s = r.x;
     const bool eq = r.y == 0.0f;
@@ -80,7 +88,7 @@ __device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, floa
     float ssd = 0.0f;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      if (col(i) < n) {
+      if (valid(i)) {
         const float d = __fsub_rn(v[i], mean);
         ssd = __fadd_rn(ssd, __fmul_rn(d, d));
       }
@@ -98,6 +106,12 @@ __device__ __forceinline__ void row_math(float (&v)[E], Col col, int64_t n, floa
   }
 }
 
+// Value of the slots past the end of a row: neutral for the row's max and sums.
+template <int OP>
+__device__ __forceinline__ float pad_value() {
+  return OP == kSoftmax ? -INFINITY : 0.0f;
+}
+
 __device__ __forceinline__ float affine(float y, const float* w, const float* b, int64_t c) {
   if (w) y = __fmul_rn(y, __ldg(w + c));
   if (b) y = __fadd_rn(y, __ldg(b + c));
@@ -106,45 +120,47 @@ __device__ __forceinline__ float affine(float y, const float* w, const float* b,
 
 // One CTA per row, the row held in registers. VEC: float4 accesses (row length % 4 == 0
 // and 16-byte aligned rows); otherwise scalar accesses, element tid + THREADS*q.
-// FULL: n == THREADS * VPT * 4 exactly (every slot valid; no bounds checks).
+// FULL: n == THREADS * VPT * 4 exactly (every slot valid; no bounds checks). Rows are
+// at most 32768 elements here, so column indices fit 32 bits.
 template <int OP, int THREADS, int VPT, bool VEC, bool FULL = false>
 __global__ void __launch_bounds__(THREADS)
 row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, int64_t n,
            float eps, const float* __restrict__ w, const float* __restrict__ b) {
   constexpr int E = VPT * 4;
   __shared__ float smem[64];
+  const int n32 = static_cast<int>(n), n4 = n32 >> 2;
+  const int tid = static_cast<int>(threadIdx.x);
+  const float pad = pad_value<OP>();
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* xr = x + row * n;
     float* orow = out + row * n;
     float v[E];
     if (VEC) {
-      const int64_t n4 = n >> 2;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        const int64_t i4 = threadIdx.x + static_cast<int64_t>(j) * THREADS;
-        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i4 < n4) t = __ldcs(reinterpret_cast<const float4*>(xr) + i4);
+        const int i4 = tid + j * THREADS;
+        float4 t = make_float4(pad, pad, pad, pad);
+        if (FULL || i4 < n4) t = __ldcs(reinterpret_cast<const float4*>(xr) + i4);
         v[4 * j + 0] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
       }
     } else {
 #pragma unroll
       for (int q = 0; q < E; ++q) {
-        const int64_t i = threadIdx.x + static_cast<int64_t>(q) * THREADS;
-        v[q] = i < n ? __ldcs(xr + i) : 0.0f;
+        const int i = tid + q * THREADS;
+        v[q] = i < n32 ? __ldcs(xr + i) : pad;
       }
     }
     const float first = OP == kLayer ? __ldg(xr) : 0.0f;
-    auto col = [](int q) -> int64_t {
-      if (FULL) return 0;  // every element valid: col(q) < n always holds
-      return VEC ? 4 * (threadIdx.x + static_cast<int64_t>(q >> 2) * THREADS) + (q & 3)
-                 : threadIdx.x + static_cast<int64_t>(q) * THREADS;
+    auto col = [&](int q) -> bool {
+      if (FULL) return true;
+      return VEC ? tid + (q >> 2) * THREADS < n4 : tid + q * THREADS < n32;
     };
     row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
     if (VEC) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        const int64_t i4 = threadIdx.x + static_cast<int64_t>(j) * THREADS;
-        if (i4 < (n >> 2)) {
+        const int i4 = tid + j * THREADS;
+        if (FULL || i4 < n4) {
           float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           if (w || b) {
             t.x = affine(t.x, w, b, 4 * i4 + 0); t.y = affine(t.y, w, b, 4 * i4 + 1);
@@ -156,8 +172,8 @@ row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, i
     } else {
 #pragma unroll
       for (int q = 0; q < E; ++q) {
-        const int64_t i = threadIdx.x + static_cast<int64_t>(q) * THREADS;
-        if (i < n) __stcs(orow + i, (w || b) ? affine(v[q], w, b, i) : v[q]);
+        const int i = tid + q * THREADS;
+        if (i < n32) __stcs(orow + i, (w || b) ? affine(v[q], w, b, i) : v[q]);
       }
     }
   }
@@ -194,13 +210,15 @@ row_staged_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t 
   int64_t row = blockIdx.x;
   if (threadIdx.x == 0 && row < rows) issue(row);
   const int n4 = static_cast<int>(n >> 2);
+  const int tid = static_cast<int>(threadIdx.x);
+  const float pad = pad_value<OP>();
   for (uint32_t it = 0; row < rows; row += gridDim.x, ++it) {
     ptx::wait_or_give_up(bar_addr, it & 1u, err, 0x301);
     float v[E];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int i4 = static_cast<int>(threadIdx.x) + j * THREADS;
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int i4 = tid + j * THREADS;
+      float4 t = make_float4(pad, pad, pad, pad);
       if (i4 < n4) t = reinterpret_cast<const float4*>(stage)[i4];
       v[4 * j + 0] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
     }
@@ -210,14 +228,12 @@ row_staged_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t 
       issue(row + gridDim.x);
     }
     const float first = OP == kLayer ? __ldg(x + row * n) : 0.0f;
-    auto col = [](int q) -> int64_t {
-      return 4 * (static_cast<int64_t>(threadIdx.x) + static_cast<int64_t>(q >> 2) * THREADS) + (q & 3);
-    };
+    auto col = [&](int q) -> bool { return tid + (q >> 2) * THREADS < n4; };
     row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
     float* orow = out + row * n;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int i4 = static_cast<int>(threadIdx.x) + j * THREADS;
+      const int i4 = tid + j * THREADS;
       if (i4 < n4) {
         float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         if (w || b) {

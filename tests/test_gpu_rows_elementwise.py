@@ -54,8 +54,8 @@ def row_close(got, cpu, exact, tol=1e-5):
 
 
 @pytest.mark.parametrize("op", ROW_OPS)
-@pytest.mark.parametrize("width", [1, 2, 7, 33, 255, 256, 257, 1023, 1024, 1025, 4095, 4096, 4097, 8192,
-                                   12000, 16384, 32768, 40000])
+@pytest.mark.parametrize("width", [1, 2, 7, 33, 255, 256, 257, 1023, 1024, 1025, 2048, 2049, 4095, 4096, 4097,
+                                   6000, 8192, 8193, 12000, 16384, 16385, 16392, 20004, 32768, 40000])
 def test_row_ops_widths(tcx, oracle, op, width):
     rows = max(1, min(64, (1 << 20) // width))
     x = (np.random.default_rng(width).normal(size=(rows, width)) * 3).astype(np.float32)
@@ -110,7 +110,8 @@ def test_bad_epsilon(tcx, op, eps):
         getattr(tcx, op)(dev(np.ones((2, 3), np.float32)), axis=-1, eps=eps)
 
 
-@pytest.mark.parametrize("width,axis", [(4096, -1), (300, -1), (64, 0), (40000, -1)])
+@pytest.mark.parametrize("width,axis", [(4096, -1), (300, -1), (64, 0), (6000, -1), (12000, -1), (20000, -1),
+                                        (40000, -1)])
 def test_affine_norms(tcx, oracle, width, axis):
     rng = np.random.default_rng(width)
     x = (rng.normal(size=(16, width)) * 3).astype(np.float32)

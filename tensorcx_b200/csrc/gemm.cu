@@ -221,7 +221,20 @@ struct GemmArgs {
   int32_t num_kb, tiles_m, tiles_n, act, vec_store;
   int64_t batches;
   BatchMap bm;
+  // split-K (single-SM kernel, one output batch): work item t covers tile t / splits and
+  // k-blocks [(t % splits) * kb_per_split, +kb_per_split); its raw partial tile goes to
+  // partial + (t % splits) * m * n, summed by splitk_reduce
+  int32_t splits, kb_per_split;
+  float* partial;
 };
+
+// k-block range of work item t
+__device__ __forceinline__ void split_range(int64_t t, const GemmArgs& g, int64_t& tile, int& split, int& kb0, int& kb1) {
+  tile = t / g.splits;
+  split = static_cast<int>(t - tile * g.splits);
+  kb0 = split * g.kb_per_split;
+  kb1 = min(g.num_kb, kb0 + g.kb_per_split);
+}
 
 __device__ __forceinline__ void tile_coords(int64_t t, const GemmArgs& g, int64_t& batch, int& mt, int& nt) {
   const int64_t per_batch = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
@@ -271,19 +284,21 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int64_t total_tiles = g.batches * g.tiles_m * g.tiles_n;
+  const int64_t total_work = g.batches * g.tiles_m * g.tiles_n * g.splits;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- TMA producer
       int64_t kb_global = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int64_t t = blockIdx.x; t < total_work && ok; t += gridDim.x) {
+        int64_t tile; int split, kb0, kb1;
+        split_range(t, g, tile, split, kb0, kb1);
         int64_t batch; int mt, nt;
-        tile_coords(t, g, batch, mt, nt);
+        tile_coords(tile, g, batch, mt, nt);
         const int64_t pa = batch_off(batch, g.bm.shape, g.bm.lhs, g.bm.rank) / (g.lhs_mk > 0 ? g.lhs_mk : 1);
         const int64_t pb = batch_off(batch, g.bm.shape, g.bm.rhs, g.bm.rank) / (g.rhs_kn > 0 ? g.rhs_kn : 1);
-        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+        for (int kb = kb0; kb < kb1; ++kb, ++kb_global) {
           const int s = static_cast<int>(kb_global % kStages);
           const uint32_t phase = static_cast<uint32_t>((kb_global / kStages) & 1);
           if (!wait_bounded(smem_u32(&empty[s]), phase ^ 1u, abort_flag, g.err, 0x101)) { ok = false; break; }
@@ -315,13 +330,15 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       int64_t kb_global = 0;
       int64_t local = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      for (int64_t t = blockIdx.x; t < total_work && ok; t += gridDim.x, ++local) {
+        int64_t tile; int split, kb0, kb1;
+        split_range(t, g, tile, split, kb0, kb1);
         const int acc = static_cast<int>(local & 1);
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_flag, g.err, 0x102)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+        for (int kb = kb0; kb < kb1; ++kb, ++kb_global) {
           const int s = static_cast<int>(kb_global % kStages);
           const uint32_t phase = static_cast<uint32_t>((kb_global / kStages) & 1);
           if (!wait_bounded(smem_u32(&full[s]), phase, abort_flag, g.err, 0x103)) { ok = false; break; }
@@ -333,7 +350,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            const uint32_t first = (kb == kb0 && kk == 0) ? 0u : 1u;
             mma_tf32(d_tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(b_hi + off), kIdesc, first);
             mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_lo + off), kIdesc, 1u);
             mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_hi + off), kIdesc, 1u);
@@ -347,16 +364,23 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
     // -------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int64_t local = 0;
-    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    for (int64_t t = blockIdx.x; t < total_work; t += gridDim.x, ++local) {
       const int acc = static_cast<int>(local & 1);
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
       if (!wait_bounded(smem_u32(&acc_full[acc]), acc_phase, abort_flag, g.err, 0x104)) break;
       tc_fence_after();
+      int64_t tile; int split, kb0, kb1;
+      split_range(t, g, tile, split, kb0, kb1);
       int64_t batch; int mt, nt;
-      tile_coords(t, g, batch, mt, nt);
+      tile_coords(tile, g, batch, mt, nt);
       const int64_t row = static_cast<int64_t>(mt) * kBM + q * 32 + lane;
       const int64_t col0 = static_cast<int64_t>(nt) * kBN;
-      float* crow = g.c + (batch * g.m + row) * g.n;
+      // split-K: the raw partial sums go to this split's slice of the workspace
+      const bool raw = g.splits > 1;
+      float* crow = raw ? g.partial + (static_cast<int64_t>(split) * g.m + row) * g.n
+                        : g.c + (batch * g.m + row) * g.n;
+      const float* bias = raw ? nullptr : g.bias;
+      const int act = raw ? TCX_ACT_NONE : g.act;
       const bool row_ok = row < g.m;
       const bool vec = g.vec_store != 0;
 #pragma unroll 1
@@ -377,16 +401,16 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               float4 v;
-              v.x = epilogue_op(__uint_as_float(r[j + 0]), g.bias, c + j + 0, g.act);
-              v.y = epilogue_op(__uint_as_float(r[j + 1]), g.bias, c + j + 1, g.act);
-              v.z = epilogue_op(__uint_as_float(r[j + 2]), g.bias, c + j + 2, g.act);
-              v.w = epilogue_op(__uint_as_float(r[j + 3]), g.bias, c + j + 3, g.act);
+              v.x = epilogue_op(__uint_as_float(r[j + 0]), bias, c + j + 0, act);
+              v.y = epilogue_op(__uint_as_float(r[j + 1]), bias, c + j + 1, act);
+              v.z = epilogue_op(__uint_as_float(r[j + 2]), bias, c + j + 2, act);
+              v.w = epilogue_op(__uint_as_float(r[j + 3]), bias, c + j + 3, act);
               *reinterpret_cast<float4*>(crow + c + j) = v;
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), g.bias, c + j, g.act);
+              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), bias, c + j, act);
           }
         }
       }
@@ -717,6 +741,75 @@ gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float
   }
 }
 
+// Split-K epilogue: out = act(sum over splits, in split order, of the raw partial
+// tiles + bias). Idle when the pre-pass flagged inf / NaN (the FFMA fallback queued
+// behind it writes the output). VEC: n % 4 == 0 and 16-byte aligned buffers.
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+splitk_reduce(const float* __restrict__ partial, float* __restrict__ out, int64_t mn, int64_t n, int splits,
+              const float* __restrict__ bias, int act, const int* __restrict__ nonfinite) {
+  if (*nonfinite) return;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (VEC) {
+    for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4; i < mn; i += stride * 4) {
+      float4 v = __ldcs(reinterpret_cast<const float4*>(partial + i));
+      for (int sp = 1; sp < splits; ++sp) {
+        const float4 w = __ldcs(reinterpret_cast<const float4*>(partial + sp * mn + i));
+        v.x = __fadd_rn(v.x, w.x); v.y = __fadd_rn(v.y, w.y); v.z = __fadd_rn(v.z, w.z); v.w = __fadd_rn(v.w, w.w);
+      }
+      const int64_t c = i % n;
+      v.x = epilogue_op(v.x, bias, c + 0, act); v.y = epilogue_op(v.y, bias, c + 1, act);
+      v.z = epilogue_op(v.z, bias, c + 2, act); v.w = epilogue_op(v.w, bias, c + 3, act);
+      *reinterpret_cast<float4*>(out + i) = v;
+    }
+  } else {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < mn; i += stride) {
+      float v = partial[i];
+      for (int sp = 1; sp < splits; ++sp) v = __fadd_rn(v, partial[sp * mn + i]);
+      out[i] = epilogue_op(v, bias, i % n, act);
+    }
+  }
+}
+
+// Skinny products (n <= 32, FFMA path): one warp per output row. Lane l accumulates
+// the k indices l, l + 32, ... for every output column in registers, then a butterfly
+// of shuffles sums each column and lane j stores column j. A rows are read coalesced;
+// the small B stays in L1.
+template <bool BT, int NMAX>
+__global__ void __launch_bounds__(256)
+gemm_skinny_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ c, int64_t m,
+                   int64_t n, int64_t k, int64_t batches, BatchMap bm, const float* __restrict__ bias, int act) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int nn = static_cast<int>(n);
+  for (int64_t rg = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); rg < batches * m;
+       rg += warps) {
+    const int64_t batch = rg / m, row = rg - batch * m;
+    const float* ar = a + batch_off(batch, bm.shape, bm.lhs, bm.rank) + row * k;
+    const float* bb = b + batch_off(batch, bm.shape, bm.rhs, bm.rank);
+    float acc[NMAX];
+#pragma unroll
+    for (int j = 0; j < NMAX; ++j) acc[j] = 0.0f;
+#pragma unroll 4
+    for (int64_t kk = lane; kk < k; kk += 32) {
+      const float av = __ldg(ar + kk);
+#pragma unroll
+      for (int j = 0; j < NMAX; ++j)
+        if (j < nn) acc[j] = fmaf(av, BT ? __ldg(bb + j * k + kk) : __ldg(bb + kk * n + j), acc[j]);
+    }
+    float mine = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NMAX; ++j) {
+      if (j >= nn) break;
+      float v = acc[j];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == j) mine = v;
+    }
+    if (lane < nn) c[(batch * m + row) * n + lane] = epilogue_op(mine, bias, lane, act);
+  }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -751,10 +844,30 @@ bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows,
 
 struct Layout {
   int64_t kp;
-  size_t off_flag, off_a, off_b, total;
+  size_t off_flag, off_a, off_b, off_partial, total;
+  int splits;  // split-K factor of the single-SM kernel (1: none)
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) once the tiles keep at least half
+// of the SM pairs busy (a pair tile takes no longer than a single-SM 128 x 256 tile).
+bool use_pair(int64_t m, int64_t n, int64_t batches, int sms) {
+  const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
+  return m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 4;
+}
+
+// Split-K factor for a single-batch product whose 128 x 256 tiles fill less than half
+// of the SMs: each split keeps >= 4 k-blocks, and tiles x splits stays within the SMs.
+int split_count(int64_t m, int64_t n, int64_t kp, int64_t batches, int sms) {
+  if (batches != 1 || use_pair(m, n, batches, sms)) return 1;
+  const int64_t tiles = ceil_div(m, kBM) * ceil_div(n, kBN);
+  const int64_t num_kb = kp / kBK;
+  if (2 * tiles > sms || num_kb < 8) return 1;
+  const int64_t want = std::max<int64_t>(1, std::min<int64_t>(num_kb / 4, sms / tiles));
+  const int64_t per = ceil_div(num_kb, want);
+  return static_cast<int>(ceil_div(num_kb, per));  // no empty split
+}
 
 Layout tensor_layout(int64_t m, int64_t n, int64_t k, int64_t nba, int64_t nbb) {
   Layout l;
@@ -762,7 +875,9 @@ Layout tensor_layout(int64_t m, int64_t n, int64_t k, int64_t nba, int64_t nbb) 
   l.off_flag = 0;
   l.off_a = 1024;
   l.off_b = align_up(l.off_a + static_cast<size_t>(2 * nba * m * l.kp) * 4, 1024);
-  l.total = align_up(l.off_b + static_cast<size_t>(2 * nbb * n * l.kp) * 4, 1024);
+  l.off_partial = align_up(l.off_b + static_cast<size_t>(2 * nbb * n * l.kp) * 4, 1024);
+  l.splits = (nba == 1 && nbb == 1) ? split_count(m, n, l.kp, 1, sm_count()) : 1;
+  l.total = l.off_partial + (l.splits > 1 ? align_up(static_cast<size_t>(l.splits * m * n) * 4, 1024) : 0);
   return l;
 }
 
@@ -844,14 +959,15 @@ void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n
 }
 
 // The tcgen05 GEMM over split planes, then the IEEE FFMA fallback that runs only when
-// the pre-pass raised *flag (reading the original lhs / rhs).
+// the pre-pass raised *flag (reading the original lhs / rhs). splits > 1 (single-SM
+// kernel, one output batch) needs `partial`: splits * m * n floats of workspace.
 int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
-                const float* lhs, const float* rhs, bool rhs_kmajor, int sms) {
-  // CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) once the tiles keep at least half
-  // of the SM pairs busy (a pair tile takes no longer than a single-SM 128 x 256 tile)
+                const float* lhs, const float* rhs, bool rhs_kmajor, int sms, int splits = 1,
+                float* partial = nullptr) {
   const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
-  const bool pair = m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 4;
+  const bool pair = use_pair(m, n, batches, sms);
+  if (pair || batches != 1 || !partial) splits = 1;
   alignas(64) CUtensorMap map_a, map_b;
   if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
     return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
@@ -881,6 +997,10 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
   g.batches = batches;
   g.bm = bm;
+  g.splits = std::max(1, splits);
+  g.kb_per_split = static_cast<int32_t>(ceil_div(g.num_kb, g.splits));
+  g.partial = partial;
+  if (g.splits > 1) g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(partial) % 16 == 0) ? 1 : 0;
   if (pair) {
     g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
     const int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
@@ -899,12 +1019,22 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     TimedLaunch timer("gemm_tf32x3", s);
     cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, g);
   } else {
-    const int64_t tiles = batches * g.tiles_m * g.tiles_n;
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+    const int64_t work = batches * g.tiles_m * g.tiles_n * g.splits;
+    const int grid = static_cast<int>(std::min<int64_t>(work, sms));
     TimedLaunch timer("gemm_tf32x3", s);
     gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
   }
   if (int st = launch_status("tcgen05 matmul")) return st;
+  if (g.splits > 1) {
+    const int64_t mn = m * n;
+    const bool vec = n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(partial) % 16 == 0;
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(vec ? mn / 4 : mn, 256), 4LL * sms));
+    TimedLaunch timer("splitk_reduce", s);
+    if (vec) splitk_reduce<true><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag);
+    else splitk_reduce<false><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag);
+    if (int st = launch_status("split-K reduce")) return st;
+  }
   // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
   const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
   const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
@@ -944,6 +1074,21 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   const int sms = sm_count();
 
   if (!use_tensor(m, n, k, path)) {
+    if (n <= 32) {
+      const int grid = static_cast<int>(std::min<int64_t>(ceil_div(batches * m, 8), 64LL * sms));
+      TimedLaunch timer("gemm_skinny", s);
+      if (n <= 8) {
+        if (rhs_kmajor) gemm_skinny_kernel<true, 8><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+        else gemm_skinny_kernel<false, 8><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+      } else if (n <= 16) {
+        if (rhs_kmajor) gemm_skinny_kernel<true, 16><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+        else gemm_skinny_kernel<false, 16><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+      } else {
+        if (rhs_kmajor) gemm_skinny_kernel<true, 32><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+        else gemm_skinny_kernel<false, 32><<<grid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act);
+      }
+      return launch_status("skinny matmul");
+    }
     const int64_t tiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, 16LL * sms));
     {
@@ -955,7 +1100,11 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   }
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return invalid("matmul extent too large for the tensor path");
   const int64_t nba = distinct_batches(bm, true, m * k), nbb = distinct_batches(bm, false, k * n);
-  const Layout lay = tensor_layout(m, n, k, nba, nbb);
+  Layout lay = tensor_layout(m, n, k, nba, nbb);
+  if (lay.splits > 1 && (batches != 1 || (workspace && workspace_bytes < lay.total && workspace_bytes >= lay.off_partial))) {
+    lay.splits = 1;  // no split-K partial area (several output batches, or a workspace sized without it)
+    lay.total = lay.off_partial;
+  }
   if (!workspace || workspace_bytes < lay.total) return invalid("matmul workspace is missing or too small");
   if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("matmul workspace must be 1024-byte aligned");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -968,8 +1117,9 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   split_a(s, lhs, wa, nba, m, k, lay.kp, flag, sms);
   split_b(s, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
   if (int st = launch_status("matmul split pre-pass")) return st;
+  float* partial = lay.splits > 1 ? reinterpret_cast<float*>(ws + lay.off_partial) : nullptr;
   return gemm_planes(s, wa, wb, nba, nbb, m, n, k, lay.kp, batches, bm, output, bias, act, flag, lhs, rhs,
-                     rhs_kmajor, sms);
+                     rhs_kmajor, sms, lay.splits, partial);
 }
 
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,

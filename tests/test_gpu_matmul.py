@@ -243,3 +243,57 @@ def test_batched_matmul_rank_limit(tcx):
     r = tcx.matmul(a, b)
     assert tuple(r.shape) == tuple(a.shape)
     np.testing.assert_array_equal(host(r).reshape(-1), np.ones(2**15, np.float32))
+
+
+@pytest.mark.parametrize("m,k,n,act", [(256, 784, 512, "relu"), (128, 4096, 256, "none"), (300, 1000, 300, "silu"),
+                                       (256, 1001, 259, "relu"), (1, 2048, 256, "none")])
+def test_split_k_small_products(tcx, oracle, m, k, n, act):
+    """Products whose 128 x 256 tiles fill few SMs split their k-blocks over CTAs; the
+    partial tiles are summed in split order with bias and activation applied after."""
+    rng = np.random.default_rng(m + k + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), bias=dev(bias), act=act, path="tensor"))
+    ref = oracle.add(oracle.matmul(a, b), bias)
+    ref = oracle.silu(ref) if act == "silu" else oracle.relu(ref) if act == "relu" else ref
+    frob_ok(got, ref, k)
+    np.testing.assert_allclose(got, ref, rtol=2e-4 * math.sqrt(k / 1024) + 1e-4, atol=1e-4 * math.sqrt(k))
+
+
+def test_split_k_nonfinite_takes_ieee_path(tcx, oracle):
+    rng = np.random.default_rng(12)
+    a = rng.uniform(-1, 1, (256, 784)).astype(np.float32)
+    b = rng.uniform(-1, 1, (784, 512)).astype(np.float32)
+    a[5, 9] = np.inf
+    b[100, 3] = np.nan
+    bias = rng.normal(size=512).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), bias=dev(bias), act="relu", path="tensor"))
+    ref = oracle.relu(oracle.add(oracle.matmul(a, b), bias))
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4, equal_nan=True)
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 512, 10), (1000, 1000, 1), (3, 5000, 32), (7, 0, 9), (513, 300, 17),
+                                   (64, 33, 8), (2, 1, 16)])
+@pytest.mark.parametrize("act", ["none", "relu", "silu"])
+def test_skinny_products(tcx, oracle, m, k, n, act):
+    """n <= 32 on the FFMA path: a warp per output row, lanes split k."""
+    rng = np.random.default_rng(m * 3 + n)
+    a = rng.normal(size=(m, k)).astype(np.float32)
+    b = rng.normal(size=(k, n)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    got = host(tcx.matmul(dev(a), dev(b), bias=dev(bias), act=act, path="auto"))
+    ref = oracle.add(oracle.matmul(a, b), bias)
+    ref = oracle.silu(ref) if act == "silu" else oracle.relu(ref) if act == "relu" else ref
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * math.sqrt(max(k, 1)))
+
+
+def test_skinny_batched_and_linear(tcx, oracle):
+    rng = np.random.default_rng(13)
+    a = rng.normal(size=(2, 3, 50, 70)).astype(np.float32)
+    b = rng.normal(size=(3, 70, 12)).astype(np.float32)
+    np.testing.assert_allclose(host(tcx.matmul(dev(a), dev(b))), oracle.matmul(a, b), rtol=1e-4, atol=1e-3)
+    x = rng.normal(size=(5, 40, 300)).astype(np.float32)
+    w = rng.uniform(-0.05, 0.05, (20, 300)).astype(np.float32)
+    bias = rng.normal(size=20).astype(np.float32)
+    frob_ok(host(tcx.linear(dev(x), dev(w), dev(bias))), oracle.linear(x, w, bias), 300)

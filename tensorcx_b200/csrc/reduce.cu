@@ -33,6 +33,12 @@ constexpr int kUnroll = 4;
 
 enum Kind { kSumF = 0, kSumI = 1, kBestMax = 2, kBestMin = 3 };
 
+// Max / min / argmax load the next kUnroll vectors before folding the current ones (their
+// compare-and-select chain is serial), so a thread always has a batch of loads in
+// flight; the sums keep their 16 independent accumulators and higher occupancy instead.
+template <int K>
+__host__ __device__ constexpr bool prefetch_kind() { return K == kBestMax || K == kBestMin; }
+
 template <typename T>
 __device__ __forceinline__ T max_identity() {
   if constexpr (std::is_same<T, float>::value) return -INFINITY;
@@ -109,10 +115,18 @@ struct BestRun {
     }
   }
   // (key, global index) of this thread's best; key 0 / INT64_MAX when it saw nothing.
+  // The winning value's bits are still in bv (selects only); the chunk is read again
+  // only for a NaN or when no element beat the identity.
   __device__ __forceinline__ void result(const uint32_t* chunk, int64_t base, uint32_t& key, int64_t& idx) const {
     int32_t at = nan_at >= 0 ? nan_at : (bi >= 0 ? bi : first);
     if (at < 0) { key = 0; idx = INT64_MAX; return; }
-    const uint32_t bits = chunk[at];
+    uint32_t bits;
+    if (nan_at < 0 && bi >= 0) {
+      if constexpr (FP) bits = __float_as_uint(bv);
+      else bits = static_cast<uint32_t>(bv);
+    } else {
+      bits = chunk[at];
+    }
     key = (K == kBestMax) ? key_max(bits, FP) : key_min(bits, FP);
     idx = base + at;
   }
@@ -189,16 +203,30 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
     a.key = 0; a.idx = INT64_MAX;
     BestRun<K, FP> best;
     constexpr bool kBestKind = K == kBestMax || K == kBestMin;
+    constexpr bool kPrefetch = prefetch_kind<K>();
     const int tid = threadIdx.x;
     int64_t tail_begin = begin;
     if (VEC && end > begin) {
       const uint4* xv = reinterpret_cast<const uint4*>(xr + begin);
       const int64_t nvec = (end - begin) >> 2;
       int64_t i = tid;
-      for (; i + (kUnroll - 1) * kStage1Threads < nvec; i += kUnroll * kStage1Threads) {
-        uint4 v[kUnroll];
+      uint4 v[kUnroll];
+      if (kPrefetch && i + (kUnroll - 1) * kStage1Threads < nvec) {
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) v[u] = ldg_stream(xv + i + u * kStage1Threads);
+      }
+      for (; i + (kUnroll - 1) * kStage1Threads < nvec; i += kUnroll * kStage1Threads) {
+        uint4 nv[kUnroll];
+        if (kPrefetch) {
+          const int64_t ni = i + kUnroll * kStage1Threads;
+          if (ni + (kUnroll - 1) * kStage1Threads < nvec) {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) nv[u] = ldg_stream(xv + ni + u * kStage1Threads);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) v[u] = ldg_stream(xv + i + u * kStage1Threads);
+        }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int64_t e = begin + 4 * (i + u * kStage1Threads) + index_base;
@@ -210,6 +238,10 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
             take<K, FP>(a, 4 * u + 2, v[u].z, e + 2);
             take<K, FP>(a, 4 * u + 3, v[u].w, e + 3);
           }
+        }
+        if (kPrefetch) {
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) v[u] = nv[u];
         }
       }
       for (; i < nvec; i += kStage1Threads) {
@@ -782,8 +814,11 @@ int load_meta(Meta& m, const int64_t* meta, int rank) {
 int64_t strided_chunks(int64_t outer, int64_t reduce, int64_t inner) {
   const int64_t count = outer * inner;
   if (inner <= 1 || count <= 0 || count >= 32768 || reduce < 256) return 1;
-  const int64_t target = 2048LL * sm_count();  // one wave of resident threads
-  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(reduce, 64), ceil_div(target, count)));
+  // one wave of resident threads: axis_chunks holds 8 rows x 4 columns in flight per
+  // thread (80 registers), 3 CTAs of 256 per SM; a thread covers 4 columns when inner % 4 == 0
+  const int64_t target = 768LL * sm_count();
+  const int64_t units = inner % 4 == 0 ? count / 4 : count;
+  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(reduce, 64), ceil_div(target, units)));
 }
 
 size_t axis_reduce_workspace(int64_t outer, int64_t reduce, int64_t inner) {
@@ -960,7 +995,9 @@ int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* in
   if (int st = load_meta(meta, index_metadata, rank)) return st;
   // long reductions over few groups: warps per (group, piece), records folded in order
   if (reduction_size >= 2048 && groups < 65536 && outer_rank < rank) {
-    const int64_t target = 64LL * sm_count();  // warps: 8 per CTA, 8 CTAs per SM
+    // about 8 waves of 8-warp CTAs (4 resident per SM): the last, partial wave costs
+    // little, and a warp's piece stays >= 1024 elements
+    const int64_t target = 256LL * sm_count();
     const int64_t pieces = std::max<int64_t>(1, std::min<int64_t>(ceil_div(reduction_size, 1024),
                                                                   ceil_div(target, groups)));
     const int last = rank - 1;
@@ -975,7 +1012,9 @@ int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* in
       auto* part = static_cast<tcx_partial*>(workspace);
       const auto* x = static_cast<const uint32_t*>(input);
       auto* o = static_cast<uint32_t*>(output);
-      const int grid1 = grid_for(groups * npieces * 32, 256), grid2 = grid_for(groups, 256);
+      // one (group, piece) per warp, CTAs scheduled as SMs free up
+      const int grid1 = static_cast<int>(std::min<int64_t>(ceil_div(groups * npieces, 8), INT32_MAX));
+      const int grid2 = grid_for(groups, 256);
       const bool fp = dtype == TCX_FLOAT32;
       TimedLaunch timer("axes_chunks", s);
       auto run = [&](auto kind_tag, auto fp_tag) {

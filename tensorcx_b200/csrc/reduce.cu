@@ -568,6 +568,10 @@ axes_chunks(const uint32_t* __restrict__ x, tcx_partial* __restrict__ part, int6
       }
     };
     int64_t r = r0 + V * lane;
+    // one reduced axis besides the innermost, stepped by at most one index per load:
+    // the walk carries into it with an add instead of re-deriving the offset
+    const bool one_mid = last - outer_rank == 1 && kStep <= e_in;
+    const int64_t s_mid = one_mid ? meta.v[2 * outer_rank + 1] : 0;
     if (r < r1) {
       int64_t q = r / e_in, p = r % e_in;
       int64_t run = base + meta_offset(q, meta, outer_rank, last);
@@ -586,9 +590,15 @@ axes_chunks(const uint32_t* __restrict__ x, tcx_partial* __restrict__ part, int6
           }
           p += kStep;
           if (p >= e_in) {
-            q += p / e_in;
-            p %= e_in;
-            run = base + meta_offset(q, meta, outer_rank, last);
+            if (one_mid) {
+              p -= e_in;
+              ++q;
+              run += s_mid;
+            } else {
+              q += p / e_in;
+              p %= e_in;
+              run = base + meta_offset(q, meta, outer_rank, last);
+            }
           }
         }
 #pragma unroll

@@ -37,6 +37,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of the phase (acquire, like try_wait). A try_wait on a phase that
+// has already completed still holds the issuing thread ~170-270 cycles on sm_100a
+// (measured), long enough for a thread issuing narrow tcgen05.mma groups to let the
+// tensor pipe drain; the bounded waits below test first and only then block.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Address of the same shared variable in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
   uint32_t r;
@@ -85,7 +99,7 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legal w
 // Waits for the phase of parity `parity`; gives up after kWaitLimitNs, recording
 // `site` in the device error word (the caller then proceeds instead of hanging).
 __device__ __forceinline__ bool wait_or_give_up(uint32_t bar, uint32_t parity, int* err, int site) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer() - start > kWaitLimitNs) {
@@ -102,7 +116,7 @@ __device__ __forceinline__ bool wait_or_give_up(uint32_t bar, uint32_t parity, i
 // `site` in the device error word and raises the CTA abort flag).
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                              int* err, int site) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;

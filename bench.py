@@ -187,6 +187,22 @@ class ClockSampler:
                 "power_w_max": max((float(p[4]) for p in use if p[4].replace(".", "").isdigit()), default=None)}
 
 
+def smi_index(torch, local):
+    """nvidia-smi's index of CUDA device `local`, matched by UUID (CUDA's enumeration
+    order and CUDA_VISIBLE_DEVICES need not follow nvidia-smi's); falls back to the
+    CUDA_VISIBLE_DEVICES entry, then to the CUDA index."""
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+        r = subprocess.run(["nvidia-smi", "-i", uuid, "--query-gpu=index", "--format=csv,noheader"],
+                           capture_output=True, text=True, timeout=20)
+        if r.returncode == 0 and r.stdout.strip().isdigit():
+            return r.stdout.strip()
+    except (OSError, subprocess.SubprocessError, RuntimeError):
+        pass
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return visible[local] if local < len(visible) else str(local)
+
+
 # ------------------------------------------------------------------ GPU arm
 class Timer:
     """CUDA-event timing on the current stream, max over ranks."""
@@ -263,8 +279,7 @@ def gpu_arm(args):
     timer = Timer(torch, dist, world)
     pk, pk_note = peaks()
     hbm_peak = float(pk["hbm_gbs"])
-    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    sampler = ClockSampler(visible[local] if local < len(visible) else str(local))
+    sampler = ClockSampler(smi_index(torch, local))
     sampler.start()
     size = args.size
     flops = 2.0 * size ** 3

@@ -541,9 +541,21 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
     xf = torch.randn(shard, device="cuda", generator=g)
     xi = torch.randint(-1000, 1001, (shard,), device="cuda", generator=g, dtype=torch.int32)
     gathered = torch.empty((world, 16), dtype=torch.uint8, device="cuda")
+    # N > 1: the records cross GPUs inside the reduction kernel (peer-memory mailboxes,
+    # tensorcx_b200.collective); NCCL all_gather of the records only without peer access
+    peer = None
+    here = torch.cuda.current_device()
+    if world > 1 and all(torch.cuda.can_device_access_peer(here, d)
+                         for d in range(torch.cuda.device_count()) if d != here):
+        from tensorcx_b200.collective import PeerReduction
+        peer = PeerReduction()
+    combine = ("in the reduction kernel over NVLink peer memory" if peer else
+               "NCCL all_gather + the combine kernel" if world > 1 else "the combine kernel")
     for name, x, op in [("sum_f32_2^28", xf, "sum"), ("argmax_f32_2^28", xf, "argmax"),
                         ("sum_i32_2^28", xi, "sum"), ("max_i32_2^28", xi, "max")]:
         def st(x=x, op=op):
+            if peer is not None:
+                return peer.reduce(x, op, base, total)
             rec = ops.reduce_partial(x, op, index_base=base)
             if world > 1:
                 dist.all_gather_into_tensor(gathered, rec)
@@ -558,9 +570,10 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         lib.tcx_sm100_timer_enable(0)
         kern = read_timer(lib)
         hbm_entry(name, 4.0 * shard, ms, "reduce_stage1", kern,
-                  {"config": f"2^28 elements total, {world} shard(s), partials combined by "
-                             f"{'NCCL all_gather' if world > 1 else 'the combine kernel'} in rank order; "
-                             "back to back when the data is >= 2x L2, else L2 flushed before each step"})
+                  {"config": f"2^28 elements total, {world} shard(s), partials combined {combine} "
+                             "in rank order; back to back when the data is >= 2x L2, else L2 flushed before each step"})
+    if peer is not None:
+        peer.close()
     del xf, xi
 
     # strided and multi-axis reductions (1 GiB each): axis 0 of [65536, 4096], and

@@ -186,6 +186,36 @@ int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype,
                              const tcx_partial* partials, int32_t nparts,
                              int64_t total_count, void* output);
 
+/* ------------------------------------------ cross-GPU fold over peer memory --- */
+
+/* The multi-GPU full reduction with its exchange step inside the kernel, in place of
+ * reduce_partial + an all-gather of the records + reduce_combine (the sharded helper
+ * of the 2/4/8-GPU path; the reference runs one device, cuda_backend.cpp:272-274).
+ * Each rank owns a mailbox: a device allocation of tcx_sm100_mailbox_bytes(world)
+ * that every rank maps through CUDA IPC (one process per GPU, peer access over
+ * NVLink / NVSwitch). The calling rank's kernel folds its shard to one record, stores
+ * it with a system-scope release into slot `rank` of every rank's mailbox, waits until
+ * all `world` records of this `epoch` are in its own mailbox (bounded by
+ * `wait_limit_ns`; on expiry the device error word is set, see
+ * tcx_sm100_device_error, and the output is undefined), and folds them in rank order
+ * exactly as tcx_sm100_reduce_combine, so every rank gets the same value.
+ * Epochs start at 1 and rise by 1 per call on every rank (two slot sets, by epoch
+ * parity, let a rank run one call ahead of a slower peer). */
+size_t tcx_sm100_mailbox_bytes(int32_t world);
+/* Allocates and zeroes a mailbox; writes its IPC handle (64 bytes) to ipc_handle. */
+int tcx_sm100_mailbox_create(int32_t world, void** mailbox, void* ipc_handle);
+/* Maps a peer's mailbox from its IPC handle; tcx_sm100_mailbox_close unmaps it. */
+int tcx_sm100_mailbox_open(const void* ipc_handle, void** peer_mailbox);
+int tcx_sm100_mailbox_close(void* peer_mailbox);
+int tcx_sm100_mailbox_free(void* mailbox);
+/* `mailboxes` is a host array of `world` device pointers: the mapped mailbox of each
+ * rank, this rank's own at [rank]. `workspace` as for tcx_sm100_reduce_partial. */
+int tcx_sm100_reduce_sharded(tcx_stream_t stream, int op, int dtype, const void* input,
+                             int64_t count, int64_t index_base, void* const* mailboxes,
+                             int32_t rank, int32_t world, uint64_t epoch, uint64_t wait_limit_ns,
+                             int64_t total_count, void* output, void* workspace,
+                             size_t workspace_bytes);
+
 /* -------------------------------------------------------------- elementwise --- */
 
 /* exp / gelu (tanh form) / silu, float32. Replaces launch_unary (cuda_kernels.h:32-33;

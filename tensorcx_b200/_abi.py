@@ -49,6 +49,13 @@ SIGNATURES = {
     "tcx_sm100_reduce_all_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _vp]),
     "tcx_sm100_reduce_partial": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _sz]),
     "tcx_sm100_reduce_combine": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i32, _i64, _vp]),
+    "tcx_sm100_mailbox_bytes": (_sz, [_i32]),
+    "tcx_sm100_mailbox_create": (ctypes.c_int, [_i32, ctypes.POINTER(_vp), _vp]),
+    "tcx_sm100_mailbox_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "tcx_sm100_mailbox_close": (ctypes.c_int, [_vp]),
+    "tcx_sm100_mailbox_free": (ctypes.c_int, [_vp]),
+    "tcx_sm100_reduce_sharded": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, ctypes.POINTER(_vp),
+                                                _i32, _i32, ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp, _sz]),
     "tcx_sm100_unary": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64]),
     "tcx_sm100_binary": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _i64, _i64p, _i32]),
     "tcx_sm100_clip": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64p, _i32]),

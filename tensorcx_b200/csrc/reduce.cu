@@ -17,6 +17,7 @@
 //    the reduction in the reference's index order (exact).
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include <algorithm>
 #include <mutex>
@@ -24,6 +25,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace tcx {
 namespace {
@@ -354,6 +356,90 @@ __global__ void combine_records(const tcx_partial* __restrict__ parts, int npart
     static_cast<float*>(out)[0] =
         total ? __fdiv_rn(__uint_as_float(bits), static_cast<float>(total)) : __int_as_float(0x7fc00000);
   else static_cast<uint32_t*>(out)[0] = K <= kSumI ? bits : best_bits;
+}
+
+// ------------------------------------------------- cross-GPU fold (peer memory)
+// Mailbox of one rank: 2 slot sets (epoch parity) x world slots of 32 bytes: the
+// sender's tcx_partial (16 B), then the epoch it belongs to (8 B).
+constexpr int kMaxRanks = 64;
+constexpr int kSlotBytes = 32;
+constexpr uint64_t kDefaultExchangeWaitNs = 2000000000ull;  // 2 s
+
+struct Mailboxes {
+  char* box[kMaxRanks];  // each rank's mailbox, mapped into this process; own at [rank]
+};
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Stage 2 of a sharded reduction fused with the exchange: the CTA folds this rank's
+// stage-1 records (as reduce_stage2), thread 0 stores the rank's record into slot
+// `rank` of every mailbox (peer stores over NVLink), releases it with the epoch at
+// system scope, waits (bounded) for all ranks' epochs in its own mailbox and folds the
+// records in rank order with the combine_records rule.
+template <int K>
+__global__ void __launch_bounds__(1024)
+reduce_stage2_exchange(const tcx_partial* __restrict__ part, int nparts, const uint32_t* __restrict__ x,
+                       int64_t index_base, Mailboxes mb, int rank, int world, uint64_t epoch, uint64_t limit_ns,
+                       int64_t total, int mode, void* out, int* err) {
+  uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0;
+  int64_t idx = INT64_MAX;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const tcx_partial p = part[i];
+    if (K == kSumF) bits = __float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(p.bits)));
+    else if (K == kSumI) bits += p.bits;
+    else if (better(p.key, p.index, key, idx)) { key = p.key; idx = p.index; }
+  }
+  block_fold<K>(bits, key, idx);
+  if (threadIdx.x != 0) return;
+  const bool sum_kind = K <= kSumI;
+  const int64_t set = static_cast<int64_t>(epoch & 1) * world;
+  {
+    const uint32_t rec_bits = sum_kind ? bits : (idx == INT64_MAX ? 0u : x[idx - index_base]);
+    const uint64_t lo = static_cast<uint64_t>(key) | (static_cast<uint64_t>(rec_bits) << 32);
+    const uint64_t hi = static_cast<uint64_t>(idx);
+    for (int r = 0; r < world; ++r) {
+      uint64_t* slot = reinterpret_cast<uint64_t*>(mb.box[r] + (set + rank) * kSlotBytes);
+      asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(slot), "l"(lo), "l"(hi) : "memory");
+      st_release_sys(slot + 2, epoch);
+    }
+  }
+  const char* mine = mb.box[rank] + set * kSlotBytes;
+  const uint64_t start = ptx::globaltimer();
+  for (int r = 0; r < world; ++r) {
+    const uint64_t* flag = reinterpret_cast<const uint64_t*>(mine + r * kSlotBytes) + 2;
+    bool late = false;
+    while (ld_acquire_sys(flag) != epoch) {
+      if (ptx::globaltimer() - start > limit_ns) { late = true; break; }
+    }
+    if (late) {
+      record_device_error(err, 0x501);
+      break;
+    }
+  }
+  uint32_t fbits = K == kSumF ? __float_as_uint(0.0f) : 0u, fkey = 0, best_bits = 0;
+  int64_t fidx = INT64_MAX;
+  for (int r = 0; r < world; ++r) {
+    const uint64_t* slot = reinterpret_cast<const uint64_t*>(mine + r * kSlotBytes);
+    uint64_t lo, hi;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "l"(slot) : "memory");
+    const uint32_t pkey = static_cast<uint32_t>(lo), pbits = static_cast<uint32_t>(lo >> 32);
+    const int64_t pidx = static_cast<int64_t>(hi);
+    if (K == kSumF) fbits = __float_as_uint(__fadd_rn(__uint_as_float(fbits), __uint_as_float(pbits)));
+    else if (K == kSumI) fbits += pbits;
+    else if (better(pkey, pidx, fkey, fidx)) { fkey = pkey; fidx = pidx; best_bits = pbits; }
+  }
+  if (mode == kOutIndex) static_cast<int32_t*>(out)[0] = static_cast<int32_t>(fidx);
+  else if (mode == kOutMean)
+    static_cast<float*>(out)[0] =
+        total ? __fdiv_rn(__uint_as_float(fbits), static_cast<float>(total)) : __int_as_float(0x7fc00000);
+  else static_cast<uint32_t*>(out)[0] = sum_kind ? fbits : best_bits;
 }
 
 // ---------------------------------------------------------------- ordered rows
@@ -976,6 +1062,108 @@ int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype, const tcx_p
     default: combine_records<kBestMin><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
   }
   return launch_status("reduction combine");
+}
+
+size_t tcx_sm100_mailbox_bytes(int32_t world) {
+  if (world <= 0 || world > kMaxRanks) return 0;
+  return (static_cast<size_t>(2 * world * kSlotBytes) + 255) / 256 * 256;
+}
+
+int tcx_sm100_mailbox_create(int32_t world, void** mailbox, void* ipc_handle) {
+  clear_error();
+  if (world <= 0 || world > kMaxRanks) return invalid("mailbox world size must be in [1, 64]");
+  if (!mailbox || !ipc_handle) return invalid("missing mailbox output");
+  const size_t bytes = tcx_sm100_mailbox_bytes(world);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return launch_status("mailbox allocation");
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return launch_status("mailbox setup");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle is 64 bytes");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *mailbox = p;
+  return TCX_OK;
+}
+
+int tcx_sm100_mailbox_open(const void* ipc_handle, void** peer_mailbox) {
+  clear_error();
+  if (!ipc_handle || !peer_mailbox) return invalid("missing mailbox handle");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(peer_mailbox, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return launch_status("mailbox open (CUDA IPC)");
+  return TCX_OK;
+}
+
+int tcx_sm100_mailbox_close(void* peer_mailbox) {
+  clear_error();
+  if (!peer_mailbox) return TCX_OK;
+  if (cudaIpcCloseMemHandle(peer_mailbox) != cudaSuccess) return launch_status("mailbox close");
+  return TCX_OK;
+}
+
+int tcx_sm100_mailbox_free(void* mailbox) {
+  clear_error();
+  if (!mailbox) return TCX_OK;
+  if (cudaFree(mailbox) != cudaSuccess) return launch_status("mailbox free");
+  return TCX_OK;
+}
+
+int tcx_sm100_reduce_sharded(tcx_stream_t stream, int op, int dtype, const void* input, int64_t count,
+                             int64_t index_base, void* const* mailboxes, int32_t rank, int32_t world,
+                             uint64_t epoch, uint64_t wait_limit_ns, int64_t total_count, void* output,
+                             void* workspace, size_t workspace_bytes) {
+  clear_error();
+  if (!valid_reduce_op(op, dtype)) return invalid("unsupported sharded reduction op/dtype");
+  if (count <= 0) return invalid("sharded reduction requires a non-empty shard");
+  if (world <= 0 || world > kMaxRanks || rank < 0 || rank >= world) return invalid("rank / world out of range");
+  if (epoch == 0) return invalid("exchange epochs start at 1");
+  if (!mailboxes || !output) return invalid("missing mailboxes or output");
+  Mailboxes mb = {};
+  for (int r = 0; r < world; ++r) {
+    if (!mailboxes[r]) return invalid("missing mailbox");
+    mb.box[r] = static_cast<char*>(mailboxes[r]);
+  }
+  const Stage1Grid g = stage1_grid(1, count);
+  const size_t need = static_cast<size_t>(g.parts) * sizeof(tcx_partial);
+  if (!workspace || workspace_bytes < need) return invalid("reduction workspace is missing or too small");
+  if (g.chunk > INT32_MAX) return invalid("reduction chunk exceeds 2^31 elements");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto* parts = static_cast<tcx_partial*>(workspace);
+  const auto* x = static_cast<const uint32_t*>(input);
+  const bool fp = dtype == TCX_FLOAT32;
+  const int mode = out_mode(op);
+  const uint64_t limit = wait_limit_ns ? wait_limit_ns : kDefaultExchangeWaitNs;
+  int* err = device_error_word();
+  TimedLaunch timer("reduce_sharded", s);
+  switch (kind_of(op, dtype)) {
+    case kSumF:
+      launch_stage1<kSumF, true>(s, x, 1, count, index_base, parts, g);
+      reduce_stage2_exchange<kSumF><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+                                                      total_count, mode, output, err);
+      break;
+    case kSumI:
+      launch_stage1<kSumI, false>(s, x, 1, count, index_base, parts, g);
+      reduce_stage2_exchange<kSumI><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+                                                      total_count, mode, output, err);
+      break;
+    case kBestMax:
+      if (fp) launch_stage1<kBestMax, true>(s, x, 1, count, index_base, parts, g);
+      else launch_stage1<kBestMax, false>(s, x, 1, count, index_base, parts, g);
+      reduce_stage2_exchange<kBestMax><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
+                                                         limit, total_count, mode, output, err);
+      break;
+    default:
+      if (fp) launch_stage1<kBestMin, true>(s, x, 1, count, index_base, parts, g);
+      else launch_stage1<kBestMin, false>(s, x, 1, count, index_base, parts, g);
+      reduce_stage2_exchange<kBestMin><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
+                                                         limit, total_count, mode, output, err);
+      break;
+  }
+  return launch_status("sharded reduction");
 }
 
 int tcx_sm100_reduce_axes(tcx_stream_t stream, int op, int dtype, const void* input, void* output,

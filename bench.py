@@ -627,6 +627,35 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                   "host-to-device through tcx_sm100_copy_to_device"}
     del host_buf, back_buf, dev_buf, host_t, back_t
 
+    # the rest of the square matmul sweep (512 ... 4096; 8192 is
+    # the headline): per-rank replicas, device-resident, pre-pass included
+    for size in (512, 1024, 2048, 4096):
+        a = torch.rand(size, size, device="cuda", generator=g) * 2 - 1
+        b = torch.rand(size, size, device="cuda", generator=g) * 2 - 1
+
+        def st(a=a, b=b):
+            return ops.matmul(a, b)
+        st()
+        reps = max(5, steps) if size >= 2048 else 50
+        read_timer(lib)
+        lib.tcx_sm100_timer_enable(1)
+        ms = timer.run(st, reps, 3, sampler) / reps
+        lib.tcx_sm100_timer_enable(0)
+        kern = read_timer(lib)
+        fl = 2.0 * size ** 3
+        k_launches, k_ms = kern.get("gemm_tf32x3", (0, 0.0))
+        k_avg = timer.max_over_ranks(k_ms / max(k_launches, 1))
+        out[f"matmul_{size}^3"] = {
+            "value": world * fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "config": f"fp32 [{size},{size}] x [{size},{size}], U(-1,1), per-rank replica, split pre-pass + GEMM "
+                      "(+ split-K reduce when the tiles fill few SMs) per step",
+            "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()},
+            "roofline": {"bound": "tensor", "achieved": fl / (k_avg * 1e-3) / 1e12 if k_avg else None,
+                         "peak": peak_3x, "unit": "TFLOP/s",
+                         "frac": (fl / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
+                         "kernel": "gemm_tf32x3", "kernel_ms": k_avg}}
+        del a, b
+
     # batched matmul + fused bias + SiLU: [64, 2048, 2048]^2, batch sharded
     nb = 64 // world
     a = torch.rand(nb, 2048, 2048, device="cuda", generator=g) * 2 - 1

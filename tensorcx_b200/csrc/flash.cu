@@ -8,11 +8,13 @@
 //   warp 0      TMA producer: the item's Q (D/32 pairs of 128x32 hi/lo tiles), then per
 //               key block D/32 K hi/lo chunks (64x32) into a 2-deep ring and two Vᵀ
 //               hi/lo chunks (Dv x 32) into another.
-//   warp 1      MMA issuer, one block ahead of the softmax: S_j = Q·K_jᵀ into TMEM buffer
-//               j % 3 (three tcgen05.mma.kind::tf32 per 8-wide k step: lo·hi, hi·lo,
-//               hi·hi), then O += P_{j-1}·V_{j-1} with P read straight from TMEM as the A
-//               operand, again as three products. The softmax of block j overlaps the
-//               MMAs of block j+1.
+//   warp 1      S issuer, ahead of the softmax: S_j = Q·K_jᵀ into TMEM buffer j % 3
+//               (three tcgen05.mma.kind::tf32 per 8-wide k step: lo·hi, hi·lo, hi·hi).
+//   warp 6      P·V issuer: O += P_j·V_j once the softmax released P_j, with P read
+//               straight from TMEM as the A operand, again as three products. Two
+//               issuing threads keep the tensor pipe fed while either one waits on a
+//               barrier (each wait costs its thread a few hundred cycles); the softmax
+//               of block j overlaps the MMAs of blocks j+1 and j-1.
 //   warps 2-5   softmax, one thread per query row (its TMEM lane): row maximum of the
 //               scaled, causally masked scores (log2 domain), p = 2^(t - m), the row sum,
 //               and the hi/lo split of p written back over S with tcgen05.st. The
@@ -58,7 +60,7 @@ constexpr int kKStage = 2 * kKTile;          // 16 KB
 constexpr int kVTileMax = kMaxDv * kFC * 4;  // 16 KB at Dv = 128
 constexpr int kVStage = 2 * kVTileMax;       // 32 KB
 constexpr int kFlashSmem = kQBytes + kKStages * kKStage + kVStages * kVStage + 1024 + 256;
-constexpr int kFlashThreads = 192;
+constexpr int kFlashThreads = 224;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSBufs = 3;
 constexpr uint32_t kColO = 384;
@@ -134,8 +136,8 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   uint64_t* q_full = pv_done + kSBufs;           // the item's Q has landed
   uint64_t* q_empty = q_full + 1;                // the item's last S has read Q
   uint64_t* o_free = q_empty + 1;                // the item's O has been read out
-  uint64_t* drain = o_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_free + 1;                  // [2]: the S issuer's and the P·V issuer's MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -152,7 +154,8 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     mbar_init(smem_u32(q_full), 1);
     mbar_init(smem_u32(q_empty), 1);
     mbar_init(smem_u32(o_free), 4);
-    mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(&drain[0]), 1);
+    mbar_init(smem_u32(&drain[1]), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -243,53 +246,18 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // -------------------------------------------------------------- MMA issuer
+      // ---------------------------------------------------------- S = Q·Kᵀ issuer
       const uint32_t id_s = idesc_tf32(kFQ, kFK);
-      const uint32_t id_o = idesc_tf32(kFQ, a.dv);
-      const uint32_t d_o = tmem + kColO;
-      int64_t k_n = 0, v_n = 0, g = 0, local = 0;  // g: blocks issued by this CTA so far
+      int64_t k_n = 0, g = 0, local = 0;  // g: blocks issued by this CTA so far
       bool ok = true;
-      // O += P·V of global block `gb` (buffer gb % 3); `first` starts the accumulator
-      int64_t item = 0;
-      auto issue_pv = [&](int64_t gb, bool first) -> bool {
-        const int buf = static_cast<int>(gb % kSBufs);
-        if (!wait_bounded(smem_u32(&p_full[buf]), static_cast<uint32_t>((gb / kSBufs) & 1), abort_flag, a.err, 0x414))
-          return false;
-        // the item's first P·V overwrites O: the previous item's O must have been read out
-        if (first && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x411))
-          return false;
-        tc_fence_after();
-        const uint32_t p_hi = tmem + static_cast<uint32_t>(buf * 128), p_lo = p_hi + kFK;
-        for (int c = 0; c < kFK / kFC; ++c, ++v_n) {
-          const int s = static_cast<int>(v_n % kVStages);
-          const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
-          if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x415)) return false;
-          tc_fence_after();
-          // descriptors built once per chunk; a k step adds 32 bytes (2 in the >> 4 field)
-          const uint64_t dv_hi = smem_desc_sw128(smem_u32(v_ring + s * kVStage));
-          const uint64_t dv_lo = smem_desc_sw128(smem_u32(v_ring + s * kVStage + kVTileMax));
-#pragma unroll
-          for (int kk = 0; kk < kFC / 8; ++kk) {
-            const uint32_t col = static_cast<uint32_t>(c * kFC + kk * 8);
-            const uint32_t acc = (first && c == 0 && kk == 0) ? 0u : 1u;
-            mma_tf32_ta(d_o, p_lo + col, dv_hi + 2 * kk, id_o, acc);
-            mma_tf32_ta(d_o, p_hi + col, dv_lo + 2 * kk, id_o, 1u);
-            mma_tf32_ta(d_o, p_hi + col, dv_hi + 2 * kk, id_o, 1u);
-          }
-          mma_commit(smem_u32(&v_empty[s]));
-        }
-        mma_commit(smem_u32(&pv_done[buf]));
-        return true;
-      };
       for (int64_t r = 0; r * gridDim.x < items && ok; ++r) {
         const int64_t w = snake_item(r, items);
         if (w < 0) continue;
         int64_t b; int qt, nkb;
         item_coords(a, w, b, qt, nkb);
         if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x410)) break;
-        item = local++;
+        ++local;
         tc_fence_after();
-        const int64_t g0 = g;
         for (int j = 0; j < nkb && ok; ++j, ++g) {
           const int buf = static_cast<int>(g % kSBufs);
           if (g >= kSBufs) {  // S overwrites the buffer's previous P: that block's P·V must be done
@@ -319,9 +287,58 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
           if (!ok) break;
           mma_commit(smem_u32(&s_full[buf]));
           if (j == nkb - 1) mma_commit(smem_u32(q_empty));  // the item's Q is no longer read
-          if (j >= 1 && !issue_pv(g - 1, j == 1)) { ok = false; break; }
         }
-        if (ok && nkb >= 1 && !issue_pv(g0 + nkb - 1, nkb == 1)) ok = false;
+      }
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {
+      // ------------------------------------------------------ O += P·V issuer
+      // A second issuing thread: the tensor pipe takes its P·V products while the S
+      // issuer waits on the K ring, and the S products while this one waits on V or P.
+      const uint32_t id_o = idesc_tf32(kFQ, a.dv);
+      const uint32_t d_o = tmem + kColO;
+      int64_t v_n = 0, g = 0, local = 0;
+      bool ok = true;
+      for (int64_t r = 0; r * gridDim.x < items && ok; ++r) {
+        const int64_t w = snake_item(r, items);
+        if (w < 0) continue;
+        int64_t b; int qt, nkb;
+        item_coords(a, w, b, qt, nkb);
+        const int64_t item = local++;
+        for (int j = 0; j < nkb && ok; ++j, ++g) {
+          const int buf = static_cast<int>(g % kSBufs);
+          if (!wait_bounded(smem_u32(&p_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x414)) {
+            ok = false;
+            break;
+          }
+          // the item's first P·V overwrites O: the previous item's O must have been read out
+          if (j == 0 && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x411)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_hi = tmem + static_cast<uint32_t>(buf * 128), p_lo = p_hi + kFK;
+          for (int c = 0; c < kFK / kFC && ok; ++c, ++v_n) {
+            const int s = static_cast<int>(v_n % kVStages);
+            const uint32_t ph = static_cast<uint32_t>((v_n / kVStages) & 1);
+            if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x415)) { ok = false; break; }
+            tc_fence_after();
+            // descriptors built once per chunk; a k step adds 32 bytes (2 in the >> 4 field)
+            const uint64_t dv_hi = smem_desc_sw128(smem_u32(v_ring + s * kVStage));
+            const uint64_t dv_lo = smem_desc_sw128(smem_u32(v_ring + s * kVStage + kVTileMax));
+#pragma unroll
+            for (int kk = 0; kk < kFC / 8; ++kk) {
+              const uint32_t col = static_cast<uint32_t>(c * kFC + kk * 8);
+              const uint32_t acc = (j == 0 && c == 0 && kk == 0) ? 0u : 1u;
+              mma_tf32_ta(d_o, p_lo + col, dv_hi + 2 * kk, id_o, acc);
+              mma_tf32_ta(d_o, p_hi + col, dv_lo + 2 * kk, id_o, 1u);
+              mma_tf32_ta(d_o, p_hi + col, dv_hi + 2 * kk, id_o, 1u);
+            }
+            mma_commit(smem_u32(&v_empty[s]));
+          }
+          if (!ok) break;
+          mma_commit(smem_u32(&pv_done[buf]));
+        }
       }
     }
   } else {
@@ -449,15 +466,17 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     }
   }
 
+  // every MMA either issuer started completes before TMEM is released
+  if ((warp == 1 || warp == 6) && lane == 0) {
+    uint64_t* d = &drain[warp == 1 ? 0 : 1];
+    mma_commit(smem_u32(d));
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(smem_u32(d), 0))
+      if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4fe); break; }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    if (lane == 0) {
-      mma_commit(smem_u32(drain));  // every issued MMA completes before TMEM is released
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(smem_u32(drain), 0))
-        if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4fe); break; }
-    }
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");

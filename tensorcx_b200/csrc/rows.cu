@@ -153,11 +153,11 @@ row_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t rows, i
       }
     }
     const float first = OP == kLayer ? __ldg(xr) : 0.0f;
-    auto col = [&](int q) -> bool {
+    auto valid = [&](int q) -> bool {
       if (FULL) return true;
       return VEC ? tid + (q >> 2) * THREADS < n4 : tid + q * THREADS < n32;
     };
-    row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
+    row_math<OP, THREADS, E>(v, valid, n, first, eps, smem);
     if (VEC) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
@@ -231,8 +231,8 @@ row_staged_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t 
       issue(row + gridDim.x);
     }
     const float first = OP == kLayer ? __ldg(x + row * n) : 0.0f;
-    auto col = [&](int q) -> bool { return tid + (q >> 2) * THREADS < n4; };
-    row_math<OP, THREADS, E>(v, col, n, first, eps, smem);
+    auto valid = [&](int q) -> bool { return tid + (q >> 2) * THREADS < n4; };
+    row_math<OP, THREADS, E>(v, valid, n, first, eps, smem);
     float* orow = out + row * n;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {

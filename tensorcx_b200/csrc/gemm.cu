@@ -88,17 +88,18 @@ __device__ __forceinline__ float4 ldg_f4(const float* p) {
 // A flat grid-stride walk over 4-wide K chunks of all rows; each thread issues 4
 // independent 128-bit loads before converting (VEC: K % 4 == 0, 16-byte aligned A),
 // so enough bytes are in flight per SM to run at HBM speed.
+// The body runs as block `bid` of `nblk` (a kernel of its own, or part of split_pair).
 template <bool VEC>
-__global__ void __launch_bounds__(256)
-split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows, int64_t k,
-           int64_t kp, int* __restrict__ nonfinite) {
+__device__ __forceinline__ void split_rows_body(const float* __restrict__ a, float* __restrict__ w, int64_t nb,
+                                                int64_t rows, int64_t k, int64_t kp, int* __restrict__ nonfinite,
+                                                int64_t bid, int64_t nblk) {
   constexpr int U = 4;
   const int64_t plane = rows * kp;
   const int64_t kq = kp >> 2;                // 4-wide chunks per row
   const int64_t total = nb * rows * kq;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t stride = nblk * blockDim.x;
   bool bad = false;
-  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+  for (int64_t base = bid * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
        base += stride * U) {
     float4 x[U];
     int64_t row[U], c[U];
@@ -137,20 +138,27 @@ split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
 }
 
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows, int64_t k,
+           int64_t kp, int* __restrict__ nonfinite) {
+  split_rows_body<VEC>(a, w, nb, rows, k, kp, nonfinite, blockIdx.x, gridDim.x);
+}
+
 // B [nb][K][N] -> W [2*nb][N][Kp] (transposed to K-major, zero padded in K).
 // A CTA moves a 32 (k) x 128 (n) tile: coalesced 128-bit loads along n (VEC: N % 4 == 0
 // and 16-byte aligned B), scalar shared-memory transpose (pitch 129: conflict-free
 // reads), 128-bit stores along k.
 template <bool VEC>
-__global__ void __launch_bounds__(256)
-split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k, int64_t n,
-           int64_t kp, int* __restrict__ nonfinite) {
+__device__ __forceinline__ void split_cols_body(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb,
+                                                int64_t k, int64_t n, int64_t kp, int* __restrict__ nonfinite,
+                                                int64_t bid, int64_t nblk) {
   __shared__ float tile[32][129];
   const int64_t plane = n * kp;
   const int64_t tiles_n = (n + 127) / 128, tiles_k = kp / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   bool bad = false;
-  for (int64_t t = blockIdx.x; t < nb * tiles_n * tiles_k; t += gridDim.x) {
+  for (int64_t t = bid; t < nb * tiles_n * tiles_k; t += nblk) {
     const int64_t b = t / (tiles_n * tiles_k), rem = t % (tiles_n * tiles_k);
     const int64_t n0 = (rem % tiles_n) * 128, k0 = (rem / tiles_n) * 32;
     const float* src = bsrc + b * k * n;
@@ -195,6 +203,29 @@ split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, in
     __syncthreads();
   }
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k, int64_t n,
+           int64_t kp, int* __restrict__ nonfinite) {
+  split_cols_body<VEC>(bsrc, w, nb, k, n, kp, nonfinite, blockIdx.x, gridDim.x);
+}
+
+// Both operands' pre-passes in one launch: blocks [0, ga) split A's rows, the others B
+// (a row split when B is K-major, else the transposing split).
+template <bool VA, bool BK, bool VB>
+__global__ void __launch_bounds__(256)
+split_pair(const float* __restrict__ a, float* __restrict__ wa, int64_t nba, int64_t m, const float* __restrict__ b,
+           float* __restrict__ wb, int64_t nbb, int64_t n, int64_t k, int64_t kp, int* __restrict__ nonfinite,
+           int ga) {
+  if (static_cast<int>(blockIdx.x) < ga) {
+    split_rows_body<VA>(a, wa, nba, m, k, kp, nonfinite, blockIdx.x, ga);
+  } else if (BK) {
+    split_rows_body<VB>(b, wb, nbb, n, k, kp, nonfinite, blockIdx.x - ga, gridDim.x - ga);
+  } else {
+    split_cols_body<VB>(b, wb, nbb, k, n, kp, nonfinite, blockIdx.x - ga, gridDim.x - ga);
+  }
 }
 
 // ------------------------------------------------------------ tcgen05 GEMM
@@ -742,14 +773,27 @@ gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float
 }
 
 // Split-K epilogue: out = act(sum over splits, in split order, of the raw partial
-// tiles + bias). Idle when the pre-pass flagged inf / NaN (the FFMA fallback queued
-// behind it writes the output). VEC: n % 4 == 0 and 16-byte aligned buffers.
+// tiles + bias). When the pre-pass flagged inf / NaN the tensor-core kernel left no
+// partials, and this kernel computes the IEEE product instead: every output element
+// accumulates a[row, kk] * b[kk, col] with fmaf in ascending kk, as the FFMA fallback
+// kernel does, so the split-K path needs no separate fallback launch.
+// VEC: n % 4 == 0 and 16-byte aligned buffers.
 template <bool VEC>
 __global__ void __launch_bounds__(256)
 splitk_reduce(const float* __restrict__ partial, float* __restrict__ out, int64_t mn, int64_t n, int splits,
-              const float* __restrict__ bias, int act, const int* __restrict__ nonfinite) {
-  if (*nonfinite) return;
+              const float* __restrict__ bias, int act, const int* __restrict__ nonfinite,
+              const float* __restrict__ lhs, const float* __restrict__ rhs, int64_t k, int rhs_kmajor) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (*nonfinite) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < mn; i += stride) {
+      const int64_t r = i / n, c = i - r * n;
+      float acc = 0.0f;
+      for (int64_t kk = 0; kk < k; ++kk)
+        acc = fmaf(__ldg(lhs + r * k + kk), __ldg(rhs_kmajor ? rhs + c * k + kk : rhs + kk * n + c), acc);
+      out[i] = epilogue_op(acc, bias, c, act);
+    }
+    return;
+  }
   if (VEC) {
     for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4; i < mn; i += stride * 4) {
       float4 v = __ldcs(reinterpret_cast<const float4*>(partial + i));
@@ -938,6 +982,25 @@ void split_a(cudaStream_t s, const float* lhs, float* wa, int64_t nba, int64_t m
   else split_rows<false><<<grid_a, 256, 0, s>>>(lhs, wa, nba, m, k, kp, flag);
 }
 
+// Both pre-passes (split_a's and split_b's work) in one launch.
+void split_both(cudaStream_t s, const float* lhs, float* wa, int64_t nba, int64_t m, const float* rhs, float* wb,
+                int64_t nbb, int64_t n, int64_t k, int64_t kp, int* flag, bool kmajor, int sms) {
+  const bool va = k % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0;
+  const bool vb = (kmajor ? k : n) % 4 == 0 && reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+  const int ga = static_cast<int>(std::min<int64_t>(ceil_div(nba * m * (kp / 4), 256 * 4), 16LL * sms));
+  const int64_t b_work = kmajor ? ceil_div(nbb * n * (kp / 4), 256 * 4) : nbb * ceil_div(n, 128) * (kp / 32);
+  const int gb = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b_work, 16LL * sms)));
+  TimedLaunch timer("split_pair", s);
+  auto go = [&](auto kernel) { kernel<<<ga + gb, 256, 0, s>>>(lhs, wa, nba, m, rhs, wb, nbb, n, k, kp, flag, ga); };
+  if (kmajor) {
+    if (va) { if (vb) go(split_pair<true, true, true>); else go(split_pair<true, true, false>); }
+    else { if (vb) go(split_pair<false, true, true>); else go(split_pair<false, true, false>); }
+  } else {
+    if (va) { if (vb) go(split_pair<true, false, true>); else go(split_pair<true, false, false>); }
+    else { if (vb) go(split_pair<false, false, true>); else go(split_pair<false, false, false>); }
+  }
+}
+
 // Split pre-pass of the right operand into K-major planes [2 * nbb, n, kp]: a row split
 // when it is already K-major ([n][k], a linear weight or key matrix), else a transpose.
 void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n, int64_t k, int64_t kp, int* flag,
@@ -1031,9 +1094,14 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
                      reinterpret_cast<uintptr_t>(partial) % 16 == 0;
     const int grid = static_cast<int>(std::min<int64_t>(ceil_div(vec ? mn / 4 : mn, 256), 4LL * sms));
     TimedLaunch timer("splitk_reduce", s);
-    if (vec) splitk_reduce<true><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag);
-    else splitk_reduce<false><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag);
-    if (int st = launch_status("split-K reduce")) return st;
+    if (vec)
+      splitk_reduce<true><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs, k,
+                                               rhs_kmajor ? 1 : 0);
+    else
+      splitk_reduce<false><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs, k,
+                                                rhs_kmajor ? 1 : 0);
+    // the reduce kernel computes the IEEE product itself when the pre-pass saw inf / NaN
+    return launch_status("split-K reduce");
   }
   // IEEE fallback for inputs with inf/NaN (idle unless the pre-pass raised the flag)
   const int64_t ftiles = batches * ceil_div(m, kFM) * ceil_div(n, kFN);
@@ -1114,8 +1182,7 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   if (2 * std::max(nba, nbb) > INT32_MAX) return invalid("too many operand batches for the tensor path");
 
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
-  split_a(s, lhs, wa, nba, m, k, lay.kp, flag, sms);
-  split_b(s, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
+  split_both(s, lhs, wa, nba, m, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
   if (int st = launch_status("matmul split pre-pass")) return st;
   float* partial = lay.splits > 1 ? reinterpret_cast<float*>(ws + lay.off_partial) : nullptr;
   return gemm_planes(s, wa, wb, nba, nbb, m, n, k, lay.kp, batches, bm, output, bias, act, flag, lhs, rhs,

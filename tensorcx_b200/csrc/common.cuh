@@ -104,6 +104,10 @@ int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* o
 // (box {32, box_rows, 1}, 128-byte swizzle) over such planes; `map` is a CUtensorMap*.
 void split_rows_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t rows, int64_t k,
                        int64_t kp, int* flag);
+// Two row splits with the same K in one launch (x1 and x2 as split_rows_planes).
+void split_rows_planes2(cudaStream_t s, const float* x1, float* planes1, int64_t nb1, int64_t rows1,
+                        const float* x2, float* planes2, int64_t nb2, int64_t rows2, int64_t k, int64_t kp,
+                        int* flag);
 void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t k, int64_t n,
                        int64_t kp, int* flag);
 bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows);

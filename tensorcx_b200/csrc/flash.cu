@@ -611,8 +611,7 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   float* wv = reinterpret_cast<float*>(ws + lay.off_v);
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("attention flag reset");
   // K-major split planes: Q [2nq][L][d], K [2nk][S][d] (rows already K-major), Vᵀ [2nv][dv][Sp]
-  split_rows_planes(s, q, wq, nq, L, d, d, flag);
-  split_rows_planes(s, k, wk, nk, S, d, d, flag);
+  split_rows_planes2(s, q, wq, nq, L, k, wk, nk, S, d, d, flag);
   split_cols_planes(s, v, wv, nv, S, dv, lay.sp, flag);
   if (int st = launch_status("attention split pre-pass")) return st;
 

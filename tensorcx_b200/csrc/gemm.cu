@@ -486,33 +486,6 @@ constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256;
 constexpr uint32_t kIdesc2 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
                              (static_cast<uint32_t>(256 >> 4) << 24);
 
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrives on the mbarrier at shared::cluster address `bar` once the pair's MMAs issued
-// so far have completed.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-// Tile load into this CTA's shared memory whose completion is counted on the mbarrier
-// at shared::cluster address `bar` (the leader's).
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
-                                                 int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const GemmArgs g) {
@@ -1399,6 +1372,11 @@ namespace tcx {
 void split_rows_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t rows, int64_t k,
                        int64_t kp, int* flag) {
   split_a(s, x, planes, nb, rows, k, kp, flag, sm_count());
+}
+void split_rows_planes2(cudaStream_t s, const float* x1, float* planes1, int64_t nb1, int64_t rows1,
+                        const float* x2, float* planes2, int64_t nb2, int64_t rows2, int64_t k, int64_t kp,
+                        int* flag) {
+  split_both(s, x1, planes1, nb1, rows1, x2, planes2, nb2, rows2, k, kp, flag, true, sm_count());
 }
 void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t k, int64_t n,
                        int64_t kp, int* flag) {

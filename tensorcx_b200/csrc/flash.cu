@@ -82,6 +82,7 @@ struct FlashArgs {
   int32_t q_tiles, kv_blocks;
   float scale_log2;        // scale * log2(e)
   int32_t causal;
+  int32_t vec8;            // out is 32-byte aligned: 32-byte stores
   float* out;              // [batches, L, dv]
   const int* nonfinite;
   int* err;
@@ -449,14 +450,19 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         TCX_LD32(rr, tmem + lane_base + kColO + cc);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (row_ok) {
+          float v[32];
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 v;
-            v.x = __fmul_rn(__uint_as_float(rr[e + 0]), inv);
-            v.y = __fmul_rn(__uint_as_float(rr[e + 1]), inv);
-            v.z = __fmul_rn(__uint_as_float(rr[e + 2]), inv);
-            v.w = __fmul_rn(__uint_as_float(rr[e + 3]), inv);
-            *reinterpret_cast<float4*>(orow + cc + e) = v;
+          for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(rr[e]), inv);
+          // each thread writes its own row: whole 32-byte sectors per store when the
+          // output allows, instead of half sectors
+          if (a.vec8) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8)
+              st_global_v8(orow + cc + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(orow + cc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
           }
         }
       }
@@ -633,6 +639,7 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   fa.scale_log2 = scale * kLog2e;
   fa.causal = causal;
   fa.out = out;
+  fa.vec8 = reinterpret_cast<uintptr_t>(out) % 32 == 0;
   fa.nonfinite = flag;
   fa.err = device_error_word();
   const int64_t items = batches * fa.q_tiles;

@@ -233,9 +233,11 @@ constexpr int kBM = 128, kBN = 256, kBK = 32, kStages = 2;
 constexpr int kTileA = kBM * kBK * 4;                   // 16 KB
 constexpr int kTileB = kBN * kBK * 4;                   // 32 KB
 constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;    // 96 KB
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kTmemCols = 2 * kBN;                      // two accumulators
-constexpr int kGemmSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kEpiWarps = 8;
+constexpr int kStoreStage = kEpiWarps * 32 * 32 * 4;     // 32 KB: a 32 x 32 staging block per epilogue warp
+constexpr int kGemmSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStoreStage;
 constexpr int kGroupM = 8;
 
 // Instruction descriptor: kind::tf32, D f32, A/B tf32, both K-major, M=128, N=256.
@@ -280,6 +282,92 @@ __device__ __forceinline__ void tile_coords(int64_t t, const GemmArgs& g, int64_
   nt = static_cast<int>(in_group / gsize);
 }
 
+// Stores one epilogue warp's 32 x 32 block of the output (lane = row, v = 32 consecutive
+// columns of that row) through a 4 KB slice of shared memory, so that each global store
+// instruction writes four whole 128-byte row segments instead of 32 half-used sectors
+// of 32 different rows (writing rows straight from the TMEM lane layout held the
+// epilogue of a 128 x 256 tile at ~10 GB/s per SM). Float4 chunks are XOR-swizzled by
+// row: conflict-free both ways. `tile` points at the block's (row 0, column 0); rows
+// >= rows_valid and columns >= cols_valid are not written; vec: 16-byte stores allowed
+// (the row pitch and base are 16-byte aligned).
+__device__ __forceinline__ void store_block_staged(float4* stage, const float (&v)[32], int lane, float* tile,
+                                                   int64_t ld, int rows_valid, int64_t cols_valid, bool vec) {
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj)
+    stage[lane * 8 + (jj ^ (lane & 7))] = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+  __syncwarp();
+  const int jj = lane & 7;
+  const int64_t cv = cols_valid - 4 * jj;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = 4 * i + (lane >> 3);
+    const float4 x = stage[rr * 8 + (jj ^ (rr & 7))];
+    if (rr < rows_valid && cv > 0) {
+      float* p = tile + rr * ld + 4 * jj;
+      if (vec && cv >= 4) {
+        *reinterpret_cast<float4*>(p) = x;
+      } else {
+        p[0] = x.x;
+        if (cv > 1) p[1] = x.y;
+        if (cv > 2) p[2] = x.z;
+        if (cv > 3) p[3] = x.w;
+      }
+    }
+  }
+  __syncwarp();  // the slice is rewritten by the next block
+}
+
+// Waits for this warp's outstanding tcgen05.ld and ties the 32 destination registers
+// to the wait, so that no use of them is scheduled before it.
+#define TCX_WAIT_LD32(r)                                                                          \
+  asm volatile("tcgen05.wait::ld.sync.aligned;"                                                   \
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), \
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),          \
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),       \
+                 "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),       \
+                 "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),       \
+                 "+r"(r[31])                                                                      \
+               :                                                                                  \
+               : "memory")
+
+// One epilogue warp's share of an accumulator tile: TMEM lanes [32 q, 32 q + 32) (the
+// quarter the warp may access) x 128 columns starting at TMEM column `tcol` and output
+// column `col0`, as four 32-column chunks with the next chunk's tcgen05.ld in flight
+// while the current one is finished and stored. `release` runs once every TMEM read of
+// the share is done. `block` points at output (row 0, column 0) of the share.
+template <typename Release>
+__device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int lane, float* block, int64_t ld,
+                                            int rows_valid, int64_t cols_left, int64_t col0, const float* bias,
+                                            int act, bool vec, bool skip, Release release) {
+  const bool plain = bias == nullptr && act == TCX_ACT_NONE;
+  uint32_t r0[32], r1[32];
+  TCX_LD32(r0, tcol);
+#pragma unroll
+  for (int ci = 0; ci < 4; ++ci) {
+    uint32_t (&cur)[32] = (ci & 1) ? r1 : r0;
+    uint32_t (&nxt)[32] = (ci & 1) ? r0 : r1;
+    TCX_WAIT_LD32(cur);
+    if (ci + 1 < 4) {
+      TCX_LD32(nxt, tcol + static_cast<uint32_t>((ci + 1) * 32));
+    } else {
+      release();
+    }
+    const int64_t left = cols_left - ci * 32;
+    if (left > 0 && rows_valid > 0 && !skip) {
+      float v[32];
+      if (plain) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
+      } else {
+        const int64_t c = col0 + ci * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = j < left ? epilogue_op(__uint_as_float(cur[j]), bias, c + j, act) : 0.0f;
+      }
+      store_block_staged(stage, v, lane, block + ci * 32, ld, rows_valid, left, vec);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const GemmArgs g) {
@@ -294,11 +382,12 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   uint64_t* drain = bars + 2 * kStages + 4;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float4* stage = reinterpret_cast<float4*>(smem + kStages * kStageBytes + 256) + ((threadIdx.x >> 5) - 2) * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 4); }
+    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), kEpiWarps); }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -393,7 +482,10 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
     }
   } else {
     // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Eight warps, two per SM sub-partition: warp w drains TMEM lane quarter w & 3 (the
+    // lanes it may access), columns [0, 128) for warps 2-5 and [128, 256) for 6-9.
+    const int q = warp & 3;
+    const int part = warp >= 6 ? 1 : 0;
     int64_t local = 0;
     for (int64_t t = blockIdx.x; t < total_work; t += gridDim.x, ++local) {
       const int acc = static_cast<int>(local & 1);
@@ -404,47 +496,22 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       split_range(t, g, tile, split, kb0, kb1);
       int64_t batch; int mt, nt;
       tile_coords(tile, g, batch, mt, nt);
-      const int64_t row = static_cast<int64_t>(mt) * kBM + q * 32 + lane;
-      const int64_t col0 = static_cast<int64_t>(nt) * kBN;
+      const int64_t row0 = static_cast<int64_t>(mt) * kBM + q * 32;  // this warp's first row
+      const int64_t col0 = static_cast<int64_t>(nt) * kBN + part * 128;
       // split-K: the raw partial sums go to this split's slice of the workspace
       const bool raw = g.splits > 1;
-      float* crow = raw ? g.partial + (static_cast<int64_t>(split) * g.m + row) * g.n
-                        : g.c + (batch * g.m + row) * g.n;
-      const float* bias = raw ? nullptr : g.bias;
-      const int act = raw ? TCX_ACT_NONE : g.act;
-      const bool row_ok = row < g.m;
-      const bool vec = g.vec_store != 0;
-#pragma unroll 1
-      for (int cc = 0; cc < kBN; cc += 32) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN + cc);
-        TCX_LD32(r, taddr);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (cc + 32 >= kBN) {
-          // all TMEM reads of this accumulator are done: hand it back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
-        }
-        if (row_ok && !*abort_flag) {
-          const int64_t c = col0 + cc;
-          if (vec && c + 32 <= g.n) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v;
-              v.x = epilogue_op(__uint_as_float(r[j + 0]), bias, c + j + 0, act);
-              v.y = epilogue_op(__uint_as_float(r[j + 1]), bias, c + j + 1, act);
-              v.z = epilogue_op(__uint_as_float(r[j + 2]), bias, c + j + 2, act);
-              v.w = epilogue_op(__uint_as_float(r[j + 3]), bias, c + j + 3, act);
-              *reinterpret_cast<float4*>(crow + c + j) = v;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), bias, c + j, act);
-          }
-        }
-      }
+      float* block = (raw ? g.partial + (static_cast<int64_t>(split) * g.m + row0) * g.n
+                          : g.c + (batch * g.m + row0) * g.n) + col0;
+      const int rows_valid = static_cast<int>(g.m - row0 < 32 ? g.m - row0 : 32);
+      const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * kBN + part * 128);
+      drain_share(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, raw ? nullptr : g.bias,
+                  raw ? TCX_ACT_NONE : g.act, g.vec_store != 0, *abort_flag != 0, [&] {
+                    // all TMEM reads of this accumulator are done: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+                  });
     }
   }
 
@@ -482,7 +549,7 @@ constexpr int kStages2 = 3;
 constexpr int kHalf = 128;                                  // rows of A and of B per CTA
 constexpr int kTile2 = kHalf * kBK * 4;                     // 16 KB
 constexpr int kStage2Bytes = 4 * kTile2;                    // A hi/lo, B hi/lo: 64 KB
-constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256;
+constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256 + kStoreStage;
 constexpr uint32_t kIdesc2 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
                              (static_cast<uint32_t>(256 >> 4) << 24);
 
@@ -501,13 +568,14 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
   uint64_t* drain = bars + 2 * kStages2 + 4;      // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float4* stage = reinterpret_cast<float4*>(smem + kStages2 * kStage2Bytes + 256) + ((threadIdx.x >> 5) - 2) * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages2; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 8); }
+    for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 2 * kEpiWarps); }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -604,7 +672,10 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
     }
   } else {
     // ------------------------------------------------------ epilogue (both CTAs)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Eight warps per CTA as in the single-SM kernel: lane quarter w & 3, columns
+    // [0, 128) for warps 2-5 and [128, 256) for 6-9.
+    const int q = warp & 3;
+    const int part = warp >= 6 ? 1 : 0;
     int64_t local = 0;
     for (int64_t t = cid; t < total_tiles; t += ncl, ++local) {
       const int acc = static_cast<int>(local & 1);
@@ -613,42 +684,19 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
       tc_fence_after();
       int64_t batch; int mt, nt;
       tile_coords(t, g, batch, mt, nt);
-      const int64_t row = static_cast<int64_t>(mt) * 2 * kHalf + static_cast<int64_t>(rank) * kHalf + q * 32 + lane;
-      const int64_t col0 = static_cast<int64_t>(nt) * kBN;
-      float* crow = g.c + (batch * g.m + row) * g.n;
-      const bool row_ok = row < g.m;
-      const bool vec = g.vec_store != 0;
-#pragma unroll 1
-      for (int cc = 0; cc < kBN; cc += 32) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN + cc);
-        TCX_LD32(r, taddr);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (cc + 32 >= kBN) {
-          // all TMEM reads of this accumulator are done: tell the leader's MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&acc_empty[acc]), 0));
-        }
-        if (row_ok && !*abort_flag) {
-          const int64_t c = col0 + cc;
-          if (vec && c + 32 <= g.n) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v;
-              v.x = epilogue_op(__uint_as_float(r[j + 0]), g.bias, c + j + 0, g.act);
-              v.y = epilogue_op(__uint_as_float(r[j + 1]), g.bias, c + j + 1, g.act);
-              v.z = epilogue_op(__uint_as_float(r[j + 2]), g.bias, c + j + 2, g.act);
-              v.w = epilogue_op(__uint_as_float(r[j + 3]), g.bias, c + j + 3, g.act);
-              *reinterpret_cast<float4*>(crow + c + j) = v;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c + j < g.n) crow[c + j] = epilogue_op(__uint_as_float(r[j]), g.bias, c + j, g.act);
-          }
-        }
-      }
+      const int64_t row0 = static_cast<int64_t>(mt) * 2 * kHalf + static_cast<int64_t>(rank) * kHalf + q * 32;
+      const int64_t col0 = static_cast<int64_t>(nt) * kBN + part * 128;
+      float* block = g.c + (batch * g.m + row0) * g.n + col0;
+      const int rows_valid = static_cast<int>(g.m - row0 < 32 ? g.m - row0 : 32);
+      const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * kBN + part * 128);
+      drain_share(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, g.bias, g.act, g.vec_store != 0,
+                  *abort_flag != 0, [&] {
+                    // all TMEM reads of this accumulator are done: tell the leader's MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&acc_empty[acc]), 0));
+                  });
     }
   }
 

@@ -226,6 +226,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// 32-byte global store (sm_100): one whole sector per thread; p 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(float* p, float a0, float a1, float a2, float a3, float a4, float a5,
+                                             float a6, float a7) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(a0), "f"(a1), "f"(a2),
+               "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7)
+               : "memory");
+}
+
 // Round to TF32 (nearest, ties away), the hi half of a 3xTF32 split.
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;

@@ -12,9 +12,12 @@
 //        warp 1      MMA issuer: per 8-wide k step, three tcgen05.mma.kind::tf32
 //                    (lo*hi, hi*lo, hi*hi) into one float32 TMEM accumulator;
 //                    tcgen05.commit releases the stage / publishes the accumulator;
-//        warps 2-5   epilogue: tcgen05.ld 32x32b from TMEM, bias + activation,
-//                    float32 stores. Two TMEM accumulators (2 x 256 columns) let the
-//                    epilogue of tile t overlap the main loop of tile t+1.
+//        warps 2-9   epilogue, two warps per SM sub-partition (a warp may read only
+//                    its TMEM lane quarter; warps 2-5 take columns 0-127, 6-9 the
+//                    rest): tcgen05.ld 32x32b with the next chunk's load in flight,
+//                    bias + activation, and row-coalesced stores through a 4 KB
+//                    shared-memory slice per warp. Two TMEM accumulators (2 x 256
+//                    columns) let the epilogue of tile t overlap the main loop of t+1.
 //      No TMA multicast anywhere (this code also runs in multi-GPU jobs).
 //   3. If the pre-pass saw inf/NaN, the GEMM exits at once and the FFMA kernel
 //      (launched behind it, idle otherwise) computes the product with IEEE

@@ -645,10 +645,19 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         fl = 2.0 * size ** 3
         k_launches, k_ms = kern.get("gemm_tf32x3", (0, 0.0))
         k_avg = timer.max_over_ranks(k_ms / max(k_launches, 1))
+        graph_ms = None
+        if size <= 1024:  # latency-bound sizes: the same call replayed from a CUDA graph
+            from tensorcx_b200.graphs import CapturedSequence
+            seq = CapturedSequence(st)
+            graph_ms = timer.run(seq, 200, 5, sampler) / 200
+            seq.release()
         out[f"matmul_{size}^3"] = {
             "value": world * fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "graph_replay": None if graph_ms is None else {
+                "ms_per_step": graph_ms, "value": world * fl / (graph_ms * 1e-3) / 1e12},
             "config": f"fp32 [{size},{size}] x [{size},{size}], U(-1,1), per-rank replica, split pre-pass + GEMM "
-                      "(+ split-K reduce when the tiles fill few SMs) per step",
+                      "(+ split-K reduce when the tiles fill few SMs) per step, called from Python "
+                      "(graph_replay: the same call captured as a CUDA graph)",
             "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()},
             "roofline": {"bound": "tensor", "achieved": fl / (k_avg * 1e-3) / 1e12 if k_avg else None,
                          "peak": peak_3x, "unit": "TFLOP/s",
@@ -727,13 +736,21 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
     mlp()
     read_timer(lib)
     lib.tcx_sm100_timer_enable(1)
-    ms = timer.run(mlp, 50, 1, sampler) / 50
+    eager_ms = timer.run(mlp, 50, 1, sampler) / 50
     lib.tcx_sm100_timer_enable(0)
     kern = read_timer(lib)
+    # the same forward replayed as one CUDA graph (no host work per op)
+    from tensorcx_b200.graphs import CapturedSequence
+    seq = CapturedSequence(mlp)
+    ms = timer.run(seq, 200, 5, sampler) / 200
+    seq.release()
     out["mlp_256x784x512x10_latency"] = {
         "value": ms, "unit": "ms", "higher_is_better": False, "ms_per_step": ms,
+        "eager_ms": eager_ms,
         "config": "x[256,784] @ W1[784,512] + b1 -> ReLU (fused epilogue) -> @ W2[512,10] + b2 -> softmax; "
-                  "per-rank replica, stream-ordered launches, no host sync inside",
+                  "per-rank replica; value: the forward captured once as a CUDA graph "
+                  "(tensorcx_b200.graphs.CapturedSequence) and replayed back to back; eager_ms: the same ops "
+                  "called from Python, stream-ordered, no host sync inside",
         "gpu_launches_per_step": sum(c for c, _ in kern.values()) / 50,
         "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()}}
     return out

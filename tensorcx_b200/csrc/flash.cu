@@ -366,21 +366,29 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         tc_fence_after();
         const int64_t key0 = static_cast<int64_t>(j) * kFK;
         // keys allowed for this row in this block: [0, lim)
-        int64_t lim = a.S - key0;
-        if (a.causal) lim = min(lim, query - key0 + 1);
-        lim = lim < 0 ? 0 : (lim > kFK ? kFK : lim);
+        int64_t lim64 = a.S - key0;
+        if (a.causal) lim64 = min(lim64, query - key0 + 1);
+        const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kFK ? kFK : lim64));
+        // the block's 64 scores of this row, both halves loaded before one wait, kept in
+        // registers for both passes (one TMEM round trip per block), scaled to log2 units
+        uint32_t s0[32], s1[32];
+        TCX_LD32(s0, tmem + lane_base + col_s);
+        TCX_LD32(s1, tmem + lane_base + col_s + 32);
+        TCX_WAIT_LD32(s0);
+        TCX_TIE32(s1);
         // pass 1: the block's row maximum (log2 domain)
         float mx = -INFINITY;
-#pragma unroll 1
-        for (int cc = 0; cc < kFK; cc += 32) {
-          uint32_t rr[32];
-          TCX_LD32(rr, tmem + lane_base + col_s + cc);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float t = __fmul_rn(__uint_as_float(rr[e]), a.scale_log2);
-            if (cc + e < lim) mx = fmaxf(mx, t);
-          }
+        for (int e = 0; e < 32; ++e) {
+          const float t = __fmul_rn(__uint_as_float(s0[e]), a.scale_log2);
+          s0[e] = __float_as_uint(t);
+          if (e < lim) mx = fmaxf(mx, t);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float t = __fmul_rn(__uint_as_float(s1[e]), a.scale_log2);
+          s1[e] = __float_as_uint(t);
+          if (32 + e < lim) mx = fmaxf(mx, t);
         }
         // raise the running maximum only when p would exceed 2^8; rescale O then
         const bool need = mx > m_use + 8.0f;
@@ -410,26 +418,24 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
           }
         }
         // pass 2: p = 2^(t - m), the row sum, P_hi over S and P_lo beside it
-#pragma unroll 1
-        for (int cc = 0; cc < kFK; cc += 32) {
-          uint32_t rr[32], lo[32];
-          TCX_LD32(rr, tmem + lane_base + col_s + cc);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        auto emit = [&](uint32_t (&sv)[32], int c0) {
+          uint32_t lo[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float t = __fmul_rn(__uint_as_float(rr[e]), a.scale_log2);
             float p = 0.0f;
-            if (cc + e < lim) {
-              asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(t, m_use)));
+            if (c0 + e < lim) {
+              asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(__uint_as_float(sv[e]), m_use)));
             }
             l = __fadd_rn(l, p);
             const float hi = tf32_rna(p);
-            rr[e] = __float_as_uint(hi);
+            sv[e] = __float_as_uint(hi);
             lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
           }
-          TCX_ST32(tmem + lane_base + col_s + cc, rr);
-          TCX_ST32(tmem + lane_base + col_lo + cc, lo);
-        }
+          TCX_ST32(tmem + lane_base + col_s + c0, sv);
+          TCX_ST32(tmem + lane_base + col_lo + c0, lo);
+        };
+        emit(s0, 0);
+        emit(s1, 32);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
@@ -444,25 +450,32 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       const float inv = 1.0f / l;
       float* orow = a.out + (b * a.L + query) * a.dv;
       const bool row_ok = query < a.L;
-#pragma unroll 1
-      for (int cc = 0; cc < a.dv; cc += 32) {
-        uint32_t rr[32];
-        TCX_LD32(rr, tmem + lane_base + kColO + cc);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      // O drained in 32-column chunks with the next chunk's TMEM load in flight
+      const int nch = a.dv / 32;
+      uint32_t o0[32], o1[32];
+      TCX_LD32(o0, tmem + lane_base + kColO);
+#pragma unroll
+      for (int ci = 0; ci < kMaxDv / 32; ++ci) {
+        if (ci >= nch) break;
+        uint32_t (&cur)[32] = (ci & 1) ? o1 : o0;
+        uint32_t (&nxt)[32] = (ci & 1) ? o0 : o1;
+        TCX_WAIT_LD32(cur);
+        if (ci + 1 < nch) TCX_LD32(nxt, tmem + lane_base + kColO + static_cast<uint32_t>((ci + 1) * 32));
         if (row_ok) {
           float v[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(rr[e]), inv);
+          for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(cur[e]), inv);
           // each thread writes its own row: whole 32-byte sectors per store when the
           // output allows, instead of half sectors
+          float* dst = orow + ci * 32;
           if (a.vec8) {
 #pragma unroll
             for (int e = 0; e < 32; e += 8)
-              st_global_v8(orow + cc + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+              st_global_v8(dst + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
           } else {
 #pragma unroll
             for (int e = 0; e < 32; e += 4)
-              *reinterpret_cast<float4*>(orow + cc + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+              *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
           }
         }
       }

@@ -320,19 +320,6 @@ __device__ __forceinline__ void store_block_staged(float4* stage, const float (&
   __syncwarp();  // the slice is rewritten by the next block
 }
 
-// Waits for this warp's outstanding tcgen05.ld and ties the 32 destination registers
-// to the wait, so that no use of them is scheduled before it.
-#define TCX_WAIT_LD32(r)                                                                          \
-  asm volatile("tcgen05.wait::ld.sync.aligned;"                                                   \
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), \
-                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),          \
-                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),       \
-                 "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),       \
-                 "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),       \
-                 "+r"(r[31])                                                                      \
-               :                                                                                  \
-               : "memory")
-
 // One epilogue warp's share of an accumulator tile: TMEM lanes [32 q, 32 q + 32) (the
 // quarter the warp may access) x 128 columns starting at TMEM column `tcol` and output
 // column `col0`, as four 32-column chunks with the next chunk's tcgen05.ld in flight

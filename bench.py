@@ -468,8 +468,7 @@ def gpu_arm(args):
                                       f"/3 for 3xTF32 (MEASURED_PEAKS bf16 {pk.get('bf16_tflops')} TFLOP/s "
                                       f"{pk_note}; bf16/6 = {float(pk.get('bf16_tflops', 0)) / 6:.1f})"},
             "context": {"cublas_tf32_tflops": tf32_tflops, "cublas_fp32_sgemm_tflops": sgemm_tflops,
-                        "split_prepass_ms": (kernels.get("split_rows", (0, 0))[1] + kernels.get("split_cols", (0, 0))[1])
-                        / max(args.steps, 1)},
+                        "split_prepass_ms": kernels.get("split_pair", (0, 0.0))[1] / max(args.steps, 1)},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * size * size * 4,
                     "d2h_bytes_per_step": size * size * 4, "ms_per_step": e2e_ms,
                     "api": "tcx_sm100_matmul_host (pinned host A, B in; C out; synchronous)",
@@ -551,7 +550,8 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         peer = PeerReduction()
     combine = ("in the reduction kernel over NVLink peer memory" if peer else
                "NCCL all_gather + the combine kernel" if world > 1 else "the combine kernel")
-    for name, x, op in [("sum_f32_2^28", xf, "sum"), ("argmax_f32_2^28", xf, "argmax"),
+    for name, x, op in [("sum_f32_2^28", xf, "sum"), ("mean_f32_2^28", xf, "mean"), ("max_f32_2^28", xf, "max"),
+                        ("min_f32_2^28", xf, "min"), ("argmax_f32_2^28", xf, "argmax"),
                         ("sum_i32_2^28", xi, "sum"), ("max_i32_2^28", xi, "max")]:
         def st(x=x, op=op):
             if peer is not None:

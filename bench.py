@@ -468,7 +468,8 @@ def gpu_arm(args):
                                       f"/3 for 3xTF32 (MEASURED_PEAKS bf16 {pk.get('bf16_tflops')} TFLOP/s "
                                       f"{pk_note}; bf16/6 = {float(pk.get('bf16_tflops', 0)) / 6:.1f})"},
             "context": {"cublas_tf32_tflops": tf32_tflops, "cublas_fp32_sgemm_tflops": sgemm_tflops,
-                        "split_prepass_ms": kernels.get("split_pair", (0, 0.0))[1] / max(args.steps, 1)},
+                        "split_prepass_ms": sum(kernels.get(name, (0, 0.0))[1] for name in ("split_lo", "split_pair"))
+                        / max(args.steps, 1)},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 2 * size * size * 4,
                     "d2h_bytes_per_step": size * size * 4, "ms_per_step": e2e_ms,
                     "api": "tcx_sm100_matmul_host (pinned host A, B in; C out; synchronous)",

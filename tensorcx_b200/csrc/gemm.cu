@@ -6,6 +6,15 @@
 //      workspace ([plane][rows][Kp], planes hi/lo per operand batch, K padded with
 //      zeros to a multiple of 32). B is transposed on the way, so both operands are
 //      K-major. The pass also flags any inf/NaN input.
+//      Raw mode (tcx_sm100_matmul and tcx_sm100_matmul_host with a row-major B, K and N
+//      multiples of 4, 16-byte aligned operands): kind::tf32 reads fp32 words and drops
+//      their low 13 mantissa bits (measured on sm_100a), so the operands themselves
+//      are the hi terms, hi = trunc_tf32(x). The pre-pass (split_lo) then writes only
+//      lo = rna_tf32(x - trunc_tf32(x)), elementwise in each operand's own layout:
+//      8 B per element instead of 12, no transpose. The GEMM reads A K-major as
+//      before and B MN-major: 32-column chunks of 32 k rows (4 KB TMA boxes with the
+//      128-byte / 32-byte-atom swizzle, layout type 1 in the MMA descriptor; the plain
+//      128-byte swizzle gives zeros for MN-major tf32 operands).
 //   2. GEMM: a persistent, warp-specialized kernel, one CTA per SM:
 //        warp 0      TMA producer: 4 tiles per k-block (A hi/lo 128x32, B hi/lo 256x32,
 //                    128B-swizzled) into a 2-stage shared-memory ring (mbarriers);
@@ -85,6 +94,49 @@ __device__ __forceinline__ void split_one(float x, float& hi, float& lo, bool& b
 
 __device__ __forceinline__ float4 ldg_f4(const float* p) {
   return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+// lo term of the raw mode: the tensor core takes x itself as hi (it drops the low 13
+// mantissa bits), so lo = rna_tf32(x - trunc_tf32(x)); x - trunc_tf32(x) is exact.
+__device__ __forceinline__ float lo_one(float x, bool& bad) {
+  bad |= !isfinite(x);
+  return tf32_rna(__fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)));
+}
+
+// Raw-mode pre-pass of both operands in one launch: A [na4 float4s] -> wa and
+// B [nb4 float4s] -> wb elementwise, in place of layout (each operand's own); raises
+// *nonfinite on inf / NaN. Both operands 16-byte aligned with element counts that are
+// multiples of 4 (K % 4 == 0 and N % 4 == 0).
+__global__ void __launch_bounds__(256)
+split_lo(const float4* __restrict__ a, float4* __restrict__ wa, int64_t na4, const float4* __restrict__ b,
+         float4* __restrict__ wb, int64_t nb4, int* __restrict__ nonfinite) {
+  bool bad = false;
+  const int64_t total = na4 + nb4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // four independent 128-bit loads in flight per thread
+  for (; i + 3 * stride < total; i += 4 * stride) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = i + u * stride;
+      x[u] = __ldg(j < na4 ? a + j : b + (j - na4));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = i + u * stride;
+      const float4 l = make_float4(lo_one(x[u].x, bad), lo_one(x[u].y, bad), lo_one(x[u].z, bad), lo_one(x[u].w, bad));
+      if (j < na4) wa[j] = l;
+      else wb[j - na4] = l;
+    }
+  }
+  for (; i < total; i += stride) {
+    const float4 x = __ldg(i < na4 ? a + i : b + (i - na4));
+    const float4 l = make_float4(lo_one(x.x, bad), lo_one(x.y, bad), lo_one(x.z, bad), lo_one(x.w, bad));
+    if (i < na4) wa[i] = l;
+    else wb[i - na4] = l;
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
 }
 
 // A [nb][rows][K] -> W [2*nb][rows][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
@@ -247,6 +299,10 @@ constexpr int kGroupM = 8;
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
                             (static_cast<uint32_t>(kBM >> 4) << 24);
 
+// The same with B MN-major (bit 16), for the raw mode.
+constexpr uint32_t kIdescMN = kIdesc | (1u << 16);
+constexpr int kChunkB = 32 * kBK * 4;  // 4 KB: 32 columns of B x 32 k rows, one TMA box
+
 struct GemmArgs {
   float* c;
   const float* bias;
@@ -262,6 +318,11 @@ struct GemmArgs {
   // partial + (t % splits) * m * n, summed by splitk_reduce
   int32_t splits, kb_per_split;
   float* partial;
+  // raw (1): the hi terms are the operands themselves (tcgen05 kind::tf32 reads fp32
+  // and drops the low 13 mantissa bits: hi = trunc_tf32(x)); map_a / map_b then hold
+  // only lo = rna_tf32(x - trunc_tf32(x)) in the operands' own layouts, and B (hi and
+  // lo) is read MN-major in 32-column chunks. raw (0): split planes, both K-major.
+  int32_t raw;
 };
 
 // k-block range of work item t
@@ -360,6 +421,7 @@ __device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int la
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
                    const GemmArgs g) {
   if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
   extern __shared__ uint8_t smem_raw[];
@@ -416,10 +478,23 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
           const uint32_t fb = smem_u32(&full[s]);
           mbar_expect_tx(fb, kStageBytes);
           const int kc = kb * kBK;
-          tma_load_3d(smem_u32(st), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa));
-          tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa + 1));
-          tma_load_3d(smem_u32(st + 2 * kTileA), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb));
-          tma_load_3d(smem_u32(st + 2 * kTileA + kTileB), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb + 1));
+          if (g.raw) {
+            // A: raw rows (hi) and lo rows, K-major; B: raw (hi) and lo, each as kBN / 32
+            // MN-major chunks of 32 columns x 32 k rows (columns past N read as zeros)
+            tma_load_3d(smem_u32(st), &map_a_hi, fb, kc, mt * kBM, static_cast<int>(pa));
+            tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(pa));
+            for (int j = 0; j < kBN / 32; ++j) {
+              tma_load_3d(smem_u32(st + 2 * kTileA + j * kChunkB), &map_b_hi, fb, nt * kBN + 32 * j, kc,
+                          static_cast<int>(pb));
+              tma_load_3d(smem_u32(st + 2 * kTileA + kTileB + j * kChunkB), &map_b, fb, nt * kBN + 32 * j, kc,
+                          static_cast<int>(pb));
+            }
+          } else {
+            tma_load_3d(smem_u32(st), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa));
+            tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa + 1));
+            tma_load_3d(smem_u32(st + 2 * kTileA), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb));
+            tma_load_3d(smem_u32(st + 2 * kTileA + kTileB), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb + 1));
+          }
         }
       }
       // Drain: every stage this thread filled must have landed before the CTA exits.
@@ -457,13 +532,20 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
           const uint32_t a_lo = a_hi + kTileA;
           const uint32_t b_hi = a_hi + 2 * kTileA;
           const uint32_t b_lo = b_hi + kTileB;
+          const uint64_t da_hi = smem_desc_sw128(a_hi), da_lo = smem_desc_sw128(a_lo);
+          // 8 k per MMA: 32 bytes along a K-major row (2 in the >> 4 address field), or
+          // 8 rows of 128 bytes in an MN-major chunk (64)
+          const uint64_t db_hi = g.raw ? smem_desc_sw128_mn(b_hi, kChunkB) : smem_desc_sw128(b_hi);
+          const uint64_t db_lo = g.raw ? smem_desc_sw128_mn(b_lo, kChunkB) : smem_desc_sw128(b_lo);
+          const uint64_t b_step = g.raw ? 64u : 2u;
+          const uint32_t idesc = g.raw ? kIdescMN : kIdesc;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
             const uint32_t first = (kb == kb0 && kk == 0) ? 0u : 1u;
-            mma_tf32(d_tmem, smem_desc_sw128(a_lo + off), smem_desc_sw128(b_hi + off), kIdesc, first);
-            mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_lo + off), kIdesc, 1u);
-            mma_tf32(d_tmem, smem_desc_sw128(a_hi + off), smem_desc_sw128(b_hi + off), kIdesc, 1u);
+            const uint64_t ka = 2u * kk, kbo = b_step * kk;
+            mma_tf32(d_tmem, da_lo + ka, db_hi + kbo, idesc, first);
+            mma_tf32(d_tmem, da_hi + ka, db_lo + kbo, idesc, 1u);
+            mma_tf32(d_tmem, da_hi + ka, db_hi + kbo, idesc, 1u);
           }
           mma_commit(smem_u32(&empty[s]));  // stage free once these MMAs have read it
         }
@@ -542,9 +624,11 @@ constexpr int kStage2Bytes = 4 * kTile2;                    // A hi/lo, B hi/lo:
 constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256 + kStoreStage;
 constexpr uint32_t kIdesc2 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
                              (static_cast<uint32_t>(256 >> 4) << 24);
+constexpr uint32_t kIdesc2MN = kIdesc2 | (1u << 16);  // B MN-major (raw mode)
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
                         const GemmArgs g) {
   // g.tiles_m counts 256-row tiles here; both CTAs of a pair return together
   if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
@@ -607,10 +691,21 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
           if (leader) mbar_expect_tx(fb_local, 2 * kStage2Bytes);  // both CTAs' halves
           const uint32_t fb = map_rank(fb_local, 0);
           const int kc = kb * kBK;
-          tma_load_3d_pair(smem_u32(st), &map_a, fb, kc, row_a, static_cast<int>(2 * pa));
-          tma_load_3d_pair(smem_u32(st + kTile2), &map_a, fb, kc, row_a, static_cast<int>(2 * pa + 1));
-          tma_load_3d_pair(smem_u32(st + 2 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb));
-          tma_load_3d_pair(smem_u32(st + 3 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb + 1));
+          if (g.raw) {  // this CTA's half of B: kHalf / 32 MN-major chunks per term
+            tma_load_3d_pair(smem_u32(st), &map_a_hi, fb, kc, row_a, static_cast<int>(pa));
+            tma_load_3d_pair(smem_u32(st + kTile2), &map_a, fb, kc, row_a, static_cast<int>(pa));
+            for (int j = 0; j < kHalf / 32; ++j) {
+              tma_load_3d_pair(smem_u32(st + 2 * kTile2 + j * kChunkB), &map_b_hi, fb, row_b + 32 * j, kc,
+                               static_cast<int>(pb));
+              tma_load_3d_pair(smem_u32(st + 3 * kTile2 + j * kChunkB), &map_b, fb, row_b + 32 * j, kc,
+                               static_cast<int>(pb));
+            }
+          } else {
+            tma_load_3d_pair(smem_u32(st), &map_a, fb, kc, row_a, static_cast<int>(2 * pa));
+            tma_load_3d_pair(smem_u32(st + kTile2), &map_a, fb, kc, row_a, static_cast<int>(2 * pa + 1));
+            tma_load_3d_pair(smem_u32(st + 2 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb));
+            tma_load_3d_pair(smem_u32(st + 3 * kTile2), &map_b, fb, kc, row_b, static_cast<int>(2 * pb + 1));
+          }
         }
       }
       if (!ok && leader) {  // the leader's fills must land before the CTA exits
@@ -642,14 +737,18 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
           tc_fence_after();
           const uint64_t a_hi = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes));
           const uint64_t a_lo = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + kTile2));
-          const uint64_t b_hi = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + 2 * kTile2));
-          const uint64_t b_lo = smem_desc_sw128(smem_u32(smem + s * kStage2Bytes + 3 * kTile2));
+          const uint32_t sb_hi = smem_u32(smem + s * kStage2Bytes + 2 * kTile2);
+          const uint32_t sb_lo = smem_u32(smem + s * kStage2Bytes + 3 * kTile2);
+          const uint64_t b_hi = g.raw ? smem_desc_sw128_mn(sb_hi, kChunkB) : smem_desc_sw128(sb_hi);
+          const uint64_t b_lo = g.raw ? smem_desc_sw128_mn(sb_lo, kChunkB) : smem_desc_sw128(sb_lo);
+          const uint64_t b_step = g.raw ? 64u : 2u;  // 8 rows of 128 B (MN-major) or 32 B (K-major)
+          const uint32_t idesc = g.raw ? kIdesc2MN : kIdesc2;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {  // 8 tf32 = 32 bytes = 2 in the >> 4 address field
             const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-            mma_tf32_pair(d_tmem, a_lo + 2 * kk, b_hi + 2 * kk, kIdesc2, first);
-            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_lo + 2 * kk, kIdesc2, 1u);
-            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_hi + 2 * kk, kIdesc2, 1u);
+            mma_tf32_pair(d_tmem, a_lo + 2 * kk, b_hi + b_step * kk, idesc, first);
+            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_lo + b_step * kk, idesc, 1u);
+            mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_hi + b_step * kk, idesc, 1u);
           }
           const uint32_t e = smem_u32(&empty[s]);
           mma_commit_pair(e);               // both CTAs' stages are free once these MMAs
@@ -883,8 +982,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D map over [planes][rows][kp] float32, box {32, box_rows, 1}, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows) {
+// 3-D map over [planes][rows][kp] float32, box {32, box_rows, 1}, 128-byte swizzle
+// (with 32-byte atoms for MN-major tf32 operands: swizzle_atom32).
+bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows,
+              bool swizzle_atom32 = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kp), static_cast<cuuint64_t>(rows),
@@ -893,7 +994,9 @@ bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows,
   const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows), 1};
   const cuuint32_t elem[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, elem,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle_atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1032,19 +1135,39 @@ void split_b(cudaStream_t s, const float* rhs, float* wb, int64_t nbb, int64_t n
   }
 }
 
+// Raw-mode pre-pass: lo terms of A (na4 float4s) and B (nb4 float4s) in their own
+// layouts, one launch (either count may be 0).
+void split_lo_launch(cudaStream_t s, const float* a, float* wa, int64_t na4, const float* b, float* wb, int64_t nb4,
+                     int* flag, int sms) {
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(na4 + nb4, 256 * 4), 16LL * sms)));
+  TimedLaunch timer("split_lo", s);
+  split_lo<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(a), reinterpret_cast<float4*>(wa), na4,
+                                reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(wb), nb4, flag);
+}
+
 // The tcgen05 GEMM over split planes, then the IEEE FFMA fallback that runs only when
 // the pre-pass raised *flag (reading the original lhs / rhs). splits > 1 (single-SM
 // kernel, one output batch) needs `partial`: splits * m * n floats of workspace.
 int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
                 const float* lhs, const float* rhs, bool rhs_kmajor, int sms, int splits = 1,
-                float* partial = nullptr) {
+                float* partial = nullptr, bool raw = false) {
   const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
   const bool pair = use_pair(m, n, batches, sms);
   if (pair || batches != 1 || !partial) splits = 1;
-  alignas(64) CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
-    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+  alignas(64) CUtensorMap map_a, map_b, map_a_hi, map_b_hi;
+  if (raw) {
+    // A and its lo [nba][m][k], boxes of 32 k x 128 rows; B and its lo [nbb][k][n],
+    // boxes of 32 columns x 32 k rows (one MN-major chunk); zeros past k and n
+    if (!make_map(&map_a, wa, nba, m, k, kBM) || !make_map(&map_a_hi, lhs, nba, m, k, kBM) ||
+        !make_map(&map_b, wb, nbb, k, n, kBK, true) || !make_map(&map_b_hi, rhs, nbb, k, n, kBK, true))
+      return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+  } else {
+    if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
+      return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+    map_a_hi = map_a;
+    map_b_hi = map_b;
+  }
 
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -1074,6 +1197,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.splits = std::max(1, splits);
   g.kb_per_split = static_cast<int32_t>(ceil_div(g.num_kb, g.splits));
   g.partial = partial;
+  g.raw = raw ? 1 : 0;
   if (g.splits > 1) g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(partial) % 16 == 0) ? 1 : 0;
   if (pair) {
     g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
@@ -1091,12 +1215,12 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     TimedLaunch timer("gemm_tf32x3", s);
-    cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, g);
+    cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, map_a_hi, map_b_hi, g);
   } else {
     const int64_t work = batches * g.tiles_m * g.tiles_n * g.splits;
     const int grid = static_cast<int>(std::min<int64_t>(work, sms));
     TimedLaunch timer("gemm_tf32x3", s);
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, g);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, map_a_hi, map_b_hi, g);
   }
   if (int st = launch_status("tcgen05 matmul")) return st;
   if (g.splits > 1) {
@@ -1193,11 +1317,21 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   if (2 * std::max(nba, nbb) > INT32_MAX) return invalid("too many operand batches for the tensor path");
 
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
-  split_both(s, lhs, wa, nba, m, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
+  // Raw mode (row-major B, K and N multiples of 4, 16-byte aligned operands): the GEMM
+  // reads A and B themselves as the hi terms and the pre-pass writes only their lo
+  // terms, in the operands' own layouts (8 B per element instead of 12, no transpose).
+  // The lo arrays fit in the split planes' workspace areas.
+  const bool raw = !rhs_kmajor && k % 4 == 0 && n % 4 == 0 && reinterpret_cast<uintptr_t>(lhs) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(rhs) % 16 == 0;
+  if (raw) {
+    split_lo_launch(s, lhs, wa, nba * m * k / 4, rhs, wb, nbb * k * n / 4, flag, sms);
+  } else {
+    split_both(s, lhs, wa, nba, m, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
+  }
   if (int st = launch_status("matmul split pre-pass")) return st;
   float* partial = lay.splits > 1 ? reinterpret_cast<float*>(ws + lay.off_partial) : nullptr;
   return gemm_planes(s, wa, wb, nba, nbb, m, n, k, lay.kp, batches, bm, output, bias, act, flag, lhs, rhs,
-                     rhs_kmajor, sms, lay.splits, partial);
+                     rhs_kmajor, sms, lay.splits, partial, raw);
 }
 
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
@@ -1336,10 +1470,14 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
   const int sms = sm_count();
   float* b_planes = reinterpret_cast<float*>(ws + p.off_bp);
   int* b_flag = reinterpret_cast<int*>(ws + p.off_bflag);
+  // raw mode as the device-buffer path takes it (the staging buffers are 1024-byte
+  // aligned), so both paths run the same kernels and give identical results
+  const bool raw = p.tensor && k % 4 == 0 && n % 4 == 0;
   if (p.tensor) {  // B's split pre-pass once, shared by every chunk
     if (cudaError_t e = cudaMemsetAsync(b_flag, 0, sizeof(int), comp); e != cudaSuccess)
       return fail(e, "matmul_host flag reset");
-    split_b(comp, b_dev, b_planes, 1, n, k, p.kp, b_flag, false, sms);
+    if (raw) split_lo_launch(comp, nullptr, nullptr, 0, b_dev, b_planes, k * n / 4, b_flag, sms);
+    else split_b(comp, b_dev, b_planes, 1, n, k, p.kp, b_flag, false, sms);
   }
   BatchMap one;
   one.rank = 0;
@@ -1366,10 +1504,11 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
       int* flag = reinterpret_cast<int*>(ws + p.off_flag[slot]);
       if (cudaError_t e = cudaMemcpyAsync(flag, b_flag, sizeof(int), cudaMemcpyDeviceToDevice, comp); e != cudaSuccess)
         return fail(e, "matmul_host flag copy");
-      split_a(comp, a_dev, a_planes, 1, rows, k, p.kp, flag, sms);
+      if (raw) split_lo_launch(comp, a_dev, a_planes, rows * k / 4, nullptr, nullptr, 0, flag, sms);
+      else split_a(comp, a_dev, a_planes, 1, rows, k, p.kp, flag, sms);
       if (int rc = launch_status("matmul_host split pre-pass")) return rc;
       if (int rc = gemm_planes(comp, a_planes, b_planes, 1, 1, rows, n, k, p.kp, 1, one, c_dev, nullptr,
-                               TCX_ACT_NONE, flag, a_dev, b_dev, false, sms))
+                               TCX_ACT_NONE, flag, a_dev, b_dev, false, sms, 1, nullptr, raw))
         return rc;
     } else {
       const int rc = run_matmul(reinterpret_cast<tcx_stream_t>(comp), a_dev, b_dev, c_dev, rows, n, k, 1, nullptr,

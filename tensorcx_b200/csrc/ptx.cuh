@@ -152,6 +152,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
+// MN-major tf32 operand tile in the 128-byte swizzle with 32-byte atoms (layout type 1,
+// what TMA's SWIZZLE_128B_ATOM_32B writes): chunks of 32 consecutive MN elements, one
+// 128-byte row per k, 4-row k groups 512 B apart, chunks `chunk_bytes` apart along MN
+// (leading byte offset). Measured on sm_100a: the plain 128-byte swizzle (type 2) with
+// an MN-major tf32 operand makes the MMA produce zeros; this form gives exact products.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t addr, uint32_t chunk_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);        // start address
+  d |= static_cast<uint64_t>(chunk_bytes >> 4) << 16;        // leading byte offset: next MN chunk
+  d |= static_cast<uint64_t>(512 >> 4) << 32;                // stride byte offset: next 4 k rows
+  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version
+  d |= static_cast<uint64_t>(1) << 61;                       // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(

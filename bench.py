@@ -458,9 +458,9 @@ def gpu_arm(args):
                        "l2": "inputs (256 MiB each) larger than the 126 MB L2; no flush"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
                          "frac": achieved / peak_3x,
-                         # DRAM bytes read + written by one gemm_tf32x3 launch at 8192^3 in one
-                         # ncu capture (profiles/gemm_tf32x3_matmul_8192_traffic.md)
-                         "traffic": 6142193408 if size == 8192 else None,
+                         # DRAM bytes read + written by one gemm_tf32x3 launch (raw mode) at
+                         # 8192^3 in one ncu capture (profiles/gemm_tf32x3_pair_matmul_8192_raw_traffic.md)
+                         "traffic": 8685800960 if size == 8192 else None,
                          "traffic_unit": "B per launch",
                          "kernel": "gemm_tf32x3 (tcgen05.mma kind::tf32 x3 per k-step)",
                          "kernel_ms": gemm_avg_ms,

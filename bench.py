@@ -459,7 +459,7 @@ def gpu_arm(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
                          "frac": achieved / peak_3x,
                          # DRAM bytes read + written by one gemm_tf32x3 launch (raw mode) at
-                         # 8192^3 in one ncu capture (profiles/gemm_tf32x3_pair_matmul_8192_raw_traffic.md)
+                         # 8192^3: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture
                          "traffic": 8685800960 if size == 8192 else None,
                          "traffic_unit": "B per launch",
                          "kernel": "gemm_tf32x3 (tcgen05.mma kind::tf32 x3 per k-step)",

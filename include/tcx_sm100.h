@@ -252,9 +252,12 @@ int tcx_sm100_fill(tcx_stream_t stream, void* output, int64_t count, uint32_t bi
 
 /* ------------------------------------------------------------------- matmul --- */
 
-/* Scratch for tcx_sm100_matmul: the tf32 hi/lo split of both operands (K-major).
- * lhs_batches / rhs_batches are the operands' own batch counts (numel / (m*k),
- * numel / (k*n)). Zero when the FFMA kernel will be used. */
+/* Scratch for tcx_sm100_matmul: the tf32 hi/lo split of both operands (K-major), or,
+ * when k and n are multiples of 4 and both operands are 16-byte aligned, only their lo
+ * terms in the operands' own layouts (the tensor cores then read the operands
+ * themselves as the hi terms); the size covers either. lhs_batches / rhs_batches are
+ * the operands' own batch counts (numel / (m*k), numel / (k*n)). Zero when the FFMA
+ * kernel will be used. */
 size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k,
                                         int64_t lhs_batches, int64_t rhs_batches, int path);
 
@@ -266,7 +269,8 @@ size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k,
  * bias != NULL or act != TCX_ACT_NONE. Replaces launch_matmul (cuda_kernels.h:43-45)
  * and, with an epilogue, the matmul -> add -> activation call chain.
  * Large products run on tcgen05 tensor cores with a 3xTF32 split
- * (hi*hi + hi*lo + lo*hi, float32 accumulation): relative Frobenius error
+ * (hi*hi + hi*lo + lo*hi, float32 accumulation; hi = the tf32 truncation of x when the
+ * operands are read in place, else its rounding): relative Frobenius error
  * <= 1e-4 * sqrt(k / 1024) against the CPU reference. Inputs holding inf or NaN are
  * computed by the FFMA kernel instead (IEEE semantics), decided on the device. */
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output,

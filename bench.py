@@ -53,7 +53,80 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--no-workloads", action="store_true", help="headline only")
+    # --case: one workload alone on cuda:0, for profilers (ncu) and quick timing
+    p.add_argument("--case", default=None,
+                   help="matmul | bmm | softmax | rmsnorm | layernorm | sum | max | min | argmax | mean | "
+                        "sum_axis0 | sum_axes02 | attention")
+    p.add_argument("--batch", type=int, default=64)
+    p.add_argument("--rows", type=int, default=16384)
+    p.add_argument("--cols", type=int, default=4096)
+    p.add_argument("--n", type=int, default=1 << 28)
+    p.add_argument("--int32", action="store_true")
+    p.add_argument("--path", default="auto")
+    p.add_argument("--repeat", type=int, default=3)
+    p.add_argument("--causal", action="store_true")
     return p.parse_args()
+
+
+def run_case(a):
+    """One hot-path workload called `--repeat` times on cuda:0 after one untimed call;
+    prints the mean device time per call (CUDA events on the current stream).
+
+        python bench.py --case matmul --size 4096 [--path tensor|ffma] [--repeat 3]
+        python bench.py --case bmm --batch 64 --size 2048
+        python bench.py --case softmax|rmsnorm|layernorm --rows 16384 --cols 4096
+        python bench.py --case sum|max|min|argmax|mean --n 268435456 [--int32]
+        python bench.py --case attention --batch 32 --rows 2048 --cols 2048 --size 128 [--causal]
+        python bench.py --case sum_axis0 --rows 65536 --cols 4096
+        python bench.py --case sum_axes02 --batch 64 --rows 4096 --cols 1024
+    """
+    import torch
+    from tensorcx_b200 import ops
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = a.case
+    if w == "matmul":
+        x = torch.rand(a.size, a.size, device="cuda", generator=g) * 2 - 1
+        y = torch.rand(a.size, a.size, device="cuda", generator=g) * 2 - 1
+        fn = lambda: ops.matmul(x, y, path=a.path)  # noqa: E731
+    elif w == "bmm":
+        x = torch.rand(a.batch, a.size, a.size, device="cuda", generator=g) * 2 - 1
+        y = torch.rand(a.batch, a.size, a.size, device="cuda", generator=g) * 2 - 1
+        bias = torch.randn(a.size, device="cuda", generator=g)
+        fn = lambda: ops.matmul(x, y, bias=bias, act="silu", path=a.path)  # noqa: E731
+    elif w in ("softmax", "rmsnorm", "layernorm"):
+        x = torch.randn(a.rows, a.cols, device="cuda", generator=g) * 3
+        f = getattr(ops, w)
+        fn = lambda: f(x, axis=-1)  # noqa: E731
+    elif w in ("sum", "max", "min", "argmax", "mean"):
+        if a.int32:
+            x = torch.randint(-1000, 1001, (a.n,), device="cuda", generator=g, dtype=torch.int32)
+        else:
+            x = torch.randn(a.n, device="cuda", generator=g)
+        f = getattr(ops, w)
+        fn = lambda: f(x)  # noqa: E731
+    elif w == "sum_axis0":
+        x = torch.randn(a.rows, a.cols, device="cuda", generator=g)
+        fn = lambda: ops.sum(x, axis=0)  # noqa: E731
+    elif w == "sum_axes02":
+        x = torch.randn(a.batch, a.rows, a.cols, device="cuda", generator=g)
+        fn = lambda: ops.sum(x, axis=(0, 2))  # noqa: E731
+    elif w == "attention":  # batch = heads, rows = queries, cols = keys, size = features
+        q = torch.randn(a.batch, a.rows, a.size, device="cuda", generator=g)
+        k = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)
+        v = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)
+        fn = lambda: ops.attention(q, k, v, is_causal=a.causal)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown workload {w}")
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.repeat):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    print(f"{w}: {s.elapsed_time(e) / a.repeat:.4f} ms per call")
 
 
 def dist_env():
@@ -62,15 +135,18 @@ def dist_env():
 
 
 # ------------------------------------------------------------------ CPU legs
-def cpu_matmul_rate(size: int, threads: int, rows_per_thread: int, a=None, b=None):
+# Rows of the size^3 product each host thread computes per CPU step: the same sample
+# in the reference arm and in the GPU arm's cpu_baseline leg, so the two agree.
+CPU_ROWS_PER_THREAD = 2
+
+
+def cpu_matmul_rate(size: int, threads: int, rows_per_thread: int, a, b, ref=None):
     """Reference cpu::matmul on `threads` disjoint row slices of the size^3 product
-    (identical per-element arithmetic to the full product). Returns (flops/s, rows)."""
+    (identical per-element arithmetic to the full product), B bound once beforehand
+    (Reference.matmul_bind_rhs) so a step is the rows' arithmetic alone. Returns
+    (flops/s, rows, seconds, rows of C)."""
     from oracle.oracle import Reference
-    ref = Reference()
-    rng = np.random.default_rng(0)
-    if a is None:
-        a = (rng.random((threads * rows_per_thread, size), dtype=np.float32) * 2 - 1)
-        b = (rng.random((size, size), dtype=np.float32) * 2 - 1)
+    ref = ref or Reference()
     outs = [None] * threads
 
     def work(t):
@@ -86,6 +162,17 @@ def cpu_matmul_rate(size: int, threads: int, rows_per_thread: int, a=None, b=Non
     dt = time.perf_counter() - t0
     rows = threads * rows_per_thread
     return 2.0 * rows * size * size / dt, rows, dt, np.concatenate(outs)
+
+
+def cpu_sample_text(size, threads, rows_per_thread):
+    return (f"cpu::matmul (reference sources, -O3) on {threads * rows_per_thread} disjoint rows of the {size}^3 "
+            f"product per step ({rows_per_thread} per thread, {threads} threads), B bound once outside the timing")
+
+
+def headline_config(size, world):
+    return {"workload": f"fp32 matmul M=N=K={size} (BASELINE configs[1], largest size)",
+            "per_gpu": f"{size}^3", "parallelism": f"independent products, {world} GPU(s)",
+            "l2": "inputs (256 MiB each) larger than the 126 MB L2; no flush"}
 
 
 def host_threads() -> int:
@@ -105,25 +192,27 @@ def reference_arm(args):
         return
     threads = host_threads()
     size = args.size
+    per = CPU_ROWS_PER_THREAD
     rng = np.random.default_rng(0)
-    a = rng.random((threads, size), dtype=np.float32) * 2 - 1
+    a = rng.random((threads * per, size), dtype=np.float32) * 2 - 1
     b = rng.random((size, size), dtype=np.float32) * 2 - 1
+    ref = Reference()
+    ref.matmul_bind_rhs(b)
     for _ in range(args.warmup):
-        cpu_matmul_rate(size, threads, 1, a, b)
+        cpu_matmul_rate(size, threads, per, a, b, ref)
     times = []
     for _ in range(args.steps):
-        rate, rows, dt, _ = cpu_matmul_rate(size, threads, 1, a, b)
+        _, _, dt, _ = cpu_matmul_rate(size, threads, per, a, b, ref)
         times.append(dt)
     mean_dt = sum(times) / len(times)
-    value = 2.0 * threads * size * size / mean_dt / 1e12
-    sample = f"cpu::matmul on {threads} disjoint rows of the {size}^3 product per step ({threads} threads)"
+    value = 2.0 * threads * per * size * size / mean_dt / 1e12
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"fp32 matmul {size}^3 (row-sliced sample)", "sample_rows_per_step": threads},
+        "config": headline_config(size, args.gpus),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
-                         "sample": sample},
+                         "sample": cpu_sample_text(size, threads, per)},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -420,24 +509,29 @@ def gpu_arm(args):
     e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
     del e2e_buf
 
-    # CPU baseline (rank 0, N = 1): the reference's cpu::matmul on a row sample
+    # CPU baseline (rank 0, N = 1): the reference's cpu::matmul on the reference arm's
+    # row sample (CPU_ROWS_PER_THREAD rows per host thread), one warm-up step, mean of 3
     cpu = None
     if rank == 0 and world == 1:
         from oracle.oracle import Reference
         if Reference.available():
             threads = host_threads()
+            per = CPU_ROWS_PER_THREAD
             a_np = a_host.numpy()
             b_np = b_host.numpy()
-            # calibrate one row, then size the sample to about 10 s of CPU work
-            r1, _, dt1, _ = cpu_matmul_rate(size, 1, 1, a_np[:1], b_np)
-            per_thread = max(1, min(8, int(10.0 / max(dt1, 1e-3))))
-            rate, rows, dt, got_rows = cpu_matmul_rate(size, threads, per_thread,
-                                                       a_np[:threads * per_thread], b_np)
+            ref = Reference()
+            ref.matmul_bind_rhs(b_np)
+            cpu_matmul_rate(size, threads, per, a_np, b_np, ref)
+            dts = []
+            for _ in range(3):
+                _, rows, dt, got_rows = cpu_matmul_rate(size, threads, per, a_np, b_np, ref)
+                dts.append(dt)
+            dt = sum(dts) / len(dts)
             gpu_rows = c_host[:rows].numpy()  # C of the last e2e step (same A, B)
             rel = float(np.linalg.norm(gpu_rows.astype(np.float64) - got_rows) / np.linalg.norm(got_rows))
-            cpu = {"value": rate / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
-                   "sample": f"cpu::matmul (reference, -O3) on {rows} rows of the {size}^3 product, "
-                             f"{threads} threads, {dt:.1f} s",
+            cpu = {"value": 2.0 * rows * size * size / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+                   "kind": "reference",
+                   "sample": cpu_sample_text(size, threads, per) + f", mean of 3 steps ({dt:.2f} s each)",
                    "gpu_rows_rel_frobenius_error": rel,
                    "tolerance": 1e-4 * math.sqrt(size / 1024)}
     del a_host, b_host, c_host
@@ -453,9 +547,7 @@ def gpu_arm(args):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (3xTF32 split on tf32 tensor cores, f32 accumulate)",
             "data": "synthetic (seeded U(-1,1), per-rank seed)",
-            "config": {"workload": f"fp32 matmul M=N=K={size} (BASELINE configs[1], largest size)",
-                       "per_gpu": f"{size}^3", "parallelism": f"independent products, {world} GPU(s)",
-                       "l2": "inputs (256 MiB each) larger than the 126 MB L2; no flush"},
+            "config": headline_config(size, world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
                          "frac": achieved / peak_3x,
                          # DRAM bytes read + written by one gemm_tf32x3 launch (raw mode) at
@@ -481,6 +573,8 @@ def gpu_arm(args):
             "kernels_in_timed_region": {k: {"launches": v[0], "total_ms": v[1]} for k, v in kernels.items()},
             "clocks": clocks,
             "workloads": workloads,
+            "strong_scaling": {k: v["strong_scaling"]["efficiency_vs_n1"] for k, v in workloads.items()
+                               if isinstance(v, dict) and "strong_scaling" in v} or None,
         }
         print(json.dumps(line))
     if world > 1:
@@ -509,6 +603,24 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
             d.update(extra)
         out[name] = d
 
+    # Strong scaling (N > 1): the same whole workload timed on rank 0's GPU alone in
+    # this run (the other ranks wait at a barrier), so each sharded workload carries its
+    # own speedup and efficiency against one GPU on the same box.
+    solo = Timer(torch, dist, 1)
+    gs = torch.Generator(device="cuda").manual_seed(4242)
+
+    def strong(name, solo_value):
+        if world == 1:
+            return
+        v1 = solo_value() if rank == 0 else None
+        timer.barrier()
+        if rank == 0 and v1:
+            vn = out[name]["value"]
+            out[name]["strong_scaling"] = {
+                "n1_value": v1, "speedup_vs_n1": vn / v1, "efficiency_vs_n1": vn / (world * v1),
+                "n1_measured": "the whole workload on rank 0's GPU alone, same run, same timing rule"}
+        torch.cuda.empty_cache()
+
     # row ops, [16384, 4096] and [4096, 32768]: rows sharded over ranks
     for name, (rows, cols), op in [("softmax_16384x4096", (16384, 4096), "softmax"),
                                    ("rmsnorm_16384x4096", (16384, 4096), "rmsnorm"),
@@ -532,6 +644,12 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                   {"config": f"[{rows},{cols}] float32, rows sharded {world} way(s), 8 B/element; "
                             "back to back when the data is >= 2x L2, else L2 flushed before each step"})
         del x, y
+
+        def solo_rows(rows=rows, cols=cols, fn=fn, kw=kw):
+            xs = torch.randn(rows, cols, device="cuda", generator=gs) * 3
+            ms1 = solo.run_hbm(lambda: fn(xs, axis=-1, **kw), steps, 2, None, 8 * rows * cols) / steps
+            return 8.0 * rows * cols / (ms1 * 1e-3) / 1e9
+        strong(name, solo_rows)
 
     # full reductions over 2^28 elements: shard + per-rank record + NCCL all-gather
     from tensorcx_b200 import shard as sharding
@@ -570,11 +688,44 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         ms = timer.run_hbm(st, steps, 2, sampler, 4 * shard) / steps
         lib.tcx_sm100_timer_enable(0)
         kern = read_timer(lib)
+        stage1 = kern.get("reduce_stage1", (0, 0.0))
+        fold = kern.get("reduce_exchange", kern.get("reduce_combine", (0, 0.0)))
         hbm_entry(name, 4.0 * shard, ms, "reduce_stage1", kern,
                   {"config": f"2^28 elements total, {world} shard(s), partials combined {combine} "
-                             "in rank order; back to back when the data is >= 2x L2, else L2 flushed before each step"})
+                             "in rank order; back to back when the data is >= 2x L2, else L2 flushed before each step",
+                   "split_ms": {"stage1": timer.max_over_ranks(stage1[1] / max(stage1[0], 1)),
+                                "exchange" if world > 1 and peer is not None else "combine":
+                                    timer.max_over_ranks(fold[1] / max(fold[0], 1)),
+                                "note": "per call, max over ranks; the exchange includes the wait for the "
+                                        "slowest peer's record"}})
+
+        def solo_reduce(x=x, op=op):
+            full = (torch.randn(total, device="cuda", generator=gs) if x.dtype == torch.float32 else
+                    torch.randint(-1000, 1001, (total,), device="cuda", generator=gs, dtype=torch.int32))
+
+            def one():
+                rec = ops.reduce_partial(full, op, index_base=0)
+                return ops.reduce_combine(rec.view(1, 16), op, full.dtype, total)
+            ms1 = solo.run_hbm(one, steps, 2, None, 4 * total) / steps
+            return 4.0 * total / (ms1 * 1e-3) / 1e9
+        strong(name, solo_reduce)
     if peer is not None:
         peer.close()
+    if world == 1:
+        # which side of the float32 sum bar holds at 2^28: relative error of the CPU's
+        # sequential sum and of the GPU's tree against the float64 sum of the same data
+        from oracle.oracle import Oracle
+        o = Oracle()
+        host = xf.cpu().numpy()
+        exact = o.sum_f64(host)
+        cpu_sum = float(o.sum(host))
+        gpu_sum = float(ops.reduce_combine(ops.reduce_partial(xf, "sum", index_base=0).view(1, 16), "sum",
+                                           xf.dtype, total).item())
+        out["sum_f32_2^28"]["error_vs_float64"] = {
+            "gpu_rel": abs(gpu_sum - exact) / abs(exact), "cpu_reference_rel": abs(cpu_sum - exact) / abs(exact),
+            "gpu_vs_cpu_rel": abs(gpu_sum - cpu_sum) / abs(cpu_sum),
+            "bar": "within 1e-5 of the CPU result, or closer to the float64 sum than the CPU"}
+        del host
     del xf, xi
 
     # strided and multi-axis reductions (1 GiB each): axis 0 of [65536, 4096], and
@@ -690,6 +841,15 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                      "peak": peak_3x, "unit": "TFLOP/s",
                      "frac": (fl / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
                      "kernel": "gemm_tf32x3", "kernel_ms": k_avg}}
+    del a, b
+
+    def solo_bmm():
+        a1 = torch.rand(64, 2048, 2048, device="cuda", generator=gs) * 2 - 1
+        b1 = torch.rand(64, 2048, 2048, device="cuda", generator=gs) * 2 - 1
+        n_b = max(3, steps // 2)
+        ms1 = solo.run(lambda: ops.matmul(a1, b1, bias=bias, act="silu"), n_b, 1) / n_b
+        return 2.0 * 64 * 2048 ** 3 / (ms1 * 1e-3) / 1e12
+    strong("bmm_bias_silu_64x2048^3", solo_bmm)
 
     # attention, [32 heads, 2048 queries, 2048 keys, 128 features]: heads sharded
     heads = max(1, 32 // world)
@@ -723,6 +883,13 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                      "kernel": "flash_tf32x3", "kernel_ms": k_avg,
                      "note": "achieved = flops of the key blocks executed (up to the causal diagonal)"}}
     del q, k, v
+
+    def solo_attention():
+        q1, k1, v1 = (torch.randn(32, 2048, 128, device="cuda", generator=gs) for _ in range(3))
+        ms1 = solo.run(lambda: ops.attention(q1, k1, v1, is_causal=True), n_att, 1) / n_att
+        return 4.0 * 32 * 2048 * 2048 * 128 / (ms1 * 1e-3) / 1e12
+    if heads * world == 32:
+        strong("attention_causal_32x2048x2048x128", solo_attention)
 
     # MLP latency (configs[0]: x[256,784] -> linear 512 + ReLU -> linear 10 -> softmax)
     x = torch.randn(256, 784, device="cuda", generator=g)
@@ -759,6 +926,9 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
 
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

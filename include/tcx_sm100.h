@@ -159,7 +159,9 @@ int tcx_sm100_reduce_all(tcx_stream_t stream, int op, int dtype, const void* inp
  * scratch is a fixed 16 KiB device array inside the library (1024 partial records),
  * held on every device that loads the library until the process exits. The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress), so
- * make that first call before any stream capture. Calls share the one array: two
+ * make that first call before any stream capture. A failed lookup is not kept (the
+ * next call retries it), and after the device's context is destroyed and recreated
+ * (cudaDeviceReset) the next call looks the address up again. Calls share the one array: two
  * calls that overlap on the GPU (e.g. on different streams) race and must be
  * serialized by the caller. Inputs whose stage-1 grid needs more than 1024 records
  * are rejected with TCX_INVALID_ARGUMENT (never on GPUs with up to 256 SMs). */

@@ -679,6 +679,13 @@ class Reference(_Lib):
         out_shape = matmul_plan(list(a.shape), list(b.shape))[0]
         return self._binary("matmul", a, b, cap=max(1, numel(out_shape)))
 
+    def matmul_bind_rhs(self, b):
+        """Copy B into the reference's CpuTensor once; later matmul_rows calls on the
+        same (contiguous float32) B use that copy instead of copying B per call."""
+        assert b.dtype == np.float32 and b.flags.c_contiguous
+        self._check(self.lib.tcxref_matmul_bind_rhs(_ptr(b), ctypes.c_int64(b.shape[0]),
+                                                    ctypes.c_int64(b.shape[1])))
+
     def matmul_rows(self, a, b, row_begin, row_end):
         """cpu::matmul on a row slice of a 2-D lhs (same per-element arithmetic)."""
         m, k = a.shape

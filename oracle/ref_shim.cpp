@@ -11,6 +11,8 @@
 // calling thread is available from tcxref_last_error().
 #include <cstdint>
 #include <cstring>
+#include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -195,9 +197,31 @@ int tcxref_attention_softmax(const float* scores, const std::int64_t* sd, int sr
   });
 }
 
+// The right operand of the row-sliced CPU baseline, copied into a CpuTensor once
+// (tcxref_matmul_bind_rhs, outside any timed region) and shared read-only by every
+// thread's tcxref_matmul_rows call on the same B. Without it each call copies the
+// whole of B (256 MiB at 8192^3) next to a few rows of arithmetic.
+struct BoundRhs {
+  const float* src = nullptr;
+  std::int64_t k = 0, n = 0;
+  std::shared_ptr<const cpu::CpuTensor> tensor;
+};
+std::mutex g_rhs_mu;
+BoundRhs g_rhs;
+
+int tcxref_matmul_bind_rhs(const float* b, std::int64_t k, std::int64_t n) {
+  return guarded([&] {
+    auto t = std::make_shared<const cpu::CpuTensor>(Shape{k, n}, std::vector<float>(b, b + k * n));
+    std::lock_guard<std::mutex> lock(g_rhs_mu);
+    g_rhs = BoundRhs{b, k, n, std::move(t)};
+    return 0;
+  });
+}
+
 // Row-slice matmul for the timed CPU baseline: cpu::matmul over rows
 // [row_begin, row_end) of a 2-D lhs, which performs exactly the per-element
-// arithmetic of the full product (cpu_backend.cpp:1251-1276).
+// arithmetic of the full product (cpu_backend.cpp:1251-1276). B comes from the bound
+// copy when it is the bound operand, else it is copied for this call.
 int tcxref_matmul_rows(const float* a, const float* b, float* out, std::int64_t m,
                        std::int64_t k, std::int64_t n, std::int64_t row_begin,
                        std::int64_t row_end) {
@@ -206,10 +230,14 @@ int tcxref_matmul_rows(const float* a, const float* b, float* out, std::int64_t 
     if (rows < 0 || row_end > m) { g_error = "bad row range"; return 1; }
     std::vector<float> slice(static_cast<std::size_t>(rows * k));
     if (rows * k) std::memcpy(slice.data(), a + row_begin * k, static_cast<std::size_t>(rows * k) * 4);
-    std::vector<float> rhs(b, b + k * n);
+    std::shared_ptr<const cpu::CpuTensor> rhs_t;
+    {
+      std::lock_guard<std::mutex> lock(g_rhs_mu);
+      if (g_rhs.src == b && g_rhs.k == k && g_rhs.n == n) rhs_t = g_rhs.tensor;
+    }
+    if (!rhs_t) rhs_t = std::make_shared<const cpu::CpuTensor>(Shape{k, n}, std::vector<float>(b, b + k * n));
     const cpu::CpuTensor lhs_t(Shape{rows, k}, std::move(slice));
-    const cpu::CpuTensor rhs_t(Shape{k, n}, std::move(rhs));
-    const auto result = cpu::matmul(lhs_t, rhs_t);
+    const auto result = cpu::matmul(lhs_t, *rhs_t);
     if (result.size()) std::memcpy(out, result.data(), static_cast<std::size_t>(result.size()) * 4);
     return 0;
   });

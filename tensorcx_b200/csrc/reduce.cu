@@ -15,6 +15,7 @@
 //    thread per row adding left to right.
 //  * Strided axes and general multi-axis selections: one thread per output, walking
 //    the reduction in the reference's index order (exact).
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -1138,27 +1139,40 @@ int tcx_sm100_reduce_sharded(tcx_stream_t stream, int op, int dtype, const void*
   const int mode = out_mode(op);
   const uint64_t limit = wait_limit_ns ? wait_limit_ns : kDefaultExchangeWaitNs;
   int* err = device_error_word();
-  TimedLaunch timer("reduce_sharded", s);
-  switch (kind_of(op, dtype)) {
+  // Two timer records: stage 1 (this rank's shard, HBM-bound) and the exchange
+  // (record stores to every peer, the bounded wait for theirs, the rank-order fold),
+  // so the time a call spends waiting on its peers shows on its own.
+  const int kind = kind_of(op, dtype);
+  {
+    TimedLaunch timer("reduce_stage1", s);
+    switch (kind) {
+      case kSumF: launch_stage1<kSumF, true>(s, x, 1, count, index_base, parts, g); break;
+      case kSumI: launch_stage1<kSumI, false>(s, x, 1, count, index_base, parts, g); break;
+      case kBestMax:
+        if (fp) launch_stage1<kBestMax, true>(s, x, 1, count, index_base, parts, g);
+        else launch_stage1<kBestMax, false>(s, x, 1, count, index_base, parts, g);
+        break;
+      default:
+        if (fp) launch_stage1<kBestMin, true>(s, x, 1, count, index_base, parts, g);
+        else launch_stage1<kBestMin, false>(s, x, 1, count, index_base, parts, g);
+        break;
+    }
+  }
+  TimedLaunch timer("reduce_exchange", s);
+  switch (kind) {
     case kSumF:
-      launch_stage1<kSumF, true>(s, x, 1, count, index_base, parts, g);
       reduce_stage2_exchange<kSumF><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kSumI:
-      launch_stage1<kSumI, false>(s, x, 1, count, index_base, parts, g);
       reduce_stage2_exchange<kSumI><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kBestMax:
-      if (fp) launch_stage1<kBestMax, true>(s, x, 1, count, index_base, parts, g);
-      else launch_stage1<kBestMax, false>(s, x, 1, count, index_base, parts, g);
       reduce_stage2_exchange<kBestMax><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
     default:
-      if (fp) launch_stage1<kBestMin, true>(s, x, 1, count, index_base, parts, g);
-      else launch_stage1<kBestMin, false>(s, x, 1, count, index_base, parts, g);
       reduce_stage2_exchange<kBestMin><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
@@ -1300,9 +1314,46 @@ int tcx_sm100_min_argmax(tcx_stream_t stream, int op, int dtype, const void* inp
 namespace {
 constexpr int kNoAllocRecords = 1024;
 constexpr int kNoAllocMaxDevices = 64;
-std::once_flag g_noalloc_once[kNoAllocMaxDevices];
-void* g_noalloc_ptr[kNoAllocMaxDevices];
-cudaError_t g_noalloc_status[kNoAllocMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// The array's device address as last looked up on a device, and the id of the CUDA
+// context it belongs to. A lookup that failed is not kept (the next call tries
+// again), and an address whose context has since been destroyed and replaced (a
+// device reset) is looked up anew, since the module, and with it the array, may now
+// sit elsewhere.
+struct NoAllocScratch {
+  std::mutex mu;
+  void* ptr = nullptr;
+  unsigned long long context_id = 0;
+};
+NoAllocScratch g_noalloc[kNoAllocMaxDevices];
+
+// Id of the calling thread's current context, or 0 when none is current or the
+// driver offers no context ids.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 }  // namespace
 
 static __device__ __align__(256) tcx_partial tcx_noalloc_records[kNoAllocRecords];
@@ -1316,17 +1367,27 @@ extern "C" int tcx_sm100_reduce_all_noalloc(tcx_stream_t stream, int op, int dty
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return launch_status("cudaGetDevice");
   if (dev < 0 || dev >= kNoAllocMaxDevices) return invalid("device index beyond the no-allocation table");
-  // Once per device, with that device current: the host-side name of the array is
-  // only a stand-in, so the kernels get the device address looked up here.
-  std::call_once(g_noalloc_once[dev], [dev] {
-    void* p = nullptr;
-    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, tcx_noalloc_records);
-    g_noalloc_ptr[dev] = p;
-  });
-  if (g_noalloc_status[dev] != cudaSuccess) {
-    set_error(std::string("cudaGetSymbolAddress(no-allocation scratch): ") +
-              cudaGetErrorString(g_noalloc_status[dev]));
-    return TCX_INTERNAL;
+  // Set-up, with this device current: the host-side name of the array is only a
+  // stand-in, so the kernels get the device address looked up here. It happens on
+  // the first call on a device, and again only after that device's context changed.
+  void* scratch = nullptr;
+  {
+    NoAllocScratch& slot = g_noalloc[dev];
+    std::lock_guard<std::mutex> lock(slot.mu);
+    const unsigned long long ctx = current_context_id();
+    if (slot.ptr == nullptr || ctx == 0 || ctx != slot.context_id) {
+      void* p = nullptr;
+      const cudaError_t rc = cudaGetSymbolAddress(&p, tcx_noalloc_records);
+      if (rc != cudaSuccess) {
+        cudaGetLastError();
+        slot.ptr = nullptr;  // not kept: the next call looks it up again
+        set_error(std::string("cudaGetSymbolAddress(no-allocation scratch): ") + cudaGetErrorString(rc));
+        return TCX_INTERNAL;
+      }
+      slot.ptr = p;
+      slot.context_id = current_context_id();  // the lookup made the primary context current
+    }
+    scratch = slot.ptr;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (count == 0) {
@@ -1341,5 +1402,5 @@ extern "C" int tcx_sm100_reduce_all_noalloc(tcx_stream_t stream, int op, int dty
     return invalid("input needs more partial records than the fixed no-allocation scratch holds (1024)");
   // Stage 1 writes every record stage 2 reads, so the previous call's contents never
   // leak into a result and nothing has to be cleared first.
-  return tree_reduce(s, op, dtype, input, 1, count, 0, out_mode(op), output, g_noalloc_ptr[dev], capacity);
+  return tree_reduce(s, op, dtype, input, 1, count, 0, out_mode(op), output, scratch, capacity);
 }

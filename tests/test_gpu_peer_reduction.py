@@ -5,7 +5,9 @@ The results must be bit-identical (same per-shard arithmetic, same rank-order fo
 
 On one GPU: world size 1 through the mailbox, and the bounded wait running out (a
 second mailbox slot that no rank ever fills) with the error reported on the host.
-With two or more GPUs: two processes (one per GPU) exchange over NVLink peer memory.
+With 2, 4 or 8 GPUs: one process per GPU exchanges over NVLink peer memory, and the
+result is checked against the record path and against the CPU oracle over the whole
+array.
 """
 import ctypes
 import os
@@ -140,10 +142,29 @@ def _worker(rank, world, port, results):
     results[rank] = out
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_exchange_matches_record_path():
+def _check_against_oracle(oracle, op, dtype, full, got_bytes):
+    """The multi-GPU result against the CPU oracle over the whole array: bit-exact for
+    int32, max, min and argmax (lowest index of the planted cross-shard ties); float32
+    sum and mean within 1e-5 relative of the CPU's sequential result, or closer to the
+    float64 sum than that result."""
+    out_dtype = np.int32 if (op == "argmax" or dtype == np.int32) else np.float32
+    got = np.frombuffer(got_bytes, dtype=out_dtype)[0]
+    want = np.asarray(getattr(oracle, op)(full)).reshape(())
+    if op in ("sum", "mean") and dtype == np.float32:
+        exact = oracle.sum_f64(full) / (full.size if op == "mean" else 1)
+        assert abs(float(got) - float(want)) <= 1e-5 * abs(float(want)) or \
+            abs(float(got) - exact) <= abs(float(want) - exact), (op, float(got), float(want), exact)
+    else:
+        assert got.tobytes() == want.astype(out_dtype).tobytes(), (op, got, want)
+    if op == "argmax":
+        assert int(got) == 11  # the first of the planted equal maxima, in shard 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_multi_gpu_exchange_matches_record_path_and_oracle(oracle, world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    world = 2
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
@@ -163,4 +184,12 @@ def test_two_gpu_exchange_matches_record_path():
         for key, (got, want) in res.items():
             assert got == want, (r, key)
     # every rank holds the same values
-    assert dict(results[0]) == dict(results[1])
+    for r in range(1, world):
+        assert dict(results[0]) == dict(results[r])
+    # and they are the reference's values for the whole array
+    res = dict(results[0])
+    res.pop("device_error")
+    for i, (op, dtype) in enumerate(OPS * 2):
+        full = _data(dtype, 3_000_017, 17 + i)
+        got, _ = res[f"{i}:{op}:{np.dtype(dtype).name}"]
+        _check_against_oracle(oracle, op, dtype, full, got)

@@ -1,7 +1,7 @@
 // CudaBackend::execute for the sm100 backend: validation and planning with the
 // unchanged tensor.cx core (validate_primitive_execution_contract, make_*_plan), then
-// one C-ABI call per primitive (include/tcx_sm100.h) on the device's stream, a
-// synchronize of that stream (the ABI stays synchronous, docs/BACKENDS.md:178-180)
+// one C-ABI call per primitive (include/tcx_sm100.h) on the calling thread's stream for
+// the device, a synchronize of that stream (the ABI stays synchronous, docs/BACKENDS.md:178-180)
 // and publication of the result slot only on success (cuda_backend.cpp:612-613 of the
 // reference). Validation messages follow the reference CUDA backend so the bindings
 // raise the same errors.
@@ -616,8 +616,20 @@ CudaBuffer::~CudaBuffer() {
   if (external_owner_ || !data_) return;
   DeviceScope scope(device_);
   if (!scope.ready()) return;
-  if (pool_) pool_->release(data_, bytes_, !exported_.load(std::memory_order_relaxed));
-  else (void)cudaFreeAsync(data_, scope.stream());
+  const bool exported = exported_.load(std::memory_order_relaxed);
+  if (pool_) {
+    pool_->release(data_, bytes_, !exported);
+    return;
+  }
+  // Backend work on this buffer has completed (every execute synchronizes its stream
+  // before returning), so a stream-ordered free on this thread's stream is safe. An
+  // exported buffer may still be read by a foreign consumer on a stream this backend
+  // does not track: wait for the device first.
+  if (exported) {
+    (void)cudaDeviceSynchronize();
+    cudaGetLastError();
+  }
+  (void)cudaFreeAsync(data_, scope.stream());
 }
 
 StorageRelation CudaBuffer::storage_relation(const Buffer& other) const {
@@ -694,6 +706,13 @@ Expected<CudaTensor> empty(Shape shape, DType dtype, int device) {
     (void)contiguous_strides(shape);
     auto buffer = CudaBuffer::create(dtype, shape, device);
     if (!buffer) return buffer.status();
+    if (buffer.value()->nbytes()) {
+      // the allocation is ordered on this thread's stream; complete it before the
+      // tensor can reach another thread's stream
+      DeviceScope scope(device);
+      if (!scope.ready()) return scope.status();
+      if (auto st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA allocation"); !st.ok()) return st;
+    }
     return CudaTensor(dtype, std::move(shape), buffer.move_value());
   } catch (const std::invalid_argument& e) {
     return invalid(e.what());

@@ -7,28 +7,49 @@
 
 namespace tensorcx::cuda {
 namespace {
-std::mutex g_mutex;
-std::vector<cudaStream_t> g_streams;
+constexpr int kMaxDevices = 64;
 
-Expected<cudaStream_t> stream_for(int device) {
-  std::lock_guard lock(g_mutex);
-  if (device < 0) return Status(StatusCode::kInvalidArgument, "negative CUDA device index");
-  if (static_cast<std::size_t>(device) >= g_streams.size()) g_streams.resize(device + 1, nullptr);
-  if (!g_streams[device]) {
-    cudaStream_t s = nullptr;
-    auto status = runtime_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "CUDA stream creation");
-    if (!status.ok()) return status;
-    // Keep memory freed back to the device's stream-ordered pool cached in the
-    // driver: repeated same-size allocations then cost no cudaMalloc.
+// Once per device: memory freed back to the device's default stream-ordered pool
+// stays reserved there, so repeated same-size allocations cost no driver call.
+std::once_flag g_pool_once[kMaxDevices];
+
+void keep_freed_memory_reserved(int device) {
+  std::call_once(g_pool_once[device], [device] {
     cudaMemPool_t pool = nullptr;
     if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
       std::uint64_t threshold = UINT64_MAX;
       (void)cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
     }
     cudaGetLastError();
-    g_streams[device] = s;
+  });
+}
+
+// One non-blocking stream per device for each host thread: concurrent executes from
+// different threads (the bindings release the GIL around them) run on different
+// streams, and each waits only for its own work. Destroyed when the thread ends
+// (work still queued on a destroyed stream completes first).
+struct ThreadStreams {
+  std::vector<cudaStream_t> by_device;
+  ~ThreadStreams() {
+    for (cudaStream_t s : by_device)
+      if (s) (void)cudaStreamDestroy(s);
   }
-  return g_streams[device];
+};
+
+Expected<cudaStream_t> stream_for(int device) {
+  if (device < 0 || device >= kMaxDevices) return Status(StatusCode::kInvalidArgument, "CUDA device index out of range");
+  thread_local ThreadStreams streams;
+  if (static_cast<std::size_t>(device) >= streams.by_device.size()) streams.by_device.resize(device + 1, nullptr);
+  cudaStream_t& s = streams.by_device[device];
+  if (!s) {
+    keep_freed_memory_reserved(device);
+    auto status = runtime_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "CUDA stream creation");
+    if (!status.ok()) {
+      s = nullptr;
+      return status;
+    }
+  }
+  return s;
 }
 }  // namespace
 

@@ -1,6 +1,7 @@
-// Per-device execution state of the sm100 backend: one non-blocking stream per
-// device (0..N-1), created on first use, plus the device's default stream-ordered
-// memory pool with a release threshold that keeps freed memory cached in the driver.
+// Per-device execution state of the sm100 backend: one non-blocking stream per device
+// (0..N-1) for each host thread, created on first use, plus the device's default
+// stream-ordered memory pool with a release threshold that keeps freed memory
+// reserved in the driver.
 // The reference pins everything to device 0 and the legacy stream
 // (cuda_context.cpp:37-47); here a tensor's Device.index selects the GPU.
 #pragma once
@@ -33,7 +34,7 @@ class DeviceScope {
 };
 
 int device_count();
-// The stream of the calling thread's current device (creating it on first use).
+// The calling thread's stream for its current device (creating it on first use).
 cudaStream_t current_device_stream();
 
 }  // namespace tensorcx::cuda

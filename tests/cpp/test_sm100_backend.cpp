@@ -15,6 +15,9 @@
 #include <vector>
 #include <thread>
 #include <atomic>
+#include <chrono>
+#include <mutex>
+#include <set>
 
 #include "tensorcx/backends/cpu/cpu_backend.h"
 #include "tensorcx/backends/cuda/cuda_backend.h"
@@ -327,6 +330,72 @@ void concurrency_contract(Backend& gpu, Backend& ref) {
   }
   for (auto& th : threads) th.join();
   check(bad.load() == 0, "concurrent executes from four threads");
+
+  // every thread gets its own stream per device
+  std::set<cudaStream_t> streams;
+  std::mutex mu;
+  std::vector<std::thread> probes;
+  for (int t = 0; t < 4; ++t)
+    probes.emplace_back([&] {
+      cuda::DeviceScope scope(0);
+      std::lock_guard lock(mu);
+      streams.insert(scope.stream());
+    });
+  for (auto& th : probes) th.join();
+  check(streams.size() == 4 && !streams.count(nullptr), "one stream per host thread");
+
+  // calls from four threads overlap: four threads doing K calls each take far less
+  // than four times one thread doing K calls (one shared, synchronized stream would
+  // serialize them)
+  const auto la = on_gpu(randn({256, 1024}, 133)), lb = on_gpu(randn({1024, 256}, 134));
+  const int calls = 200;
+  auto wall = [&](int nthreads) {
+    std::atomic<int> errors{0};
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nthreads; ++t)
+      pool.emplace_back([&] {
+        for (int i = 0; i < calls; ++i) {
+          Tensor m;
+          if (!run(gpu, desc(OpKind::kMatmul), {la, lb}, m).ok()) ++errors;
+        }
+      });
+    for (auto& th : pool) th.join();
+    check(errors.load() == 0, "overlap calls succeed");
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  };
+  (void)wall(4);  // warm every thread's stream and allocations
+  const double one = wall(1), four = wall(4);
+  std::printf("concurrency: %d matmul [256,1024]x[1024,256] calls: 1 thread %.2f ms, 4 threads x %d calls %.2f ms "
+              "(%.2fx the work in %.2fx the time)\n", calls, one, calls, four, 4.0, four / one);
+  check(four < 3.0 * one, "four threads' calls overlap (wall < 3x one thread's)");
+}
+
+// A block returned to the pool from another thread is reused behind that thread's
+// work: the owner's stream waits on the event recorded at the return.
+void cross_thread_pool_contract(Backend& gpu, Backend& ref) {
+  auto pool = std::make_shared<cuda::MemoryPool>(1 << 26, 16);
+  check(pool->enter().ok(), "cross-thread pool enter");
+  const auto a = randn({128, 64}, 141), b = randn({64, 96}, 142);
+  Tensor made;
+  check(run(gpu, desc(OpKind::kMatmul), {on_gpu(a), on_gpu(b)}, made).ok(), "pool matmul");
+  const auto hits_before = pool->stats().hits;
+  std::thread other([&] {
+    Tensor scaled;
+    (void)run(gpu, axis_op(OpKind::kSoftmax, -1), {made}, scaled);  // work on this thread's stream
+    made = Tensor{};  // the last owner dies here: the block goes back from this thread
+  });
+  other.join();
+  check(pool->stats().cached_blocks >= 1 && pool->stats().readiness_failures == 0,
+        "block returned from another thread is cached with its event");
+  Tensor again;
+  check(run(gpu, desc(OpKind::kMatmul), {on_gpu(a), on_gpu(b)}, again).ok(), "pool matmul again");
+  check(pool->stats().hits > hits_before, "the returned block is reused");
+  Tensor r;
+  check(run(ref, desc(OpKind::kMatmul), {cpu::to_core_tensor(a), cpu::to_core_tensor(b)}, r).ok(), "reference matmul");
+  check(close(download(again), cpu::from_core_tensor(r), 1e-4, 1e-4), "result in the reused block");
+  again = Tensor{};
+  check(pool->exit().ok() && pool->stats().in_use_bytes == 0, "cross-thread pool exit");
 }
 }  // namespace
 
@@ -439,6 +508,7 @@ int main() {
   pool_contract();
   surface_contract();
   concurrency_contract(gpu, ref);
+  cross_thread_pool_contract(gpu, ref);
   // the same ops inside a real stream-ordered pool scope
   {
     auto pool = std::make_shared<cuda::MemoryPool>(1 << 28, 64);

@@ -584,6 +584,7 @@ def gpu_arm(args):
 
 def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x, sampler):
     """The other hot-path workloads of BASELINE configs[2..4], device-resident."""
+    from tensorcx_b200 import _abi
     out = {}
     steps = max(5, args.steps)
     g = torch.Generator(device="cuda").manual_seed(77 + rank)
@@ -727,6 +728,35 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
             "bar": "within 1e-5 of the CPU result, or closer to the float64 sum than the CPU"}
         del host
     del xf, xi
+
+    # device-side seeded generation of 2^28 standard normals (each rank its slice of one
+    # stream, at its global offset): HBM-bound, 4 B written per element
+    gen_n = total // world
+    gen_out = torch.empty(gen_n, device="cuda")
+
+    def st_gen():
+        _abi.check(lib.tcx_sm100_random(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), 0,
+                                        ctypes.c_void_p(gen_out.data_ptr()), gen_n, 2024, rank * gen_n, 0.0, 1.0))
+    st_gen()
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    ms = timer.run_hbm(st_gen, steps, 2, sampler, 4 * gen_n) / steps
+    lib.tcx_sm100_timer_enable(0)
+    kern = read_timer(lib)
+    hbm_entry("randn_2^28", 4.0 * gen_n, ms, "random", kern,
+              {"config": f"2^28 float32 N(0,1) from the Philox4x32-10 stream of one seed, {world} slice(s) at "
+                         "their global offsets, 4 B written per element"})
+    del gen_out
+
+    def solo_gen():
+        full = torch.empty(total, device="cuda")
+
+        def one():
+            _abi.check(lib.tcx_sm100_random(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), 0,
+                                            ctypes.c_void_p(full.data_ptr()), total, 2024, 0, 0.0, 1.0))
+        ms1 = solo.run_hbm(one, steps, 2, None, 4 * total) / steps
+        return 4.0 * total / (ms1 * 1e-3) / 1e9
+    strong("randn_2^28", solo_gen)
 
     # strided and multi-axis reductions (1 GiB each): axis 0 of [65536, 4096], and
     # axes (0, 2) of [64, 4096, 1024]; outer rows sharded

@@ -353,6 +353,19 @@ int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, con
 int tcx_sm100_copy_to_device(tcx_stream_t stream, void* dst, const void* src, size_t bytes);
 int tcx_sm100_copy_to_host(tcx_stream_t stream, void* dst, const void* src, size_t bytes);
 
+/* Seeded float32 generation on the device, in place of drawing on the host and
+ * uploading: tensor.cx's randn (python/tensorcx/tensor.py:485-497) draws with NumPy
+ * and copies through from_cpu (cpp/tensorcx/backends/cuda/cuda_backend.cpp:215-236).
+ * Writes elements [offset, offset + count) of the stream of `seed` into out[0, count).
+ * The stream is counter-based (Philox4x32-10): element e depends only on (seed, e),
+ * so slices generated at different offsets (e.g. one per GPU) concatenate to the
+ * stream generated whole. NORMAL: mean a, standard deviation b (Box-Muller); UNIFORM:
+ * [a, b) with 24 random bits per value. The numbers differ from NumPy's generator
+ * (PCG64 + ziggurat), which no device generator reproduces. */
+enum { TCX_RANDOM_NORMAL = 0, TCX_RANDOM_UNIFORM = 1 };
+int tcx_sm100_random(tcx_stream_t stream, int distribution, float* out, int64_t count, uint64_t seed,
+                     uint64_t offset, float a, float b);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -360,6 +360,21 @@ class Oracle(_Lib):
     def argmax(self, x, axis=None):
         return self._min_argmax(4, x, axis)
 
+    def philox4x32_10(self, counter, key):
+        """The published Philox4x32-10 block function (tcxo_philox4x32_10)."""
+        ctr = (ctypes.c_uint32 * 4)(*[int(c) & 0xffffffff for c in counter])
+        k = (ctypes.c_uint32 * 2)(*[int(c) & 0xffffffff for c in key])
+        out = (ctypes.c_uint32 * 4)()
+        self.lib.tcxo_philox4x32_10(ctr, k, out)
+        return list(out)
+
+    def random(self, dist, count, seed, offset=0, a=0.0, b=1.0):
+        """Checker of tcx_sm100_random: `dist` "normal" (mean a, std b) or "uniform" [a, b)."""
+        out = np.empty(count, np.float32)
+        self.lib.tcxo_random(ctypes.c_int({"normal": 0, "uniform": 1}[dist]), _ptr(out), ctypes.c_int64(count),
+                             ctypes.c_uint64(seed), ctypes.c_uint64(offset), ctypes.c_float(a), ctypes.c_float(b))
+        return out
+
     def sum_f64(self, x):
         x = np.ascontiguousarray(x, dtype=np.float32)
         return float(self.lib.tcxo_sum_f64(_ptr(x), ctypes.c_int64(x.size)))

@@ -388,3 +388,51 @@ double tcxo_sum_f64(const float* x, int64_t count) {
 /* word helpers exported for the Python side's self-checks */
 uint32_t tcxo_float_bits(float f) { return fbits(f); }
 float tcxo_bits_float(uint32_t w) { return bitsf(w); }
+
+/* ------------------------------------------------------------------ generation
+ * Checker of tcx_sm100_random (no reference counterpart: tensor.cx draws randn on the
+ * host with NumPy, python/tensorcx/tensor.py:485-497). Restates the published
+ * Philox4x32-10 (Salmon et al., SC'11) and the generator's value mapping; the Philox
+ * words and the uniform values are bit-exact, the normal values use double precision
+ * logarithm / square root / sine / cosine (the device uses float32 ones, so they agree
+ * within a few float32 ulps, not bit for bit). Pinned by known answers in
+ * tests/test_oracle.py: Philox4x32-10 of a zero counter and key, and the C++26
+ * std::philox4x32 requirement that its 10000th output after default seeding (key
+ * 20111115) is 1955073260. */
+void tcxo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+  uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3], k0 = key[0], k1 = key[1];
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0, n1 = (uint32_t)p1;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1, n3 = (uint32_t)p0;
+    c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* Elements [offset, offset + count) of the stream of `seed`: dist 0 normal (mean a,
+ * std b), 1 uniform [a, b). */
+void tcxo_random(int dist, float* out, int64_t count, uint64_t seed, uint64_t offset, float a, float b) {
+  const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  const float inv24 = 5.9604644775390625e-08f;
+  for (int64_t i = 0; i < count; ++i) {
+    const uint64_t e = offset + (uint64_t)i, blk = e >> 2;
+    const uint32_t ctr[4] = {(uint32_t)blk, (uint32_t)(blk >> 32), 0u, 0u};
+    uint32_t w[4];
+    tcxo_philox4x32_10(ctr, key, w);
+    const int lane = (int)(e & 3);
+    if (dist == 1) {
+      const float u = (float)(w[lane] >> 8) * inv24;
+      out[i] = fmaf(b - a, u, a);
+    } else {
+      const int p = lane >> 1;
+      const float u1 = (float)((w[2 * p] >> 8) + 1u) * inv24, u2 = (float)(w[2 * p + 1] >> 8) * inv24;
+      const double r = sqrt(-2.0 * log((double)u1));
+      const double t = 2.0 * 3.14159265358979323846 * (double)u2;
+      const float z = (float)((lane & 1) ? r * sin(t) : r * cos(t));
+      out[i] = fmaf(b, z, a);
+    }
+  }
+}

@@ -18,6 +18,7 @@ OP = dict(add=1, multiply=2, matmul=3, sum=4, max=5, mean=6, exp=7, gelu=8, silu
           rmsnorm=11, layernorm=12, subtract=13, divide=14, min=41, argmax=42, clip=43)
 ACT = dict(none=0, silu=1, relu=2)
 MATMUL_PATH = dict(auto=0, ffma=1, tensor=2)
+RANDOM = dict(normal=0, uniform=1)
 
 _vp, _i64, _sz, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t, ctypes.c_int32, ctypes.c_float
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -73,6 +74,7 @@ SIGNATURES = {
                                            _i64p, _i64p, _i64p, _i32, _i64p, _f32, _i32, _vp, _sz]),
     "tcx_sm100_copy_to_device": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
     "tcx_sm100_copy_to_host": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
+    "tcx_sm100_random": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _i64, ctypes.c_uint64, ctypes.c_uint64, _f32, _f32]),
     "tcx_sm100_matmul_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int]),
     "tcx_sm100_matmul": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i32,
                                         _vp, ctypes.c_int, ctypes.c_int, _vp, _sz]),

@@ -22,7 +22,9 @@
 #include "tensorcx/backends/cuda/cuda_context.h"
 #include "tensorcx/backends/cuda/cuda_device.h"
 #include "tensorcx/backends/cuda/cuda_external_storage.h"
+#include "tensorcx/backends/cuda/cuda_kernel.h"
 #include "tensorcx/backends/cuda/cuda_memory_pool.h"
+#include "tensorcx/backends/cuda/cuda_profile.h"
 #include "tensorcx/core/inference.h"
 #include "tensorcx/core/math.h"
 #include "tensorcx/core/shape.h"
@@ -154,6 +156,14 @@ class Executor {
 
   void* ptr(std::size_t i) const { return in_[i].buffer()->data(); }
 
+  // One C-ABI call inside the profiler's compute span and device interval named `name`
+  // (the reference's launch_* names); its completion wait happens inside the span.
+  template <typename Call>
+  Status launch(const char* name, const char* what, Call&& call) {
+    ProfiledLaunch profiled(name, scope_.stream());
+    return profiled.complete(abi_status(call(), what));
+  }
+
   Expected<std::shared_ptr<CudaBuffer>> output(DType dtype, const Shape& shape) {
     return CudaBuffer::create(dtype, shape, scope_.device());
   }
@@ -176,6 +186,7 @@ class Executor {
     const auto count = numel(desc.shape);
     if (count) {
       if (desc.dtype == DType::kBool) {
+        ProfileScope span(ProfileCategory::kMemset, "cudaMemsetAsync", "cuda", buffer.value()->nbytes());
         auto st = runtime_status(cudaMemsetAsync(buffer.value()->data(), e_.op.scalar_value != 0,
                                                  buffer.value()->nbytes(), scope_.stream()),
                                  "CUDA bool fill");
@@ -191,7 +202,8 @@ class Executor {
           const auto v = static_cast<float>(e_.op.scalar_value);
           std::memcpy(&bits, &v, 4);
         }
-        auto st = abi_status(tcx_sm100_fill(abi_stream(scope_), buffer.value()->data(), count, bits), "CUDA fill");
+        auto st = launch("launch_fill", "CUDA fill", [&] {
+          return tcx_sm100_fill(abi_stream(scope_), buffer.value()->data(), count, bits); });
         if (!st.ok()) return st;
       }
     }
@@ -212,13 +224,12 @@ class Executor {
       const auto nbb = plan.k * plan.n != 0 ? numel(in_[1].shape()) / (plan.k * plan.n) : 1;
       Scratch ws(tcx_sm100_matmul_workspace_bytes(plan.m, plan.n, plan.k, nba, nbb, TCX_MATMUL_AUTO), scope_);
       if (!ws.status().ok()) return ws.status();
-      auto st = abi_status(
-          tcx_sm100_matmul(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
+      auto st = launch("launch_matmul", "CUDA matmul", [&] {
+        return tcx_sm100_matmul(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
                            static_cast<float*>(buffer.value()->data()), plan.m, plan.n, plan.k, batches,
                            plan.batch_shape.data(), plan.lhs_batch_strides.data(), plan.rhs_batch_strides.data(),
                            static_cast<std::int32_t>(plan.batch_shape.size()), nullptr, TCX_ACT_NONE,
-                           TCX_MATMUL_AUTO, ws.data(), ws.bytes()),
-          "CUDA matmul");
+                           TCX_MATMUL_AUTO, ws.data(), ws.bytes()); });
       if (!st.ok()) return st;
     }
     return publish(out, DType::kFloat32, plan.output_shape, buffer.move_value());
@@ -243,12 +254,12 @@ class Executor {
     if (numel(shape)) {
       Scratch ws(tcx_sm100_linear_workspace_bytes(rows, w[1], w[0], TCX_MATMUL_AUTO), scope_);
       if (!ws.status().ok()) return ws.status();
-      auto st = abi_status(tcx_sm100_linear(abi_stream(scope_), static_cast<const float*>(ptr(0)),
+      auto st = launch("launch_matmul", "CUDA linear", [&] {
+        return tcx_sm100_linear(abi_stream(scope_), static_cast<const float*>(ptr(0)),
                                             static_cast<const float*>(ptr(1)),
                                             in_.size() == 3 ? static_cast<const float*>(ptr(2)) : nullptr,
                                             static_cast<float*>(buffer.value()->data()), rows, w[1], w[0],
-                                            TCX_ACT_NONE, TCX_MATMUL_AUTO, ws.data(), ws.bytes()),
-                           "CUDA linear");
+                                            TCX_ACT_NONE, TCX_MATMUL_AUTO, ws.data(), ws.bytes()); });
       if (!st.ok()) return st;
     }
     return publish(out, DType::kFloat32, shape, buffer.move_value());
@@ -262,14 +273,13 @@ class Executor {
     if (!buffer) return buffer.status();
     const auto rank = plan.shape.size();
     if (numel(plan.shape)) {
-      auto st = abi_status(
-          tcx_sm100_attention_softmax(abi_stream(scope_), static_cast<const float*>(ptr(0)),
+      auto st = launch("launch_attention_softmax", "CUDA attention softmax", [&] {
+        return tcx_sm100_attention_softmax(abi_stream(scope_), static_cast<const float*>(ptr(0)),
                                       plan.mask_kind ? ptr(1) : nullptr, static_cast<std::int32_t>(plan.mask_kind),
                                       static_cast<float*>(buffer.value()->data()), plan.shape.data(),
                                       plan.metadata.data() + rank,
                                       plan.mask_kind ? plan.metadata.data() + 2 * rank : nullptr,
-                                      static_cast<std::int32_t>(rank), plan.scale, e_.op.causal ? 1 : 0),
-          "CUDA attention softmax");
+                                      static_cast<std::int32_t>(rank), plan.scale, e_.op.causal ? 1 : 0); });
       if (!st.ok()) return st;
     }
     return publish(out, DType::kFloat32, plan.shape, buffer.move_value());
@@ -345,15 +355,14 @@ class Executor {
                scope_);
     if (!ws.status().ok()) return ws.status();
     const auto srank = scores.size();
-    auto st = abi_status(
-        tcx_sm100_attention(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
+    auto st = launch("launch_attention", "CUDA attention", [&] {
+      return tcx_sm100_attention(abi_stream(scope_), static_cast<const float*>(ptr(0)), static_cast<const float*>(ptr(1)),
                             static_cast<const float*>(ptr(2)), plan.mask_kind ? ptr(3) : nullptr,
                             static_cast<std::int32_t>(plan.mask_kind), static_cast<float*>(buffer.value()->data()),
                             queries, keys, features, v.back(), batch.data(), qs.data(), ks.data(), vs.data(),
                             static_cast<std::int32_t>(rank),
                             plan.mask_kind ? plan.metadata.data() + 2 * srank : nullptr, scale,
-                            e_.op.causal ? 1 : 0, ws.data(), ws.bytes()),
-        "CUDA attention");
+                            e_.op.causal ? 1 : 0, ws.data(), ws.bytes()); });
     if (!st.ok()) return st;
     return publish(out, DType::kFloat32, shape, buffer.move_value());
   }
@@ -372,6 +381,7 @@ class Executor {
       auto buffer = output(dtype, e_.op.reduction_axes->empty() ? t.shape : plan.output_shape);
       if (!buffer) return buffer.status();
       if (e_.op.reduction_axes->empty()) {  // no axes: an independent copy
+        ProfileScope span(ProfileCategory::kCopy, "device_to_device", "cuda", in_[0].nbytes());
         auto st = runtime_status(cudaMemcpyAsync(buffer.value()->data(), ptr(0), in_[0].nbytes(),
                                                  cudaMemcpyDeviceToDevice, scope_.stream()),
                                  "CUDA copy");
@@ -382,12 +392,11 @@ class Executor {
       if (groups) {
         Scratch ws(tcx_sm100_reduce_workspace_bytes(groups * plan.reduction_size), scope_);
         if (!ws.status().ok()) return ws.status();
-        auto st = abi_status(
-            tcx_sm100_reduce_axes(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(), groups,
+        auto st = launch("launch_reduce_axes", "CUDA multi-axis reduction", [&] {
+          return tcx_sm100_reduce_axes(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(), groups,
                                   plan.reduction_size, plan.index_metadata.data(),
                                   static_cast<std::int32_t>(plan.output_shape.size()),
-                                  static_cast<std::int32_t>(t.shape.size()), ws.data(), ws.bytes()),
-            "CUDA multi-axis reduction");
+                                  static_cast<std::int32_t>(t.shape.size()), ws.data(), ws.bytes()); });
         if (!st.ok()) return st;
       }
       return publish(out, dtype, plan.output_shape, buffer.move_value());
@@ -400,10 +409,10 @@ class Executor {
     if (a.value().outer * a.value().inner != 0) {
       Scratch ws(tcx_sm100_axis_workspace_bytes(code, a.value().outer, a.value().reduce, a.value().inner), scope_);
       if (!ws.status().ok()) return ws.status();
-      auto st = abi_status(tcx_sm100_axis(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(),
+      auto st = launch("launch_axis", "CUDA axis reduction", [&] {
+        return tcx_sm100_axis(abi_stream(scope_), code, dt, ptr(0), buffer.value()->data(),
                                           a.value().outer, a.value().reduce, a.value().inner, 0.0f, ws.data(),
-                                          ws.bytes()),
-                           "CUDA axis reduction");
+                                          ws.bytes()); });
       if (!st.ok()) return st;
     }
     return publish(out, dtype, a.value().reduced_shape, buffer.move_value());
@@ -423,10 +432,10 @@ class Executor {
     auto buffer = output(DType::kFloat32, t.shape);
     if (!buffer) return buffer.status();
     if (numel(t.shape)) {
-      auto st = abi_status(tcx_sm100_axis(abi_stream(scope_), static_cast<int>(e_.op.kind), TCX_FLOAT32, ptr(0),
+      auto st = launch("launch_axis", "CUDA row operation", [&] {
+        return tcx_sm100_axis(abi_stream(scope_), static_cast<int>(e_.op.kind), TCX_FLOAT32, ptr(0),
                                           buffer.value()->data(), a.value().outer, a.value().reduce,
-                                          a.value().inner, eps, nullptr, 0),
-                           "CUDA row operation");
+                                          a.value().inner, eps, nullptr, 0); });
       if (!st.ok()) return st;
     }
     return publish(out, DType::kFloat32, t.shape, buffer.move_value());
@@ -453,11 +462,10 @@ class Executor {
       std::size_t next = 1;
       const float* w = op.has_weight ? static_cast<const float*>(ptr(next++)) : nullptr;
       const float* b = op.has_bias ? static_cast<const float*>(ptr(next)) : nullptr;
-      auto st = abi_status(
-          tcx_sm100_affine_norm(abi_stream(scope_), op.kind == OpKind::kAffineRmsNorm ? TCX_OP_RMSNORM : TCX_OP_LAYERNORM,
+      auto st = launch("launch_axis", "CUDA affine normalization", [&] {
+        return tcx_sm100_affine_norm(abi_stream(scope_), op.kind == OpKind::kAffineRmsNorm ? TCX_OP_RMSNORM : TCX_OP_LAYERNORM,
                                 static_cast<const float*>(ptr(0)), static_cast<float*>(buffer.value()->data()),
-                                a.value().outer, a.value().reduce, a.value().inner, eps.value(), w, b),
-          "CUDA affine normalization");
+                                a.value().outer, a.value().reduce, a.value().inner, eps.value(), w, b); });
       if (!st.ok()) return st;
     }
     return publish(out, DType::kFloat32, x.shape, buffer.move_value());
@@ -468,10 +476,10 @@ class Executor {
     const auto& t = e_.inputs[0];
     auto buffer = output(DType::kFloat32, t.shape);
     if (!buffer) return buffer.status();
-    auto st = abi_status(tcx_sm100_unary(abi_stream(scope_), static_cast<int>(e_.op.kind),
+    auto st = launch("launch_unary", "CUDA unary", [&] {
+      return tcx_sm100_unary(abi_stream(scope_), static_cast<int>(e_.op.kind),
                                          static_cast<const float*>(ptr(0)),
-                                         static_cast<float*>(buffer.value()->data()), numel(t.shape)),
-                         "CUDA unary");
+                                         static_cast<float*>(buffer.value()->data()), numel(t.shape)); });
     if (!st.ok()) return st;
     return publish(out, DType::kFloat32, t.shape, buffer.move_value());
   }
@@ -494,12 +502,12 @@ class Executor {
     }
     auto buffer = output(l.dtype, shape);
     if (!buffer) return buffer.status();
-    auto st = abi_status(tcx_sm100_binary(abi_stream(scope_), static_cast<int>(kind),
+    auto st = launch(metadata.empty() ? "launch_binary" : "launch_broadcast_binary", "CUDA binary", [&] {
+      return tcx_sm100_binary(abi_stream(scope_), static_cast<int>(kind),
                                           l.dtype == DType::kFloat32 ? TCX_FLOAT32 : TCX_INT32, ptr(0), ptr(1),
                                           buffer.value()->data(), numel(shape),
                                           metadata.empty() ? nullptr : metadata.data(),
-                                          metadata.empty() ? 0 : static_cast<std::int32_t>(shape.size())),
-                         "CUDA binary");
+                                          metadata.empty() ? 0 : static_cast<std::int32_t>(shape.size())); });
     if (!st.ok()) return st;
     return publish(out, l.dtype, shape, buffer.move_value());
   }
@@ -513,17 +521,17 @@ class Executor {
     if (plan.groups) {
       Status st;
       if (e_.op.kind == OpKind::kClip) {
-        st = abi_status(tcx_sm100_clip(abi_stream(scope_), dt, ptr(0), ptr(1), ptr(2), buffer.value()->data(),
-                                       plan.groups, plan.metadata.data(), static_cast<std::int32_t>(plan.rank)),
-                        "CUDA clip");
+        st = launch("launch_math", "CUDA clip", [&] {
+          return tcx_sm100_clip(abi_stream(scope_), dt, ptr(0), ptr(1), ptr(2), buffer.value()->data(),
+                                       plan.groups, plan.metadata.data(), static_cast<std::int32_t>(plan.rank)); });
       } else {
         Scratch ws(tcx_sm100_reduce_workspace_bytes(plan.groups * plan.reduce), scope_);
         if (!ws.status().ok()) return ws.status();
-        st = abi_status(tcx_sm100_min_argmax(abi_stream(scope_), static_cast<int>(e_.op.kind), dt, ptr(0),
+        st = launch("launch_math", "CUDA min/argmax", [&] {
+          return tcx_sm100_min_argmax(abi_stream(scope_), static_cast<int>(e_.op.kind), dt, ptr(0),
                                              buffer.value()->data(), plan.groups, plan.reduce,
                                              plan.metadata.data(), static_cast<std::int32_t>(plan.rank),
-                                             ws.data(), ws.bytes()),
-                        "CUDA min/argmax");
+                                             ws.data(), ws.bytes()); });
       }
       if (!st.ok()) return st;
     }
@@ -551,6 +559,7 @@ Expected<std::shared_ptr<CudaBuffer>> CudaBuffer::create(DType dtype, const Shap
       buffer->data_ = p.value();
       buffer->pool_ = std::move(pool);
     } else {
+      ProfileScope span(ProfileCategory::kAllocation, "cudaMallocAsync", "cuda", buffer->bytes_);
       auto st = runtime_status(cudaMallocAsync(&buffer->data_, buffer->bytes_, scope.stream()), "CUDA allocation");
       if (!st.ok()) return st;
     }
@@ -625,6 +634,7 @@ CudaBuffer::~CudaBuffer() {
   // before returning), so a stream-ordered free on this thread's stream is safe. An
   // exported buffer may still be read by a foreign consumer on a stream this backend
   // does not track: wait for the device first.
+  ProfileScope span(ProfileCategory::kDeallocation, "cudaFreeAsync", "cuda", bytes_);
   if (exported) {
     (void)cudaDeviceSynchronize();
     cudaGetLastError();
@@ -711,6 +721,7 @@ Expected<CudaTensor> empty(Shape shape, DType dtype, int device) {
       // tensor can reach another thread's stream
       DeviceScope scope(device);
       if (!scope.ready()) return scope.status();
+      ProfileScope wait(ProfileCategory::kSynchronize, "cudaStreamSynchronize", "cuda");
       if (auto st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA allocation"); !st.ok()) return st;
     }
     return CudaTensor(dtype, std::move(shape), buffer.move_value());
@@ -726,6 +737,7 @@ Expected<CudaTensor> from_cpu(const cpu::CpuTensor& tensor, int device) {
     DeviceScope scope(device);
     if (!scope.ready()) return scope.status();
     // pinned staging with parallel host copies for large pageable tensors (synchronous)
+    ProfileScope span(ProfileCategory::kCopy, "host_to_device", "cuda", buffer.value()->nbytes());
     auto st = abi_status(tcx_sm100_copy_to_device(abi_stream(scope), buffer.value()->data(), tensor.data(),
                                                   buffer.value()->nbytes()),
                          "CUDA upload");
@@ -739,6 +751,7 @@ Expected<cpu::CpuTensor> to_cpu(const CudaTensor& tensor) {
   if (tensor.nbytes()) {
     DeviceScope scope(tensor.buffer()->device());
     if (!scope.ready()) return scope.status();
+    ProfileScope span(ProfileCategory::kCopy, "device_to_host", "cuda", tensor.nbytes());
     auto st = abi_status(tcx_sm100_copy_to_host(abi_stream(scope), result.mutable_data(), tensor.buffer()->data(),
                                                 tensor.nbytes()),
                          "CUDA download");
@@ -749,9 +762,10 @@ Expected<cpu::CpuTensor> to_cpu(const CudaTensor& tensor) {
 
 // ------------------------------------------------------------------ execute
 Status CudaBackend::execute(const BackendExecution& e) {
+  ProfileScope profile(ProfileCategory::kDispatch, "execute", "cuda", std::nullopt,
+                       e.op_class == BackendOpClass::kPrimitive ? std::optional{e.op.kind} : std::nullopt);
   try {
-    if (e.op_class == BackendOpClass::kKernel)
-      return {StatusCode::kUnavailable, "the sm100 backend serves primitives; compiled kernels are not supported"};
+    if (e.op_class == BackendOpClass::kKernel) return execute_compiled_kernel(e);
     if (auto st = validate_primitive_execution_contract(e, "cuda"); !st.ok()) return st;
     std::vector<CudaTensor> in;
     in.reserve(e.inputs.size());
@@ -768,6 +782,7 @@ Status CudaBackend::execute(const BackendExecution& e) {
     Tensor result;
     Executor ex(e, in, scope);
     if (auto st = ex.run(result); !st.ok()) return st;
+    // every launch already waited inside its span; this only catches stray work (a copy)
     if (auto st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA stream synchronize"); !st.ok())
       return st;
     e.outputs[0] = std::move(result);  // publish only on success

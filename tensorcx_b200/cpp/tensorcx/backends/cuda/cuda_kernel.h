@@ -1,7 +1,9 @@
 // Compiled-kernel surface of the reference backend (cpp/tensorcx/backends/cuda/
-// cuda_kernel.h:7-37), kept so the bindings that load DSL-compiled PTX link unchanged.
-// Compiled kernels are not part of this backend's data path: every entry reports
-// kUnavailable with a message saying so, and modules are never created.
+// cuda_kernel.h:7-37), which the bindings that load generated PTX link against: PTX
+// for sm_100a with a manifest line, one entry with three float32 tensor slots and a
+// uint32 guard, launched on the calling thread's stream into a private result
+// (the output template copy is skipped when the manifest promises a full per-thread
+// write; see cuda_kernel.cpp).
 #pragma once
 
 #include <memory>
@@ -17,8 +19,9 @@ struct KernelSignature {
   std::uint32_t output_index{0}, guard_index{0};
 };
 
-// A textual description of a compiled kernel's interface (argument kinds, operation,
-// output and guard positions), stable for equal inputs.
+// The manifest line a producer writes at the top of the PTX ("// " + manifest): the
+// contract version (v2 = write-per-thread-no-output-read), platform, target, operation,
+// argument kinds, output and guard positions.
 std::string kernel_manifest(const KernelSignature& signature, const std::string& operation = "add",
                             bool write_per_thread_no_output_read = false);
 Status compiled_kernel_support();
@@ -37,7 +40,9 @@ class CudaKernelModule {
                               std::uint32_t threads, std::uint32_t block) const;
 
  private:
-  CudaKernelModule() = default;
+  CudaKernelModule();
+  struct Impl;
+  std::unique_ptr<Impl> impl_;
   KernelSignature signature_;
   std::string id_, entry_;
 };

@@ -12,6 +12,7 @@
 #include <stdexcept>
 
 #include "tensorcx/backends/cuda/cuda_device.h"
+#include "tensorcx/core/profiling.h"
 
 namespace tensorcx::cuda {
 namespace {
@@ -149,6 +150,7 @@ Status MemoryPool::drop_idle_locked(int device, bool every_device) {
 }
 
 Expected<void*> MemoryPool::allocate(std::size_t bytes) {
+  ProfileScope span(ProfileCategory::kMemoryPool, "pool_acquire", "cuda", bytes);
   std::lock_guard lock(mutex_);
   if (t_entered != this || !stats_.active) return invalid("memory pool allocation outside its active scope");
   if (bytes == 0) return invalid("memory pool allocation of zero bytes");
@@ -189,6 +191,7 @@ Expected<void*> MemoryPool::allocate(std::size_t bytes) {
 
 void MemoryPool::release(void* pointer, std::size_t bytes, bool reusable, bool /*context_ready*/) noexcept {
   try {
+    ProfileScope span(ProfileCategory::kMemoryPool, "pool_release", "cuda", bytes);
     std::lock_guard lock(mutex_);
     stats_.in_use_bytes -= bytes;
     const bool fits = stats_.cached_blocks < stats_.max_cached_blocks &&

@@ -1,0 +1,126 @@
+// Seeded float32 generation on the device (the reference draws its randn values on
+// the host with NumPy and uploads them: python/tensorcx/tensor.py:485-497,
+// cpp/tensorcx/backends/cuda/cuda_backend.cpp:215-236).
+//
+// Bit stream: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC'11), counter-based: element e of the logical stream takes word
+// e % 4 of Philox(counter = (e / 4 as a 64-bit number, 0, 0), key = seed). A value
+// depends only on (seed, e), so any grid shape, and any split of the stream into
+// slices (shards at offsets), gives the same numbers. It does not reproduce NumPy's
+// PCG64 / ziggurat stream bit for bit; nothing on the device can.
+//
+// Distributions:
+//  * uniform [a, b): u = (w >> 8) * 2^-24 (24 random bits, exact), value = fma(b - a, u, a);
+//  * normal (mean a, std b): Box-Muller on the pair of words (2p, 2p + 1) of a block,
+//    u1 = ((w0 >> 8) + 1) * 2^-24 in (0, 1], u2 = (w1 >> 8) * 2^-24,
+//    r = sqrt(-2 ln u1), element 2p gets r cos(2 pi u2), element 2p + 1 r sin(2 pi u2),
+//    value = fma(b, z, a).
+//
+// HBM-bound: 4 bytes written per element; each thread makes one Philox block (four
+// elements, one 128-bit store when the four land inside the output and aligned).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace tcx {
+namespace {
+
+constexpr uint32_t kPhiloxM0 = 0xD2511F53u, kPhiloxM1 = 0xCD9E8D57u;  // round multipliers
+constexpr uint32_t kPhiloxW0 = 0x9E3779B9u, kPhiloxW1 = 0xBB67AE85u;  // key schedule (Weyl)
+constexpr float kTwoPow24Inv = 5.9604644775390625e-08f;               // 2^-24
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(kPhiloxM0, c.x), lo0 = kPhiloxM0 * c.x;
+    const uint32_t hi1 = __umulhi(kPhiloxM1, c.z), lo1 = kPhiloxM1 * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += kPhiloxW0;
+    k.y += kPhiloxW1;
+  }
+  return c;
+}
+
+template <bool NORMAL>
+__device__ __forceinline__ float4 block_values(uint4 w, float a, float b) {
+  float4 v;
+  if constexpr (NORMAL) {
+    const float u1a = __fmul_rn(static_cast<float>((w.x >> 8) + 1u), kTwoPow24Inv);
+    const float u2a = __fmul_rn(static_cast<float>(w.y >> 8), kTwoPow24Inv);
+    const float u1b = __fmul_rn(static_cast<float>((w.z >> 8) + 1u), kTwoPow24Inv);
+    const float u2b = __fmul_rn(static_cast<float>(w.w >> 8), kTwoPow24Inv);
+    const float ra = sqrtf(-2.0f * logf(u1a)), rb = sqrtf(-2.0f * logf(u1b));
+    float sa, ca, sb, cb;
+    sincospif(2.0f * u2a, &sa, &ca);
+    sincospif(2.0f * u2b, &sb, &cb);
+    v.x = __fmaf_rn(b, __fmul_rn(ra, ca), a);
+    v.y = __fmaf_rn(b, __fmul_rn(ra, sa), a);
+    v.z = __fmaf_rn(b, __fmul_rn(rb, cb), a);
+    v.w = __fmaf_rn(b, __fmul_rn(rb, sb), a);
+  } else {
+    const float span = __fsub_rn(b, a);
+    v.x = __fmaf_rn(span, __fmul_rn(static_cast<float>(w.x >> 8), kTwoPow24Inv), a);
+    v.y = __fmaf_rn(span, __fmul_rn(static_cast<float>(w.y >> 8), kTwoPow24Inv), a);
+    v.z = __fmaf_rn(span, __fmul_rn(static_cast<float>(w.z >> 8), kTwoPow24Inv), a);
+    v.w = __fmaf_rn(span, __fmul_rn(static_cast<float>(w.w >> 8), kTwoPow24Inv), a);
+  }
+  return v;
+}
+
+// Elements [offset, offset + count) of the stream into out[0, count). Thread t of the
+// grid-stride loop makes Philox block first_block + t: elements 4 * block ... + 3.
+template <bool NORMAL>
+__global__ void __launch_bounds__(256)
+random_kernel(float* __restrict__ out, int64_t count, uint64_t offset, uint2 key, float a, float b) {
+  const uint64_t first_block = offset >> 2;
+  const uint64_t end = offset + static_cast<uint64_t>(count);
+  const uint64_t blocks = ((end + 3) >> 2) - first_block;
+  const bool out_aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < blocks;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t blk = first_block + i;
+    const uint4 w = philox4x32_10(make_uint4(static_cast<uint32_t>(blk), static_cast<uint32_t>(blk >> 32), 0u, 0u), key);
+    const float4 v = block_values<NORMAL>(w, a, b);
+    const uint64_t e0 = blk << 2;
+    if (e0 >= offset && e0 + 4 <= end && out_aligned && ((e0 - offset) & 3) == 0) {
+      __stcs(reinterpret_cast<float4*>(out + (e0 - offset)), v);  // streaming: written once, read later
+    } else {
+      const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t e = e0 + j;
+        if (e >= offset && e < end) out[e - offset] = vals[j];
+      }
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tcx
+
+using namespace tcx;
+
+extern "C" int tcx_sm100_random(tcx_stream_t stream, int distribution, float* out, int64_t count, uint64_t seed,
+                                uint64_t offset, float a, float b) {
+  clear_error();
+  if (distribution != TCX_RANDOM_NORMAL && distribution != TCX_RANDOM_UNIFORM)
+    return invalid("unknown random distribution");
+  if (count < 0) return invalid("negative element count");
+  if (count == 0) return TCX_OK;
+  if (!out) return invalid("missing output");
+  if (offset > UINT64_MAX - static_cast<uint64_t>(count) - 3) return invalid("stream offset overflows");
+  if (!(a == a) || !(b == b) || a == INFINITY || a == -INFINITY || b == INFINITY || b == -INFINITY)
+    return invalid("distribution parameters must be finite");
+  if (distribution == TCX_RANDOM_NORMAL && b < 0) return invalid("normal standard deviation must be non-negative");
+  if (distribution == TCX_RANDOM_UNIFORM && !(a <= b)) return invalid("uniform bounds need low <= high");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const uint64_t blocks = ((offset + static_cast<uint64_t>(count) + 3) >> 2) - (offset >> 2);
+  const uint64_t want = (blocks + 255) / 256;
+  const int grid = static_cast<int>(want < static_cast<uint64_t>(8 * sm_count()) ? want : 8 * sm_count());
+  const uint2 key = make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
+  TimedLaunch timer("random", s);
+  if (distribution == TCX_RANDOM_NORMAL) random_kernel<true><<<grid, 256, 0, s>>>(out, count, offset, key, a, b);
+  else random_kernel<false><<<grid, 256, 0, s>>>(out, count, offset, key, a, b);
+  return launch_status("random generation");
+}

@@ -26,7 +26,7 @@ from ._abi import ACT, FLOAT32, INT32, MATMUL_PATH, OP, Partial, check, i64_arra
 __all__ = ["matmul", "sum", "max", "mean", "min", "argmax", "softmax", "rmsnorm", "layernorm",
            "exp", "gelu", "silu", "add", "subtract", "multiply", "divide", "clip", "relu",
            "bias_act", "linear", "attention", "scaled_dot_product_attention", "attention_softmax",
-           "reduce_partial", "reduce_combine", "Partial"]
+           "reduce_partial", "reduce_combine", "Partial", "randn", "rand_uniform"]
 
 
 def _dtype(t: torch.Tensor) -> int:
@@ -595,3 +595,55 @@ def scaled_dot_product_attention(query: torch.Tensor, key: torch.Tensor, value: 
 
 
 attention = scaled_dot_product_attention
+
+
+# -------------------------------------------------------------------- generation
+def _shape_of(shape) -> tuple[int, ...]:
+    dims = (shape,) if isinstance(shape, (int, np.integer)) else tuple(shape)
+    out = []
+    for d in dims:
+        if isinstance(d, (bool, np.bool_)) or not isinstance(d, (int, np.integer)):
+            raise TypeError("shape dimensions must be integers")
+        if d < 0:
+            raise ValueError("shape dimensions must be non-negative")
+        out.append(int(d))
+    return tuple(out)
+
+
+def _seed_of(seed) -> int:
+    if seed is None:
+        import secrets
+        return secrets.randbits(64)
+    if isinstance(seed, (bool, np.bool_)) or not isinstance(seed, (int, np.integer)) or not 0 <= seed < 2**64:
+        raise ValueError("seed must be an integer in [0, 2**64)")
+    return int(seed)
+
+
+def _generate(kind: int, shape, seed, offset: int, a: float, b: float, device) -> torch.Tensor:
+    dims = _shape_of(shape)
+    if isinstance(offset, (bool, np.bool_)) or not isinstance(offset, (int, np.integer)) or offset < 0:
+        raise ValueError("offset must be a non-negative integer")
+    s = _seed_of(seed)
+    out = torch.empty(dims, dtype=torch.float32, device=device)
+    if not out.is_cuda:
+        raise ValueError("generation targets a CUDA device")
+    check(lib().tcx_sm100_random(_stream(), kind, _ptr(out), out.numel(), s, int(offset), a, b))
+    return out
+
+
+def randn(shape, dtype: str = "float32", device="cuda", seed: int | None = None, *, offset: int = 0) -> torch.Tensor:
+    """tensor.cx's randn (python/tensorcx/tensor.py:485-497) made on the device:
+    standard normal float32 from the counter-based stream of `seed`
+    (tcx_sm100_random). Element i is stream element offset + i, so shards made at
+    their global offsets concatenate to the whole tensor. The values are not NumPy's
+    default_rng(seed) values (a host-only PCG64 + ziggurat stream)."""
+    if dtype not in ("float32", torch.float32):
+        raise ValueError("randn only supports float32")
+    return _generate(0, shape, seed, offset, 0.0, 1.0, device)
+
+
+def rand_uniform(shape, low: float = 0.0, high: float = 1.0, device="cuda", seed: int | None = None, *,
+                 offset: int = 0) -> torch.Tensor:
+    """Uniform float32 on [low, high) from the same counter-based stream (24 random
+    bits per value)."""
+    return _generate(1, shape, seed, offset, float(low), float(high), device)

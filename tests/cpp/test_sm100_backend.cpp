@@ -5,6 +5,7 @@
 // descriptors must fail with kInvalidArgument and leave result slots untouched; the
 // memory pool's OOM / free-failure accounting is driven by an injected PoolRuntime
 // (host fakes, no GPU memory exhausted).
+#include <array>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -26,6 +27,7 @@
 #include "tensorcx/backends/cuda/cuda_kernel.h"
 #include "tensorcx/backends/cuda/cuda_device.h"
 #include "tensorcx/backends/cuda/cuda_memory_pool.h"
+#include "tensorcx/core/profiling.h"
 
 using namespace tensorcx;
 
@@ -228,8 +230,8 @@ void error_contract(Backend& gpu) {
   check(outputs[0].device.type == "sentinel", "rejected calls leave the result slot untouched");
 }
 
-// The rest of the reference's backend surface: driver contexts, compiled kernels
-// (unavailable by design) and the external-storage registry and lease.
+// The rest of the reference's backend surface: driver contexts and the
+// external-storage registry and lease.
 struct FakeAccess final : StorageAccess {
   Status validate() const override { return Status::Ok(); }
 };
@@ -257,11 +259,189 @@ struct FakeStorage final : cuda::ExternalStorage {
   void poison() noexcept override {}
 };
 
+// ---------------------------------------------------------------- compiled kernels
+// A generated elementwise add as a producer would emit it for sm_100a: one guarded
+// store per thread, no output reads (written by hand here; the body is plain PTX).
+const char* kAddBody = R"(.version 8.7
+.target sm_100a
+.address_size 64
+
+.visible .entry tensorcx_add_v1(
+	.param .u64 p_a,
+	.param .u64 p_b,
+	.param .u64 p_out,
+	.param .u32 p_n
+)
+{
+	.reg .pred 	%p<2>;
+	.reg .b32 	%r<6>;
+	.reg .f32 	%f<4>;
+	.reg .b64 	%rd<8>;
+
+	ld.param.u64 	%rd1, [p_a];
+	ld.param.u64 	%rd2, [p_b];
+	ld.param.u64 	%rd3, [p_out];
+	ld.param.u32 	%r1, [p_n];
+	mov.u32 	%r2, %ctaid.x;
+	mov.u32 	%r3, %ntid.x;
+	mov.u32 	%r4, %tid.x;
+	mad.lo.s32 	%r5, %r2, %r3, %r4;
+	setp.ge.u32 	%p1, %r5, %r1;
+	@%p1 bra 	$L_done;
+	cvta.to.global.u64 	%rd4, %rd1;
+	cvta.to.global.u64 	%rd5, %rd2;
+	cvta.to.global.u64 	%rd6, %rd3;
+	mul.wide.u32 	%rd7, %r5, 4;
+	add.s64 	%rd4, %rd4, %rd7;
+	add.s64 	%rd5, %rd5, %rd7;
+	add.s64 	%rd6, %rd6, %rd7;
+	ld.global.f32 	%f1, [%rd4];
+	ld.global.f32 	%f2, [%rd5];
+	add.rn.f32 	%f3, %f1, %f2;
+	st.global.f32 	[%rd6], %f3;
+$L_done:
+	ret;
+}
+)";
+
+std::string add_ptx(bool v2, const std::string& body = kAddBody) {
+  return "// " + cuda::kernel_manifest(cuda::KernelSignature{"tttu", 2, 3}, "add", v2) + "\n" + body;
+}
+
+std::vector<KernelArgument> add_args(const Tensor& a, const Tensor& b, const Tensor& out, std::uint32_t n) {
+  std::vector<KernelArgument> args(4);
+  args[0] = {KernelArgumentKind::kTensor, &a, 0};
+  args[1] = {KernelArgumentKind::kTensor, &b, 0};
+  args[2] = {KernelArgumentKind::kTensor, &out, 0};
+  args[3] = {KernelArgumentKind::kUInt32, nullptr, n};
+  return args;
+}
+
+std::size_t count_named(const ProfileResult& r, const char* name) {
+  std::size_t n = 0;
+  for (const auto& e : r.events) n += std::strcmp(e.name, name) == 0;
+  return n;
+}
+
+void compiled_kernel_contract() {
+  check(cuda::compiled_kernel_support().ok(), "compiled kernels supported on sm_100");
+  const cuda::KernelSignature sig{"tttu", 2, 3};
+  // rejected before any JIT: target, manifest, signature, entry
+  std::string wrong_target = add_ptx(true);
+  wrong_target.replace(wrong_target.find("sm_100a\n.address"), 7, "sm_90a ");
+  check(cuda::CudaKernelModule::load(wrong_target, "tensorcx_add_v1", sig).status().code() ==
+            StatusCode::kInvalidArgument, "PTX for another target rejected");
+  check(!cuda::CudaKernelModule::load(kAddBody, "tensorcx_add_v1", sig), "PTX without a manifest rejected");
+  check(!cuda::CudaKernelModule::load(add_ptx(true), "tensorcx_add_v1", cuda::KernelSignature{"tttt", 2, 3}),
+        "malformed signature rejected");
+  check(!cuda::CudaKernelModule::load(add_ptx(true), "tensorcx_relu_v1", sig), "unknown entry rejected");
+  auto v2 = cuda::CudaKernelModule::load(add_ptx(true), "tensorcx_add_v1", sig);
+  auto v1 = cuda::CudaKernelModule::load(add_ptx(false), "tensorcx_add_v1", sig);
+  check(v2.has_value() && v1.has_value(), "v1 and v2 modules load");
+  if (!v2 || !v1) return;
+  check(v2.value()->artifact_id() != v1.value()->artifact_id(), "distinct artifact ids");
+
+  const std::uint32_t n = 1000;
+  const auto ha = randn({n}, 151), hb = randn({n}, 152);
+  std::vector<float> seven(n, 7.0f);
+  const Tensor a = on_gpu(ha), b = on_gpu(hb), templ = on_gpu(cpu::CpuTensor(Shape{n}, seven));
+  auto sum_of = [&](const cpu::CpuTensor& x, const cpu::CpuTensor& y, std::uint32_t upto, const std::vector<float>& rest) {
+    std::vector<float> v(n);
+    for (std::uint32_t i = 0; i < n; ++i) v[i] = i < upto ? x.float_data()[i] + y.float_data()[i] : rest[i];
+    return cpu::CpuTensor(Shape{n}, std::move(v));
+  };
+
+  // v2, every element written: no template copy, a private result, template untouched
+  auto token = begin_profile(1000, true);
+  auto full = cuda::launch_compiled_kernel(v2.value(), add_args(a, b, templ, n), n, 128);
+  auto prof = end_profile(token);
+  check(full.has_value() && close(download(cuda::to_core_tensor(full.value())), sum_of(ha, hb, n, seven), 0, 0),
+        "v2 full write: a + b");
+  check(count_named(prof, "device_to_device") == 0, "v2 full write: no output template copy");
+  bool timed = false;
+  for (const auto& d : prof.device_events) timed = timed || (std::strcmp(d.name, "generated_kernel") == 0 && !d.error);
+  check(timed, "generated kernel launch has a device interval");
+  check(close(download(templ), cpu::CpuTensor(Shape{n}, seven), 0, 0), "output template unchanged");
+
+  // v2, an input aliasing the template keeps reading the template's values
+  auto alias = cuda::launch_compiled_kernel(v2.value(), add_args(templ, b, templ, n), n, 256);
+  check(alias.has_value() &&
+            close(download(cuda::to_core_tensor(alias.value())), sum_of(cpu::CpuTensor(Shape{n}, seven), hb, n, seven), 0, 0),
+        "v2 full write: aliased input reads the template");
+
+  // v1: the result starts as a copy of the template, aliased inputs read the copy
+  token = begin_profile(1000, true);
+  auto copied = cuda::launch_compiled_kernel(v1.value(), add_args(templ, b, templ, n), n, 128);
+  prof = end_profile(token);
+  check(copied.has_value() &&
+            close(download(cuda::to_core_tensor(copied.value())), sum_of(cpu::CpuTensor(Shape{n}, seven), hb, n, seven), 0, 0),
+        "v1: aliased input reads the template copy");
+  check(count_named(prof, "device_to_device") == 1, "v1: one output template copy");
+
+  // v2 but partial work: the untouched suffix keeps the template's bits
+  auto partial = cuda::launch_compiled_kernel(v2.value(), add_args(a, b, templ, n - 37), n - 37, 96);
+  check(partial.has_value() &&
+            close(download(cuda::to_core_tensor(partial.value())), sum_of(ha, hb, n - 37, seven), 0, 0),
+        "partial launch: suffix keeps the template");
+
+  // zero work: no launch, a distinct copy of the template
+  auto zero = cuda::launch_compiled_kernel(v2.value(), add_args(a, b, templ, 0), 0, 32);
+  check(zero.has_value() && zero.value().buffer()->data() != cuda::from_core_tensor(templ).value().buffer()->data() &&
+            close(download(cuda::to_core_tensor(zero.value())), cpu::CpuTensor(Shape{n}, seven), 0, 0),
+        "zero work: a private copy of the template");
+
+  // guard and block limits
+  check(!cuda::launch_compiled_kernel(v2.value(), add_args(a, b, templ, n - 1), n, 128), "guard must equal threads");
+  check(!cuda::launch_compiled_kernel(v2.value(), add_args(a, b, templ, n), n, 4096), "block size limit");
+  // an unknown artifact id through the backend
+  std::array<Tensor, 1> outs{templ};
+  const auto args = add_args(a, b, templ, n);
+  BackendExecution e{BackendOpClass::kKernel, {}, {}, outs, LaunchConfig{n, 1, 1, 128, 1, 1},
+                     CompilationTarget{KernelArtifactKind::kBinary, "no-such-artifact", "tensorcx_add_v1"}, args};
+  cuda::CudaBackend backend;
+  check(backend.execute(e).code() == StatusCode::kInvalidArgument, "unknown artifact rejected");
+}
+
+// ---------------------------------------------------------------- profiling records
+// With a profile active, every execute is a dispatch span, every launch a compute_sync
+// span with a device interval of the same name, pool traffic pool_acquire/_release.
+void profiling_contract(Backend& gpu) {
+  const Tensor a = on_gpu(randn({64, 96}, 161)), b = on_gpu(randn({96, 80}, 162));
+  auto pool = std::make_shared<cuda::MemoryPool>(1 << 24, 16);
+  check(pool->enter().ok(), "profiling pool enter");
+  const auto token = begin_profile(4096, true);
+  Tensor m, s, sum, add;
+  check(run(gpu, desc(OpKind::kMatmul), {a, b}, m).ok(), "profiled matmul");
+  check(run(gpu, axis_op(OpKind::kSoftmax, -1), {m}, s).ok(), "profiled softmax");
+  check(run(gpu, desc(OpKind::kAdd), {s, s}, add).ok(), "profiled add");
+  check(run(gpu, axes_op(OpKind::kSum, {0, 1}), {add}, sum).ok(), "profiled sum");
+  m = s = add = sum = Tensor{};
+  const auto r = end_profile(token);
+  check(pool->exit().ok(), "profiling pool exit");
+  check(count_named(r, "execute") == 4, "one dispatch span per execute");
+  for (const auto& e : r.events)
+    if (std::strcmp(e.name, "execute") == 0) check(e.operation.has_value(), "dispatch span carries the operation");
+  check(count_named(r, "pool_acquire") >= 4 && count_named(r, "pool_release") >= 4, "pool spans");
+  std::set<std::string> names;
+  for (const auto& d : r.device_events) {
+    names.insert(d.name);
+    check(d.error == nullptr && d.elapsed_ms && *d.elapsed_ms >= 0, std::string("device interval measured: ") + d.name);
+    bool paired = false;
+    for (const auto& h : r.events)
+      paired = paired || (h.id == d.host_event_id && h.category == ProfileCategory::kCompute &&
+                          std::strcmp(h.name, d.name) == 0);
+    check(paired, std::string("device interval belongs to its compute_sync span: ") + d.name);
+  }
+  check(names.count("launch_matmul") && names.count("launch_axis") && names.count("launch_binary") &&
+            names.count("launch_reduce_axes"),
+        "launch names of the reference backend");
+  check(r.device_events.size() == 4, "one device interval per launch");
+  // no profile: nothing recorded, nothing timed
+  Tensor quiet;
+  check(run(gpu, desc(OpKind::kExp), {a}, quiet).ok(), "unprofiled call");
+}
+
 void surface_contract() {
-  check(cuda::compiled_kernel_support().code() == StatusCode::kUnavailable, "compiled kernels: unavailable");
-  auto module = cuda::CudaKernelModule::load(".version 8.7", "entry", cuda::KernelSignature{"ff", 1, 0});
-  check(!module && module.status().code() == StatusCode::kUnavailable, "kernel module load: unavailable");
-  check(!cuda::kernel_manifest(cuda::KernelSignature{"ff", 1, 0}).empty(), "kernel manifest text");
   check(cuda::current_process(), "current process");
   auto ctx = cuda::PrimaryContext::acquire();
   check(ctx.has_value() && ctx.value()->get() != nullptr, "primary context retained");
@@ -507,6 +687,8 @@ int main() {
   error_contract(gpu);
   pool_contract();
   surface_contract();
+  compiled_kernel_contract();
+  profiling_contract(gpu);
   concurrency_contract(gpu, ref);
   cross_thread_pool_contract(gpu, ref);
   // the same ops inside a real stream-ordered pool scope

@@ -13,8 +13,11 @@
 //  * uniform [a, b): u = (w >> 8) * 2^-24 (24 random bits, exact), value = fma(b - a, u, a);
 //  * normal (mean a, std b): Box-Muller on the pair of words (2p, 2p + 1) of a block,
 //    u1 = ((w0 >> 8) + 1) * 2^-24 in (0, 1], u2 = (w1 >> 8) * 2^-24,
-//    r = sqrt(-2 ln u1), element 2p gets r cos(2 pi u2), element 2p + 1 r sin(2 pi u2),
-//    value = fma(b, z, a).
+//    r = sqrt(-2 ln u1), t = fma(u2, 2 pi, -pi) in [-pi, pi) (a uniform angle),
+//    element 2p gets r cos t, element 2p + 1 r sin t, value = fma(b, z, a). The sine and
+//    cosine are the SFU's (__sincosf: absolute error at most 2^-21.41 on [-pi, pi]);
+//    the logarithm and square root are the accurate ones, since r near 0 (u1 near 1)
+//    would magnify a coarse logarithm's absolute error.
 //
 // HBM-bound: 4 bytes written per element; each thread makes one Philox block (four
 // elements, one 128-bit store when the four land inside the output and aligned).
@@ -29,6 +32,7 @@ namespace {
 constexpr uint32_t kPhiloxM0 = 0xD2511F53u, kPhiloxM1 = 0xCD9E8D57u;  // round multipliers
 constexpr uint32_t kPhiloxW0 = 0x9E3779B9u, kPhiloxW1 = 0xBB67AE85u;  // key schedule (Weyl)
 constexpr float kTwoPow24Inv = 5.9604644775390625e-08f;               // 2^-24
+constexpr float kPi = 3.14159265358979323846f, kTwoPi = 6.28318530717958647692f;
 
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
 #pragma unroll
@@ -52,8 +56,8 @@ __device__ __forceinline__ float4 block_values(uint4 w, float a, float b) {
     const float u2b = __fmul_rn(static_cast<float>(w.w >> 8), kTwoPow24Inv);
     const float ra = sqrtf(-2.0f * logf(u1a)), rb = sqrtf(-2.0f * logf(u1b));
     float sa, ca, sb, cb;
-    sincospif(2.0f * u2a, &sa, &ca);
-    sincospif(2.0f * u2b, &sb, &cb);
+    __sincosf(__fmaf_rn(u2a, kTwoPi, -kPi), &sa, &ca);
+    __sincosf(__fmaf_rn(u2b, kTwoPi, -kPi), &sb, &cb);
     v.x = __fmaf_rn(b, __fmul_rn(ra, ca), a);
     v.y = __fmaf_rn(b, __fmul_rn(ra, sa), a);
     v.z = __fmaf_rn(b, __fmul_rn(rb, cb), a);

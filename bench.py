@@ -604,6 +604,18 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
             d.update(extra)
         out[name] = d
 
+    def measure_hbm(st, working_bytes):
+        """(ms per step, per-kernel times): the step time with the library's timing hooks
+        off (their events between launches would block the programmatic-launch overlap
+        of back-to-back kernels), then the per-kernel times from a shorter pass with the
+        hooks on."""
+        ms_ = timer.run_hbm(st, steps, 2, sampler, working_bytes) / steps
+        read_timer(lib)
+        lib.tcx_sm100_timer_enable(1)
+        timer.run_hbm(st, max(3, steps // 2), 1, None, working_bytes)
+        lib.tcx_sm100_timer_enable(0)
+        return ms_, read_timer(lib)
+
     # Strong scaling (N > 1): the same whole workload timed on rank 0's GPU alone in
     # this run (the other ranks wait at a barrier), so each sharded workload carries its
     # own speedup and efficiency against one GPU on the same box.
@@ -636,11 +648,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         def st(x=x, fn=fn, kw=kw):
             return fn(x, axis=-1, **kw)
         st()
-        read_timer(lib)
-        lib.tcx_sm100_timer_enable(1)
-        ms = timer.run_hbm(st, steps, 2, sampler, 8 * r * cols) / steps
-        lib.tcx_sm100_timer_enable(0)
-        kern = read_timer(lib)
+        ms, kern = measure_hbm(st, 8 * r * cols)
         hbm_entry(name, 8.0 * r * cols, ms, "row_kernel", kern,
                   {"config": f"[{rows},{cols}] float32, rows sharded {world} way(s), 8 B/element; "
                             "back to back when the data is >= 2x L2, else L2 flushed before each step"})
@@ -684,11 +692,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                 recs = rec.view(1, 16)
             return ops.reduce_combine(recs, op, x.dtype, total)
         st()
-        read_timer(lib)
-        lib.tcx_sm100_timer_enable(1)
-        ms = timer.run_hbm(st, steps, 2, sampler, 4 * shard) / steps
-        lib.tcx_sm100_timer_enable(0)
-        kern = read_timer(lib)
+        ms, kern = measure_hbm(st, 4 * shard)
         stage1 = kern.get("reduce_stage1", (0, 0.0))
         fold = kern.get("reduce_exchange", kern.get("reduce_combine", (0, 0.0)))
         hbm_entry(name, 4.0 * shard, ms, "reduce_stage1", kern,
@@ -738,11 +742,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         _abi.check(lib.tcx_sm100_random(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), 0,
                                         ctypes.c_void_p(gen_out.data_ptr()), gen_n, 2024, rank * gen_n, 0.0, 1.0))
     st_gen()
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    ms = timer.run_hbm(st_gen, steps, 2, sampler, 4 * gen_n) / steps
-    lib.tcx_sm100_timer_enable(0)
-    kern = read_timer(lib)
+    ms, kern = measure_hbm(st_gen, 4 * gen_n)
     hbm_entry("randn_2^28", 4.0 * gen_n, ms, "random", kern,
               {"config": f"2^28 float32 N(0,1) from the Philox4x32-10 stream of one seed, {world} slice(s) at "
                          "their global offsets, 4 B written per element"})
@@ -767,11 +767,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         def st(x=x, axis=axis):
             return ops.sum(x, axis=axis)
         st()
-        read_timer(lib)
-        lib.tcx_sm100_timer_enable(1)
-        ms = timer.run_hbm(st, steps, 2, sampler, 4 * x.numel()) / steps
-        lib.tcx_sm100_timer_enable(0)
-        kern = read_timer(lib)
+        ms, kern = measure_hbm(st, 4 * x.numel())
         hbm_entry(name, 4.0 * x.numel(), ms, "axis_chunks" if axis == 0 else "axes_chunks", kern,
                   {"config": f"float32 {list(shape)} sum over axis {axis} per rank (leading axis sharded "
                              f"{world} way(s)), 4 B/element; partials per rank are not combined across ranks; "
@@ -819,9 +815,10 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
             return ops.matmul(a, b)
         st()
         reps = max(5, steps) if size >= 2048 else 50
+        ms = timer.run(st, reps, 3, sampler) / reps  # timing hooks off: no event records per launch
         read_timer(lib)
         lib.tcx_sm100_timer_enable(1)
-        ms = timer.run(st, reps, 3, sampler) / reps
+        timer.run(st, max(3, reps // 2), 1)
         lib.tcx_sm100_timer_enable(0)
         kern = read_timer(lib)
         fl = 2.0 * size ** 3
@@ -932,9 +929,10 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         h = ops.matmul(x, w1, bias=b1, act="relu")
         return ops.softmax(ops.matmul(h, w2, bias=b2), axis=-1)
     mlp()
+    eager_ms = timer.run(mlp, 50, 1, sampler) / 50  # timing hooks off
     read_timer(lib)
     lib.tcx_sm100_timer_enable(1)
-    eager_ms = timer.run(mlp, 50, 1, sampler) / 50
+    timer.run(mlp, 20, 1)
     lib.tcx_sm100_timer_enable(0)
     kern = read_timer(lib)
     # the same forward replayed as one CUDA graph (no host work per op)
@@ -949,7 +947,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                   "per-rank replica; value: the forward captured once as a CUDA graph "
                   "(tensorcx_b200.graphs.CapturedSequence) and replayed back to back; eager_ms: the same ops "
                   "called from Python, stream-ordered, no host sync inside",
-        "gpu_launches_per_step": sum(c for c, _ in kern.values()) / 50,
+        "gpu_launches_per_step": sum(c for c, _ in kern.values()) / 20,
         "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()}}
     return out
 

@@ -60,6 +60,15 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
   return v;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization (launch_after) may start while the kernel before it in the stream is
+// still running; dependents_may_launch() in that earlier kernel lets it be scheduled,
+// and wait_for_prior_grid() in it blocks until the earlier grid has finished and its
+// memory is visible (a no-op for a kernel launched the ordinary way). The fold kernels
+// are then resident when stage 1 ends instead of paying a launch.
+__device__ __forceinline__ void dependents_may_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_for_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 struct Acc {
   float f[4 * kUnroll];
   uint32_t u[4 * kUnroll];
@@ -266,6 +275,7 @@ reduce_stage1(const uint32_t* __restrict__ x, int64_t rows, int64_t n, int64_t c
       else take<K, FP>(a, 0, __ldg(xr + j), j + index_base);
     }
 
+    if (row + gridDim.y >= rows) dependents_may_launch();  // this CTA's last row: its loads are done
     uint32_t bits = 0, key = a.key;
     int64_t idx = a.idx;
     if constexpr (kBestKind) best.result(xr + begin, begin + index_base, key, idx);
@@ -323,6 +333,8 @@ template <int K>
 __global__ void __launch_bounds__(1024)
 reduce_stage2(const tcx_partial* __restrict__ part, int nparts, int64_t rows, int64_t n,
               const uint32_t* __restrict__ x, int64_t index_base, int mode, void* out) {
+  wait_for_prior_grid();
+  dependents_may_launch();
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0;
     int64_t idx = INT64_MAX;
@@ -343,6 +355,7 @@ reduce_stage2(const tcx_partial* __restrict__ part, int nparts, int64_t rows, in
 template <int K>
 __global__ void combine_records(const tcx_partial* __restrict__ parts, int nparts,
                                 int64_t total, int mode, void* out) {
+  wait_for_prior_grid();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0, best_bits = 0;
   int64_t idx = INT64_MAX;
@@ -389,6 +402,7 @@ __global__ void __launch_bounds__(1024)
 reduce_stage2_exchange(const tcx_partial* __restrict__ part, int nparts, const uint32_t* __restrict__ x,
                        int64_t index_base, Mailboxes mb, int rank, int world, uint64_t epoch, uint64_t limit_ns,
                        int64_t total, int mode, void* out, int* err) {
+  wait_for_prior_grid();
   uint32_t bits = K == kSumF ? __float_as_uint(0.0f) : 0u, key = 0;
   int64_t idx = INT64_MAX;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
@@ -398,36 +412,43 @@ reduce_stage2_exchange(const tcx_partial* __restrict__ part, int nparts, const u
     else if (better(p.key, p.index, key, idx)) { key = p.key; idx = p.index; }
   }
   block_fold<K>(bits, key, idx);
-  if (threadIdx.x != 0) return;
   const bool sum_kind = K <= kSumI;
   const int64_t set = static_cast<int64_t>(epoch & 1) * world;
-  {
+  __shared__ uint64_t s_rec[2];
+  __shared__ int s_late;
+  if (threadIdx.x == 0) {
     const uint32_t rec_bits = sum_kind ? bits : (idx == INT64_MAX ? 0u : x[idx - index_base]);
-    const uint64_t lo = static_cast<uint64_t>(key) | (static_cast<uint64_t>(rec_bits) << 32);
-    const uint64_t hi = static_cast<uint64_t>(idx);
-    for (int r = 0; r < world; ++r) {
-      uint64_t* slot = reinterpret_cast<uint64_t*>(mb.box[r] + (set + rank) * kSlotBytes);
-      asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(slot), "l"(lo), "l"(hi) : "memory");
-      st_release_sys(slot + 2, epoch);
-    }
+    s_rec[0] = static_cast<uint64_t>(key) | (static_cast<uint64_t>(rec_bits) << 32);
+    s_rec[1] = static_cast<uint64_t>(idx);
+    s_late = 0;
   }
+  __syncthreads();
+  // one thread per rank: store this rank's record into slot `rank` of rank r's mailbox
+  // (a peer store over NVLink), release it with the epoch, then wait (bounded) for rank
+  // r's record in this rank's own mailbox
   const char* mine = mb.box[rank] + set * kSlotBytes;
-  const uint64_t start = ptx::globaltimer();
-  for (int r = 0; r < world; ++r) {
+  if (threadIdx.x < world) {
+    const int r = threadIdx.x;
+    uint64_t* slot = reinterpret_cast<uint64_t*>(mb.box[r] + (set + rank) * kSlotBytes);
+    asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(slot), "l"(s_rec[0]), "l"(s_rec[1]) : "memory");
+    st_release_sys(slot + 2, epoch);
     const uint64_t* flag = reinterpret_cast<const uint64_t*>(mine + r * kSlotBytes) + 2;
-    bool late = false;
+    const uint64_t start = ptx::globaltimer();
     while (ld_acquire_sys(flag) != epoch) {
-      if (ptx::globaltimer() - start > limit_ns) { late = true; break; }
-    }
-    if (late) {
-      record_device_error(err, 0x501);
-      break;
+      if (ptx::globaltimer() - start > limit_ns) {
+        atomicExch(&s_late, 1);
+        break;
+      }
     }
   }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  if (s_late) record_device_error(err, 0x501);
   uint32_t fbits = K == kSumF ? __float_as_uint(0.0f) : 0u, fkey = 0, best_bits = 0;
   int64_t fidx = INT64_MAX;
   for (int r = 0; r < world; ++r) {
     const uint64_t* slot = reinterpret_cast<const uint64_t*>(mine + r * kSlotBytes);
+    (void)ld_acquire_sys(slot + 2);  // pairs with rank r's release (its waiter saw the epoch)
     uint64_t lo, hi;
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "l"(slot) : "memory");
     const uint32_t pkey = static_cast<uint32_t>(lo), pbits = static_cast<uint32_t>(lo >> 32);
@@ -789,6 +810,22 @@ __global__ void fill_word(uint32_t* out, uint32_t value) { *out = value; }
 
 
 // ------------------------------------------------------------------- host side
+// Launches `kernel` with programmatic stream serialization: it may be scheduled while
+// the previous kernel in the stream runs and waits for it in wait_for_prior_grid().
+template <typename... Params, typename... Args>
+void launch_after(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 int kind_of(int op, int dtype) {
   if (op == TCX_OP_SUM || op == TCX_OP_MEAN) return dtype == TCX_FLOAT32 ? kSumF : kSumI;
   if (op == TCX_OP_MAX || op == TCX_OP_ARGMAX) return kBestMax;
@@ -846,21 +883,21 @@ int tree_reduce(cudaStream_t s, int op, int dtype, const void* input, int64_t ro
   switch (kind) {
     case kSumF:
       launch_stage1<kSumF, true>(s, x, rows, n, index_base, parts, g);
-      reduce_stage2<kSumF><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kSumF>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     case kSumI:
       launch_stage1<kSumI, false>(s, x, rows, n, index_base, parts, g);
-      reduce_stage2<kSumI><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kSumI>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     case kBestMax:
       if (fp) launch_stage1<kBestMax, true>(s, x, rows, n, index_base, parts, g);
       else launch_stage1<kBestMax, false>(s, x, rows, n, index_base, parts, g);
-      reduce_stage2<kBestMax><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kBestMax>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     default:
       if (fp) launch_stage1<kBestMin, true>(s, x, rows, n, index_base, parts, g);
       else launch_stage1<kBestMin, false>(s, x, rows, n, index_base, parts, g);
-      reduce_stage2<kBestMin><<<grid2, 1024, 0, s>>>(parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kBestMin>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
   }
   return launch_status("tree reduction");
@@ -1057,10 +1094,10 @@ int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype, const tcx_p
   const int mode = out_mode(op);
   TimedLaunch timer("reduce_combine", s);
   switch (kind_of(op, dtype)) {
-    case kSumF: combine_records<kSumF><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
-    case kSumI: combine_records<kSumI><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
-    case kBestMax: combine_records<kBestMax><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
-    default: combine_records<kBestMin><<<1, 32, 0, s>>>(partials, nparts, total_count, mode, output); break;
+    case kSumF: launch_after(combine_records<kSumF>, 1, 32, s, partials, nparts, total_count, mode, output); break;
+    case kSumI: launch_after(combine_records<kSumI>, 1, 32, s, partials, nparts, total_count, mode, output); break;
+    case kBestMax: launch_after(combine_records<kBestMax>, 1, 32, s, partials, nparts, total_count, mode, output); break;
+    default: launch_after(combine_records<kBestMin>, 1, 32, s, partials, nparts, total_count, mode, output); break;
   }
   return launch_status("reduction combine");
 }
@@ -1161,19 +1198,19 @@ int tcx_sm100_reduce_sharded(tcx_stream_t stream, int op, int dtype, const void*
   TimedLaunch timer("reduce_exchange", s);
   switch (kind) {
     case kSumF:
-      reduce_stage2_exchange<kSumF><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+      launch_after(reduce_stage2_exchange<kSumF>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kSumI:
-      reduce_stage2_exchange<kSumI><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+      launch_after(reduce_stage2_exchange<kSumI>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kBestMax:
-      reduce_stage2_exchange<kBestMax><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
+      launch_after(reduce_stage2_exchange<kBestMax>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
     default:
-      reduce_stage2_exchange<kBestMin><<<1, 1024, 0, s>>>(parts, g.parts, x, index_base, mb, rank, world, epoch,
+      launch_after(reduce_stage2_exchange<kBestMin>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
   }

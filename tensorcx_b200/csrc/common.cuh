@@ -31,6 +31,33 @@ inline int launch_status(const char* what) {
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization (launch_after) may start while the kernel before it in the stream is
+// still running; dependents_may_launch() in that earlier kernel lets it be scheduled,
+// and wait_for_prior_grid() in it blocks until the earlier grid has finished and its
+// memory is visible (a no-op for a kernel launched the ordinary way). The later
+// kernel's launch and set-up then overlap the earlier kernel's tail.
+__device__ __forceinline__ void dependents_may_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_for_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launches `kernel` with programmatic stream serialization (see above); `dynamic_smem`
+// bytes of dynamic shared memory.
+template <typename... Params, typename... Args>
+void launch_after(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s, size_t dynamic_smem,
+                  Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = dynamic_smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 // Device-side error word (see tcx_sm100_device_error); bounded waits set it.
 __device__ __forceinline__ void record_device_error(int* word, int code) {
   if (word) atomicCAS(word, 0, code);

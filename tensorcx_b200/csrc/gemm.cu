@@ -137,6 +137,7 @@ split_lo(const float4* __restrict__ a, float4* __restrict__ wa, int64_t na4, con
     else wb[i - na4] = l;
   }
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
+  dependents_may_launch();  // the GEMM behind may start its set-up
 }
 
 // A [nb][rows][K] -> W [2*nb][rows][Kp] (plane 2b hi, 2b+1 lo), zero padded in K.
@@ -198,6 +199,7 @@ __global__ void __launch_bounds__(256)
 split_rows(const float* __restrict__ a, float* __restrict__ w, int64_t nb, int64_t rows, int64_t k,
            int64_t kp, int* __restrict__ nonfinite) {
   split_rows_body<VEC>(a, w, nb, rows, k, kp, nonfinite, blockIdx.x, gridDim.x);
+  dependents_may_launch();
 }
 
 // B [nb][K][N] -> W [2*nb][N][Kp] (transposed to K-major, zero padded in K).
@@ -265,6 +267,7 @@ __global__ void __launch_bounds__(256)
 split_cols(const float* __restrict__ bsrc, float* __restrict__ w, int64_t nb, int64_t k, int64_t n,
            int64_t kp, int* __restrict__ nonfinite) {
   split_cols_body<VEC>(bsrc, w, nb, k, n, kp, nonfinite, blockIdx.x, gridDim.x);
+  dependents_may_launch();
 }
 
 // Both operands' pre-passes in one launch: blocks [0, ga) split A's rows, the others B
@@ -281,27 +284,50 @@ split_pair(const float* __restrict__ a, float* __restrict__ wa, int64_t nba, int
   } else {
     split_cols_body<VB>(b, wb, nbb, k, n, kp, nonfinite, blockIdx.x - ga, gridDim.x - ga);
   }
+  dependents_may_launch();
 }
 
 // ------------------------------------------------------------ tcgen05 GEMM
-constexpr int kBM = 128, kBN = 256, kBK = 32, kStages = 2;
+constexpr int kBM = 128, kBN = 256, kBK = 32;
 constexpr int kTileA = kBM * kBK * 4;                   // 16 KB
-constexpr int kTileB = kBN * kBK * 4;                   // 32 KB
-constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;    // 96 KB
 constexpr int kGemmThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
-constexpr int kTmemCols = 2 * kBN;                      // two accumulators
+constexpr int kTmemCols = 2 * kBN;                      // two 256-column accumulators (CTA-pair kernel)
 constexpr int kEpiWarps = 8;
 constexpr int kStoreStage = kEpiWarps * 32 * 32 * 4;     // 32 KB: a 32 x 32 staging block per epilogue warp
-constexpr int kGemmSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStoreStage;
 constexpr int kGroupM = 8;
-
-// Instruction descriptor: kind::tf32, D f32, A/B tf32, both K-major, M=128, N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
-
-// The same with B MN-major (bit 16), for the raw mode.
-constexpr uint32_t kIdescMN = kIdesc | (1u << 16);
 constexpr int kChunkB = 32 * kBK * 4;  // 4 KB: 32 columns of B x 32 k rows, one TMA box
+
+// Starts the TMA unit's fetch of the four tensor maps (kernel parameters) while the
+// CTA sets up, so the first loads do not wait for them.
+__device__ __forceinline__ void prefetch_maps(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,
+                                              const CUtensorMap& d) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a)) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&b)) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&c)) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&d)) : "memory");
+}
+
+// Tile shape of the single-SM kernel: 128 x BN outputs per work item, BN = 256 (large
+// products, two 96 KB stages) or 128 (products whose 128 x 256 tiles leave SMs idle:
+// twice the work items, half the epilogue per item, three 64 KB stages). Narrower N
+// tiles would be shared-memory bound: each MMA reads its 128 x 8 A slice again, and at
+// N = 64 that is ~21 flop per byte read against the ~32 the tensor pipe needs at
+// 128 B/clock.
+template <int BN>
+struct SingleTile {
+  static constexpr int kTileB = BN * kBK * 4;
+  static constexpr int kStages = BN == 256 ? 2 : 3;
+  static constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;
+  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kStoreStage;
+  // instruction descriptor: kind::tf32, D f32, A/B tf32, both K-major, M = 128, N = BN;
+  // the MN variant sets bit 16 (B MN-major, the raw mode)
+  static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                     (static_cast<uint32_t>(kBM >> 4) << 24);
+  static constexpr uint32_t kIdescMN = kIdesc | (1u << 16);
+  static constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp (two warps per lane quarter)
+  static_assert(kSmem <= 232448, "shared memory per CTA");
+};
 
 struct GemmArgs {
   float* c;
@@ -382,11 +408,11 @@ __device__ __forceinline__ void store_block_staged(float4* stage, const float (&
 }
 
 // One epilogue warp's share of an accumulator tile: TMEM lanes [32 q, 32 q + 32) (the
-// quarter the warp may access) x 128 columns starting at TMEM column `tcol` and output
-// column `col0`, as four 32-column chunks with the next chunk's tcgen05.ld in flight
+// quarter the warp may access) x 32 NCH columns starting at TMEM column `tcol` and output
+// column `col0`, as NCH 32-column chunks with the next chunk's tcgen05.ld in flight
 // while the current one is finished and stored. `release` runs once every TMEM read of
 // the share is done. `block` points at output (row 0, column 0) of the share.
-template <typename Release>
+template <int NCH = 4, typename Release>
 __device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int lane, float* block, int64_t ld,
                                             int rows_valid, int64_t cols_left, int64_t col0, const float* bias,
                                             int act, bool vec, bool skip, Release release) {
@@ -394,11 +420,11 @@ __device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int la
   uint32_t r0[32], r1[32];
   TCX_LD32(r0, tcol);
 #pragma unroll
-  for (int ci = 0; ci < 4; ++ci) {
+  for (int ci = 0; ci < NCH; ++ci) {
     uint32_t (&cur)[32] = (ci & 1) ? r1 : r0;
     uint32_t (&nxt)[32] = (ci & 1) ? r0 : r1;
     TCX_WAIT_LD32(cur);
-    if (ci + 1 < 4) {
+    if (ci + 1 < NCH) {
       TCX_LD32(nxt, tcol + static_cast<uint32_t>((ci + 1) * 32));
     } else {
       release();
@@ -419,11 +445,14 @@ __device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int la
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
                    const GemmArgs g) {
-  if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
+  using T = SingleTile<BN>;
+  constexpr int kStages = T::kStages, kStageBytes = T::kStageBytes, kTileB = T::kTileB, kTmemCols = T::kTmemCols;
+  if (threadIdx.x == 0) prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -455,8 +484,11 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int64_t total_work = g.batches * g.tiles_m * g.tiles_n * g.splits;
+  // Set-up is done; the pre-pass launched before this kernel must now be complete. With
+  // inf / NaN in the inputs it raised the flag: no work here, the FFMA kernel queued
+  // behind this one computes the product.
+  wait_for_prior_grid();
+  const int64_t total_work = *g.nonfinite ? 0 : g.batches * g.tiles_m * g.tiles_n * g.splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -479,21 +511,21 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
           mbar_expect_tx(fb, kStageBytes);
           const int kc = kb * kBK;
           if (g.raw) {
-            // A: raw rows (hi) and lo rows, K-major; B: raw (hi) and lo, each as kBN / 32
+            // A: raw rows (hi) and lo rows, K-major; B: raw (hi) and lo, each as BN / 32
             // MN-major chunks of 32 columns x 32 k rows (columns past N read as zeros)
             tma_load_3d(smem_u32(st), &map_a_hi, fb, kc, mt * kBM, static_cast<int>(pa));
             tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(pa));
-            for (int j = 0; j < kBN / 32; ++j) {
-              tma_load_3d(smem_u32(st + 2 * kTileA + j * kChunkB), &map_b_hi, fb, nt * kBN + 32 * j, kc,
+            for (int j = 0; j < BN / 32; ++j) {
+              tma_load_3d(smem_u32(st + 2 * kTileA + j * kChunkB), &map_b_hi, fb, nt * BN + 32 * j, kc,
                           static_cast<int>(pb));
-              tma_load_3d(smem_u32(st + 2 * kTileA + kTileB + j * kChunkB), &map_b, fb, nt * kBN + 32 * j, kc,
+              tma_load_3d(smem_u32(st + 2 * kTileA + kTileB + j * kChunkB), &map_b, fb, nt * BN + 32 * j, kc,
                           static_cast<int>(pb));
             }
           } else {
             tma_load_3d(smem_u32(st), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa));
             tma_load_3d(smem_u32(st + kTileA), &map_a, fb, kc, mt * kBM, static_cast<int>(2 * pa + 1));
-            tma_load_3d(smem_u32(st + 2 * kTileA), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb));
-            tma_load_3d(smem_u32(st + 2 * kTileA + kTileB), &map_b, fb, kc, nt * kBN, static_cast<int>(2 * pb + 1));
+            tma_load_3d(smem_u32(st + 2 * kTileA), &map_b, fb, kc, nt * BN, static_cast<int>(2 * pb));
+            tma_load_3d(smem_u32(st + 2 * kTileA + kTileB), &map_b, fb, kc, nt * BN, static_cast<int>(2 * pb + 1));
           }
         }
       }
@@ -522,7 +554,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_flag, g.err, 0x102)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = kb0; kb < kb1; ++kb, ++kb_global) {
           const int s = static_cast<int>(kb_global % kStages);
           const uint32_t phase = static_cast<uint32_t>((kb_global / kStages) & 1);
@@ -538,7 +570,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
           const uint64_t db_hi = g.raw ? smem_desc_sw128_mn(b_hi, kChunkB) : smem_desc_sw128(b_hi);
           const uint64_t db_lo = g.raw ? smem_desc_sw128_mn(b_lo, kChunkB) : smem_desc_sw128(b_lo);
           const uint64_t b_step = g.raw ? 64u : 2u;
-          const uint32_t idesc = g.raw ? kIdescMN : kIdesc;
+          const uint32_t idesc = g.raw ? T::kIdescMN : T::kIdesc;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint32_t first = (kb == kb0 && kk == 0) ? 0u : 1u;
@@ -555,7 +587,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   } else {
     // -------------------------------------------------------------- epilogue
     // Eight warps, two per SM sub-partition: warp w drains TMEM lane quarter w & 3 (the
-    // lanes it may access), columns [0, 128) for warps 2-5 and [128, 256) for 6-9.
+    // lanes it may access), columns [0, BN / 2) for warps 2-5 and [BN / 2, BN) for 6-9.
     const int q = warp & 3;
     const int part = warp >= 6 ? 1 : 0;
     int64_t local = 0;
@@ -569,15 +601,15 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       int64_t batch; int mt, nt;
       tile_coords(tile, g, batch, mt, nt);
       const int64_t row0 = static_cast<int64_t>(mt) * kBM + q * 32;  // this warp's first row
-      const int64_t col0 = static_cast<int64_t>(nt) * kBN + part * 128;
+      const int64_t col0 = static_cast<int64_t>(nt) * BN + part * (BN / 2);
       // split-K: the raw partial sums go to this split's slice of the workspace
       const bool raw = g.splits > 1;
       float* block = (raw ? g.partial + (static_cast<int64_t>(split) * g.m + row0) * g.n
                           : g.c + (batch * g.m + row0) * g.n) + col0;
       const int rows_valid = static_cast<int>(g.m - row0 < 32 ? g.m - row0 : 32);
       const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                            static_cast<uint32_t>(acc * kBN + part * 128);
-      drain_share(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, raw ? nullptr : g.bias,
+                            static_cast<uint32_t>(acc * BN + part * (BN / 2));
+      drain_share<T::kChunks>(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, raw ? nullptr : g.bias,
                   raw ? TCX_ACT_NONE : g.act, g.vec_store != 0, *abort_flag != 0, [&] {
                     // all TMEM reads of this accumulator are done: hand it back to the MMA warp
                     tc_fence_before();
@@ -587,6 +619,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
     }
   }
 
+  dependents_may_launch();  // the split-K reduce / fallback behind may start its set-up
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -631,7 +664,7 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
                         const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
                         const GemmArgs g) {
   // g.tiles_m counts 256-row tiles here; both CTAs of a pair return together
-  if (*g.nonfinite) return;  // the FFMA kernel queued behind this one does the work
+  if (threadIdx.x == 0) prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2Bytes);
@@ -666,8 +699,9 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int64_t total_tiles = g.batches * g.tiles_m * g.tiles_n;
+  // as in the single-SM kernel: the pre-pass must be complete; the flag means no work
+  wait_for_prior_grid();
+  const int64_t total_tiles = *g.nonfinite ? 0 : g.batches * g.tiles_m * g.tiles_n;
   const int64_t cid = cluster_index(), ncl = cluster_count();
 
   if (warp == 0) {
@@ -789,6 +823,7 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
     }
   }
 
+  dependents_may_launch();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -820,6 +855,7 @@ __global__ void __launch_bounds__(256)
 gemm_ffma_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ c,
                  int64_t m, int64_t n, int64_t k, int64_t batches, BatchMap bm,
                  const float* __restrict__ bias, int act, const int* __restrict__ nonfinite, int mode) {
+  wait_for_prior_grid();
   if (mode == 1 && !*nonfinite) return;
   __shared__ float as[kFK][kFM + 4];
   __shared__ float bs[kFK][kFN + 4];
@@ -893,6 +929,7 @@ __global__ void __launch_bounds__(256)
 splitk_reduce(const float* __restrict__ partial, float* __restrict__ out, int64_t mn, int64_t n, int splits,
               const float* __restrict__ bias, int act, const int* __restrict__ nonfinite,
               const float* __restrict__ lhs, const float* __restrict__ rhs, int64_t k, int rhs_kmajor) {
+  wait_for_prior_grid();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   if (*nonfinite) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < mn; i += stride) {
@@ -1015,11 +1052,18 @@ bool use_pair(int64_t m, int64_t n, int64_t batches, int sms) {
   return m >= 2 * kHalf && n >= kBN && pair_tiles >= sms / 4;
 }
 
-// Split-K factor for a single-batch product whose 128 x 256 tiles fill less than half
+// N tile of the single-SM kernel: 128 when 128 x 256 tiles would leave SMs without a
+// tile (small products: more, smaller work items, each with half the epilogue) or when
+// N <= 128 (a 256-wide tile would be half empty), else 256.
+int single_bn(int64_t m, int64_t n, int64_t batches, int sms) {
+  return n <= 128 || batches * ceil_div(m, kBM) * ceil_div(n, kBN) < sms ? 128 : kBN;
+}
+
+// Split-K factor for a single-batch product whose 128 x BN tiles fill less than half
 // of the SMs: each split keeps >= 4 k-blocks, and tiles x splits stays within the SMs.
 int split_count(int64_t m, int64_t n, int64_t kp, int64_t batches, int sms) {
   if (batches != 1 || use_pair(m, n, batches, sms)) return 1;
-  const int64_t tiles = ceil_div(m, kBM) * ceil_div(n, kBN);
+  const int64_t tiles = ceil_div(m, kBM) * ceil_div(n, single_bn(m, n, batches, sms));
   const int64_t num_kb = kp / kBK;
   if (2 * tiles > sms || num_kb < 8) return 1;
   const int64_t want = std::max<int64_t>(1, std::min<int64_t>(num_kb / 4, sms / tiles));
@@ -1154,6 +1198,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
                 float* partial = nullptr, bool raw = false) {
   const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
   const bool pair = use_pair(m, n, batches, sms);
+  const int bn = pair ? kBN : single_bn(m, n, batches, sms);
   if (pair || batches != 1 || !partial) splits = 1;
   alignas(64) CUtensorMap map_a, map_b, map_a_hi, map_b_hi;
   if (raw) {
@@ -1163,7 +1208,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
         !make_map(&map_b, wb, nbb, k, n, kBK, true) || !make_map(&map_b_hi, rhs, nbb, k, n, kBK, true))
       return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
   } else {
-    if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : kBN))
+    if (!make_map(&map_a, wa, 2 * nba, m, kp, kBM) || !make_map(&map_b, wb, 2 * nbb, n, kp, pair ? kHalf : bn))
       return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
     map_a_hi = map_a;
     map_b_hi = map_b;
@@ -1173,8 +1218,10 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem) !=
-            cudaSuccess ||
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SingleTile<256>::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tf32x3_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SingleTile<128>::kSmem) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemm2Smem) !=
             cudaSuccess)
       return launch_status("gemm smem attribute");
@@ -1189,7 +1236,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.lhs_mk = m * k; g.rhs_kn = k * n;
   g.num_kb = static_cast<int32_t>(kp / kBK);
   g.tiles_m = static_cast<int32_t>(ceil_div(m, kBM));
-  g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
+  g.tiles_n = static_cast<int32_t>(ceil_div(n, bn));
   g.act = act;
   g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0) ? 1 : 0;
   g.batches = batches;
@@ -1200,6 +1247,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.raw = raw ? 1 : 0;
   if (g.splits > 1) g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(partial) % 16 == 0) ? 1 : 0;
   if (pair) {
+    g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
     g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
     const int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
     cudaLaunchConfig_t cfg = {};
@@ -1207,20 +1255,28 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = kGemm2Smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set-up overlaps the pre-pass
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     TimedLaunch timer("gemm_tf32x3", s);
     cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, map_a_hi, map_b_hi, g);
   } else {
     const int64_t work = batches * g.tiles_m * g.tiles_n * g.splits;
     const int grid = static_cast<int>(std::min<int64_t>(work, sms));
     TimedLaunch timer("gemm_tf32x3", s);
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(map_a, map_b, map_a_hi, map_b_hi, g);
+    // launched behind the pre-pass so that its set-up overlaps the pre-pass's tail
+    if (bn == 128)
+      launch_after(gemm_tf32x3_kernel<128>, grid, kGemmThreads, s, SingleTile<128>::kSmem, map_a, map_b, map_a_hi,
+                   map_b_hi, g);
+    else
+      launch_after(gemm_tf32x3_kernel<256>, grid, kGemmThreads, s, SingleTile<256>::kSmem, map_a, map_b, map_a_hi,
+                   map_b_hi, g);
   }
   if (int st = launch_status("tcgen05 matmul")) return st;
   if (g.splits > 1) {
@@ -1230,11 +1286,11 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     const int grid = static_cast<int>(std::min<int64_t>(ceil_div(vec ? mn / 4 : mn, 256), 4LL * sms));
     TimedLaunch timer("splitk_reduce", s);
     if (vec)
-      splitk_reduce<true><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs, k,
-                                               rhs_kmajor ? 1 : 0);
+      launch_after(splitk_reduce<true>, grid, 256, s, 0, partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs,
+                   k, rhs_kmajor ? 1 : 0);
     else
-      splitk_reduce<false><<<grid, 256, 0, s>>>(partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs, k,
-                                                rhs_kmajor ? 1 : 0);
+      launch_after(splitk_reduce<false>, grid, 256, s, 0, partial, output, mn, n, g.splits, bias, act, flag, lhs, rhs,
+                   k, rhs_kmajor ? 1 : 0);
     // the reduce kernel computes the IEEE product itself when the pre-pass saw inf / NaN
     return launch_status("split-K reduce");
   }
@@ -1243,8 +1299,8 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   const int fgrid = static_cast<int>(std::min<int64_t>(ftiles, 16LL * sms));
   {
     TimedLaunch timer("gemm_ffma_fallback", s);
-    if (rhs_kmajor) gemm_ffma_kernel<true><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
-    else gemm_ffma_kernel<false><<<fgrid, 256, 0, s>>>(lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+    if (rhs_kmajor) launch_after(gemm_ffma_kernel<true>, fgrid, 256, s, 0, lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
+    else launch_after(gemm_ffma_kernel<false>, fgrid, 256, s, 0, lhs, rhs, output, m, n, k, batches, bm, bias, act, flag, 1);
   }
   return launch_status("matmul fallback");
 }

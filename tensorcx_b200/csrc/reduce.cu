@@ -60,15 +60,6 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
   return v;
 }
 
-// Programmatic dependent launch: a kernel launched with programmatic stream
-// serialization (launch_after) may start while the kernel before it in the stream is
-// still running; dependents_may_launch() in that earlier kernel lets it be scheduled,
-// and wait_for_prior_grid() in it blocks until the earlier grid has finished and its
-// memory is visible (a no-op for a kernel launched the ordinary way). The fold kernels
-// are then resident when stage 1 ends instead of paying a launch.
-__device__ __forceinline__ void dependents_may_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void wait_for_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 struct Acc {
   float f[4 * kUnroll];
   uint32_t u[4 * kUnroll];
@@ -810,22 +801,6 @@ __global__ void fill_word(uint32_t* out, uint32_t value) { *out = value; }
 
 
 // ------------------------------------------------------------------- host side
-// Launches `kernel` with programmatic stream serialization: it may be scheduled while
-// the previous kernel in the stream runs and waits for it in wait_for_prior_grid().
-template <typename... Params, typename... Args>
-void launch_after(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
-}
-
 int kind_of(int op, int dtype) {
   if (op == TCX_OP_SUM || op == TCX_OP_MEAN) return dtype == TCX_FLOAT32 ? kSumF : kSumI;
   if (op == TCX_OP_MAX || op == TCX_OP_ARGMAX) return kBestMax;
@@ -883,21 +858,21 @@ int tree_reduce(cudaStream_t s, int op, int dtype, const void* input, int64_t ro
   switch (kind) {
     case kSumF:
       launch_stage1<kSumF, true>(s, x, rows, n, index_base, parts, g);
-      launch_after(reduce_stage2<kSumF>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kSumF>, grid2, 1024, s, 0, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     case kSumI:
       launch_stage1<kSumI, false>(s, x, rows, n, index_base, parts, g);
-      launch_after(reduce_stage2<kSumI>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kSumI>, grid2, 1024, s, 0, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     case kBestMax:
       if (fp) launch_stage1<kBestMax, true>(s, x, rows, n, index_base, parts, g);
       else launch_stage1<kBestMax, false>(s, x, rows, n, index_base, parts, g);
-      launch_after(reduce_stage2<kBestMax>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kBestMax>, grid2, 1024, s, 0, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
     default:
       if (fp) launch_stage1<kBestMin, true>(s, x, rows, n, index_base, parts, g);
       else launch_stage1<kBestMin, false>(s, x, rows, n, index_base, parts, g);
-      launch_after(reduce_stage2<kBestMin>, grid2, 1024, s, parts, g.parts, rows, n, x, index_base, mode, out);
+      launch_after(reduce_stage2<kBestMin>, grid2, 1024, s, 0, parts, g.parts, rows, n, x, index_base, mode, out);
       break;
   }
   return launch_status("tree reduction");
@@ -1094,10 +1069,10 @@ int tcx_sm100_reduce_combine(tcx_stream_t stream, int op, int dtype, const tcx_p
   const int mode = out_mode(op);
   TimedLaunch timer("reduce_combine", s);
   switch (kind_of(op, dtype)) {
-    case kSumF: launch_after(combine_records<kSumF>, 1, 32, s, partials, nparts, total_count, mode, output); break;
-    case kSumI: launch_after(combine_records<kSumI>, 1, 32, s, partials, nparts, total_count, mode, output); break;
-    case kBestMax: launch_after(combine_records<kBestMax>, 1, 32, s, partials, nparts, total_count, mode, output); break;
-    default: launch_after(combine_records<kBestMin>, 1, 32, s, partials, nparts, total_count, mode, output); break;
+    case kSumF: launch_after(combine_records<kSumF>, 1, 32, s, 0, partials, nparts, total_count, mode, output); break;
+    case kSumI: launch_after(combine_records<kSumI>, 1, 32, s, 0, partials, nparts, total_count, mode, output); break;
+    case kBestMax: launch_after(combine_records<kBestMax>, 1, 32, s, 0, partials, nparts, total_count, mode, output); break;
+    default: launch_after(combine_records<kBestMin>, 1, 32, s, 0, partials, nparts, total_count, mode, output); break;
   }
   return launch_status("reduction combine");
 }
@@ -1198,19 +1173,19 @@ int tcx_sm100_reduce_sharded(tcx_stream_t stream, int op, int dtype, const void*
   TimedLaunch timer("reduce_exchange", s);
   switch (kind) {
     case kSumF:
-      launch_after(reduce_stage2_exchange<kSumF>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+      launch_after(reduce_stage2_exchange<kSumF>, 1, 1024, s, 0, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kSumI:
-      launch_after(reduce_stage2_exchange<kSumI>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
+      launch_after(reduce_stage2_exchange<kSumI>, 1, 1024, s, 0, parts, g.parts, x, index_base, mb, rank, world, epoch, limit,
                                                       total_count, mode, output, err);
       break;
     case kBestMax:
-      launch_after(reduce_stage2_exchange<kBestMax>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch,
+      launch_after(reduce_stage2_exchange<kBestMax>, 1, 1024, s, 0, parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
     default:
-      launch_after(reduce_stage2_exchange<kBestMin>, 1, 1024, s, parts, g.parts, x, index_base, mb, rank, world, epoch,
+      launch_after(reduce_stage2_exchange<kBestMin>, 1, 1024, s, 0, parts, g.parts, x, index_base, mb, rank, world, epoch,
                                                          limit, total_count, mode, output, err);
       break;
   }

@@ -909,7 +909,35 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                      "frac": (executed / (k_avg * 1e-3) / 1e12) / peak_3x if k_avg else None,
                      "kernel": "flash_tf32x3", "kernel_ms": k_avg,
                      "note": "achieved = flops of the key blocks executed (up to the causal diagonal)"}}
-    del q, k, v
+
+    # the same product with a float additive mask [2048, 2048] (-inf entries mask keys),
+    # broadcast over the heads: read inside the fused kernel
+    mgen = torch.Generator(device="cuda").manual_seed(99)
+    amask = torch.randn(2048, 2048, device="cuda", generator=mgen)
+    amask[torch.rand(2048, 2048, device="cuda", generator=mgen) < 0.1] = float("-inf")
+
+    def st_masked():
+        return ops.attention(q, k, v, amask)
+    st_masked()
+    ms_m = timer.run(st_masked, n_att, 1, sampler) / n_att
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
+    timer.run(st_masked, max(3, n_att // 2), 1)
+    lib.tcx_sm100_timer_enable(0)
+    kern_m = read_timer(lib)
+    fl_m = 4.0 * heads * 2048 * 2048 * 128
+    km_launches, km_ms = kern_m.get("flash_tf32x3", (0, 0.0))
+    km_avg = timer.max_over_ranks(km_ms / max(km_launches, 1))
+    out["attention_masked_32x2048x2048x128"] = {
+        "value": world * fl_m / (ms_m * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_m,
+        "config": f"q,k,v [32,2048,128] float32, float32 additive mask [2048,2048] (10 % -inf) broadcast over "
+                  f"heads, not causal, heads sharded {world} way(s); 4*H*L*S*D flops",
+        "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern_m.items()},
+        "roofline": {"bound": "tensor", "achieved": fl_m / (km_avg * 1e-3) / 1e12 if km_avg else None,
+                     "peak": peak_3x, "unit": "TFLOP/s",
+                     "frac": (fl_m / (km_avg * 1e-3) / 1e12) / peak_3x if km_avg else None,
+                     "kernel": "flash_tf32x3", "kernel_ms": km_avg}}
+    del amask, q, k, v
 
     def solo_attention():
         q1, k1, v1 = (torch.randn(32, 2048, 128, device="cuda", generator=gs) for _ in range(3))

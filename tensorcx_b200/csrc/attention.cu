@@ -517,9 +517,9 @@ int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, con
     const size_t need = flash_workspace_bytes(queries, keys, features, value_features, qn, kn, vn);
     if (!workspace || workspace_bytes < need) return invalid("attention workspace is missing or too small");
     if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("attention workspace must be 1024-byte aligned");
-    return attention_fused(s, q, k, v, output, queries, keys, features, value_features, batches, batch_shape,
-                           q_batch_strides, k_batch_strides, v_batch_strides, batch_rank, scale, causal != 0,
-                           workspace, workspace_bytes);
+    return attention_fused(s, q, k, v, mask, mask_kind, mask_strides, output, queries, keys, features,
+                           value_features, batches, batch_shape, q_batch_strides, k_batch_strides, v_batch_strides,
+                           batch_rank, scale, causal != 0, workspace, workspace_bytes);
   }
   const size_t need = tcx_sm100_attention_workspace_bytes(batches, queries, keys, features, value_features, qn, kn, vn,
                                                           mask_kind);

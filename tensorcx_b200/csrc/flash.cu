@@ -27,9 +27,16 @@
 // Every wait is bounded (4 s of %globaltimer), with the same abort / drain / TMEM
 // release discipline as the GEMM. No TMA multicast.
 //
-// Non-finite inputs (flagged by the split pre-pass) make the kernel exit at once; a
-// row-wise IEEE kernel queued behind it (idle otherwise) computes the result the way
-// the reference composite does (core/inference.cpp:123-160).
+// Masks (the reference's kAttention mask input: bool, false = masked; or float32,
+// added to the scaled scores, -inf = masked) are read inside the kernel: each softmax
+// thread loads its row's 64 mask entries of the next key block while it waits for that
+// block's S, through the mask's broadcast strides. A row with no unmasked key is all
+// zeros, as in the reference.
+//
+// Non-finite inputs (flagged by the split pre-pass, and NaN / +inf in a float mask,
+// flagged by a scan of the mask) make the kernel exit at once; a row-wise IEEE kernel
+// queued behind it (idle otherwise) computes the result the way the reference
+// composite does (core/inference.cpp:123-160), mask included.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -84,6 +91,13 @@ struct FlashArgs {
   int32_t causal;
   int32_t vec8;            // out is 32-byte aligned: 32-byte stores
   float* out;              // [batches, L, dv]
+  // mask (kind 1 bool, 2 float32): element strides per merged batch axis, along the
+  // queries and along the keys (0 or 1); mask_vec: a row's 64 entries of a key block
+  // may be read with 16-byte loads
+  const void* mask;
+  int64_t ms[kMaxFlashBatchRank];
+  int64_t mq, mk;
+  int32_t mask_vec;
   const int* nonfinite;
   int* err;
 };
@@ -98,6 +112,78 @@ __device__ __forceinline__ void batch_planes(const FlashArgs& a, int64_t b, int6
     pv += i * a.vs[d];
   }
 }
+
+__device__ __forceinline__ int64_t mask_offset(const FlashArgs& a, int64_t b) {
+  int64_t off = 0;
+  for (int d = a.rank - 1; d >= 0; --d) {
+    off += (b % a.shape[d]) * a.ms[d];
+    b /= a.shape[d];
+  }
+  return off;
+}
+
+// One row's mask entries for key block [key0, key0 + 64): MK 1 as 64 keep bits (1 =
+// unmasked), MK 2 as 64 biases already in log2 units (-inf = masked). Entries at or past
+// `valid` are not read.
+template <int MK>
+struct MaskBlock {
+  uint32_t keep[2];
+  float bias[MK == 2 ? 64 : 1];
+  __device__ __forceinline__ void load(const FlashArgs& a, int64_t row_off, int64_t key0, int valid) {
+    if constexpr (MK == 1) {
+      const unsigned char* m = static_cast<const unsigned char*>(a.mask) + row_off;
+      if (a.mk == 0) {
+        const uint32_t all = m[0] ? 0xffffffffu : 0u;
+        keep[0] = keep[1] = all;
+      } else if (a.mask_vec && valid == 64) {
+        const uint4* v = reinterpret_cast<const uint4*>(m + key0);
+        uint32_t bits[2] = {0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 w = __ldg(v + i);
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int byte = 0; byte < 4; ++byte)
+              if ((words[j] >> (8 * byte)) & 0xffu) bits[i >> 1] |= 1u << (((i & 1) * 16) + j * 4 + byte);
+        }
+        keep[0] = bits[0];
+        keep[1] = bits[1];
+      } else {
+        keep[0] = keep[1] = 0u;
+        for (int e = 0; e < valid; ++e)
+          if (m[key0 + e]) keep[e >> 5] |= 1u << (e & 31);
+      }
+    } else if constexpr (MK == 2) {
+      const float* m = static_cast<const float*>(a.mask) + row_off;
+      if (a.mk == 0) {
+        const float v = __fmul_rn(m[0], kLog2e);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) bias[e] = v;
+      } else if (a.mask_vec && valid == 64) {
+        const float4* v = reinterpret_cast<const float4*>(m + key0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 w = __ldg(v + i);
+          bias[4 * i] = __fmul_rn(w.x, kLog2e);
+          bias[4 * i + 1] = __fmul_rn(w.y, kLog2e);
+          bias[4 * i + 2] = __fmul_rn(w.z, kLog2e);
+          bias[4 * i + 3] = __fmul_rn(w.w, kLog2e);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) bias[e] = e < valid ? __fmul_rn(m[key0 + e], kLog2e) : -INFINITY;
+      }
+    }
+  }
+  // the scaled score t of entry e with the mask applied
+  __device__ __forceinline__ float apply(float t, int e) const {
+    if constexpr (MK == 1) return (keep[e >> 5] >> (e & 31)) & 1u ? t : -INFINITY;
+    else if constexpr (MK == 2) return bias[e] == -INFINITY ? -INFINITY : __fadd_rn(t, bias[e]);
+    else return t;
+  }
+};
 
 // Item of round r for this CTA: rounds alternate direction over the grid (a snake), so
 // with items ordered longest first each CTA's total stays near the mean (causal items
@@ -117,6 +203,7 @@ __device__ __forceinline__ void item_coords(const FlashArgs& a, int64_t w, int64
   nkb = a.causal ? min(a.kv_blocks, (qt + 1) * (kFQ / kFK)) : a.kv_blocks;
 }
 
+template <int MK>
 __global__ void __launch_bounds__(kFlashThreads, 1)
 flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const FlashArgs a) {
@@ -354,21 +441,29 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       int64_t b; int qt, nkb;
       item_coords(a, w, b, qt, nkb);
       const int64_t query = static_cast<int64_t>(qt) * kFQ + row_in_tile;
+      const bool row_ok = query < a.L;
+      const int64_t mrow = MK ? mask_offset(a, b) + (row_ok ? query : 0) * a.mq : 0;
       float m_use = -INFINITY, l = 0.0f;
       bool aborted = false;
       for (int j = 0; j < nkb; ++j, ++g) {
         const int buf = static_cast<int>(g % kSBufs);
         const uint32_t col_s = static_cast<uint32_t>(buf * 128), col_lo = col_s + kFK;
-        if (!wait_bounded(smem_u32(&s_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x421)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
         const int64_t key0 = static_cast<int64_t>(j) * kFK;
         // keys allowed for this row in this block: [0, lim)
         int64_t lim64 = a.S - key0;
         if (a.causal) lim64 = min(lim64, query - key0 + 1);
         const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kFK ? kFK : lim64));
+        // this row's mask entries of the block, loaded while S is still being computed
+        MaskBlock<MK> mb;
+        if constexpr (MK != 0) {
+          const int64_t left = a.S - key0;
+          mb.load(a, mrow, key0, row_ok ? static_cast<int>(left < kFK ? left : kFK) : 0);
+        }
+        if (!wait_bounded(smem_u32(&s_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x421)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
         // the block's 64 scores of this row, both halves loaded before one wait, kept in
         // registers for both passes (one TMEM round trip per block), scaled to log2 units
         uint32_t s0[32], s1[32];
@@ -380,13 +475,13 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         float mx = -INFINITY;
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float t = __fmul_rn(__uint_as_float(s0[e]), a.scale_log2);
+          const float t = mb.apply(__fmul_rn(__uint_as_float(s0[e]), a.scale_log2), e);
           s0[e] = __float_as_uint(t);
           if (e < lim) mx = fmaxf(mx, t);
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float t = __fmul_rn(__uint_as_float(s1[e]), a.scale_log2);
+          const float t = mb.apply(__fmul_rn(__uint_as_float(s1[e]), a.scale_log2), 32 + e);
           s1[e] = __float_as_uint(t);
           if (32 + e < lim) mx = fmaxf(mx, t);
         }
@@ -423,7 +518,8 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             float p = 0.0f;
-            if (c0 + e < lim) {
+            // masked entries (-inf) give 0, also while every earlier key was masked (m_use -inf)
+            if (c0 + e < lim && (MK == 0 || __uint_as_float(sv[e]) != -INFINITY)) {
               asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(__uint_as_float(sv[e]), m_use)));
             }
             l = __fadd_rn(l, p);
@@ -447,9 +543,8 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err, 0x422))
         break;
       tc_fence_after();
-      const float inv = 1.0f / l;
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;  // no unmasked key: a zero row
       float* orow = a.out + (b * a.L + query) * a.dv;
-      const bool row_ok = query < a.L;
       // O drained in 32-column chunks with the next chunk's TMEM load in flight
       const int nch = a.dv / 32;
       uint32_t o0[32], o1[32];
@@ -508,6 +603,7 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 // over keys in order, recomputing the dot products per pass instead of storing them.
 constexpr int kRowThreads = 128;
 
+template <int MK>
 __global__ void __launch_bounds__(kRowThreads)
 flash_rows_fallback(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                     FlashArgs a, int64_t d, float scale, const int* __restrict__ flag) {
@@ -528,11 +624,21 @@ flash_rows_fallback(const float* __restrict__ q, const float* __restrict__ k, co
     for (int i = threadIdx.x; i < d; i += kRowThreads) qrow[i] = qr[i];
     __syncthreads();
     const int64_t keys = a.causal ? (query + 1 < a.S ? query + 1 : a.S) : a.S;
+    const int64_t mrow = MK ? mask_offset(a, b) + query * a.mq : 0;
+    // cpu_inference.cpp:26-33: a false bool entry or a -inf float entry masks the key;
+    // otherwise score * scale + bias
     auto score = [&](int64_t key) {
+      float bias = 0.0f;
+      if constexpr (MK == 1) {
+        if (!static_cast<const unsigned char*>(a.mask)[mrow + key * a.mk]) return -INFINITY;
+      } else if constexpr (MK == 2) {
+        bias = static_cast<const float*>(a.mask)[mrow + key * a.mk];
+        if (bias == -INFINITY) return -INFINITY;
+      }
       float acc = 0.0f;
       const float* kr = kb + key * d;
       for (int64_t i = 0; i < d; ++i) acc = __fadd_rn(acc, __fmul_rn(qrow[i], kr[i]));
-      return __fmul_rn(acc, scale);
+      return MK == 2 ? __fadd_rn(__fmul_rn(acc, scale), bias) : __fmul_rn(acc, scale);
     };
     float mx = -INFINITY;
     bool nan = false;
@@ -567,6 +673,18 @@ flash_rows_fallback(const float* __restrict__ q, const float* __restrict__ k, co
   }
 }
 
+// NaN or +inf anywhere in a float mask raises *flag (the fused kernel's arithmetic
+// assumes finite or -inf biases; the IEEE row kernel then gives the reference's NaN rows).
+__global__ void __launch_bounds__(256) mask_scan(const float* __restrict__ m, int64_t n, int* __restrict__ flag) {
+  bool bad = false;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float x = __ldg(m + i);
+    bad |= x != x || x == INFINITY;
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+
 size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
 struct FlashLayout {
@@ -589,7 +707,7 @@ FlashLayout flash_layout(int64_t L, int64_t S, int64_t d, int64_t dv, int64_t nq
 
 bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t value_features, int mask_kind,
                     int batch_rank) {
-  return mask_kind == 0 && queries > 0 && keys > 0 && features % kFC == 0 && features <= 128 &&
+  return mask_kind >= 0 && mask_kind <= 2 && queries > 0 && keys > 0 && features % kFC == 0 && features <= 128 &&
          value_features % kFC == 0 && value_features > 0 && value_features <= kMaxDv &&
          batch_rank <= kMaxFlashBatchRank && queries <= INT32_MAX / 2 && keys <= INT32_MAX / 2;
 }
@@ -599,11 +717,21 @@ size_t flash_workspace_bytes(int64_t queries, int64_t keys, int64_t features, in
   return flash_layout(queries, keys, features, value_features, q_batches, k_batches, v_batches).total;
 }
 
-int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, float* out, int64_t L,
-                    int64_t S, int64_t d, int64_t dv, int64_t batches, const int64_t* batch_shape,
-                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int32_t rank,
-                    float scale, int causal, void* workspace, size_t workspace_bytes) {
+int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, const void* mask,
+                    int mask_kind, const int64_t* mask_strides, float* out, int64_t L, int64_t S, int64_t d,
+                    int64_t dv, int64_t batches, const int64_t* batch_shape, const int64_t* q_strides,
+                    const int64_t* k_strides, const int64_t* v_strides, int32_t rank, float scale, int causal,
+                    void* workspace, size_t workspace_bytes) {
   FlashArgs fa{};
+  // mask strides (elements) over [batch..., L, S]: the keys' must be 0 or 1
+  if (mask_kind) {
+    for (int i = 0; i < rank + 2; ++i)
+      if (mask_strides[i] < 0) return invalid("negative attention strides");
+    if (mask_strides[rank + 1] > 1) return invalid("attention last-axis strides must be 0 or 1");
+    fa.mask = mask;
+    fa.mq = mask_strides[rank];
+    fa.mk = mask_strides[rank + 1];
+  }
   fa.L = L; fa.S = S; fa.dp = static_cast<int32_t>(d); fa.dv = static_cast<int32_t>(dv);
   fa.batches = batches;
   // batch strides in matrix units; collapse extent-1 axes
@@ -616,6 +744,7 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     fa.qs[fa.rank] = q_strides[i] / (L * d);
     fa.ks[fa.rank] = k_strides[i] / (S * d);
     fa.vs[fa.rank] = v_strides[i] / (S * dv);
+    fa.ms[fa.rank] = mask_kind ? mask_strides[i] : 0;
     if (q_strides[i]) nq *= batch_shape[i];
     if (k_strides[i]) nk *= batch_shape[i];
     if (v_strides[i]) nv *= batch_shape[i];
@@ -632,7 +761,21 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   // K-major split planes: Q [2nq][L][d], K [2nk][S][d] (rows already K-major), Vᵀ [2nv][dv][Sp]
   split_rows_planes2(s, q, wq, nq, L, k, wk, nk, S, d, d, flag);
   split_cols_planes(s, v, wv, nv, S, dv, lay.sp, flag);
+  const int sms = sm_count();
+  if (mask_kind == 2) {
+    // the mask's storage: 1 + sum of (extent - 1) * stride over [batch..., L, S]
+    int64_t extent = 1 + (L - 1) * fa.mq + (S - 1) * fa.mk;
+    for (int i = 0; i < rank; ++i) extent += (batch_shape[i] - 1) * mask_strides[i];
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(extent, 256 * 8), 8LL * sms)));
+    mask_scan<<<grid, 256, 0, s>>>(static_cast<const float*>(mask), extent, flag);
+  }
   if (int st = launch_status("attention split pre-pass")) return st;
+  if (mask_kind) {
+    const int64_t unit = mask_kind == 1 ? 16 : 4;  // elements per 16 bytes
+    bool vec = reinterpret_cast<uintptr_t>(mask) % 16 == 0 && fa.mq % unit == 0;
+    for (int i = 0; i < fa.rank; ++i) vec = vec && fa.ms[i] % unit == 0;
+    fa.mask_vec = vec ? 1 : 0;
+  }
 
   alignas(64) CUtensorMap map_q, map_k, map_v;
   if (!encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) || !encode_planes_map(&map_k, wk, 2 * nk, S, d, kFK) ||
@@ -642,8 +785,12 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(flash_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(flash_tf32x3_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(flash_tf32x3_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(flash_tf32x3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
+            cudaSuccess)
       return launch_status("flash smem attribute");
     attr_done[dev] = true;
   }
@@ -656,17 +803,20 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   fa.nonfinite = flag;
   fa.err = device_error_word();
   const int64_t items = batches * fa.q_tiles;
-  const int sms = sm_count();
   {
     TimedLaunch timer("flash_tf32x3", s);
-    flash_tf32x3_kernel<<<static_cast<int>(std::min<int64_t>(items, sms)), kFlashThreads, kFlashSmem, s>>>(
-        map_q, map_k, map_v, fa);
+    const int grid = static_cast<int>(std::min<int64_t>(items, sms));
+    if (mask_kind == 1) flash_tf32x3_kernel<1><<<grid, kFlashThreads, kFlashSmem, s>>>(map_q, map_k, map_v, fa);
+    else if (mask_kind == 2) flash_tf32x3_kernel<2><<<grid, kFlashThreads, kFlashSmem, s>>>(map_q, map_k, map_v, fa);
+    else flash_tf32x3_kernel<0><<<grid, kFlashThreads, kFlashSmem, s>>>(map_q, map_k, map_v, fa);
   }
   if (int st = launch_status("fused attention")) return st;
   {
     TimedLaunch timer("flash_rows_fallback", s);
     const int grid = static_cast<int>(std::min<int64_t>(batches * L, 8LL * sms));
-    flash_rows_fallback<<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
+    if (mask_kind == 1) flash_rows_fallback<1><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
+    else if (mask_kind == 2) flash_rows_fallback<2><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
+    else flash_rows_fallback<0><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
   }
   return launch_status("attention fallback");
 }

@@ -544,6 +544,68 @@ def test_fused_attention_nonfinite_inputs(tcx, oracle, where, value):
             attn_check(got, oracle.attention(q, k, v, None, causal))
 
 
+FUSED_MASKS = [
+    # (mask shape relative to [batch=2, L, S], kind): full, broadcast over batch or queries,
+    # constant along keys (key stride 0), a scalar
+    ("LS", "bool"), ("LS", "additive"), ("B1S", "bool"), ("B1S", "additive"), ("1S", "additive"),
+    ("L1", "bool"), ("L1", "additive"), ("scalar", "bool"), ("BLS", "additive")]
+
+
+def fused_mask(kind, form, b, lq, lk, seed=43):
+    shape = {"LS": (lq, lk), "B1S": (b, 1, lk), "1S": (1, lk), "L1": (lq, 1), "scalar": (), "BLS": (b, lq, lk)}[form]
+    rng = np.random.default_rng(seed)
+    if kind == "bool":
+        m = rng.random(shape) > 0.35
+        if form == "scalar":
+            return np.array(True)
+        if form in ("LS", "L1"):
+            m[min(2, lq - 1)] = False  # a fully masked row: zeros
+        return m
+    m = rng.normal(size=shape).astype(np.float32)
+    m[rng.random(shape) < 0.3] = -np.inf
+    if form in ("LS", "L1", "BLS"):
+        m[..., min(2, lq - 1), :] = -np.inf
+    return m
+
+
+@pytest.mark.parametrize("lq,lk,d,dv", [(130, 200, 32, 32), (64, 257, 64, 96), (200, 128, 128, 64)])
+@pytest.mark.parametrize("form,kind", FUSED_MASKS)
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_attention_masked(tcx, oracle, lq, lk, d, dv, form, kind, causal):
+    """Masks inside the fused tcgen05 kernel (feature sizes that are multiples of 32):
+    every broadcast form of a bool or float mask, -inf entries, rows with no unmasked
+    key (zeros), keys that do not fill the last 64-key block, causal or not; against
+    the restated reference composite and NumPy."""
+    q, k, v = gauss((2, lq, d), 21), gauss((2, lk, d), 22), gauss((2, lk, dv), 23)
+    mask = fused_mask(kind, form, 2, lq, lk)
+    got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask), is_causal=causal))
+    attn_check(got, oracle.attention(q, k, v, mask, causal))
+    attn_check(got, numpy_attention(q, k, v, mask, causal))
+
+
+def test_fused_attention_masked_unaligned_rows(tcx, oracle):
+    """Mask rows that do not start on a 16-byte boundary (odd key count) take the
+    element-wise mask loads."""
+    q, k, v = gauss((1, 70, 32), 24), gauss((1, 131, 32), 25), gauss((1, 131, 32), 26)
+    for kind in ("bool", "additive"):
+        mask = fused_mask(kind, "LS", 1, 70, 131, seed=44)
+        got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask)))
+        attn_check(got, oracle.attention(q, k, v, mask, False))
+
+
+@pytest.mark.parametrize("value", [np.nan, np.inf])
+def test_fused_attention_mask_nonfinite(tcx, oracle, value):
+    """NaN or +inf in a float mask sends the call to the IEEE row kernel: the reference
+    composite's NaN rows (a NaN score, or +inf - +inf)."""
+    q, k, v = gauss((1, 70, 32), 27), gauss((1, 90, 32), 28), gauss((1, 90, 32), 29)
+    mask = fused_mask("additive", "LS", 1, 70, 90, seed=45)
+    mask[5, 7] = value
+    for causal in (False, True):
+        got = host(tcx.attention(dev(q), dev(k), dev(v), dev(mask), is_causal=causal))
+        with np.errstate(all="ignore"):
+            attn_check(got, oracle.attention(q, k, v, mask, causal))
+
+
 # ------------------------------------------------------------ min / argmax / clip
 MIN_CASES = [((), None), ((), 0), ((), -1), ((), ()), ((2, 3, 4), None), ((2, 3, 4), 0), ((2, 3, 4), -1),
              ((2, 3, 4), (0, 2)), ((2, 3, 4), (-1, 0)), ((2, 3, 4), ()), ((0, 3), 1), ((2, 0, 3), 0)]

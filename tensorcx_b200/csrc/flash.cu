@@ -597,6 +597,462 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   }
 }
 
+// ------------------------------------------------------------- CTA-pair form
+// The same fused attention on work items of 256 queries computed by a cluster of two
+// CTAs on two SMs with tcgen05.mma.cta_group::2 (M = 256): CTA r holds the Q hi/lo of
+// queries [256 t + 128 r, +128) and, of every 64-key block, the K hi/lo of keys
+// [32 r, 32 r + 32) and the Vᵀ hi/lo of value rows [Dv r / 2, Dv (r + 1) / 2), at the
+// same shared-memory offsets; each SM's TMEM receives its 128 query rows of S, P and O.
+// The leader's S and P·V issuers drive both SMs: every instruction does twice the work
+// of the single-SM kernel's, and a K stage holds two 32-feature chunks, so one barrier
+// wait covers 24 MMAs instead of 12 (the single-SM kernel's issuers spent ~40 % of
+// their time in barrier rounds). Both CTAs' TMA loads complete on the leader's full
+// barriers, the leader's commits arrive on both CTAs' barriers (one commit per CTA, no
+// multicast), and both CTAs' softmax warps arrive on the leader's P-ready and O-free
+// barriers. Everything else (softmax, masks, rescaling, the bounded waits) is the
+// single-SM kernel's.
+constexpr int kPQ = 2 * kFQ;                   // queries per pair item
+constexpr int kPKeys = kFK / 2;                // keys of a block per CTA (32)
+constexpr int kPKC = 2;                        // feature chunks per K stage
+constexpr int kPKStages = 2;
+constexpr int kPKTile = kPKeys * kFC * 4;      // 4 KB: 32 keys x 32 features
+constexpr int kPKStage = kPKC * 2 * kPKTile;   // 16 KB
+constexpr int kPVC = 2;                        // key chunks per V stage (a whole block)
+constexpr int kPVFills = kFK / (kFC * kPVC);   // V stage fills per key block
+constexpr int kPVStages = 2;
+constexpr int kPVTileMax = (kMaxDv / 2) * kFC * 4;  // 8 KB: Dv / 2 rows x 32 keys
+constexpr int kPVStage = kPVC * 2 * kPVTileMax;     // 32 KB
+constexpr int kPairSmem = kQBytes + kPKStages * kPKStage + kPVStages * kPVStage + 1024 + 256;
+static_assert(kPairSmem <= 232448, "shared memory per CTA");
+
+__device__ __forceinline__ void mma_tf32_pair_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Commit to the barrier at `bar` in both CTAs of the pair.
+__device__ __forceinline__ void commit_both(uint32_t bar) {
+  mma_commit_pair(bar);
+  mma_commit_pair(map_rank(bar, 1));
+}
+
+__device__ __forceinline__ int64_t snake_item_pair(int64_t r, int64_t items, int64_t cid, int64_t ncl) {
+  const int64_t w = r * ncl + ((r & 1) ? ncl - 1 - cid : cid);
+  return w < items ? w : -1;
+}
+
+__device__ __forceinline__ void item_coords_pair(const FlashArgs& a, int64_t w, int64_t& b, int& qt, int& nkb) {
+  qt = a.q_tiles - 1 - static_cast<int>(w / a.batches);  // q_tiles counts 256-query tiles here
+  b = w % a.batches;
+  nkb = a.causal ? min(a.kv_blocks, (qt + 1) * (kPQ / kFK)) : a.kv_blocks;
+}
+
+template <int MK>
+__global__ void __launch_bounds__(kFlashThreads, 1)
+flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                  const __grid_constant__ CUtensorMap map_v, const FlashArgs a) {
+  if (*a.nonfinite) return;  // both CTAs of a pair read the same flag and return together
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_res = smem;
+  uint8_t* k_ring = smem + kQBytes;
+  uint8_t* v_ring = k_ring + kPKStages * kPKStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kPVStages * kPVStage);
+  uint64_t* k_full = bars;                       // [kPKStages] (the leader's count both CTAs' bytes)
+  uint64_t* k_empty = k_full + kPKStages;        // [kPKStages]
+  uint64_t* v_full = k_empty + kPKStages;        // [kPVStages]
+  uint64_t* v_empty = v_full + kPVStages;        // [kPVStages]
+  uint64_t* s_full = v_empty + kPVStages;        // [kSBufs]
+  uint64_t* p_full = s_full + kSBufs;            // [kSBufs] (the leader's: 8 softmax warps)
+  uint64_t* pv_done = p_full + kSBufs;           // [kSBufs]
+  uint64_t* q_full = pv_done + kSBufs;
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* o_free = q_empty + 1;                // (the leader's: 8 softmax warps)
+  uint64_t* drain = o_free + 1;                  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int dchunks = a.dp / kFC;
+  const int kfills = (dchunks + kPKC - 1) / kPKC;  // K stage fills per key block
+  const uint32_t v_tile = static_cast<uint32_t>(a.dv / 2) * kFC * 4;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPKStages; ++s) { mbar_init(smem_u32(&k_full[s]), 1); mbar_init(smem_u32(&k_empty[s]), 1); }
+    for (int s = 0; s < kPVStages; ++s) { mbar_init(smem_u32(&v_full[s]), 1); mbar_init(smem_u32(&v_empty[s]), 1); }
+    for (int b = 0; b < kSBufs; ++b) {
+      mbar_init(smem_u32(&s_full[b]), 1);
+      mbar_init(smem_u32(&p_full[b]), 8);
+      mbar_init(smem_u32(&pv_done[b]), 1);
+    }
+    mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_empty), 1);
+    mbar_init(smem_u32(o_free), 8);
+    mbar_init(smem_u32(&drain[0]), 1);
+    mbar_init(smem_u32(&drain[1]), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive or load
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int64_t items = a.batches * a.q_tiles;
+  const int64_t cid = cluster_index(), ncl = cluster_count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------- TMA producer (both CTAs)
+      int64_t kf = 0, vf = 0, local = 0;  // K and V stage fills, items
+      bool ok = true;
+      for (int64_t r = 0; r * ncl < items && ok; ++r) {
+        const int64_t w = snake_item_pair(r, items, cid, ncl);
+        if (w < 0) continue;
+        int64_t b; int qt, nkb;
+        item_coords_pair(a, w, b, qt, nkb);
+        int64_t pq, pk, pv;
+        batch_planes(a, b, pq, pk, pv);
+        if (!wait_bounded(smem_u32(q_empty), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x480)) break;
+        ++local;
+        {
+          const uint32_t fb_local = smem_u32(q_full);
+          if (leader) mbar_expect_tx(fb_local, static_cast<uint32_t>(2 * 2 * dchunks * kQTile));
+          const uint32_t fb = map_rank(fb_local, 0);
+          const int row = qt * kPQ + static_cast<int>(rank) * kFQ;
+          for (int c = 0; c < dchunks; ++c) {
+            tma_load_3d_pair(smem_u32(q_res + (2 * c) * kQTile), &map_q, fb, c * kFC, row, static_cast<int>(2 * pq));
+            tma_load_3d_pair(smem_u32(q_res + (2 * c + 1) * kQTile), &map_q, fb, c * kFC, row,
+                             static_cast<int>(2 * pq + 1));
+          }
+        }
+        auto load_k = [&](int j) {
+          const int key = j * kFK + static_cast<int>(rank) * kPKeys;
+          for (int f = 0; f < kfills; ++f, ++kf) {
+            const int s = static_cast<int>(kf % kPKStages);
+            const uint32_t ph = static_cast<uint32_t>((kf / kPKStages) & 1);
+            if (!wait_bounded(smem_u32(&k_empty[s]), ph ^ 1u, abort_flag, a.err, 0x481)) return false;
+            const int c0 = f * kPKC, nc = min(kPKC, dchunks - c0);
+            uint8_t* st = k_ring + s * kPKStage;
+            const uint32_t fb_local = smem_u32(&k_full[s]);
+            if (leader) mbar_expect_tx(fb_local, static_cast<uint32_t>(2 * nc * 2 * kPKTile));
+            const uint32_t fb = map_rank(fb_local, 0);
+            for (int c = 0; c < nc; ++c) {
+              tma_load_3d_pair(smem_u32(st + (2 * c) * kPKTile), &map_k, fb, (c0 + c) * kFC, key,
+                               static_cast<int>(2 * pk));
+              tma_load_3d_pair(smem_u32(st + (2 * c + 1) * kPKTile), &map_k, fb, (c0 + c) * kFC, key,
+                               static_cast<int>(2 * pk + 1));
+            }
+          }
+          return true;
+        };
+        auto load_v = [&](int j) {
+          const int vrow = static_cast<int>(rank) * (a.dv / 2);
+          for (int f = 0; f < kPVFills; ++f) {
+            const int s = static_cast<int>(vf % kPVStages);
+            const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
+            if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x482)) return false;
+            ++vf;  // counted once issued: an aborting leader settles only the fills made
+            uint8_t* st = v_ring + s * kPVStage;
+            const uint32_t fb_local = smem_u32(&v_full[s]);
+            if (leader) mbar_expect_tx(fb_local, 2 * kPVC * 2 * v_tile);
+            const uint32_t fb = map_rank(fb_local, 0);
+            for (int c = 0; c < kPVC; ++c) {
+              const int key = j * kFK + (f * kPVC + c) * kFC;
+              tma_load_3d_pair(smem_u32(st + (2 * c) * kPVTileMax), &map_v, fb, key, vrow, static_cast<int>(2 * pv));
+              tma_load_3d_pair(smem_u32(st + (2 * c + 1) * kPVTileMax), &map_v, fb, key, vrow,
+                               static_cast<int>(2 * pv + 1));
+            }
+          }
+          return true;
+        };
+        for (int j = 0; j < nkb && ok; ++j) {
+          ok = load_k(j);
+          if (ok && j >= 1) ok = load_v(j - 1);
+        }
+        if (ok && nkb >= 1) ok = load_v(nkb - 1);
+      }
+      if ((!ok || *abort_flag) && leader) {  // both CTAs' fills land on the leader's barriers
+        auto settle = [&](uint64_t* full, int stages, int64_t n, int site) {
+          for (int s = 0; s < stages; ++s) {
+            const int64_t fills = n > s ? (n - s + stages - 1) / stages : 0;
+            if (!fills) continue;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(smem_u32(&full[s]), static_cast<uint32_t>((fills - 1) & 1)))
+              if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, site); break; }
+          }
+        };
+        settle(k_full, kPKStages, kf, 0x4f4);
+        settle(v_full, kPVStages, vf, 0x4f5);
+        settle(q_full, 1, local, 0x4f6);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------- S = Q·Kᵀ issuer (leader)
+      const uint32_t id_s = idesc_tf32(kPQ, kFK);
+      int64_t kf = 0, g = 0, local = 0;
+      bool ok = true;
+      for (int64_t r = 0; r * ncl < items && ok; ++r) {
+        const int64_t w = snake_item_pair(r, items, cid, ncl);
+        if (w < 0) continue;
+        int64_t b; int qt, nkb;
+        item_coords_pair(a, w, b, qt, nkb);
+        if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x490)) break;
+        ++local;
+        tc_fence_after();
+        for (int j = 0; j < nkb && ok; ++j, ++g) {
+          const int buf = static_cast<int>(g % kSBufs);
+          if (g >= kSBufs) {
+            if (!wait_bounded(smem_u32(&pv_done[buf]), static_cast<uint32_t>(((g - kSBufs) / kSBufs) & 1), abort_flag,
+                              a.err, 0x492)) { ok = false; break; }
+            tc_fence_after();
+          }
+          const uint32_t d_s = tmem + static_cast<uint32_t>(buf * 128);
+          for (int f = 0; f < kfills; ++f, ++kf) {
+            const int s = static_cast<int>(kf % kPKStages);
+            const uint32_t ph = static_cast<uint32_t>((kf / kPKStages) & 1);
+            if (!wait_bounded(smem_u32(&k_full[s]), ph, abort_flag, a.err, 0x493)) { ok = false; break; }
+            tc_fence_after();
+            const int c0 = f * kPKC, nc = min(kPKC, dchunks - c0);
+            for (int c = 0; c < nc; ++c) {
+              const uint64_t dq_hi = smem_desc_sw128(smem_u32(q_res + (2 * (c0 + c)) * kQTile));
+              const uint64_t dq_lo = smem_desc_sw128(smem_u32(q_res + (2 * (c0 + c) + 1) * kQTile));
+              const uint64_t dk_hi = smem_desc_sw128(smem_u32(k_ring + s * kPKStage + (2 * c) * kPKTile));
+              const uint64_t dk_lo = smem_desc_sw128(smem_u32(k_ring + s * kPKStage + (2 * c + 1) * kPKTile));
+#pragma unroll
+              for (int kk = 0; kk < kFC / 8; ++kk) {
+                const uint32_t acc = (c0 + c == 0 && kk == 0) ? 0u : 1u;
+                mma_tf32_pair(d_s, dq_lo + 2 * kk, dk_hi + 2 * kk, id_s, acc);
+                mma_tf32_pair(d_s, dq_hi + 2 * kk, dk_lo + 2 * kk, id_s, 1u);
+                mma_tf32_pair(d_s, dq_hi + 2 * kk, dk_hi + 2 * kk, id_s, 1u);
+              }
+            }
+            commit_both(smem_u32(&k_empty[s]));
+          }
+          if (!ok) break;
+          commit_both(smem_u32(&s_full[buf]));
+          if (j == nkb - 1) commit_both(smem_u32(q_empty));
+        }
+      }
+    }
+  } else if (warp == 6) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------- O += P·V issuer (leader)
+      const uint32_t id_o = idesc_tf32(kPQ, a.dv);
+      const uint32_t d_o = tmem + kColO;
+      int64_t vf = 0, g = 0, local = 0;
+      bool ok = true;
+      for (int64_t r = 0; r * ncl < items && ok; ++r) {
+        const int64_t w = snake_item_pair(r, items, cid, ncl);
+        if (w < 0) continue;
+        int64_t b; int qt, nkb;
+        item_coords_pair(a, w, b, qt, nkb);
+        const int64_t item = local++;
+        for (int j = 0; j < nkb && ok; ++j, ++g) {
+          const int buf = static_cast<int>(g % kSBufs);
+          if (!wait_bounded(smem_u32(&p_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x494)) {
+            ok = false;
+            break;
+          }
+          if (j == 0 && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x491)) {
+            ok = false;
+            break;
+          }
+          const uint32_t p_hi = tmem + static_cast<uint32_t>(buf * 128), p_lo = p_hi + kFK;
+          for (int f = 0; f < kPVFills && ok; ++f, ++vf) {
+            const int s = static_cast<int>(vf % kPVStages);
+            const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
+            if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x495)) { ok = false; break; }
+            tc_fence_after();
+            for (int c = 0; c < kPVC; ++c) {
+              const uint64_t dv_hi = smem_desc_sw128(smem_u32(v_ring + s * kPVStage + (2 * c) * kPVTileMax));
+              const uint64_t dv_lo = smem_desc_sw128(smem_u32(v_ring + s * kPVStage + (2 * c + 1) * kPVTileMax));
+#pragma unroll
+              for (int kk = 0; kk < kFC / 8; ++kk) {
+                const uint32_t col = static_cast<uint32_t>((f * kPVC + c) * kFC + kk * 8);
+                const uint32_t acc = (j == 0 && f == 0 && c == 0 && kk == 0) ? 0u : 1u;
+                mma_tf32_pair_ta(d_o, p_lo + col, dv_hi + 2 * kk, id_o, acc);
+                mma_tf32_pair_ta(d_o, p_hi + col, dv_lo + 2 * kk, id_o, 1u);
+                mma_tf32_pair_ta(d_o, p_hi + col, dv_hi + 2 * kk, id_o, 1u);
+              }
+            }
+            commit_both(smem_u32(&v_empty[s]));
+          }
+          if (!ok) break;
+          commit_both(smem_u32(&pv_done[buf]));
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------- softmax (both CTAs)
+    const int quarter = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int row_in_tile = quarter * 32 + lane;
+    int64_t g = 0;
+    for (int64_t r = 0; r * ncl < items; ++r) {
+      const int64_t w = snake_item_pair(r, items, cid, ncl);
+      if (w < 0) continue;
+      int64_t b; int qt, nkb;
+      item_coords_pair(a, w, b, qt, nkb);
+      const int64_t query = static_cast<int64_t>(qt) * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile;
+      const bool row_ok = query < a.L;
+      const int64_t mrow = MK ? mask_offset(a, b) + (row_ok ? query : 0) * a.mq : 0;
+      float m_use = -INFINITY, l = 0.0f;
+      bool aborted = false;
+      for (int j = 0; j < nkb; ++j, ++g) {
+        const int buf = static_cast<int>(g % kSBufs);
+        const uint32_t col_s = static_cast<uint32_t>(buf * 128), col_lo = col_s + kFK;
+        const int64_t key0 = static_cast<int64_t>(j) * kFK;
+        int64_t lim64 = a.S - key0;
+        if (a.causal) lim64 = min(lim64, query - key0 + 1);
+        const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > kFK ? kFK : lim64));
+        MaskBlock<MK> mb;
+        if constexpr (MK != 0) {
+          const int64_t left = a.S - key0;
+          mb.load(a, mrow, key0, row_ok ? static_cast<int>(left < kFK ? left : kFK) : 0);
+        }
+        if (!wait_bounded(smem_u32(&s_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x4a1)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        uint32_t s0[32], s1[32];
+        TCX_LD32(s0, tmem + lane_base + col_s);
+        TCX_LD32(s1, tmem + lane_base + col_s + 32);
+        TCX_WAIT_LD32(s0);
+        TCX_TIE32(s1);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float t = mb.apply(__fmul_rn(__uint_as_float(s0[e]), a.scale_log2), e);
+          s0[e] = __float_as_uint(t);
+          if (e < lim) mx = fmaxf(mx, t);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float t = mb.apply(__fmul_rn(__uint_as_float(s1[e]), a.scale_log2), 32 + e);
+          s1[e] = __float_as_uint(t);
+          if (32 + e < lim) mx = fmaxf(mx, t);
+        }
+        const bool need = mx > m_use + 8.0f;
+        float alpha = 1.0f;
+        if (need) {
+          alpha = j == 0 ? 0.0f : exp2f(m_use - mx);
+          m_use = mx;
+        }
+        l = __fmul_rn(l, alpha);
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          const int64_t gp = g - 1;
+          if (!wait_bounded(smem_u32(&pv_done[gp % kSBufs]), static_cast<uint32_t>((gp / kSBufs) & 1), abort_flag, a.err,
+                            0x4a3)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < a.dv; cc += 32) {
+            uint32_t rr[32];
+            TCX_LD32(rr, tmem + lane_base + kColO + cc);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__fmul_rn(__uint_as_float(rr[e]), alpha));
+            TCX_ST32(tmem + lane_base + kColO + cc, rr);
+          }
+        }
+        auto emit = [&](uint32_t (&sv)[32], int c0) {
+          uint32_t lo[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float p = 0.0f;
+            if (c0 + e < lim && (MK == 0 || __uint_as_float(sv[e]) != -INFINITY)) {
+              asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(__uint_as_float(sv[e]), m_use)));
+            }
+            l = __fadd_rn(l, p);
+            const float hi = tf32_rna(p);
+            sv[e] = __float_as_uint(hi);
+            lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
+          }
+          TCX_ST32(tmem + lane_base + col_s + c0, sv);
+          TCX_ST32(tmem + lane_base + col_lo + c0, lo);
+        };
+        emit(s0, 0);
+        emit(s1, 32);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&p_full[buf]), 0));
+      }
+      if (aborted) break;
+      const int64_t gl = g - 1;
+      if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err,
+                        0x4a2))
+        break;
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      float* orow = a.out + (b * a.L + query) * a.dv;
+      const int nch = a.dv / 32;
+      uint32_t o0[32], o1[32];
+      TCX_LD32(o0, tmem + lane_base + kColO);
+#pragma unroll
+      for (int ci = 0; ci < kMaxDv / 32; ++ci) {
+        if (ci >= nch) break;
+        uint32_t (&cur)[32] = (ci & 1) ? o1 : o0;
+        uint32_t (&nxt)[32] = (ci & 1) ? o0 : o1;
+        TCX_WAIT_LD32(cur);
+        if (ci + 1 < nch) TCX_LD32(nxt, tmem + lane_base + kColO + static_cast<uint32_t>((ci + 1) * 32));
+        if (row_ok) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(cur[e]), inv);
+          float* dst = orow + ci * 32;
+          if (a.vec8) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8)
+              st_global_v8(dst + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(o_free), 0));
+    }
+  }
+
+  // every MMA the leader's issuers started completes before either CTA releases its TMEM
+  if ((warp == 1 || warp == 6) && lane == 0) {
+    uint64_t* d = &drain[warp == 1 ? 0 : 1];
+    if (leader) commit_both(smem_u32(d));
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(smem_u32(d), 0))
+      if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, 0x4fd); break; }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+  cluster_sync_all();  // neither CTA leaves while the other may still touch its barriers
+}
+
 // IEEE fallback, used only when the pre-pass saw inf / NaN: one CTA per (batch, query)
 // row computes the scores as float32 dot products in feature order (as the reference
 // matmul), the masked softmax of core/inference.cpp / cpu_inference.cpp, and P·V summed
@@ -777,9 +1233,16 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     fa.mask_vec = vec ? 1 : 0;
   }
 
+  // CTA pairs (256 queries per item) for unmasked products with more than one 128-query
+  // tile: each CTA loads 32 of a block's 64 keys and half of Vᵀ's rows. Measured on
+  // [32, 2048, 2048, 128]: 0.487 against 0.512 ms per call without a mask, 0.302
+  // against 0.306 causal; with a float mask the pair is slower (0.674 against 0.636 ms
+  // kernel), its two SMs' softmax warps both gating every P·V.
+  const bool pair = L > kFQ && mask_kind == 0;
   alignas(64) CUtensorMap map_q, map_k, map_v;
-  if (!encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) || !encode_planes_map(&map_k, wk, 2 * nk, S, d, kFK) ||
-      !encode_planes_map(&map_v, wv, 2 * nv, dv, lay.sp, static_cast<int>(dv)))
+  if (!encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) ||
+      !encode_planes_map(&map_k, wk, 2 * nk, S, d, pair ? kPKeys : kFK) ||
+      !encode_planes_map(&map_v, wv, 2 * nv, dv, lay.sp, static_cast<int>(pair ? dv / 2 : dv)))
     return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -790,11 +1253,13 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
         cudaFuncSetAttribute(flash_tf32x3_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
             cudaSuccess ||
         cudaFuncSetAttribute(flash_tf32x3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFlashSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(flash_pair_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem) !=
             cudaSuccess)
       return launch_status("flash smem attribute");
     attr_done[dev] = true;
   }
-  fa.q_tiles = static_cast<int32_t>(ceil_div(L, kFQ));
+  fa.q_tiles = static_cast<int32_t>(ceil_div(L, pair ? kPQ : kFQ));
   fa.kv_blocks = static_cast<int32_t>(ceil_div(S, kFK));
   fa.scale_log2 = scale * kLog2e;
   fa.causal = causal;
@@ -803,7 +1268,23 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   fa.nonfinite = flag;
   fa.err = device_error_word();
   const int64_t items = batches * fa.q_tiles;
-  {
+  if (pair) {
+    TimedLaunch timer("flash_tf32x3", s);
+    const int clusters = static_cast<int>(std::min<int64_t>(items, sms / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kFlashThreads);
+    cfg.dynamicSmemBytes = kPairSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, flash_pair_kernel<0>, map_q, map_k, map_v, fa);  // unmasked only
+  } else {
     TimedLaunch timer("flash_tf32x3", s);
     const int grid = static_cast<int>(std::min<int64_t>(items, sms));
     if (mask_kind == 1) flash_tf32x3_kernel<1><<<grid, kFlashThreads, kFlashSmem, s>>>(map_q, map_k, map_v, fa);

@@ -1475,17 +1475,40 @@ struct Streams {
     }
     return e;
   }
-  ~Streams() {
-    for (cudaEvent_t ev : {b_ready, a_ready, c_ready})
-      if (ev) cudaEventDestroy(ev);
+  void release() {
+    for (cudaEvent_t* ev : {&b_ready, &a_ready, &c_ready})
+      if (*ev) cudaEventDestroy(*ev), *ev = nullptr;
     for (int i = 0; i < kHostSlots; ++i) {
-      if (a_free[i]) cudaEventDestroy(a_free[i]);
-      if (c_free[i]) cudaEventDestroy(c_free[i]);
+      if (a_free[i]) cudaEventDestroy(a_free[i]), a_free[i] = nullptr;
+      if (c_free[i]) cudaEventDestroy(c_free[i]), c_free[i] = nullptr;
     }
-    for (cudaStream_t st : {in, comp, out})
-      if (st) cudaStreamDestroy(st);
+    for (cudaStream_t* st : {&in, &comp, &out})
+      if (*st) cudaStreamDestroy(*st), *st = nullptr;
   }
+  ~Streams() { release(); }
 };
+
+// The calling thread's upload / compute / download streams and events for the current
+// device, created on its first call and kept until the thread ends (each call returns
+// with all three streams idle, so the next call may reuse them as they are).
+Streams* host_streams() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  thread_local Streams lanes[64];
+  thread_local bool made[64] = {};
+  if (!made[dev]) {
+    if (lanes[dev].create() != cudaSuccess) {
+      cudaGetLastError();
+      lanes[dev].release();
+      return nullptr;
+    }
+    made[dev] = true;
+  }
+  return &lanes[dev];
+}
 }  // namespace
 
 extern "C" {
@@ -1506,11 +1529,12 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
   if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("matmul workspace must be 1024-byte aligned");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* b_dev = reinterpret_cast<float*>(ws + p.off_b);
-  Streams st;
-  if (cudaError_t e = st.create(); e != cudaSuccess) {
-    set_error(std::string("matmul_host streams: ") + cudaGetErrorString(e));
+  Streams* lane = host_streams();
+  if (!lane) {
+    set_error("matmul_host: could not create its streams and events");
     return TCX_INTERNAL;
   }
+  Streams& st = *lane;
   auto fail = [](cudaError_t e, const char* what) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
     return TCX_INTERNAL;

@@ -17,7 +17,8 @@
 //               of block j overlaps the MMAs of blocks j+1 and j-1.
 //   warps 2-5   softmax, one thread per query row (its TMEM lane): row maximum of the
 //               scaled, causally masked scores (log2 domain), p = 2^(t - m), the row sum,
-//               and the hi/lo split of p written back over S with tcgen05.st. The
+//               and p written back over S with tcgen05.st (the tensor core reads it as
+//               tf32, the hi term) with p - trunc_tf32(p) beside it (the lo term). The
 //               running maximum is raised only when a block's maximum exceeds it by more
 //               than 8 (p stays <= 256), and only then is O (in TMEM) rescaled; at the end
 //               O / sum is stored to HBM.
@@ -472,19 +473,20 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         TCX_WAIT_LD32(s0);
         TCX_TIE32(s1);
         // pass 1: the block's row maximum (log2 domain)
-        float mx = -INFINITY;
+        float mxv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const float t = mb.apply(__fmul_rn(__uint_as_float(s0[e]), a.scale_log2), e);
           s0[e] = __float_as_uint(t);
-          if (e < lim) mx = fmaxf(mx, t);
+          if (e < lim) mxv[e & 3] = fmaxf(mxv[e & 3], t);
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const float t = mb.apply(__fmul_rn(__uint_as_float(s1[e]), a.scale_log2), 32 + e);
           s1[e] = __float_as_uint(t);
-          if (32 + e < lim) mx = fmaxf(mx, t);
+          if (32 + e < lim) mxv[e & 3] = fmaxf(mxv[e & 3], t);
         }
+        const float mx = fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3]));
         // raise the running maximum only when p would exceed 2^8; rescale O then
         const bool need = mx > m_use + 8.0f;
         float alpha = 1.0f;
@@ -513,6 +515,11 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
           }
         }
         // pass 2: p = 2^(t - m), the row sum, P_hi over S and P_lo beside it
+        // The tensor core reads float32 operands as tf32 by dropping the low 13 mantissa
+        // bits, so p itself is the hi term of the 3xTF32 split and p - trunc_tf32(p)
+        // (exact) the lo term: no conversions (two per element were most of this loop's
+        // time), at most 2^-20 of p lost against a rounded split.
+        float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         auto emit = [&](uint32_t (&sv)[32], int c0) {
           uint32_t lo[32];
 #pragma unroll
@@ -522,16 +529,16 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             if (c0 + e < lim && (MK == 0 || __uint_as_float(sv[e]) != -INFINITY)) {
               asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(__uint_as_float(sv[e]), m_use)));
             }
-            l = __fadd_rn(l, p);
-            const float hi = tf32_rna(p);
-            sv[e] = __float_as_uint(hi);
-            lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
+            lsum[e & 3] = __fadd_rn(lsum[e & 3], p);
+            sv[e] = __float_as_uint(p);
+            lo[e] = __float_as_uint(__fsub_rn(p, __uint_as_float(__float_as_uint(p) & 0xFFFFE000u)));
           }
           TCX_ST32(tmem + lane_base + col_s + c0, sv);
           TCX_ST32(tmem + lane_base + col_lo + c0, lo);
         };
         emit(s0, 0);
         emit(s1, 32);
+        l = __fadd_rn(l, __fadd_rn(__fadd_rn(lsum[0], lsum[1]), __fadd_rn(lsum[2], lsum[3])));
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
@@ -934,19 +941,20 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         TCX_LD32(s1, tmem + lane_base + col_s + 32);
         TCX_WAIT_LD32(s0);
         TCX_TIE32(s1);
-        float mx = -INFINITY;
+        float mxv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const float t = mb.apply(__fmul_rn(__uint_as_float(s0[e]), a.scale_log2), e);
           s0[e] = __float_as_uint(t);
-          if (e < lim) mx = fmaxf(mx, t);
+          if (e < lim) mxv[e & 3] = fmaxf(mxv[e & 3], t);
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const float t = mb.apply(__fmul_rn(__uint_as_float(s1[e]), a.scale_log2), 32 + e);
           s1[e] = __float_as_uint(t);
-          if (32 + e < lim) mx = fmaxf(mx, t);
+          if (32 + e < lim) mxv[e & 3] = fmaxf(mxv[e & 3], t);
         }
+        const float mx = fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3]));
         const bool need = mx > m_use + 8.0f;
         float alpha = 1.0f;
         if (need) {
@@ -972,6 +980,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
             TCX_ST32(tmem + lane_base + kColO + cc, rr);
           }
         }
+        // The tensor core reads float32 operands as tf32 by dropping the low 13 mantissa
+        // bits, so p itself is the hi term of the 3xTF32 split and p - trunc_tf32(p)
+        // (exact) the lo term: no conversions (two per element were most of this loop's
+        // time), at most 2^-20 of p lost against a rounded split.
+        float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         auto emit = [&](uint32_t (&sv)[32], int c0) {
           uint32_t lo[32];
 #pragma unroll
@@ -980,16 +993,16 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
             if (c0 + e < lim && (MK == 0 || __uint_as_float(sv[e]) != -INFINITY)) {
               asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fsub_rn(__uint_as_float(sv[e]), m_use)));
             }
-            l = __fadd_rn(l, p);
-            const float hi = tf32_rna(p);
-            sv[e] = __float_as_uint(hi);
-            lo[e] = __float_as_uint(tf32_rna(__fsub_rn(p, hi)));
+            lsum[e & 3] = __fadd_rn(lsum[e & 3], p);
+            sv[e] = __float_as_uint(p);
+            lo[e] = __float_as_uint(__fsub_rn(p, __uint_as_float(__float_as_uint(p) & 0xFFFFE000u)));
           }
           TCX_ST32(tmem + lane_base + col_s + c0, sv);
           TCX_ST32(tmem + lane_base + col_lo + c0, lo);
         };
         emit(s0, 0);
         emit(s1, 32);
+        l = __fadd_rn(l, __fadd_rn(__fadd_rn(lsum[0], lsum[1]), __fadd_rn(lsum[2], lsum[3])));
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();

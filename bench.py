@@ -79,6 +79,7 @@ def run_case(a):
         python bench.py --case attention --batch 32 --rows 2048 --cols 2048 --size 128 [--causal]
         python bench.py --case sum_axis0 --rows 65536 --cols 4096
         python bench.py --case sum_axes02 --batch 64 --rows 4096 --cols 1024
+        python bench.py --case randn|rand --n 268435456
     """
     import torch
     from tensorcx_b200 import ops
@@ -111,6 +112,9 @@ def run_case(a):
     elif w == "sum_axes02":
         x = torch.randn(a.batch, a.rows, a.cols, device="cuda", generator=g)
         fn = lambda: ops.sum(x, axis=(0, 2))  # noqa: E731
+    elif w in ("randn", "rand"):
+        gen = ops.randn if w == "randn" else ops.rand_uniform
+        fn = lambda: gen((a.n,), seed=2024)  # noqa: E731
     elif w == "attention":  # batch = heads, rows = queries, cols = keys, size = features
         q = torch.randn(a.batch, a.rows, a.size, device="cuda", generator=g)
         k = torch.randn(a.batch, a.cols, a.size, device="cuda", generator=g)

@@ -128,7 +128,9 @@ int matmul_run(cudaStream_t stream, const float* lhs, const float* rhs, float* o
 // Split pre-pass of the 3xTF32 tensor path (gemm.cu): nb matrices [rows, k] -> K-major
 // hi/lo planes [2 * nb, rows, kp]; the column form transposes nb matrices [k, n] into
 // [2 * nb, n, kp]. Both raise *flag on inf / NaN. encode_planes_map builds the TMA map
-// (box {32, box_rows, 1}, 128-byte swizzle) over such planes; `map` is a CUtensorMap*.
+// (box {32, box_rows, 1}, 128-byte swizzle) over such planes, or over any stack of
+// `planes` row-major [rows, kp] float32 matrices; with mn_atom32 the swizzle has 32-byte
+// atoms (the layout of MN-major tf32 MMA operands). `map` is a CUtensorMap*.
 void split_rows_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t rows, int64_t k,
                        int64_t kp, int* flag);
 // Two row splits with the same K in one launch (x1 and x2 as split_rows_planes).
@@ -137,7 +139,11 @@ void split_rows_planes2(cudaStream_t s, const float* x1, float* planes1, int64_t
                         int* flag);
 void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb, int64_t k, int64_t n,
                        int64_t kp, int* flag);
-bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows);
+bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows,
+                       bool mn_atom32 = false);
+// Raw-mode lo terms (gemm.cu split_lo): lo[i] = rna_tf32(x[i] - trunc_tf32(x[i])) for n4
+// 16-byte words, elementwise in x's own layout; raises *flag on inf / NaN.
+void split_lo_planes(cudaStream_t s, const float* x, float* lo, int64_t n4, int* flag);
 
 // Fused attention (flash.cu): eligibility, workspace and launch.
 bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t value_features, int mask_kind,

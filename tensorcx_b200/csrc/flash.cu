@@ -1,10 +1,13 @@
 // Fused attention on sm_100a: O = softmax(scale * Q·Kᵀ) · V in one persistent,
 // warp-specialized kernel, the scores and probabilities never leaving the SM.
 //
-// Operands are the 3xTF32 split planes (hi = rna_tf32(x), lo = rna_tf32(x - hi)) of
-// Q [L, D], K [S, D] and Vᵀ [Dv, S], all K-major, made by the matmul pre-pass. One work
-// item is 128 queries of one batch, whose Q hi/lo stays in shared memory; key blocks of
-// 64 are visited in order:
+// Two kernels. The single-SM kernel (masks, at most 128 queries, Dv 32 or 96, operands
+// not 16-byte aligned) reads the 3xTF32 split planes (hi = rna_tf32(x),
+// lo = rna_tf32(x - hi)) of Q [L, D], K [S, D] and Vᵀ [Dv, S], all K-major, made by the
+// matmul pre-pass. The CTA-pair kernel below (the unmasked products over 128 queries)
+// reads q, k and v in place and needs only K's lo terms from a pre-pass. One work item
+// of the single-SM kernel is 128 queries of one batch, whose Q hi/lo stays in shared
+// memory; key blocks of 64 are visited in order:
 //   warp 0      TMA producer: the item's Q (D/32 pairs of 128x32 hi/lo tiles), then per
 //               key block D/32 K hi/lo chunks (64x32) into a 2-deep ring and two Vᵀ
 //               hi/lo chunks (Dv x 32) into another.
@@ -34,10 +37,11 @@
 // block's S, through the mask's broadcast strides. A row with no unmasked key is all
 // zeros, as in the reference.
 //
-// Non-finite inputs (flagged by the split pre-pass, and NaN / +inf in a float mask,
-// flagged by a scan of the mask) make the kernel exit at once; a row-wise IEEE kernel
-// queued behind it (idle otherwise) computes the result the way the reference
-// composite does (core/inference.cpp:123-160), mask included.
+// Non-finite inputs (flagged by the split pre-pass, by the pair kernel's converters and
+// scan, and NaN / +inf in a float mask, flagged by a scan of the mask) hand the call to
+// a row-wise IEEE kernel queued behind the fused one (idle otherwise), which computes
+// the result the way the reference composite does (core/inference.cpp:123-160), mask
+// included; the single-SM kernel exits at once when the pre-pass raised the flag.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -101,6 +105,13 @@ struct FlashArgs {
   int32_t mask_vec;
   const int* nonfinite;
   int* err;
+  // the CTA-pair kernel reads q, k, v in place ([planes][rows][features] float32,
+  // 16-byte aligned), checks the Q and V tiles it loads for inf / NaN, scans the rows
+  // [tail_row, S) of the v_planes V planes that no item loads, and raises *flag on a hit
+  const float* v;
+  int64_t v_planes;
+  int64_t tail_row;
+  int* flag;
 };
 
 __device__ __forceinline__ void batch_planes(const FlashArgs& a, int64_t b, int64_t& pq, int64_t& pk, int64_t& pv) {
@@ -587,6 +598,7 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     }
   }
 
+  dependents_may_launch();  // the fallback kernel behind may start launching
   // every MMA either issuer started completes before TMEM is released
   if ((warp == 1 || warp == 6) && lane == 0) {
     uint64_t* d = &drain[warp == 1 ? 0 : 1];
@@ -606,30 +618,44 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 
 // ------------------------------------------------------------- CTA-pair form
 // The same fused attention on work items of 256 queries computed by a cluster of two
-// CTAs on two SMs with tcgen05.mma.cta_group::2 (M = 256): CTA r holds the Q hi/lo of
-// queries [256 t + 128 r, +128) and, of every 64-key block, the K hi/lo of keys
-// [32 r, 32 r + 32) and the Vᵀ hi/lo of value rows [Dv r / 2, Dv (r + 1) / 2), at the
+// CTAs on two SMs with tcgen05.mma.cta_group::2 (M = 256), reading q, k and v where they
+// lie, with no pre-pass: CTA r holds queries [256 t + 128 r, +128) of Q, of every
+// 64-key block the keys [32 r, 32 r + 32) of K, and the value columns
+// [Dv r / 2, Dv (r + 1) / 2) of V (MN-major: V's rows are the P·V contraction), at the
 // same shared-memory offsets; each SM's TMEM receives its 128 query rows of S, P and O.
+// TMA brings the float32 tiles themselves, which the tensor core reads as the hi terms
+// (kind::tf32 drops the low 13 mantissa bits). K's lo terms, lo = rna_tf32(x -
+// trunc_tf32(x)), come from a pre-pass ([nk][S][D] beside K's layout, which also checks
+// K for inf / NaN); for Q (once per item) and V four converter warps per CTA write each
+// tile's lo terms beside it, checking it on the way, and arrive on the leader's ready
+// barriers, on which the MMA issuers wait. A scanner warp checks the V rows no item
+// loads (causal, keys past the last query tile). On a hit the row-wise IEEE kernel
+// queued behind this one recomputes the whole result. (Converting K in the kernel too
+// made it 15-18 % slower: the K ring is two stages deep and each stage is consumed in
+// ~1.2 us, and the conversion sat between the TMA landing and the S products.)
 // The leader's S and P·V issuers drive both SMs: every instruction does twice the work
 // of the single-SM kernel's, and a K stage holds two 32-feature chunks, so one barrier
-// wait covers 24 MMAs instead of 12 (the single-SM kernel's issuers spent ~40 % of
-// their time in barrier rounds). Both CTAs' TMA loads complete on the leader's full
-// barriers, the leader's commits arrive on both CTAs' barriers (one commit per CTA, no
-// multicast), and both CTAs' softmax warps arrive on the leader's P-ready and O-free
-// barriers. Everything else (softmax, masks, rescaling, the bounded waits) is the
+// wait covers 24 MMAs instead of 12. The leader's commits arrive on both CTAs' barriers
+// (one commit per CTA, no multicast), and both CTAs' softmax warps arrive on the
+// leader's P-ready and O-free barriers. Softmax, rescaling and the bounded waits are the
 // single-SM kernel's.
+//   warp 0      TMA producer (Q and V on this CTA's barriers, K on the leader's)
+//   warp 1      S issuer (leader)          warp 6      P·V issuer (leader)
+//   warps 2-5   softmax and epilogue       warps 7-10  lo-term converters
+//   warp 11     non-finite scan
 constexpr int kPQ = 2 * kFQ;                   // queries per pair item
 constexpr int kPKeys = kFK / 2;                // keys of a block per CTA (32)
 constexpr int kPKC = 2;                        // feature chunks per K stage
 constexpr int kPKStages = 2;
 constexpr int kPKTile = kPKeys * kFC * 4;      // 4 KB: 32 keys x 32 features
 constexpr int kPKStage = kPKC * 2 * kPKTile;   // 16 KB
-constexpr int kPVC = 2;                        // key chunks per V stage (a whole block)
-constexpr int kPVFills = kFK / (kFC * kPVC);   // V stage fills per key block
 constexpr int kPVStages = 2;
-constexpr int kPVTileMax = (kMaxDv / 2) * kFC * 4;  // 8 KB: Dv / 2 rows x 32 keys
-constexpr int kPVStage = kPVC * 2 * kPVTileMax;     // 32 KB
-constexpr int kPairSmem = kQBytes + kPKStages * kPKStage + kPVStages * kPVStage + 1024 + 256;
+constexpr int kPVTile = 32 * kFC * 4;          // 4 KB: 32 keys x 32 value columns, MN-major
+constexpr int kPVHalf = 2 * (kMaxDv / 64) * kPVTile;  // 16 KB: a block's hi (or lo) tiles
+constexpr int kPVStage = 2 * kPVHalf;          // 32 KB: hi tiles, then lo tiles
+constexpr int kPairThreads = 384;
+constexpr int kConvWarp0 = 7, kScanWarp = 11;
+constexpr int kPairSmem = kQBytes + kPKStages * kPKStage + kPVStages * kPVStage + 1024 + 512;
 static_assert(kPairSmem <= 232448, "shared memory per CTA");
 
 __device__ __forceinline__ void mma_tf32_pair_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
@@ -658,11 +684,48 @@ __device__ __forceinline__ void item_coords_pair(const FlashArgs& a, int64_t w, 
   nkb = a.causal ? min(a.kv_blocks, (qt + 1) * (kPQ / kFK)) : a.kv_blocks;
 }
 
+// The lo term of a float32 word x: x - trunc_tf32(x) (exact), rounded to tf32 (to
+// nearest, ties away from zero, as cvt.rna.tf32.f32) by adding half a tf32 ulp to the
+// magnitude bits and dropping the low 13.
+__device__ __forceinline__ uint32_t lo_term(uint32_t x) {
+  const uint32_t d = __float_as_uint(__fsub_rn(__uint_as_float(x), __uint_as_float(x & 0xFFFFE000u)));
+  return (d + 0x1000u) & 0xFFFFE000u;
+}
+
+__device__ __forceinline__ uint32_t nonfinite4(uint4 w) {
+  const uint32_t e = 0x7F800000u;
+  return ((w.x & e) == e) | ((w.y & e) == e) | ((w.z & e) == e) | ((w.w & e) == e);
+}
+
+// Converter thread t (0..127) writes the lo terms of the 16-byte words t, t + 128, ... of
+// the `bytes` of float32 tiles at shared address hi into the same offsets from lo, and
+// notes an inf / NaN among them in `bad`.
+__device__ __forceinline__ void write_lo(uint32_t hi, uint32_t lo, int bytes, int t, uint32_t& bad) {
+#pragma unroll 4
+  for (int off = t * 16; off < bytes; off += 128 * 16) {
+    uint4 x;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(hi + off));
+    bad |= nonfinite4(x);
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(lo + off), "r"(lo_term(x.x)), "r"(lo_term(x.y)),
+                 "r"(lo_term(x.z)), "r"(lo_term(x.w))
+                 : "memory");
+  }
+}
+
+// A converter warp's lo writes become visible to the tensor core (the async proxy), then
+// its lane 0 arrives on the leader's copy of the ready barrier `bar` (four warps of each
+// CTA arrive: count 8).
+__device__ __forceinline__ void publish_lo(uint32_t bar, int lane) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) mbar_arrive_cluster(map_rank(bar, 0));
+}
+
 template <int MK>
-__global__ void __launch_bounds__(kFlashThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
 flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                  const __grid_constant__ CUtensorMap map_v, const FlashArgs a) {
-  if (*a.nonfinite) return;  // both CTAs of a pair read the same flag and return together
+                  const __grid_constant__ CUtensorMap map_klo, const __grid_constant__ CUtensorMap map_v,
+                  const FlashArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_res = smem;
@@ -671,13 +734,15 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(v_ring + kPVStages * kPVStage);
   uint64_t* k_full = bars;                       // [kPKStages] (the leader's count both CTAs' bytes)
   uint64_t* k_empty = k_full + kPKStages;        // [kPKStages]
-  uint64_t* v_full = k_empty + kPKStages;        // [kPVStages]
+  uint64_t* v_full = k_empty + kPKStages;        // [kPVStages] this CTA's V tiles landed
   uint64_t* v_empty = v_full + kPVStages;        // [kPVStages]
-  uint64_t* s_full = v_empty + kPVStages;        // [kSBufs]
+  uint64_t* v_ready = v_empty + kPVStages;       // [kPVStages] (the leader's: 8 converter warps)
+  uint64_t* s_full = v_ready + kPVStages;        // [kSBufs]
   uint64_t* p_full = s_full + kSBufs;            // [kSBufs] (the leader's: 8 softmax warps)
   uint64_t* pv_done = p_full + kSBufs;           // [kSBufs]
   uint64_t* q_full = pv_done + kSBufs;
-  uint64_t* q_empty = q_full + 1;
+  uint64_t* q_ready = q_full + 1;                // (the leader's: 8 converter warps)
+  uint64_t* q_empty = q_ready + 1;
   uint64_t* o_free = q_empty + 1;                // (the leader's: 8 softmax warps)
   uint64_t* drain = o_free + 1;                  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
@@ -688,16 +753,21 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   const bool leader = rank == 0;
   const int dchunks = a.dp / kFC;
   const int kfills = (dchunks + kPKC - 1) / kPKC;  // K stage fills per key block
-  const uint32_t v_tile = static_cast<uint32_t>(a.dv / 2) * kFC * 4;
+  const int nvc = a.dv / 64;                      // 32-column V chunks per CTA
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPKStages; ++s) { mbar_init(smem_u32(&k_full[s]), 1); mbar_init(smem_u32(&k_empty[s]), 1); }
-    for (int s = 0; s < kPVStages; ++s) { mbar_init(smem_u32(&v_full[s]), 1); mbar_init(smem_u32(&v_empty[s]), 1); }
+    for (int s = 0; s < kPVStages; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+      mbar_init(smem_u32(&v_ready[s]), 8);
+    }
     for (int b = 0; b < kSBufs; ++b) {
       mbar_init(smem_u32(&s_full[b]), 1);
       mbar_init(smem_u32(&p_full[b]), 8);
       mbar_init(smem_u32(&pv_done[b]), 1);
     }
     mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_ready), 8);
     mbar_init(smem_u32(q_empty), 1);
     mbar_init(smem_u32(o_free), 8);
     mbar_init(smem_u32(&drain[0]), 1);
@@ -735,15 +805,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         if (!wait_bounded(smem_u32(q_empty), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x480)) break;
         ++local;
         {
-          const uint32_t fb_local = smem_u32(q_full);
-          if (leader) mbar_expect_tx(fb_local, static_cast<uint32_t>(2 * 2 * dchunks * kQTile));
-          const uint32_t fb = map_rank(fb_local, 0);
+          const uint32_t fb = smem_u32(q_full);
+          mbar_expect_tx(fb, static_cast<uint32_t>(dchunks * kQTile));
           const int row = qt * kPQ + static_cast<int>(rank) * kFQ;
-          for (int c = 0; c < dchunks; ++c) {
-            tma_load_3d_pair(smem_u32(q_res + (2 * c) * kQTile), &map_q, fb, c * kFC, row, static_cast<int>(2 * pq));
-            tma_load_3d_pair(smem_u32(q_res + (2 * c + 1) * kQTile), &map_q, fb, c * kFC, row,
-                             static_cast<int>(2 * pq + 1));
-          }
+          for (int c = 0; c < dchunks; ++c)
+            tma_load_3d(smem_u32(q_res + (2 * c) * kQTile), &map_q, fb, c * kFC, row, static_cast<int>(pq));
         }
         auto load_k = [&](int j) {
           const int key = j * kFK + static_cast<int>(rank) * kPKeys;
@@ -757,32 +823,28 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
             if (leader) mbar_expect_tx(fb_local, static_cast<uint32_t>(2 * nc * 2 * kPKTile));
             const uint32_t fb = map_rank(fb_local, 0);
             for (int c = 0; c < nc; ++c) {
-              tma_load_3d_pair(smem_u32(st + (2 * c) * kPKTile), &map_k, fb, (c0 + c) * kFC, key,
-                               static_cast<int>(2 * pk));
-              tma_load_3d_pair(smem_u32(st + (2 * c + 1) * kPKTile), &map_k, fb, (c0 + c) * kFC, key,
-                               static_cast<int>(2 * pk + 1));
+              tma_load_3d_pair(smem_u32(st + (2 * c) * kPKTile), &map_k, fb, (c0 + c) * kFC, key, static_cast<int>(pk));
+              tma_load_3d_pair(smem_u32(st + (2 * c + 1) * kPKTile), &map_klo, fb, (c0 + c) * kFC, key,
+                               static_cast<int>(pk));
             }
           }
           return true;
         };
+        // V of block j: this CTA's value columns as nvc MN-major chunks, for each half of
+        // the block's keys, tiles [key half][chunk]; keys past S read as zeros
         auto load_v = [&](int j) {
-          const int vrow = static_cast<int>(rank) * (a.dv / 2);
-          for (int f = 0; f < kPVFills; ++f) {
-            const int s = static_cast<int>(vf % kPVStages);
-            const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
-            if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x482)) return false;
-            ++vf;  // counted once issued: an aborting leader settles only the fills made
-            uint8_t* st = v_ring + s * kPVStage;
-            const uint32_t fb_local = smem_u32(&v_full[s]);
-            if (leader) mbar_expect_tx(fb_local, 2 * kPVC * 2 * v_tile);
-            const uint32_t fb = map_rank(fb_local, 0);
-            for (int c = 0; c < kPVC; ++c) {
-              const int key = j * kFK + (f * kPVC + c) * kFC;
-              tma_load_3d_pair(smem_u32(st + (2 * c) * kPVTileMax), &map_v, fb, key, vrow, static_cast<int>(2 * pv));
-              tma_load_3d_pair(smem_u32(st + (2 * c + 1) * kPVTileMax), &map_v, fb, key, vrow,
-                               static_cast<int>(2 * pv + 1));
-            }
-          }
+          const int s = static_cast<int>(vf % kPVStages);
+          const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
+          if (!wait_bounded(smem_u32(&v_empty[s]), ph ^ 1u, abort_flag, a.err, 0x482)) return false;
+          ++vf;  // counted once issued: an aborting producer settles only the fills made
+          uint8_t* st = v_ring + s * kPVStage;
+          const uint32_t fb = smem_u32(&v_full[s]);
+          mbar_expect_tx(fb, static_cast<uint32_t>(2 * nvc * kPVTile));
+          const int col = static_cast<int>(rank) * (a.dv / 2);
+          for (int h = 0; h < 2; ++h)
+            for (int c = 0; c < nvc; ++c)
+              tma_load_3d(smem_u32(st + (h * nvc + c) * kPVTile), &map_v, fb, col + c * kFC, j * kFK + h * 32,
+                          static_cast<int>(pv));
           return true;
         };
         for (int j = 0; j < nkb && ok; ++j) {
@@ -791,7 +853,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         }
         if (ok && nkb >= 1) ok = load_v(nkb - 1);
       }
-      if ((!ok || *abort_flag) && leader) {  // both CTAs' fills land on the leader's barriers
+      if (!ok || *abort_flag) {  // Q and V fills land on this CTA's barriers, K on the leader's
         auto settle = [&](uint64_t* full, int stages, int64_t n, int site) {
           for (int s = 0; s < stages; ++s) {
             const int64_t fills = n > s ? (n - s + stages - 1) / stages : 0;
@@ -801,7 +863,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
               if (globaltimer() - t0 > kWaitLimitNs) { record_device_error(a.err, site); break; }
           }
         };
-        settle(k_full, kPKStages, kf, 0x4f4);
+        if (leader) settle(k_full, kPKStages, kf, 0x4f4);
         settle(v_full, kPVStages, vf, 0x4f5);
         settle(q_full, 1, local, 0x4f6);
       }
@@ -817,7 +879,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         if (w < 0) continue;
         int64_t b; int qt, nkb;
         item_coords_pair(a, w, b, qt, nkb);
-        if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x490)) break;
+        if (!wait_bounded(smem_u32(q_ready), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x490)) break;
         ++local;
         tc_fence_after();
         for (int j = 0; j < nkb && ok; ++j, ++g) {
@@ -858,7 +920,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   } else if (warp == 6) {
     if (lane == 0 && leader) {
       // --------------------------------------------------- O += P·V issuer (leader)
-      const uint32_t id_o = idesc_tf32(kPQ, a.dv);
+      const uint32_t id_o = idesc_tf32(kPQ, a.dv) | (1u << 16);  // B (V) MN-major
       const uint32_t d_o = tmem + kColO;
       int64_t vf = 0, g = 0, local = 0;
       bool ok = true;
@@ -879,22 +941,23 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
             break;
           }
           const uint32_t p_hi = tmem + static_cast<uint32_t>(buf * 128), p_lo = p_hi + kFK;
-          for (int f = 0; f < kPVFills && ok; ++f, ++vf) {
+          {
             const int s = static_cast<int>(vf % kPVStages);
             const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
-            if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x495)) { ok = false; break; }
+            ++vf;
+            if (!wait_bounded(smem_u32(&v_ready[s]), ph, abort_flag, a.err, 0x495)) { ok = false; break; }
             tc_fence_after();
-            for (int c = 0; c < kPVC; ++c) {
-              const uint64_t dv_hi = smem_desc_sw128(smem_u32(v_ring + s * kPVStage + (2 * c) * kPVTileMax));
-              const uint64_t dv_lo = smem_desc_sw128(smem_u32(v_ring + s * kPVStage + (2 * c + 1) * kPVTileMax));
+            const uint32_t v_hi = smem_u32(v_ring + s * kPVStage), v_lo = v_hi + kPVHalf;
 #pragma unroll
-              for (int kk = 0; kk < kFC / 8; ++kk) {
-                const uint32_t col = static_cast<uint32_t>((f * kPVC + c) * kFC + kk * 8);
-                const uint32_t acc = (j == 0 && f == 0 && c == 0 && kk == 0) ? 0u : 1u;
-                mma_tf32_pair_ta(d_o, p_lo + col, dv_hi + 2 * kk, id_o, acc);
-                mma_tf32_pair_ta(d_o, p_hi + col, dv_lo + 2 * kk, id_o, 1u);
-                mma_tf32_pair_ta(d_o, p_hi + col, dv_hi + 2 * kk, id_o, 1u);
-              }
+            for (int t = 0; t < kFK / 8; ++t) {  // 8 keys per MMA: 8 rows of 128 B in a chunk
+              const uint32_t off = static_cast<uint32_t>((t >> 2) * nvc * kPVTile + (t & 3) * 1024);
+              const uint64_t dv_hi = smem_desc_sw128_mn(v_hi + off, kPVTile);
+              const uint64_t dv_lo = smem_desc_sw128_mn(v_lo + off, kPVTile);
+              const uint32_t col = static_cast<uint32_t>(t * 8);
+              const uint32_t acc = (j == 0 && t == 0) ? 0u : 1u;
+              mma_tf32_pair_ta(d_o, p_lo + col, dv_hi, id_o, acc);
+              mma_tf32_pair_ta(d_o, p_hi + col, dv_lo, id_o, 1u);
+              mma_tf32_pair_ta(d_o, p_hi + col, dv_hi, id_o, 1u);
             }
             commit_both(smem_u32(&v_empty[s]));
           }
@@ -903,7 +966,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         }
       }
     }
-  } else {
+  } else if (warp >= 2 && warp <= 5) {
     // -------------------------------------------------------- softmax (both CTAs)
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -1046,8 +1109,57 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(o_free), 0));
     }
+  } else if (warp >= kConvWarp0 && warp < kScanWarp) {
+    // ------------------------------------------------ lo-term converters (both CTAs)
+    // The producer's Q and V fills in its order (K's lo terms come from the pre-pass).
+    const int t = static_cast<int>(threadIdx.x) - kConvWarp0 * 32;
+    int64_t vf = 0, local = 0;
+    uint32_t bad = 0;
+    bool ok = true;
+    for (int64_t r = 0; r * ncl < items && ok; ++r) {
+      const int64_t w = snake_item_pair(r, items, cid, ncl);
+      if (w < 0) continue;
+      int64_t b; int qt, nkb;
+      item_coords_pair(a, w, b, qt, nkb);
+      if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x4b0)) break;
+      ++local;
+      for (int c = 0; c < dchunks; ++c)
+        write_lo(smem_u32(q_res + (2 * c) * kQTile), smem_u32(q_res + (2 * c + 1) * kQTile), kQTile, t, bad);
+      publish_lo(smem_u32(q_ready), lane);
+      auto conv_v = [&]() {
+        const int s = static_cast<int>(vf % kPVStages);
+        const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
+        ++vf;
+        if (!wait_bounded(smem_u32(&v_full[s]), ph, abort_flag, a.err, 0x4b2)) return false;
+        const uint32_t st = smem_u32(v_ring + s * kPVStage);
+        write_lo(st, st + kPVHalf, 2 * nvc * kPVTile, t, bad);
+        publish_lo(smem_u32(&v_ready[s]), lane);
+        return true;
+      };
+      for (int j = 0; j < nkb && ok; ++j) ok = conv_v();
+    }
+    // every tile this CTA loaded was checked on the way: Q whole, V up to the last key
+    // any item reaches (the pre-pass checked all of K)
+    if (__any_sync(0xffffffffu, bad != 0) && lane == 0) atomicExch(a.flag, 1);
+  } else if (warp == kScanWarp) {
+    // ------------------------------------------------------ non-finite scan (both CTAs)
+    // The V rows no item loads (causal, keys past the last query tile): rows
+    // [a.tail_row, S) of every plane, 16-byte words split evenly over the CTAs.
+    uint32_t bad = 0;
+    const int64_t cta = blockIdx.x, nct = gridDim.x, rows = a.S - a.tail_row;
+    if (rows > 0) {
+      const uint4* p = reinterpret_cast<const uint4*>(a.v);
+      const int64_t row_words = a.dv / 4, per_plane = rows * row_words;
+      const int64_t n = a.v_planes * per_plane, lo = n * cta / nct, hi = n * (cta + 1) / nct;
+      for (int64_t i = lo + lane; i < hi; i += 32) {
+        const int64_t plane = i / per_plane;
+        bad |= nonfinite4(__ldg(p + (plane * a.S + a.tail_row) * row_words + (i - plane * per_plane)));
+      }
+    }
+    if (__any_sync(0xffffffffu, bad != 0) && lane == 0) atomicExch(a.flag, 1);
   }
 
+  dependents_may_launch();  // the fallback kernel behind may start launching
   // every MMA the leader's issuers started completes before either CTA releases its TMEM
   if ((warp == 1 || warp == 6) && lane == 0) {
     uint64_t* d = &drain[warp == 1 ? 0 : 1];
@@ -1066,8 +1178,9 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   cluster_sync_all();  // neither CTA leaves while the other may still touch its barriers
 }
 
-// IEEE fallback, used only when the pre-pass saw inf / NaN: one CTA per (batch, query)
-// row computes the scores as float32 dot products in feature order (as the reference
+// IEEE fallback, used only when the pre-pass or the pair kernel's scan saw inf / NaN
+// (launched behind the fused kernel with programmatic stream serialization: it waits
+// for that grid before reading the flag): one CTA per (batch, query) row computes the scores as float32 dot products in feature order (as the reference
 // matmul), the masked softmax of core/inference.cpp / cpu_inference.cpp, and P·V summed
 // over keys in order, recomputing the dot products per pass instead of storing them.
 constexpr int kRowThreads = 128;
@@ -1076,6 +1189,7 @@ template <int MK>
 __global__ void __launch_bounds__(kRowThreads)
 flash_rows_fallback(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                     FlashArgs a, int64_t d, float scale, const int* __restrict__ flag) {
+  wait_for_prior_grid();
   if (!*flag) return;
   __shared__ float qrow[kMaxDv];
   __shared__ float p_chunk[kRowThreads];
@@ -1227,9 +1341,21 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   float* wk = reinterpret_cast<float*>(ws + lay.off_k);
   float* wv = reinterpret_cast<float*>(ws + lay.off_v);
   if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("attention flag reset");
-  // K-major split planes: Q [2nq][L][d], K [2nk][S][d] (rows already K-major), Vᵀ [2nv][dv][Sp]
-  split_rows_planes2(s, q, wq, nq, L, k, wk, nk, S, d, d, flag);
-  split_cols_planes(s, v, wv, nv, S, dv, lay.sp, flag);
+  // CTA pairs (256 queries per item) for unmasked products with more than one 128-query
+  // tile, reading q, k, v in place (no pre-pass): they need 16-byte aligned operands and
+  // whole 32-column V chunks per CTA (Dv 64 or 128). Measured on [32, 2048, 2048, 128]
+  // with the split pre-pass: 0.487 against 0.512 ms per call without a mask, 0.302
+  // against 0.306 causal; with a float mask the pair is slower (0.674 against 0.636 ms
+  // kernel), its two SMs' softmax warps both gating every P·V.
+  auto aligned16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool pair = L > kFQ && mask_kind == 0 && dv % 64 == 0 && aligned16(q) && aligned16(k) && aligned16(v);
+  if (pair) {
+    split_lo_planes(s, k, wk, nk * S * d / 4, flag);  // K's lo terms [nk][S][d]
+  } else {
+    // K-major split planes: Q [2nq][L][d], K [2nk][S][d] (rows already K-major), Vᵀ [2nv][dv][Sp]
+    split_rows_planes2(s, q, wq, nq, L, k, wk, nk, S, d, d, flag);
+    split_cols_planes(s, v, wv, nv, S, dv, lay.sp, flag);
+  }
   const int sms = sm_count();
   if (mask_kind == 2) {
     // the mask's storage: 1 + sum of (extent - 1) * stride over [batch..., L, S]
@@ -1246,17 +1372,13 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     fa.mask_vec = vec ? 1 : 0;
   }
 
-  // CTA pairs (256 queries per item) for unmasked products with more than one 128-query
-  // tile: each CTA loads 32 of a block's 64 keys and half of Vᵀ's rows. Measured on
-  // [32, 2048, 2048, 128]: 0.487 against 0.512 ms per call without a mask, 0.302
-  // against 0.306 causal; with a float mask the pair is slower (0.674 against 0.636 ms
-  // kernel), its two SMs' softmax warps both gating every P·V.
-  const bool pair = L > kFQ && mask_kind == 0;
-  alignas(64) CUtensorMap map_q, map_k, map_v;
-  if (!encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) ||
-      !encode_planes_map(&map_k, wk, 2 * nk, S, d, pair ? kPKeys : kFK) ||
-      !encode_planes_map(&map_v, wv, 2 * nv, dv, lay.sp, static_cast<int>(pair ? dv / 2 : dv)))
-    return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
+  alignas(64) CUtensorMap map_q, map_k, map_klo, map_v;
+  const bool mapped =
+      pair ? encode_planes_map(&map_q, q, nq, L, d, kFQ) && encode_planes_map(&map_k, k, nk, S, d, kPKeys) &&
+                 encode_planes_map(&map_klo, wk, nk, S, d, kPKeys) && encode_planes_map(&map_v, v, nv, S, dv, 32, true)
+           : encode_planes_map(&map_q, wq, 2 * nq, L, d, kFQ) && encode_planes_map(&map_k, wk, 2 * nk, S, d, kFK) &&
+                 encode_planes_map(&map_v, wv, 2 * nv, dv, lay.sp, static_cast<int>(dv));
+  if (!mapped) return (set_error("cuTensorMapEncodeTiled failed"), TCX_INTERNAL);
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1280,13 +1402,17 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   fa.vec8 = reinterpret_cast<uintptr_t>(out) % 32 == 0;
   fa.nonfinite = flag;
   fa.err = device_error_word();
+  fa.v = v;
+  fa.v_planes = nv;
+  fa.tail_row = causal ? std::min<int64_t>(S, static_cast<int64_t>(fa.q_tiles) * kPQ) : S;
+  fa.flag = flag;
   const int64_t items = batches * fa.q_tiles;
   if (pair) {
     TimedLaunch timer("flash_tf32x3", s);
     const int clusters = static_cast<int>(std::min<int64_t>(items, sms / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
-    cfg.blockDim = dim3(kFlashThreads);
+    cfg.blockDim = dim3(kPairThreads);
     cfg.dynamicSmemBytes = kPairSmem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1296,7 +1422,7 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, flash_pair_kernel<0>, map_q, map_k, map_v, fa);  // unmasked only
+    cudaLaunchKernelEx(&cfg, flash_pair_kernel<0>, map_q, map_k, map_klo, map_v, fa);  // unmasked only
   } else {
     TimedLaunch timer("flash_tf32x3", s);
     const int grid = static_cast<int>(std::min<int64_t>(items, sms));
@@ -1307,10 +1433,13 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   if (int st = launch_status("fused attention")) return st;
   {
     TimedLaunch timer("flash_rows_fallback", s);
-    const int grid = static_cast<int>(std::min<int64_t>(batches * L, 8LL * sms));
-    if (mask_kind == 1) flash_rows_fallback<1><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
-    else if (mask_kind == 2) flash_rows_fallback<2><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
-    else flash_rows_fallback<0><<<grid, kRowThreads, 0, s>>>(q, k, v, fa, d, scale, flag);
+    // idle unless a non-finite input was seen: a small grid (rows in a grid-stride loop)
+    // keeps its launch and exit short
+    const int grid = static_cast<int>(std::min<int64_t>(batches * L, 2LL * sms));
+    const int* f = flag;
+    if (mask_kind == 1) launch_after(flash_rows_fallback<1>, grid, kRowThreads, s, 0, q, k, v, fa, d, scale, f);
+    else if (mask_kind == 2) launch_after(flash_rows_fallback<2>, grid, kRowThreads, s, 0, q, k, v, fa, d, scale, f);
+    else launch_after(flash_rows_fallback<0>, grid, kRowThreads, s, 0, q, k, v, fa, d, scale, f);
   }
   return launch_status("attention fallback");
 }

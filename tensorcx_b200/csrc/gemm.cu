@@ -1639,7 +1639,11 @@ void split_cols_planes(cudaStream_t s, const float* x, float* planes, int64_t nb
                        int64_t kp, int* flag) {
   split_b(s, x, planes, nb, n, k, kp, flag, false, sm_count());
 }
-bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows) {
-  return make_map(static_cast<CUtensorMap*>(map), base, planes, rows, kp, box_rows);
+void split_lo_planes(cudaStream_t s, const float* x, float* lo, int64_t n4, int* flag) {
+  split_lo_launch(s, x, lo, n4, nullptr, nullptr, 0, flag, sm_count());
+}
+bool encode_planes_map(void* map, const float* base, int64_t planes, int64_t rows, int64_t kp, int box_rows,
+                       bool mn_atom32) {
+  return make_map(static_cast<CUtensorMap*>(map), base, planes, rows, kp, box_rows, mn_atom32);
 }
 }  // namespace tcx

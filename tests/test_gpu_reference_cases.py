@@ -544,6 +544,32 @@ def test_fused_attention_nonfinite_inputs(tcx, oracle, where, value):
             attn_check(got, oracle.attention(q, k, v, None, causal))
 
 
+@pytest.mark.parametrize("where,index", [("q", (0, 150, 5)), ("k", (1, 350, 7)), ("v", (0, 399, 63)),
+                                         ("v", (1, 0, 0))])
+@pytest.mark.parametrize("value", [np.inf, np.nan])
+@pytest.mark.parametrize("lq", [300, 200])
+def test_fused_attention_pair_nonfinite_inputs(tcx, oracle, where, index, value, lq):
+    """The CTA-pair kernel (over 128 queries, Dv 64 or 128) reads q, k, v in place and
+    checks them for inf / NaN on the way; a hit anywhere, even at keys no query reaches
+    causally (with 200 queries, k and v rows 256-399 are never loaded and are scanned
+    apart), hands the call to the IEEE row kernel."""
+    q, k, v = gauss((2, lq, 64), 17), gauss((2, 400, 64), 18), gauss((2, 400, 64), 19)
+    {"q": q, "k": k, "v": v}[where][index] = value
+    for causal in (False, True):
+        got = host(tcx.attention(dev(q), dev(k), dev(v), is_causal=causal))
+        with np.errstate(all="ignore"):
+            attn_check(got, oracle.attention(q, k, v, None, causal))
+
+
+def test_fused_attention_pair_broadcast(tcx, oracle):
+    """Broadcast batch axes through the pair kernel's in-place operand maps: k shared
+    over the first batch axis, v over the second."""
+    q, k, v = gauss((3, 2, 300, 64), 20), gauss((1, 2, 260, 64), 21), gauss((3, 1, 260, 128), 22)
+    for causal in (False, True):
+        got = host(tcx.attention(dev(q), dev(k), dev(v), scale=0.4, is_causal=causal))
+        attn_check(got, oracle.attention(q, k, v, None, causal, 0.4))
+
+
 FUSED_MASKS = [
     # (mask shape relative to [batch=2, L, S], kind): full, broadcast over batch or queries,
     # constant along keys (key stride 0), a scalar

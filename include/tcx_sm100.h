@@ -42,8 +42,9 @@ typedef struct CUstream_st* tcx_stream_t;
 /* tensorcx::StatusCode */
 enum { TCX_OK = 0, TCX_INVALID_ARGUMENT = 1, TCX_UNAVAILABLE = 2, TCX_INTERNAL = 3 };
 
-/* tensorcx::DType (cpp/tensorcx/core/dtype.h:8-12); bool is not on this path. */
-enum { TCX_FLOAT32 = 0, TCX_INT32 = 1 };
+/* tensorcx::DType (cpp/tensorcx/core/dtype.h:8-12); bool (one byte, 0 or 1) only in
+ * the tensor operations at the end of this header. */
+enum { TCX_FLOAT32 = 0, TCX_INT32 = 1, TCX_BOOL = 2 };
 
 /* tensorcx::OpKind values (cpp/tensorcx/core/operation.h:12-63) for the ops on this
  * path, so a host backend can pass OpDesc::kind through unchanged. */
@@ -51,7 +52,12 @@ enum {
   TCX_OP_ADD = 1, TCX_OP_MULTIPLY = 2, TCX_OP_MATMUL = 3, TCX_OP_SUM = 4, TCX_OP_MAX = 5,
   TCX_OP_MEAN = 6, TCX_OP_EXP = 7, TCX_OP_GELU = 8, TCX_OP_SILU = 9, TCX_OP_SOFTMAX = 10,
   TCX_OP_RMSNORM = 11, TCX_OP_LAYERNORM = 12, TCX_OP_SUBTRACT = 13, TCX_OP_DIVIDE = 14,
-  TCX_OP_MIN = 41, TCX_OP_ARGMAX = 42, TCX_OP_CLIP = 43
+  TCX_OP_NEGATE = 15, TCX_OP_ADD_SCALAR = 16, TCX_OP_SUBTRACT_SCALAR = 17, TCX_OP_MULTIPLY_SCALAR = 18,
+  TCX_OP_DIVIDE_SCALAR = 19, TCX_OP_EQUAL = 24, TCX_OP_NOT_EQUAL = 25, TCX_OP_LESS = 26,
+  TCX_OP_LESS_EQUAL = 27, TCX_OP_GREATER = 28, TCX_OP_GREATER_EQUAL = 29, TCX_OP_LOGICAL_AND = 30,
+  TCX_OP_LOGICAL_OR = 31, TCX_OP_LOGICAL_XOR = 32, TCX_OP_LOGICAL_NOT = 33, TCX_OP_WHERE = 34,
+  TCX_OP_ANY = 35, TCX_OP_ALL = 36, TCX_OP_LOG = 38, TCX_OP_SQRT = 39, TCX_OP_ABS = 40,
+  TCX_OP_MIN = 41, TCX_OP_ARGMAX = 42, TCX_OP_CLIP = 43, TCX_OP_TOPK = 44
 };
 
 /* Activation applied after the bias add in fused chains. ReLU is tensor.cx's
@@ -365,6 +371,83 @@ int tcx_sm100_copy_to_host(tcx_stream_t stream, void* dst, const void* src, size
 enum { TCX_RANDOM_NORMAL = 0, TCX_RANDOM_UNIFORM = 1 };
 int tcx_sm100_random(tcx_stream_t stream, int distribution, float* out, int64_t count, uint64_t seed,
                      uint64_t offset, float a, float b);
+
+/* -------------------------------------------------------- tensor operations --- */
+/* The reference CUDA backend's remaining primitives (data movement, predicates, casts,
+ * scalar arithmetic, topk, embedding), off the hot path but needed for a drop-in
+ * device="cuda". Stream-ordered like the rest; results as the reference's kernels and
+ * CPU backend, bit for bit (log within 1 ulp: CUDA's logf against std::log). */
+
+/* One-input elementwise ops over `count` float32 or int32 words: TCX_OP_NEGATE,
+ * TCX_OP_{ADD,SUBTRACT,MULTIPLY,DIVIDE}_SCALAR (scalar rounded to float32, or an int32
+ * value; scalar_left puts it on the left; no int32 divide), TCX_OP_LOG / TCX_OP_SQRT
+ * (float32), TCX_OP_ABS (float32: sign cleared; int32: wraps at INT_MIN). Replaces
+ * launch_unary's negate, launch_scalar and math_kernel codes 0-2 (primitives.cu:14-32,
+ * elementwise.cu:110-116, math.cu:29-41). */
+int tcx_sm100_map(tcx_stream_t stream, int op, int dtype, const void* input, void* output, int64_t count,
+                  double scalar, int32_t scalar_left);
+
+/* Cast between TCX_FLOAT32, TCX_INT32 and TCX_BOOL. float32 -> int32 truncates toward
+ * zero; a value that is not finite or lies outside [-2^31, 2^31) raises the device int
+ * *invalid_flag (cleared first; required for this pair), which the caller reads before
+ * using the output. Same dtype copies. Replaces launch_validate_int32_cast, launch_cast
+ * and launch_bool_cast (elementwise.cu:85-107, predicate.cu:62-71). */
+int tcx_sm100_cast(tcx_stream_t stream, int src_dtype, int dst_dtype, const void* input, void* output,
+                   int64_t count, int* invalid_flag);
+
+/* Comparisons (TCX_OP_EQUAL .. TCX_OP_GREATER_EQUAL: float32, int32 or bool inputs, bool
+ * output), logical ops (bool) and TCX_OP_WHERE (bool condition a, branches b and c of
+ * `dtype`, output `dtype`), with broadcasting: metadata = output shape, then the element
+ * strides of each input (0 = broadcast), (1 + inputs) * rank values, as
+ * make_predicate_plan builds them (core/predicate.cpp). Replaces launch_predicate
+ * (predicate.cu:19-61). */
+int tcx_sm100_predicate(tcx_stream_t stream, int op, int dtype, const void* a, const void* b, const void* c,
+                        void* output, int64_t count, const int64_t* metadata, int32_t rank);
+
+/* any (TCX_OP_ANY) / all (TCX_OP_ALL) of bool elements over the reduction plan's
+ * (extent, stride) pairs (make_boolean_reduction_plan). Replaces launch_bool_reduce. */
+int tcx_sm100_bool_reduce(tcx_stream_t stream, int op, const void* input, void* output, int64_t groups,
+                          int64_t reduction_size, const int64_t* index_metadata, int32_t rank);
+
+/* Transpose / slice: output element i (contiguous over `shape`) = input[offset +
+ * sum(coord * input_strides)], 1- or 4-byte elements (make_transpose_plan /
+ * make_slice_plan). A transpose of the last two axes goes through 32 x 32 shared-memory
+ * tiles. Replaces launch_transpose (elementwise.cu:62-76). */
+int tcx_sm100_index_copy(tcx_stream_t stream, int32_t element_bytes, const void* input, void* output, int64_t count,
+                         const int64_t* shape, const int64_t* input_strides, int32_t rank, int64_t offset);
+
+/* One input of a concat: input element i goes to output (i / block) * output_block +
+ * offset + i % block (make_concat_plan). Replaces launch_concat (elementwise.cu:78-83). */
+int tcx_sm100_concat(tcx_stream_t stream, int32_t element_bytes, const void* input, void* output, int64_t count,
+                     int64_t block, int64_t output_block, int64_t offset);
+
+/* masked_select (make_masked_select_plan): first the number of selected mask positions
+ * into the device int64 *selected (the output's leading extent; the caller reads it and
+ * sizes the output), then the copy of each selected position's block of `block`
+ * elements in order. Both calls take the same workspace, which carries the per-tile
+ * offsets from the first to the second. Replaces launch_mask_prefix / launch_prefix_step
+ * / launch_mask_copy (predicate.cu:76-101). */
+size_t tcx_sm100_masked_select_workspace_bytes(int64_t mask_count);
+int tcx_sm100_masked_select_count(tcx_stream_t stream, const void* mask, int64_t mask_count, int64_t* selected,
+                                  void* workspace, size_t workspace_bytes);
+int tcx_sm100_masked_select(tcx_stream_t stream, int32_t element_bytes, const void* input, const void* mask,
+                            int64_t mask_count, int64_t block, void* output, const void* workspace,
+                            size_t workspace_bytes);
+
+/* topk along one axis (make_math_plan code 6): `groups` output groups of k values (the
+ * input's dtype) and int32 indices, group g reading elements base + j * inner. Order as
+ * the reference: largest: NaN first, then larger, ties to the lower index; smallest:
+ * smaller first, NaN last; unsorted: the selected indices ascending. Replaces
+ * math_kernel code 6 (math.cu:61-76). */
+int tcx_sm100_topk(tcx_stream_t stream, int dtype, const void* input, void* values, int32_t* indices, int64_t groups,
+                   int64_t reduction_size, int64_t inner, int64_t k, int32_t largest, int32_t sorted);
+
+/* Embedding gather: output row i = weight row indices[i] (float32 rows of `width`); an
+ * index outside [0, vocabulary) raises the device int *invalid_flag (cleared first),
+ * which the caller reads. Replaces launch_embedding_validate / launch_embedding_gather
+ * (inference.cu:8-15). */
+int tcx_sm100_embedding(tcx_stream_t stream, const int32_t* indices, int64_t rows, const float* weight,
+                        int64_t vocabulary, int64_t width, float* output, int* invalid_flag);
 
 #ifdef __cplusplus
 }  /* extern "C" */

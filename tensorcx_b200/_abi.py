@@ -13,9 +13,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libtcx_sm100.so")
 
 OK, INVALID_ARGUMENT, UNAVAILABLE, INTERNAL = 0, 1, 2, 3
-FLOAT32, INT32 = 0, 1
+FLOAT32, INT32, BOOL = 0, 1, 2
 OP = dict(add=1, multiply=2, matmul=3, sum=4, max=5, mean=6, exp=7, gelu=8, silu=9, softmax=10,
-          rmsnorm=11, layernorm=12, subtract=13, divide=14, min=41, argmax=42, clip=43)
+          rmsnorm=11, layernorm=12, subtract=13, divide=14, negate=15, add_scalar=16, subtract_scalar=17,
+          multiply_scalar=18, divide_scalar=19, equal=24, not_equal=25, less=26, less_equal=27, greater=28,
+          greater_equal=29, logical_and=30, logical_or=31, logical_xor=32, logical_not=33, where=34, any=35,
+          all=36, log=38, sqrt=39, abs=40, min=41, argmax=42, clip=43, topk=44)
 ACT = dict(none=0, silu=1, relu=2)
 MATMUL_PATH = dict(auto=0, ffma=1, tensor=2)
 RANDOM = dict(normal=0, uniform=1)
@@ -75,6 +78,17 @@ SIGNATURES = {
     "tcx_sm100_copy_to_device": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
     "tcx_sm100_copy_to_host": (ctypes.c_int, [_vp, _vp, _vp, _sz]),
     "tcx_sm100_random": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _i64, ctypes.c_uint64, ctypes.c_uint64, _f32, _f32]),
+    "tcx_sm100_map": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, ctypes.c_double, _i32]),
+    "tcx_sm100_cast": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _i64, _vp]),
+    "tcx_sm100_predicate": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64p, _i32]),
+    "tcx_sm100_bool_reduce": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64p, _i32]),
+    "tcx_sm100_index_copy": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i64, _i64p, _i64p, _i32, _i64]),
+    "tcx_sm100_concat": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64]),
+    "tcx_sm100_masked_select_workspace_bytes": (_sz, [_i64]),
+    "tcx_sm100_masked_select_count": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _sz]),
+    "tcx_sm100_masked_select": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _sz]),
+    "tcx_sm100_topk": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32]),
+    "tcx_sm100_embedding": (ctypes.c_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "tcx_sm100_matmul_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int]),
     "tcx_sm100_matmul": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i32,
                                         _vp, ctypes.c_int, ctypes.c_int, _vp, _sz]),

@@ -27,6 +27,7 @@
 #include "tensorcx/backends/cuda/cuda_profile.h"
 #include "tensorcx/core/inference.h"
 #include "tensorcx/core/math.h"
+#include "tensorcx/core/predicate.h"
 #include "tensorcx/core/shape.h"
 
 namespace tensorcx::cuda {
@@ -125,14 +126,32 @@ bool is_binary(OpKind k) {
   return k == OpKind::kAdd || k == OpKind::kSubtract || k == OpKind::kMultiply || k == OpKind::kDivide;
 }
 
+bool is_scalar_map(OpKind k) {
+  return k == OpKind::kNegate || k == OpKind::kAddScalar || k == OpKind::kSubtractScalar ||
+         k == OpKind::kMultiplyScalar || k == OpKind::kDivideScalar;
+}
+
+int abi_dtype(DType d) { return d == DType::kFloat32 ? TCX_FLOAT32 : d == DType::kInt32 ? TCX_INT32 : TCX_BOOL; }
+
 class Executor {
  public:
   Executor(const BackendExecution& e, std::vector<CudaTensor>& in, const DeviceScope& scope)
       : e_(e), in_(in), scope_(scope) {}
 
-  Status run(Tensor& out) {
+  // `second` receives topk's indices (the op's second output); other ops leave it.
+  Status run(Tensor& out, Tensor& second) {
     const auto kind = e_.op.kind;
     if (kind == OpKind::kFill) return fill(out);
+    if (is_scalar_map(kind)) return scalar_map(out);
+    if (kind == OpKind::kLog || kind == OpKind::kSqrt || kind == OpKind::kAbs) return unary_math(out);
+    if (kind == OpKind::kTopK) return topk(out, second);
+    if (kind == OpKind::kCast) return cast(out);
+    if (kind == OpKind::kTranspose || kind == OpKind::kSlice) return index_copy(out);
+    if (kind == OpKind::kConcat) return concat(out);
+    if (is_predicate_elementwise(kind)) return predicate(out);
+    if (kind == OpKind::kAny || kind == OpKind::kAll) return bool_reduce(out);
+    if (kind == OpKind::kMaskedSelect) return masked_select(out);
+    if (kind == OpKind::kEmbedding) return embedding(out);
     if (kind == OpKind::kMatmul) return matmul(out);
     if (kind == OpKind::kLinear) return linear(out);
     if (kind == OpKind::kSum || kind == OpKind::kMax || kind == OpKind::kMean) return reduction(out);
@@ -143,10 +162,7 @@ class Executor {
     if (kind == OpKind::kMin || kind == OpKind::kArgmax || kind == OpKind::kClip) return math(out);
     if (kind == OpKind::kAttentionSoftmax) return attention_softmax(out);
     if (kind == OpKind::kAttention) return attention(out);
-    return {StatusCode::kUnavailable,
-            "operation is not on the sm100 hot path (served ops: fill, matmul, linear, sum, max, mean, min, "
-            "argmax, clip, softmax, rmsnorm, layernorm and their affine forms, exp, gelu, silu, add, subtract, "
-            "multiply, divide, attention, attention softmax)"};
+    return {StatusCode::kUnavailable, "unsupported CUDA operation"};
   }
 
  private:
@@ -537,6 +553,241 @@ class Executor {
     }
     return publish(out, plan.dtype, plan.shape, buffer.move_value());
   }
+
+  // The host reads a device int the previous launch wrote (cast range, embedding index).
+  Expected<int> read_flag(const Scratch& flag) {
+    int value = 0;
+    ProfileScope span(ProfileCategory::kCopy, "device_to_host", "cuda", sizeof(int));
+    auto st = runtime_status(cudaMemcpyAsync(&value, flag.data(), sizeof(int), cudaMemcpyDeviceToHost, scope_.stream()),
+                             "CUDA flag readback");
+    if (!st.ok()) return st;
+    st = runtime_status(cudaStreamSynchronize(scope_.stream()), "CUDA flag readback");
+    if (!st.ok()) return st;
+    return value;
+  }
+
+  // negate and scalar arithmetic (cuda_backend.cpp:452-466 and 585-587 of the reference):
+  // float32, or int32 except divide, with an integral int32 scalar.
+  Status scalar_map(Tensor& out) {
+    const auto kind = e_.op.kind;
+    const auto& t = e_.inputs[0];
+    const bool integer_ok = kind != OpKind::kDivideScalar;
+    if (t.dtype != DType::kFloat32 && !(t.dtype == DType::kInt32 && integer_ok))
+      return invalid("CUDA operation only supports float32 for this dtype");
+    if (t.dtype == DType::kInt32 && kind != OpKind::kNegate && !is_int32_representable(e_.op.scalar_value))
+      return invalid("fill/arithmetic scalar must be an integer in int32 range");
+    auto buffer = output(t.dtype, t.shape);
+    if (!buffer) return buffer.status();
+    if (numel(t.shape)) {
+      auto st = launch(kind == OpKind::kNegate ? "launch_unary" : "launch_scalar", "CUDA elementwise", [&] {
+        return tcx_sm100_map(abi_stream(scope_), static_cast<int>(kind), abi_dtype(t.dtype), ptr(0),
+                             buffer.value()->data(), numel(t.shape), e_.op.scalar_value, e_.op.scalar_left ? 1 : 0); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, t.dtype, t.shape, buffer.move_value());
+  }
+
+  // log / sqrt / abs through make_math_plan (codes 0-2).
+  Status unary_math(Tensor& out) {
+    const auto plan = make_math_plan(e_.op, e_.inputs);
+    auto buffer = output(plan.dtype, plan.shape);
+    if (!buffer) return buffer.status();
+    if (plan.groups) {
+      auto st = launch("launch_math", "CUDA math", [&] {
+        return tcx_sm100_map(abi_stream(scope_), static_cast<int>(e_.op.kind), abi_dtype(plan.dtype), ptr(0),
+                             buffer.value()->data(), plan.groups, 0.0, 0); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, plan.dtype, plan.shape, buffer.move_value());
+  }
+
+  // topk through make_math_plan (code 6): values and int32 indices.
+  Status topk(Tensor& out, Tensor& indices_out) {
+    const auto plan = make_math_plan(e_.op, e_.inputs);
+    auto values = output(plan.dtype, plan.shape);
+    if (!values) return values.status();
+    auto indices = output(DType::kInt32, plan.shape);
+    if (!indices) return indices.status();
+    if (plan.groups) {
+      auto st = launch("launch_math", "CUDA topk", [&] {
+        return tcx_sm100_topk(abi_stream(scope_), abi_dtype(plan.dtype), ptr(0), values.value()->data(),
+                              static_cast<std::int32_t*>(indices.value()->data()), plan.groups, plan.reduce, plan.inner,
+                              plan.k, e_.op.largest ? 1 : 0, e_.op.sorted ? 1 : 0); });
+      if (!st.ok()) return st;
+    }
+    indices_out = to_core_tensor(CudaTensor(DType::kInt32, plan.shape, indices.move_value()));
+    return publish(out, plan.dtype, plan.shape, values.move_value());
+  }
+
+  // cast (cuda_backend.cpp:399-440 of the reference): float32 / int32 / bool; a
+  // float32 -> int32 cast checks the range on the device and fails before publishing.
+  Status cast(Tensor& out) {
+    const auto& t = e_.inputs[0];
+    const auto target = e_.op.target_dtype;
+    if (target != DType::kFloat32 && target != DType::kInt32 && target != DType::kBool)
+      return invalid("unsupported cast target dtype");
+    auto buffer = output(target, t.shape);
+    if (!buffer) return buffer.status();
+    const auto count = numel(t.shape);
+    if (count) {
+      const bool checked = t.dtype == DType::kFloat32 && target == DType::kInt32;
+      Scratch flag(checked ? sizeof(int) : 0, scope_);
+      if (!flag.status().ok()) return flag.status();
+      auto st = launch("launch_cast", "CUDA tensor cast", [&] {
+        return tcx_sm100_cast(abi_stream(scope_), abi_dtype(t.dtype), abi_dtype(target), ptr(0), buffer.value()->data(),
+                              count, checked ? static_cast<int*>(flag.data()) : nullptr); });
+      if (!st.ok()) return st;
+      if (checked) {
+        auto bad = read_flag(flag);
+        if (!bad) return bad.status();
+        if (bad.value()) return invalid("float32 to int32 cast requires finite values in [-2147483648, 2147483648)");
+      }
+    }
+    return publish(out, target, t.shape, buffer.move_value());
+  }
+
+  // transpose / slice (cuda_backend.cpp:342-375 of the reference): one index copy.
+  Status index_copy(Tensor& out) {
+    const auto& t = e_.inputs[0];
+    const auto plan = e_.op.kind == OpKind::kTranspose
+                          ? make_transpose_plan(t.shape, e_.op.axes)
+                          : make_slice_plan(t.shape, e_.op.slice_starts, e_.op.slice_steps, e_.op.slice_shape);
+    auto buffer = output(t.dtype, plan.output_shape);
+    if (!buffer) return buffer.status();
+    const auto count = numel(plan.output_shape);
+    if (count) {
+      auto st = launch("launch_transpose", "CUDA index copy", [&] {
+        return tcx_sm100_index_copy(abi_stream(scope_), static_cast<std::int32_t>(dtype_size(t.dtype)), ptr(0),
+                                    buffer.value()->data(), count, plan.output_shape.data(), plan.input_strides.data(),
+                                    static_cast<std::int32_t>(plan.output_shape.size()), plan.offset); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, t.dtype, plan.output_shape, buffer.move_value());
+  }
+
+  // concat (cuda_backend.cpp:376-398 of the reference): one block copy per input.
+  Status concat(Tensor& out) {
+    const auto dtype = e_.inputs[0].dtype;
+    std::vector<Shape> shapes;
+    for (const auto& t : e_.inputs) {
+      if (t.dtype != dtype) return invalid("concat dtypes must match");
+      shapes.push_back(t.shape);
+    }
+    const auto plan = make_concat_plan(shapes, e_.op.axis);
+    auto buffer = output(dtype, plan.output_shape);
+    if (!buffer) return buffer.status();
+    if (numel(plan.output_shape)) {
+      const Dim output_block = plan.output_shape[plan.axis] * plan.inner;
+      Dim offset = 0;
+      for (std::size_t i = 0; i < e_.inputs.size(); ++i) {
+        const Dim block = e_.inputs[i].shape[plan.axis] * plan.inner;
+        const Dim count = numel(e_.inputs[i].shape);
+        if (count) {
+          auto st = launch("launch_concat", "CUDA concat", [&] {
+            return tcx_sm100_concat(abi_stream(scope_), static_cast<std::int32_t>(dtype_size(dtype)), ptr(i),
+                                    buffer.value()->data(), count, block, output_block, offset); });
+          if (!st.ok()) return st;
+        }
+        offset += block;
+      }
+    }
+    return publish(out, dtype, plan.output_shape, buffer.move_value());
+  }
+
+  // comparisons, logical ops and where (make_predicate_plan).
+  Status predicate(Tensor& out) {
+    const auto plan = make_predicate_plan(e_.op, e_.inputs);
+    auto buffer = output(plan.output_dtype, plan.output_shape);
+    if (!buffer) return buffer.status();
+    const auto count = numel(plan.output_shape);
+    if (count) {
+      Shape metadata = plan.output_shape;
+      for (const auto& strides : plan.input_strides) metadata.insert(metadata.end(), strides.begin(), strides.end());
+      const auto kind = e_.op.kind;
+      const auto dtype = e_.inputs[kind == OpKind::kWhere ? 1 : 0].dtype;
+      auto st = launch("launch_predicate", "CUDA predicate", [&] {
+        return tcx_sm100_predicate(abi_stream(scope_), static_cast<int>(kind), abi_dtype(dtype), ptr(0),
+                                   e_.inputs.size() > 1 ? ptr(1) : nullptr, e_.inputs.size() > 2 ? ptr(2) : nullptr,
+                                   buffer.value()->data(), count, metadata.data(),
+                                   static_cast<std::int32_t>(plan.output_shape.size())); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, plan.output_dtype, plan.output_shape, buffer.move_value());
+  }
+
+  // any / all (make_boolean_reduction_plan).
+  Status bool_reduce(Tensor& out) {
+    const auto& t = e_.inputs[0];
+    if (t.dtype != DType::kBool) return invalid("any/all require bool tensors");
+    const auto plan = make_boolean_reduction_plan(e_.op, t.shape);
+    auto buffer = output(DType::kBool, plan.output_shape);
+    if (!buffer) return buffer.status();
+    const auto groups = numel(plan.output_shape);
+    if (groups) {
+      auto st = launch("launch_bool_reduce", "CUDA bool reduction", [&] {
+        return tcx_sm100_bool_reduce(abi_stream(scope_), static_cast<int>(e_.op.kind), ptr(0), buffer.value()->data(),
+                                     groups, plan.reduction_size, plan.index_metadata.data(),
+                                     static_cast<std::int32_t>(t.shape.size())); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, DType::kBool, plan.output_shape, buffer.move_value());
+  }
+
+  // masked_select (make_masked_select_plan): count on the device, read it, then copy.
+  Status masked_select(Tensor& out) {
+    const auto& t = e_.inputs[0];
+    const auto& mask = e_.inputs[1];
+    const auto plan = make_masked_select_plan(t, mask);
+    const auto count = numel(mask.shape);
+    Scratch ws(tcx_sm100_masked_select_workspace_bytes(count) + 64, scope_);
+    if (!ws.status().ok()) return ws.status();
+    auto* selected_dev = reinterpret_cast<std::int64_t*>(static_cast<char*>(ws.data()) + ws.bytes() - 64);
+    Dim selected = 0;
+    if (count) {
+      auto st = launch("launch_mask_prefix", "CUDA mask count", [&] {
+        return tcx_sm100_masked_select_count(abi_stream(scope_), ptr(1), count, selected_dev, ws.data(),
+                                             ws.bytes() - 64); });
+      if (!st.ok()) return st;
+      ProfileScope span(ProfileCategory::kCopy, "device_to_host", "cuda", sizeof(Dim));
+      st = runtime_status(cudaMemcpyAsync(&selected, selected_dev, sizeof(Dim), cudaMemcpyDeviceToHost, scope_.stream()),
+                          "CUDA mask result count");
+      if (!st.ok()) return st;
+      st = runtime_status(cudaStreamSynchronize(scope_.stream()), "CUDA mask result count");
+      if (!st.ok()) return st;
+    }
+    Shape shape{selected};
+    shape.insert(shape.end(), plan.tail_shape.begin(), plan.tail_shape.end());
+    auto buffer = output(t.dtype, shape);
+    if (!buffer) return buffer.status();
+    if (selected && numel(t.shape)) {
+      auto st = launch("launch_mask_copy", "CUDA masked selection", [&] {
+        return tcx_sm100_masked_select(abi_stream(scope_), static_cast<std::int32_t>(dtype_size(t.dtype)), ptr(0),
+                                       ptr(1), count, plan.block_size, buffer.value()->data(), ws.data(),
+                                       ws.bytes() - 64); });
+      if (!st.ok()) return st;
+    }
+    return publish(out, t.dtype, shape, buffer.move_value());
+  }
+
+  // embedding (make_embedding_plan): gather with the index range checked on the device.
+  Status embedding(Tensor& out) {
+    const auto plan = make_embedding_plan(e_.inputs);
+    auto buffer = output(DType::kFloat32, plan.shape);
+    if (!buffer) return buffer.status();
+    if (plan.indices) {
+      Scratch flag(sizeof(int), scope_);
+      if (!flag.status().ok()) return flag.status();
+      auto st = launch("launch_embedding_gather", "CUDA embedding", [&] {
+        return tcx_sm100_embedding(abi_stream(scope_), static_cast<const std::int32_t*>(ptr(0)), plan.indices,
+                                   static_cast<const float*>(ptr(1)), plan.vocabulary, plan.width,
+                                   static_cast<float*>(buffer.value()->data()), static_cast<int*>(flag.data())); });
+      if (!st.ok()) return st;
+      auto bad = read_flag(flag);
+      if (!bad) return bad.status();
+      if (bad.value()) return invalid("embedding index out of range");
+    }
+    return publish(out, DType::kFloat32, plan.shape, buffer.move_value());
+  }
 };
 
 }  // namespace
@@ -779,13 +1030,14 @@ Status CudaBackend::execute(const BackendExecution& e) {
       if (t.buffer()->device() != device) return invalid("device mismatch between CUDA inputs");
     DeviceScope scope(device);
     if (!scope.ready()) return scope.status();
-    Tensor result;
+    Tensor result, second;
     Executor ex(e, in, scope);
-    if (auto st = ex.run(result); !st.ok()) return st;
+    if (auto st = ex.run(result, second); !st.ok()) return st;
     // every launch already waited inside its span; this only catches stray work (a copy)
     if (auto st = runtime_status(cudaStreamSynchronize(scope.stream()), "CUDA stream synchronize"); !st.ok())
       return st;
     e.outputs[0] = std::move(result);  // publish only on success
+    if (e.op.kind == OpKind::kTopK && e.outputs.size() > 1) e.outputs[1] = std::move(second);
     return Status::Ok();
   } catch (const std::invalid_argument& err) {
     return invalid(err.what());

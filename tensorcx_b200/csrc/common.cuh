@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "tcx_sm100.h"
 
@@ -112,6 +113,12 @@ __device__ __forceinline__ uint32_t key_min(uint32_t b, bool fp) {
 }
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Merges adjacent axes that stay affine for every operand and drops unit axes
+// (elementwise.cu): strides[k] is operand k's stride vector over `shape` (rank entries);
+// on return out_shape and strides hold the collapsed axes. Returns the collapsed rank.
+int collapse(const int64_t* shape, std::vector<std::vector<int64_t>>& strides, int rank,
+             std::vector<int64_t>& out_shape);
 
 // One-axis sum/max/mean over [outer, reduce, inner] (reduce.cu).
 int axis_reduce(cudaStream_t s, int op, int dtype, const void* input, void* output,

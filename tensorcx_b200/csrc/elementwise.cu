@@ -184,6 +184,8 @@ int ew_grid(int64_t n) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256 * 4), 8LL * sm_count() * 4)));
 }
 
+}  // namespace
+
 // Merges adjacent axes that stay affine for every operand; drops unit axes.
 // groups[k] are stride vectors (one per operand), all of `rank` entries.
 int collapse(const int64_t* shape, std::vector<std::vector<int64_t>>& strides, int rank,
@@ -209,7 +211,6 @@ int collapse(const int64_t* shape, std::vector<std::vector<int64_t>>& strides, i
   return static_cast<int>(out_shape.size());
 }
 
-}  // namespace
 }  // namespace tcx
 
 using namespace tcx;

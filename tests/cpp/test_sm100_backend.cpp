@@ -72,11 +72,14 @@ Tensor on_gpu(const cpu::CpuTensor& t, int device = 0) {
   return cuda::to_core_tensor(c.value());
 }
 
-Status run(Backend& backend, OpDesc op, std::vector<Tensor> inputs, Tensor& out) {
-  std::vector<Tensor> outputs(1);
+Status run(Backend& backend, OpDesc op, std::vector<Tensor> inputs, Tensor& out, Tensor* second = nullptr) {
+  std::vector<Tensor> outputs(second ? 2 : 1);
   BackendExecution e{BackendOpClass::kPrimitive, op, inputs, outputs, std::nullopt, std::nullopt, {}};
   auto st = backend.execute(e);
-  if (st.ok()) out = outputs[0];
+  if (st.ok()) {
+    out = outputs[0];
+    if (second) *second = outputs[1];
+  }
   return st;
 }
 
@@ -88,11 +91,11 @@ cpu::CpuTensor download(const Tensor& t) {
   return h.move_value();
 }
 
-// |gpu - cpu| <= atol + rtol |cpu| elementwise (NaN == NaN), or exact for int32.
+// |gpu - cpu| <= atol + rtol |cpu| elementwise (NaN == NaN), or exact for int32 and bool.
 bool close(const cpu::CpuTensor& a, const cpu::CpuTensor& b, double rtol, double atol) {
   if (a.shape() != b.shape() || a.dtype() != b.dtype()) return false;
-  if (a.dtype() == DType::kInt32) {
-    return std::memcmp(a.data(), b.data(), static_cast<std::size_t>(a.size()) * 4) == 0;
+  if (a.dtype() != DType::kFloat32) {
+    return std::memcmp(a.data(), b.data(), static_cast<std::size_t>(a.size()) * dtype_size(a.dtype())) == 0;
   }
   auto x = a.float_data(), y = b.float_data();
   for (std::size_t i = 0; i < x.size(); ++i) {
@@ -129,9 +132,10 @@ void compare(Backend& gpu, Backend& ref, const Case& c, int device = 0) {
     gin.push_back(on_gpu(t, device));
     cin.push_back(cpu::to_core_tensor(t));
   }
-  Tensor g, r;
-  auto gs = run(gpu, c.op, gin, g);
-  auto rs = run(ref, c.op, cin, r);
+  Tensor g, r, g2, r2;
+  const bool two = c.op.kind == OpKind::kTopK;
+  auto gs = run(gpu, c.op, gin, g, two ? &g2 : nullptr);
+  auto rs = run(ref, c.op, cin, r, two ? &r2 : nullptr);
   if (!rs.ok()) {
     check(!gs.ok() && gs.code() == rs.code(), c.name + ": CPU rejects (" + rs.message() + "), GPU must too");
     return;
@@ -143,7 +147,34 @@ void compare(Backend& gpu, Backend& ref, const Case& c, int device = 0) {
     check(sum_close(download(g), cpu::from_core_tensor(r), c.inputs[0], n), c.name + ": full sum vs CPU / exact");
   } else {
     check(close(download(g), cpu::from_core_tensor(r), c.rtol, c.atol), c.name + ": parity with CpuBackend");
+    if (two) check(close(download(g2), cpu::from_core_tensor(r2), 0, 0), c.name + ": indices parity with CpuBackend");
   }
+}
+
+// inputs with the float32 edge values of the elementwise ops: signed zeros, infinities,
+// NaN, subnormals, negatives and values near the int32 range limits
+cpu::CpuTensor specials(std::uint32_t seed) {
+  auto t = randn({4, 64}, seed, 3.0f);
+  std::vector<float> v(t.float_data().begin(), t.float_data().end());
+  const float edge[] = {0.0f, -0.0f, INFINITY, -INFINITY, NAN, 1e-40f, -1e-40f, 2147483520.0f, -2147483648.0f,
+                        2147483648.0f, 1e30f, -7.5f, 7.5f, 0.4999f, -0.5f, 1.0f};
+  for (std::size_t i = 0; i < sizeof(edge) / sizeof(edge[0]); ++i) v[i * 13 % v.size()] = edge[i];
+  return cpu::CpuTensor(t.shape(), std::move(v));
+}
+
+cpu::CpuTensor randk(Shape shape, std::uint32_t seed, int distinct) {  // many ties
+  std::mt19937 g(seed);
+  std::vector<float> v(static_cast<std::size_t>(numel(shape)));
+  for (auto& x : v) x = static_cast<float>(static_cast<int>(g() % distinct) - distinct / 2);
+  return cpu::CpuTensor(shape, std::move(v));
+}
+
+cpu::CpuTensor indices_i32(Shape shape, std::uint32_t seed, int vocabulary, bool out_of_range = false) {
+  std::mt19937 g(seed);
+  std::vector<std::int32_t> v(static_cast<std::size_t>(numel(shape)));
+  for (auto& x : v) x = static_cast<std::int32_t>(g() % vocabulary);
+  if (out_of_range && !v.empty()) v[v.size() / 2] = vocabulary;
+  return cpu::CpuTensor(shape, std::move(v));
 }
 
 OpDesc desc(OpKind k) { OpDesc op; op.kind = k; return op; }
@@ -665,6 +696,126 @@ int main() {
     cases.push_back({"attention softmax", sm, {randn({2, 5, 600}, 118, 4.0f), randn({600}, 119)}, 1e-5, 1e-7});
     OpDesc bad = att;
     cases.push_back({"attention feature mismatch", bad, {randn({3, 4}, 120), randn({5, 3}, 121), randn({5, 2}, 122)}, 0, 0});
+  }
+  // the rest of the reference CUDA backend's primitives (tensor_ops.cu)
+  {
+    for (auto k : {OpKind::kNegate, OpKind::kAddScalar, OpKind::kSubtractScalar, OpKind::kMultiplyScalar,
+                   OpKind::kDivideScalar}) {
+      for (bool left : {false, true}) {
+        OpDesc op = desc(k);
+        op.scalar_value = 0.3;
+        op.scalar_left = left;
+        cases.push_back({"scalar f32", op, {specials(131)}, 0, 0});
+        op.scalar_value = -7;
+        cases.push_back({"scalar i32", op, {randi({1000}, 132)}, 0, 0});
+        op.scalar_value = 2.5;
+        cases.push_back({"scalar i32 fractional rejected", op, {randi({10}, 133)}, 0, 0});
+      }
+    }
+    cases.push_back({"log", desc(OpKind::kLog), {specials(134)}, 1.2e-7, 0});
+    cases.push_back({"sqrt", desc(OpKind::kSqrt), {specials(135)}, 0, 0});
+    cases.push_back({"abs f32", desc(OpKind::kAbs), {specials(136)}, 0, 0});
+    {
+      std::vector<std::int32_t> w{INT32_MIN, -1, 0, 1, INT32_MAX, -5};
+      cases.push_back({"abs i32 wrap", desc(OpKind::kAbs), {cpu::CpuTensor(Shape{6}, w)}, 0, 0});
+    }
+    cases.push_back({"log i32 rejected", desc(OpKind::kLog), {randi({8}, 137)}, 0, 0});
+    for (auto [from, to] : std::vector<std::pair<DType, DType>>{
+             {DType::kInt32, DType::kFloat32}, {DType::kFloat32, DType::kBool}, {DType::kBool, DType::kFloat32},
+             {DType::kInt32, DType::kBool}, {DType::kBool, DType::kInt32}, {DType::kFloat32, DType::kFloat32},
+             {DType::kBool, DType::kBool}}) {
+      OpDesc op = desc(OpKind::kCast);
+      op.target_dtype = to;
+      const auto in = from == DType::kFloat32 ? specials(138) : from == DType::kInt32 ? randi({3, 70}, 139) : randb({3, 70}, 140);
+      cases.push_back({"cast", op, {in}, 0, 0});
+    }
+    {
+      OpDesc op = desc(OpKind::kCast);
+      op.target_dtype = DType::kInt32;
+      cases.push_back({"cast f32->i32", op, {randn({5, 77}, 141, 1e6f)}, 0, 0});
+      cases.push_back({"cast f32->i32 out of range rejected", op, {specials(142)}, 0, 0});
+    }
+    for (auto axes : std::vector<Shape>{{1, 0}, {0, 2, 1}, {2, 0, 1}, {1, 2, 0}}) {
+      OpDesc op = desc(OpKind::kTranspose);
+      op.axes = axes;
+      const Shape shape = axes.size() == 2 ? Shape{300, 77} : Shape{6, 130, 70};
+      cases.push_back({"transpose", op, {randn(shape, 143)}, 0, 0});
+      cases.push_back({"transpose bool", op, {randb(shape, 144)}, 0, 0});
+    }
+    {
+      OpDesc op = desc(OpKind::kSlice);
+      op.slice_starts = {1, 0, 5};
+      op.slice_steps = {2, 1, 3};
+      op.slice_shape = {3, 9, 20};
+      cases.push_back({"slice", op, {randn({7, 9, 70}, 145)}, 0, 0});
+      cases.push_back({"slice i32", op, {randi({7, 9, 70}, 146)}, 0, 0});
+    }
+    for (std::int64_t axis : {0, 1, -1}) {
+      OpDesc op = desc(OpKind::kConcat);
+      op.axis = axis;
+      const auto a = axis == 0 ? Shape{3, 8, 12} : axis == 1 ? Shape{4, 5, 12} : Shape{4, 8, 5};
+      const auto b = axis == 0 ? Shape{2, 8, 12} : axis == 1 ? Shape{4, 3, 12} : Shape{4, 8, 16};
+      cases.push_back({"concat", op, {randn(a, 147), randn(b, 148), randn(a, 149)}, 0, 0});
+      cases.push_back({"concat bool", op, {randb(a, 150), randb(b, 151)}, 0, 0});
+    }
+    {
+      OpDesc op = desc(OpKind::kConcat);
+      op.axis = 0;
+      cases.push_back({"concat dtype mismatch", op, {randn({2, 3}, 152), randi({2, 3}, 153)}, 0, 0});
+    }
+    for (auto k : {OpKind::kEqual, OpKind::kNotEqual, OpKind::kLess, OpKind::kLessEqual, OpKind::kGreater,
+                   OpKind::kGreaterEqual}) {
+      cases.push_back({"compare f32", desc(k), {randk({40, 33}, 154, 7), randk({33}, 155, 7)}, 0, 0});
+      cases.push_back({"compare specials", desc(k), {specials(156), specials(157)}, 0, 0});
+      cases.push_back({"compare i32", desc(k), {randi({5, 1, 9}, 158), randi({7, 9}, 159)}, 0, 0});
+      cases.push_back({"compare bool", desc(k), {randb({6, 10}, 160), randb({6, 10}, 161)}, 0, 0});
+    }
+    for (auto k : {OpKind::kLogicalAnd, OpKind::kLogicalOr, OpKind::kLogicalXor})
+      cases.push_back({"logical", desc(k), {randb({8, 1, 50}, 162), randb({3, 50}, 163)}, 0, 0});
+    cases.push_back({"logical not", desc(OpKind::kLogicalNot), {randb({300}, 164)}, 0, 0});
+    cases.push_back({"logical on f32 rejected", desc(OpKind::kLogicalAnd), {randn({3}, 165), randn({3}, 166)}, 0, 0});
+    cases.push_back({"where f32", desc(OpKind::kWhere), {randb({4, 1}, 167), specials(168), randn({64}, 170)}, 0, 0});
+    cases.push_back({"where i32", desc(OpKind::kWhere), {randb({5, 7}, 171), randi({5, 7}, 172), randi({1, 7}, 173)}, 0, 0});
+    cases.push_back({"where bool", desc(OpKind::kWhere), {randb({9}, 174), randb({9}, 175), randb({9}, 176)}, 0, 0});
+    for (auto k : {OpKind::kAny, OpKind::kAll}) {
+      cases.push_back({"bool reduce axis", axis_op(k, 1), {randb({7, 100, 3}, 177)}, 0, 0});
+      cases.push_back({"bool reduce axes", axes_op(k, {0, 2}), {randb({7, 100, 3}, 178)}, 0, 0});
+      cases.push_back({"bool reduce all axes", axes_op(k, {0, 1, 2}), {randb({7, 100, 3}, 179)}, 0, 0});
+      cases.push_back({"bool reduce f32 rejected", axis_op(k, 0), {randn({4}, 180)}, 0, 0});
+    }
+    cases.push_back({"masked select rows", desc(OpKind::kMaskedSelect), {randn({50, 7, 3}, 181), randb({50}, 182)}, 0, 0});
+    cases.push_back({"masked select elements", desc(OpKind::kMaskedSelect),
+                     {randi({300, 41}, 183), randb({300, 41}, 184)}, 0, 0});
+    cases.push_back({"masked select many tiles", desc(OpKind::kMaskedSelect),
+                     {randn({20000}, 185), randb({20000}, 186)}, 0, 0});
+    cases.push_back({"masked select bool", desc(OpKind::kMaskedSelect), {randb({64, 2}, 187), randb({64}, 188)}, 0, 0});
+    for (bool largest : {true, false}) {
+      for (bool sorted : {true, false}) {
+        OpDesc op = desc(OpKind::kTopK);
+        op.k = 5;
+        op.largest = largest;
+        op.sorted = sorted;
+        op.axis = -1;
+        cases.push_back({"topk ties", op, {randk({6, 40}, 189, 9)}, 0, 0});
+        cases.push_back({"topk specials", op, {specials(190)}, 0, 0});
+        op.axis = 0;
+        cases.push_back({"topk axis 0", op, {randn({33, 4, 6}, 191)}, 0, 0});
+        op.k = 33;
+        cases.push_back({"topk k = axis", op, {randi({33, 5}, 192)}, 0, 0});
+      }
+    }
+    {
+      OpDesc op = desc(OpKind::kTopK);
+      op.k = 0;
+      op.axis = 1;
+      cases.push_back({"topk k = 0", op, {randn({3, 9}, 193)}, 0, 0});
+      op.k = 10;
+      cases.push_back({"topk k too large rejected", op, {randn({3, 9}, 194)}, 0, 0});
+    }
+    cases.push_back({"embedding", desc(OpKind::kEmbedding), {indices_i32({4, 33}, 195, 500), randn({500, 64}, 196)}, 0, 0});
+    cases.push_back({"embedding odd width", desc(OpKind::kEmbedding), {indices_i32({70}, 197, 9), randn({9, 7}, 198)}, 0, 0});
+    cases.push_back({"embedding out of range rejected", desc(OpKind::kEmbedding),
+                     {indices_i32({10}, 199, 20, true), randn({20, 8}, 200)}, 0, 0});
   }
   for (const auto& c : cases) compare(gpu, ref, c);
 

@@ -5,8 +5,8 @@ with NumPy's default_rng on the host, python/tensorcx/tensor.py:485-497), so the
 oracle here is the published Philox4x32-10 block function restated in C
 (oracle/tcx_oracle.c), pinned below by two known answers, plus the generator's value
 mapping. On the GPU: uniform values and the stream layout are bit-exact against the
-oracle; normal values agree within a few float32 ulps (the device uses float32
-log / sqrt / sincospi, the oracle double precision); slices at offsets concatenate
+oracle; normal values agree within 4e-6 (the device uses the SFU log2 / rsqrt /
+sincos and a series near u1 = 1, the oracle double precision); slices at offsets concatenate
 to the whole stream; full-size moments hold.
 """
 import ctypes
@@ -83,7 +83,7 @@ def test_uniform_bit_exact(tcx, oracle, count, offset, shift, seed):
 def test_normal_matches_oracle(tcx, oracle, count, offset, shift):
     got = _device("normal", count, 99, offset, 0.5, 2.0, shift)
     want = oracle.random("normal", count, 99, offset, 0.5, 2.0)
-    # float32 log / sqrt / sincospi on the device against double on the host
+    # SFU log2 / rsqrt / sincos (with a series near u1 = 1) on the device against double
     np.testing.assert_allclose(got, want, rtol=4e-6, atol=4e-6)
 
 

@@ -41,6 +41,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -349,7 +350,120 @@ struct GemmArgs {
   // only lo = rna_tf32(x - trunc_tf32(x)) in the operands' own layouts, and B (hi and
   // lo) is read MN-major in 32-column chunks. raw (0): split planes, both K-major.
   int32_t raw;
+  // CTA-pair kernel: the output leaves through TMA tile stores (map_c over [batches][m][n]
+  // float32, 32 x 32 boxes, 128-byte swizzle); needs n % 4 == 0 and a 16-byte aligned c
+  int32_t tma_out;
+  // Stream-K tail of the CTA-pair kernel. Tiles [0, dp_tiles) go round-robin over the
+  // clusters (whole waves); the k-blocks of tiles [dp_tiles, total) form one sequence
+  // (tile-major) cut into equal contiguous ranges, one per cluster (sk_range). A tile
+  // whose k-blocks fall into several ranges is finished by the cluster holding its last
+  // k-block: the clusters before it store their raw partial accumulators in their slot
+  // of sk_partial (256 x 256 floats per cluster, in epilogue-warp order) and count their
+  // epilogue warps in sk_count[2 * cluster + rank] (zeroed before the launch); the
+  // finishing cluster waits for the counts, adds the partials in k order, then applies
+  // bias / activation and stores. dp_tiles == total: no stream-K.
+  int64_t dp_tiles;
+  float* sk_partial;
+  unsigned* sk_count;
 };
+
+// ------------------------------------------------------------ stream-K ranges
+constexpr int kMaxSkSources = 4;       // partial slots a finishing cluster may add (ring refills beyond 6 images)
+constexpr int kSkSlotFloats = 256 * 256;
+
+// Cluster c's range of the stream-K k-block sequence (U k-blocks over ncl clusters).
+__host__ __device__ __forceinline__ int64_t sk_bound(int64_t c, int64_t u, int64_t ncl) { return c * u / ncl; }
+
+// The clusters before `cid` holding the first k-blocks of stream-K tile `ta` (up to
+// where cid's range starts) are [first, cid), in k order; this returns `first`. Every
+// range is non-empty (u >= ncl), so they are consecutive.
+__host__ __device__ __forceinline__ int64_t sk_first_source(int64_t cid, int64_t ta, int64_t kb, int64_t u,
+                                                           int64_t ncl) {
+  int64_t c = cid - 1;
+  while (c > 0 && sk_bound(c, u, ncl) > ta * kb) --c;
+  return c;
+}
+
+// What one work unit of the CTA-pair kernel does with its accumulator.
+enum UnitKind { kWhole = 0, kPartial = 1, kFinish = 2 };
+
+struct PairUnit {
+  int64_t tile;
+  int kb0, kb1;  // k-blocks [kb0, kb1)
+  int kind;
+};
+
+// Unit i of cluster cid, in the order all three roles of the cluster walk them: its
+// round-robin whole tiles, then its stream-K range as (1) the first k-blocks of the tile
+// the range ends in (a partial: the rest of that tile lies in later ranges), (2) the
+// whole tiles inside the range, (3) the last k-blocks of the tile the range starts in
+// (finishing it with the partials of earlier ranges, stored long before). false: no unit i.
+__device__ __forceinline__ bool pair_unit(const GemmArgs& g, int64_t total, int64_t cid, int64_t ncl, int64_t i,
+                                          PairUnit& u) {
+  const int64_t dp = g.dp_tiles < total ? g.dp_tiles : total;
+  const int64_t n_dp = cid < dp ? (dp - cid + ncl - 1) / ncl : 0;
+  const int kb = g.num_kb;
+  if (i < n_dp) {
+    u.tile = cid + i * ncl;
+    u.kb0 = 0;
+    u.kb1 = kb;
+    u.kind = kWhole;
+    return true;
+  }
+  int64_t j = i - n_dp;
+  const int64_t sk = total - dp, un = sk * kb;
+  if (sk <= 0) return false;
+  const int64_t lo = sk_bound(cid, un, ncl), hi = sk_bound(cid + 1, un, ncl);
+  if (lo >= hi) return false;
+  const int64_t ta = lo / kb, tb = (hi - 1) / kb;
+  const int ka = static_cast<int>(lo - ta * kb), ke = static_cast<int>(hi - tb * kb);  // ke in [1, kb]
+  if (ta == tb) {
+    if (j > 0) return false;
+    u.tile = dp + ta;
+    u.kb0 = ka;
+    u.kb1 = ke;
+    u.kind = (ka == 0 && ke == kb) ? kWhole : (ke == kb ? kFinish : kPartial);
+    return true;
+  }
+  const bool head = ke < kb, tail = ka > 0;
+  const int64_t f0 = tail ? ta + 1 : ta, f1 = head ? tb - 1 : tb;  // whole tiles [f0, f1]
+  const int64_t nf = f1 >= f0 ? f1 - f0 + 1 : 0;
+  if (head) {
+    if (j == 0) {
+      u.tile = dp + tb;
+      u.kb0 = 0;
+      u.kb1 = ke;
+      u.kind = kPartial;
+      return true;
+    }
+    --j;
+  }
+  if (j < nf) {
+    u.tile = dp + f0 + j;
+    u.kb0 = 0;
+    u.kb1 = kb;
+    u.kind = kWhole;
+    return true;
+  }
+  if (tail && j == nf) {
+    u.tile = dp + ta;
+    u.kb0 = ka;
+    u.kb1 = kb;
+    u.kind = kFinish;
+    return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // k-block range of work item t
 __device__ __forceinline__ void split_range(int64_t t, const GemmArgs& g, int64_t& tile, int& split, int& kb0, int& kb1) {
@@ -443,6 +557,135 @@ __device__ __forceinline__ void drain_share(uint32_t tcol, float4* stage, int la
       store_block_staged(stage, v, lane, block + ci * 32, ld, rows_valid, left, vec);
     }
   }
+}
+
+// ------------------------------------------------ CTA-pair epilogue (bulk stores)
+// Each epilogue warp of the pair kernel owns a 4 KB staging slice (1024-byte aligned):
+// a 32 x 32 float block in the 128-byte-swizzled image (row = lane, 16-byte chunk j of
+// the row at position j ^ (row & 7)), which is both what a SWIZZLE_128B tensor map
+// stores from and conflict-free for the lanes' 16-byte writes. Output blocks leave the
+// slice through one TMA tile store (the map clips the tensor's edges); stream-K partial
+// blocks through one plain bulk store of the image itself. Before rewriting the slice,
+// lane 0 waits until the previous bulk store has read it.
+__device__ __forceinline__ void stage_image(float4* slice, const uint32_t (&r)[32], int lane) {
+  if (lane == 0) bulk_wait_read();
+  __syncwarp();
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj)
+    slice[lane * 8 + (jj ^ (lane & 7))] = make_float4(__uint_as_float(r[4 * jj]), __uint_as_float(r[4 * jj + 1]),
+                                                      __uint_as_float(r[4 * jj + 2]), __uint_as_float(r[4 * jj + 3]));
+  fence_async_shared();  // the writes become visible to the bulk copy
+  __syncwarp();
+}
+
+// What one pair-kernel epilogue warp does with its share (4 chunks of 32 x 32) of a
+// work unit's accumulator (PairUnit kinds), when the output leaves through TMA tile
+// stores (otherwise the kernel drains with drain_share and runs without stream-K):
+//   kWhole   bias / activation, then TMA tile stores through map_c;
+//   kPartial the raw accumulator to the stream-K partial slot `part` (4 KB images, chunk
+//            ci at part + 1024 ci), as bulk stores;
+//   kFinish  first adds the partial images of the nsrc clusters holding the tile's earlier
+//            k-blocks (src, src + kSkSlotFloats, ..., in k order), which `ring` (this
+//            warp's 24 KB of the idle pipeline stages: six 4 KB slots with one mbarrier
+//            each at ring_bars) receives by bulk loads, then as kWhole.
+struct PairOut {
+  const CUtensorMap* map_c;
+  int rows_valid, cols_left;  // of the share, from its (row 0, column 0)
+  int col0, row0, batch;      // the share's column, row and batch in map_c
+};
+
+template <int MODE, typename Release>
+__device__ __forceinline__ void drain_pair(uint32_t tcol, float4* slice, int lane, const PairOut& o, const float* bias,
+                                           int act, bool skip, Release release, float* part, const float* src,
+                                           int nsrc, float4* ring, uint32_t ring_bars, int* err) {
+  const bool plain = bias == nullptr && act == TCX_ACT_NONE;
+  const int items = MODE == kFinish ? 4 * nsrc : 0;  // (chunk, source) images, chunk-major
+  if constexpr (MODE == kFinish) {
+    if (lane == 0) {
+      fence_async_global();  // the sources' counts were acquired: their images are visible
+      for (int q = 0; q < items && q < 6; ++q) {
+        const uint32_t bar = ring_bars + 8 * q;
+        mbar_expect_tx(bar, 4096);
+        bulk_load(smem_u32(ring + 256 * q), src + (q % nsrc) * kSkSlotFloats + (q / nsrc) * 1024, 4096, bar);
+      }
+    }
+  }
+  uint32_t r0[32], r1[32];
+  TCX_LD32(r0, tcol);
+#pragma unroll
+  for (int ci = 0; ci < 4; ++ci) {
+    uint32_t (&cur)[32] = (ci & 1) ? r1 : r0;
+    uint32_t (&nxt)[32] = (ci & 1) ? r0 : r1;
+    TCX_WAIT_LD32(cur);
+    if (ci + 1 < 4) {
+      TCX_LD32(nxt, tcol + static_cast<uint32_t>((ci + 1) * 32));
+    } else {
+      release();
+    }
+    if constexpr (MODE == kPartial) {
+      stage_image(slice, cur, lane);
+      if (lane == 0) {
+        bulk_store(part + ci * 1024, smem_u32(slice), 4096);
+        bulk_commit();
+      }
+      continue;
+    }
+    if (MODE == kFinish && nsrc > 0) {
+      // (source 0 + source 1 + ...) + own accumulator
+      float t[32];
+      for (int p = 0; p < nsrc; ++p) {
+        const int q = ci * nsrc + p;
+        const uint32_t bar = ring_bars + 8 * (q % 6);
+        wait_or_give_up(bar, static_cast<uint32_t>((q / 6) & 1), err, 0x207);
+        const float4* img = ring + 256 * (q % 6);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float4 x = img[lane * 8 + (jj ^ (lane & 7))];
+          if (p == 0) {
+            t[4 * jj] = x.x; t[4 * jj + 1] = x.y; t[4 * jj + 2] = x.z; t[4 * jj + 3] = x.w;
+          } else {
+            t[4 * jj] = __fadd_rn(t[4 * jj], x.x);
+            t[4 * jj + 1] = __fadd_rn(t[4 * jj + 1], x.y);
+            t[4 * jj + 2] = __fadd_rn(t[4 * jj + 2], x.z);
+            t[4 * jj + 3] = __fadd_rn(t[4 * jj + 3], x.w);
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && q + 6 < items) {  // refill the slot just read
+          fence_async_shared();
+          const int q2 = q + 6;
+          mbar_expect_tx(bar, 4096);
+          bulk_load(smem_u32(ring + 256 * (q2 % 6)), src + (q2 % nsrc) * kSkSlotFloats + (q2 / nsrc) * 1024, 4096,
+                    bar);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cur[j] = __float_as_uint(__fadd_rn(t[j], __uint_as_float(cur[j])));
+    }
+    const int left = o.cols_left - ci * 32;
+    if (left > 0 && o.rows_valid > 0 && !skip) {
+      if (!plain) {
+        const int64_t c = o.col0 + ci * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          cur[j] = __float_as_uint(j < left ? epilogue_op(__uint_as_float(cur[j]), bias, c + j, act) : 0.0f);
+      }
+      stage_image(slice, cur, lane);
+      if (lane == 0) {
+        tma_store_3d(o.map_c, smem_u32(slice), o.col0 + ci * 32, o.row0, o.batch);
+        bulk_commit();
+      }
+    }
+  }
+}
+
+// The finishing drain of a stream-K tile (once per cluster and call), kept out of line so
+// that its partial loads do not raise the register pressure of the kernel's other paths.
+template <typename Release>
+__device__ __noinline__ void drain_finish(uint32_t tcol, float4* slice, int lane, const PairOut o, const float* bias,
+                                          int act, bool skip, Release release, const float* src, int nsrc,
+                                          float4* ring, uint32_t ring_bars, int* err) {
+  drain_pair<kFinish>(tcol, slice, lane, o, bias, act, skip, release, nullptr, src, nsrc, ring, ring_bars, err);
 }
 
 template <int BN>
@@ -654,7 +897,11 @@ constexpr int kStages2 = 3;
 constexpr int kHalf = 128;                                  // rows of A and of B per CTA
 constexpr int kTile2 = kHalf * kBK * 4;                     // 16 KB
 constexpr int kStage2Bytes = 4 * kTile2;                    // A hi/lo, B hi/lo: 64 KB
-constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 256 + kStoreStage;
+// stages, alignment slack, 1 KB of barriers (and the stream-K ring's), staging slices
+constexpr int kGemm2Smem = kStages2 * kStage2Bytes + 1024 + 1024 + kStoreStage;
+constexpr int kRingSlots = 6;  // stream-K partial images in flight per epilogue warp (24 KB of the stages)
+static_assert(kEpiWarps * kRingSlots * 4096 <= kStages2 * kStage2Bytes, "stream-K ring in the pipeline stages");
+static_assert(kGemm2Smem <= 232448, "shared memory per CTA");
 constexpr uint32_t kIdesc2 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
                              (static_cast<uint32_t>(256 >> 4) << 24);
 constexpr uint32_t kIdesc2MN = kIdesc2 | (1u << 16);  // B MN-major (raw mode)
@@ -662,9 +909,12 @@ constexpr uint32_t kIdesc2MN = kIdesc2 | (1u << 16);  // B MN-major (raw mode)
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
-                        const GemmArgs g) {
+                        const __grid_constant__ CUtensorMap map_c, const GemmArgs g) {
   // g.tiles_m counts 256-row tiles here; both CTAs of a pair return together
-  if (threadIdx.x == 0) prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
+  if (threadIdx.x == 0) {
+    prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
+    if (g.tma_out) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_c)) : "memory");
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2Bytes);
@@ -675,7 +925,10 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
   uint64_t* drain = bars + 2 * kStages2 + 4;      // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float4* stage = reinterpret_cast<float4*>(smem + kStages2 * kStage2Bytes + 256) + ((threadIdx.x >> 5) - 2) * 256;
+  uint64_t* ring_bars = bars + 2 * kStages2 + 6;  // [kEpiWarps][kRingSlots] (stream-K finishing)
+  // this epilogue warp's staging slice (4 KB, 1024-byte aligned) and stream-K ring
+  float4* stage = reinterpret_cast<float4*>(smem + kStages2 * kStage2Bytes + 1024) + ((threadIdx.x >> 5) - 2) * 256;
+  float4* ring = reinterpret_cast<float4*>(smem) + ((threadIdx.x >> 5) - 2) * kRingSlots * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -684,6 +937,7 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
     for (int s = 0; s < kStages2; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
     for (int s = 0; s < 2; ++s) { mbar_init(smem_u32(&acc_full[s]), 1); mbar_init(smem_u32(&acc_empty[s]), 2 * kEpiWarps); }
     mbar_init(smem_u32(drain), 1);
+    for (int i = 0; i < kEpiWarps * kRingSlots; ++i) mbar_init(smem_u32(&ring_bars[i]), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -709,14 +963,15 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
       // ------------------------------------------------------ TMA producer (both CTAs)
       int64_t kb_global = 0;
       bool ok = true;
-      for (int64_t t = cid; t < total_tiles && ok; t += ncl) {
+      PairUnit u;
+      for (int64_t i = 0; ok && pair_unit(g, total_tiles, cid, ncl, i, u); ++i) {
         int64_t batch; int mt, nt;
-        tile_coords(t, g, batch, mt, nt);
+        tile_coords(u.tile, g, batch, mt, nt);
         const int64_t pa = batch_off(batch, g.bm.shape, g.bm.lhs, g.bm.rank) / (g.lhs_mk > 0 ? g.lhs_mk : 1);
         const int64_t pb = batch_off(batch, g.bm.shape, g.bm.rhs, g.bm.rank) / (g.rhs_kn > 0 ? g.rhs_kn : 1);
         const int row_a = mt * 2 * kHalf + static_cast<int>(rank) * kHalf;
         const int row_b = nt * 2 * kHalf + static_cast<int>(rank) * kHalf;
-        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++kb_global) {
           const int s = static_cast<int>(kb_global % kStages2);
           const uint32_t phase = static_cast<uint32_t>((kb_global / kStages2) & 1);
           if (!wait_bounded(smem_u32(&empty[s]), phase ^ 1u, abort_flag, g.err, 0x201)) { ok = false; break; }
@@ -758,13 +1013,14 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
       // ------------------------------------------------------ MMA issuer (leader only)
       int64_t kb_global = 0, local = 0;
       bool ok = true;
-      for (int64_t t = cid; t < total_tiles && ok; t += ncl, ++local) {
+      PairUnit u;
+      for (int64_t i = 0; ok && pair_unit(g, total_tiles, cid, ncl, i, u); ++i, ++local) {
         const int acc = static_cast<int>(local & 1);
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!wait_bounded(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_flag, g.err, 0x202)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-        for (int kb = 0; kb < g.num_kb; ++kb, ++kb_global) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++kb_global) {
           const int s = static_cast<int>(kb_global % kStages2);
           const uint32_t phase = static_cast<uint32_t>((kb_global / kStages2) & 1);
           if (!wait_bounded(smem_u32(&full[s]), phase, abort_flag, g.err, 0x203)) { ok = false; break; }
@@ -779,7 +1035,7 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
           const uint32_t idesc = g.raw ? kIdesc2MN : kIdesc2;
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {  // 8 tf32 = 32 bytes = 2 in the >> 4 address field
-            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            const uint32_t first = (kb == u.kb0 && kk == 0) ? 0u : 1u;
             mma_tf32_pair(d_tmem, a_lo + 2 * kk, b_hi + b_step * kk, idesc, first);
             mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_lo + b_step * kk, idesc, 1u);
             mma_tf32_pair(d_tmem, a_hi + 2 * kk, b_hi + b_step * kk, idesc, 1u);
@@ -799,28 +1055,84 @@ gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
     // [0, 128) for warps 2-5 and [128, 256) for 6-9.
     const int q = warp & 3;
     const int part = warp >= 6 ? 1 : 0;
+    // this warp's share of a 256 x 256 partial slot: four 4 KB block images
+    const int64_t share = (static_cast<int64_t>(rank) * kEpiWarps + (warp - 2)) * 4096;
+    const uint32_t my_ring_bars = smem_u32(ring_bars + (warp - 2) * kRingSlots);
     int64_t local = 0;
-    for (int64_t t = cid; t < total_tiles; t += ncl, ++local) {
+    PairUnit u;
+    for (int64_t i = 0; pair_unit(g, total_tiles, cid, ncl, i, u); ++i, ++local) {
       const int acc = static_cast<int>(local & 1);
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
       if (!wait_bounded(smem_u32(&acc_full[acc]), acc_phase, abort_flag, g.err, 0x204)) break;
       tc_fence_after();
       int64_t batch; int mt, nt;
-      tile_coords(t, g, batch, mt, nt);
+      tile_coords(u.tile, g, batch, mt, nt);
       const int64_t row0 = static_cast<int64_t>(mt) * 2 * kHalf + static_cast<int64_t>(rank) * kHalf + q * 32;
       const int64_t col0 = static_cast<int64_t>(nt) * kBN + part * 128;
-      float* block = g.c + (batch * g.m + row0) * g.n + col0;
       const int rows_valid = static_cast<int>(g.m - row0 < 32 ? g.m - row0 : 32);
       const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(acc * kBN + part * 128);
-      drain_share(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, g.bias, g.act, g.vec_store != 0,
-                  *abort_flag != 0, [&] {
-                    // all TMEM reads of this accumulator are done: tell the leader's MMA warp
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&acc_empty[acc]), 0));
-                  });
+      auto release = [&] {
+        // all TMEM reads of this accumulator are done: tell the leader's MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&acc_empty[acc]), 0));
+      };
+      const bool skip = *abort_flag != 0;
+      PairOut o;
+      o.map_c = &map_c;
+      o.rows_valid = rows_valid;
+      o.cols_left = static_cast<int>(g.n - col0);
+      o.col0 = static_cast<int>(col0);
+      o.row0 = static_cast<int>(row0);
+      o.batch = static_cast<int>(batch);
+      if (u.kind == kPartial) {
+        // raw partial of the tile's first k-blocks into this cluster's slot; the count is
+        // raised once the stores have completed (even after an abort, so that the
+        // finishing cluster does not wait out its limit)
+        drain_pair<kPartial>(tcol, stage, lane, o, g.bias, g.act, skip, release,
+                             g.sk_partial + cid * kSkSlotFloats + share, nullptr, 0, ring, my_ring_bars, g.err);
+        if (lane == 0) {
+          bulk_wait();
+          fence_async_global();
+          __threadfence();
+          red_release_add(g.sk_count + 2 * cid + rank, 1u);
+        }
+        __syncwarp();
+      } else if (u.kind == kFinish) {
+        // the clusters holding the tile's first k-blocks stored their partials first
+        // thing in their stream-K ranges; wait for their counts (bounded), then add
+        const int64_t dp = g.dp_tiles < total_tiles ? g.dp_tiles : total_tiles;
+        const int64_t first = sk_first_source(cid, u.tile - dp, g.num_kb, (total_tiles - dp) * g.num_kb, ncl);
+        const int n = static_cast<int>(cid - first);  // 1 or 2: the host keeps it <= kMaxSkSources
+        bool waited = true;
+        if (lane == 0) {
+          for (int64_t c = first; c < cid && waited; ++c) {
+            const unsigned* cnt = g.sk_count + 2 * c + rank;
+            const uint64_t start = globaltimer();
+            while (ld_acquire_u32(cnt) < static_cast<unsigned>(kEpiWarps)) {
+              if (globaltimer() - start > kWaitLimitNs) {
+                record_device_error(g.err, 0x205);
+                waited = false;
+                break;
+              }
+            }
+          }
+        }
+        waited = __shfl_sync(0xffffffffu, waited ? 1 : 0, 0) != 0;
+        drain_finish(tcol, stage, lane, o, g.bias, g.act, skip || !waited, release,
+                     g.sk_partial + first * kSkSlotFloats + share, waited ? n : 0, ring, my_ring_bars, g.err);
+      } else if (g.tma_out) {
+        drain_pair<kWhole>(tcol, stage, lane, o, g.bias, g.act, skip, release, nullptr, nullptr, 0, ring,
+                           my_ring_bars, g.err);
+      } else {
+        float* block = g.c + (batch * g.m + row0) * g.n + col0;
+        drain_share(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, g.bias, g.act, g.vec_store != 0,
+                    skip, release);
+      }
     }
+    if (lane == 0) bulk_wait();  // this warp's bulk stores complete before the CTA exits
+    __syncwarp();
   }
 
   dependents_may_launch();
@@ -1037,11 +1349,33 @@ bool make_map(CUtensorMap* map, const float* base, int64_t planes, int64_t rows,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D map over the output [batches][m][n] float32 for the pair kernel's TMA tile stores:
+// 32 x 32 boxes in the 128-byte swizzle (the epilogue's staging image). n % 4 == 0 and c
+// 16-byte aligned.
+bool make_out_map(CUtensorMap* map, float* c, int64_t batches, int64_t m, int64_t n) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m),
+                              static_cast<cuuint64_t>(batches)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(n * 4), static_cast<cuuint64_t>(m * n * 4)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, c, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct Layout {
   int64_t kp;
   size_t off_flag, off_a, off_b, off_partial, total;
-  int splits;  // split-K factor of the single-SM kernel (1: none)
+  int splits;    // split-K factor of the single-SM kernel (1: none)
+  int sk_slots;  // stream-K partial slots of the CTA-pair kernel at off_partial (0: none)
 };
+
+// The workspace's first 1024 bytes: the inf / NaN flag (int at 0) and, from byte
+// kSkCountOff, the stream-K counters (two per cluster), all zeroed by one memset per call.
+constexpr size_t kSkCountOff = 64;
+constexpr int kMaxSkSlots = static_cast<int>((1024 - kSkCountOff) / 8);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -1079,8 +1413,38 @@ Layout tensor_layout(int64_t m, int64_t n, int64_t k, int64_t nba, int64_t nbb) 
   l.off_b = align_up(l.off_a + static_cast<size_t>(2 * nba * m * l.kp) * 4, 1024);
   l.off_partial = align_up(l.off_b + static_cast<size_t>(2 * nbb * n * l.kp) * 4, 1024);
   l.splits = (nba == 1 && nbb == 1) ? split_count(m, n, l.kp, 1, sm_count()) : 1;
-  l.total = l.off_partial + (l.splits > 1 ? align_up(static_cast<size_t>(l.splits * m * n) * 4, 1024) : 0);
+  // products that run on CTA pairs get one stream-K slot per cluster (judged on the
+  // operand batches; a product that reaches the pair kernel only through broadcast
+  // batches runs without stream-K)
+  l.sk_slots = (l.splits == 1 && use_pair(m, n, std::max(nba, nbb), sm_count()))
+                   ? std::min(sm_count() / 2, kMaxSkSlots) : 0;
+  l.total = l.off_partial + (l.splits > 1 ? align_up(static_cast<size_t>(l.splits * m * n) * 4, 1024)
+                                          : static_cast<size_t>(l.sk_slots) * kSkSlotFloats * 4);
   return l;
+}
+
+// Stream-K split of `tiles` pair tiles of kb k-blocks over `clusters` clusters: the number
+// of tiles left to whole round-robin waves (dp_tiles; == tiles: no stream-K). Used only
+// when the last wave would leave at least half of the clusters idle and the balance saves
+// each cluster at least 16 k-blocks (the finishing epilogue's partial read costs about
+// eight): the stream-K part is that partial wave plus one whole wave, so
+// every range covers one to one and a half tiles, a tile spans at most two ranges, and
+// the partial of a split tile is the first thing its cluster computes (the finishing
+// cluster never waits for it). Measured on one B200: with fewer tiles than clusters, or a
+// last wave more than half full, the finishing epilogue's extra partial read, and the
+// clusters' loss of lock-step k positions (the operand panels fall out of L2 when they
+// exceed it), cost as much as the balance gains.
+int64_t sk_dp_tiles(int64_t tiles, int64_t kb, int64_t clusters) {
+  const int64_t r = tiles % clusters;
+  if (tiles <= clusters || r == 0 || 2 * r > clusters || (clusters - r) * kb < 16 * clusters) return tiles;
+  const int64_t sk = r + clusters, un = sk * kb;
+  for (int64_t c = 0; c < clusters; ++c) {
+    const int64_t lo = sk_bound(c, un, clusters), hi = sk_bound(c + 1, un, clusters);
+    const int64_t ta = lo / kb;
+    if (lo % kb != 0 && hi >= (ta + 1) * kb && c - sk_first_source(c, ta, kb, un, clusters) > kMaxSkSources)
+      return tiles;
+  }
+  return tiles - sk;
 }
 
 bool use_tensor(int64_t m, int64_t n, int64_t k, int path) {
@@ -1195,7 +1559,7 @@ void split_lo_launch(cudaStream_t s, const float* a, float* wa, int64_t na4, con
 int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, int64_t m, int64_t n, int64_t k,
                 int64_t kp, int64_t batches, const BatchMap& bm, float* output, const float* bias, int act, int* flag,
                 const float* lhs, const float* rhs, bool rhs_kmajor, int sms, int splits = 1,
-                float* partial = nullptr, bool raw = false) {
+                float* partial = nullptr, bool raw = false, int sk_slots = 0) {
   const int64_t pair_tiles = batches * ceil_div(m, 2 * kHalf) * ceil_div(n, kBN);
   const bool pair = use_pair(m, n, batches, sms);
   const int bn = pair ? kBN : single_bn(m, n, batches, sms);
@@ -1215,6 +1579,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   }
 
   static bool attr_done[64] = {false};
+  static int pair_fit[64] = {0};  // co-resident pair clusters (stream-K waits need them all resident)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
@@ -1225,8 +1590,26 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
         cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemm2Smem) !=
             cudaSuccess)
       return launch_status("gemm smem attribute");
+    cudaLaunchConfig_t probe = {};
+    probe.gridDim = dim3(2 * (sms / 2));
+    probe.blockDim = dim3(kGemmThreads);
+    probe.dynamicSmemBytes = kGemm2Smem;
+    cudaLaunchAttribute pattr[1];
+    pattr[0].id = cudaLaunchAttributeClusterDimension;
+    pattr[0].val.clusterDim.x = 2;
+    pattr[0].val.clusterDim.y = 1;
+    pattr[0].val.clusterDim.z = 1;
+    probe.attrs = pattr;
+    probe.numAttrs = 1;
+    int fit = 0;
+    if (cudaOccupancyMaxActiveClusters(&fit, gemm_tf32x3_pair_kernel, &probe) != cudaSuccess) {
+      cudaGetLastError();
+      fit = 0;  // unknown: no stream-K
+    }
+    pair_fit[dev] = fit;
     attr_done[dev] = true;
   }
+  const int sk_clusters = (dev >= 0 && dev < 64) ? std::min(pair_fit[dev], sms / 2) : 0;
   GemmArgs g;
   g.c = output;
   g.bias = bias;
@@ -1246,10 +1629,29 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.partial = partial;
   g.raw = raw ? 1 : 0;
   if (g.splits > 1) g.vec_store = (n % 4 == 0 && reinterpret_cast<uintptr_t>(partial) % 16 == 0) ? 1 : 0;
+  g.dp_tiles = pair_tiles;
+  g.sk_partial = nullptr;
+  g.sk_count = nullptr;
+  g.tma_out = 0;
+  alignas(64) CUtensorMap map_c;
+  memset(&map_c, 0, sizeof(map_c));
   if (pair) {
+    if (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0 && make_out_map(&map_c, output, batches, m, n))
+      g.tma_out = 1;
     g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
     g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
-    const int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
+    int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
+    // stream-K over the last waves' tiles: partial slots at `partial`, counters beside
+    // the flag (both in the workspace, the counters zeroed with the flag)
+    if (g.tma_out && partial && sk_clusters >= 1 && sk_slots >= sk_clusters) {
+      const int64_t dp = sk_dp_tiles(pair_tiles, g.num_kb, sk_clusters);
+      if (dp < pair_tiles) {
+        g.dp_tiles = dp;
+        g.sk_partial = partial;
+        g.sk_count = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(flag) + kSkCountOff);
+        clusters = sk_clusters;
+      }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(kGemmThreads);
@@ -1265,7 +1667,7 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     TimedLaunch timer("gemm_tf32x3", s);
-    cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, map_a_hi, map_b_hi, g);
+    cudaLaunchKernelEx(&cfg, gemm_tf32x3_pair_kernel, map_a, map_b, map_a_hi, map_b_hi, map_c, g);
   } else {
     const int64_t work = batches * g.tiles_m * g.tiles_n * g.splits;
     const int grid = static_cast<int>(std::min<int64_t>(work, sms));
@@ -1360,8 +1762,13 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return invalid("matmul extent too large for the tensor path");
   const int64_t nba = distinct_batches(bm, true, m * k), nbb = distinct_batches(bm, false, k * n);
   Layout lay = tensor_layout(m, n, k, nba, nbb);
-  if (lay.splits > 1 && (batches != 1 || (workspace && workspace_bytes < lay.total && workspace_bytes >= lay.off_partial))) {
-    lay.splits = 1;  // no split-K partial area (several output batches, or a workspace sized without it)
+  if (lay.splits > 1 && batches != 1) {
+    lay.splits = 1;  // no split-K with several output batches
+    lay.total = lay.off_partial;
+  }
+  if (workspace && workspace_bytes < lay.total && workspace_bytes >= lay.off_partial) {
+    lay.splits = 1;  // a workspace sized without the split-K / stream-K area: neither
+    lay.sk_slots = 0;
     lay.total = lay.off_partial;
   }
   if (!workspace || workspace_bytes < lay.total) return invalid("matmul workspace is missing or too small");
@@ -1372,7 +1779,9 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
   float* wb = reinterpret_cast<float*>(ws + lay.off_b);
   if (2 * std::max(nba, nbb) > INT32_MAX) return invalid("too many operand batches for the tensor path");
 
-  if (cudaMemsetAsync(flag, 0, sizeof(int), s) != cudaSuccess) return launch_status("matmul flag reset");
+  // the flag and, with stream-K slots, the stream-K counters beside it
+  const size_t reset = lay.sk_slots > 0 ? kSkCountOff + 8 * static_cast<size_t>(lay.sk_slots) : sizeof(int);
+  if (cudaMemsetAsync(flag, 0, reset, s) != cudaSuccess) return launch_status("matmul flag reset");
   // Raw mode (row-major B, K and N multiples of 4, 16-byte aligned operands): the GEMM
   // reads A and B themselves as the hi terms and the pre-pass writes only their lo
   // terms, in the operands' own layouts (8 B per element instead of 12, no transpose).
@@ -1385,9 +1794,9 @@ static int run_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, f
     split_both(s, lhs, wa, nba, m, rhs, wb, nbb, n, k, lay.kp, flag, rhs_kmajor, sms);
   }
   if (int st = launch_status("matmul split pre-pass")) return st;
-  float* partial = lay.splits > 1 ? reinterpret_cast<float*>(ws + lay.off_partial) : nullptr;
+  float* partial = (lay.splits > 1 || lay.sk_slots > 0) ? reinterpret_cast<float*>(ws + lay.off_partial) : nullptr;
   return gemm_planes(s, wa, wb, nba, nbb, m, n, k, lay.kp, batches, bm, output, bias, act, flag, lhs, rhs,
-                     rhs_kmajor, sms, lay.splits, partial, raw);
+                     rhs_kmajor, sms, lay.splits, partial, raw, lay.sk_slots);
 }
 
 int tcx_sm100_matmul(tcx_stream_t stream, const float* lhs, const float* rhs, float* output, int64_t m,
@@ -1419,7 +1828,8 @@ struct HostPlan {
   int64_t chunk_m, chunks, kp;
   bool tensor;  // chunks run the tcgen05 path with B split once; else run_matmul per chunk
   size_t off_b, off_bp, off_bflag, off_a[kHostSlots], off_ap[kHostSlots], off_c[kHostSlots],
-      off_flag[kHostSlots], off_ws, ws_bytes, total;
+      off_flag[kHostSlots], off_ws, off_sk, ws_bytes, total;
+  int sk_slots;  // stream-K slots shared by the chunks' GEMMs (they run one after another)
 };
 
 // Row chunks of A (and C). The PCIe uploads are the floor of the whole call; chunks
@@ -1455,7 +1865,10 @@ HostPlan host_plan(int64_t m, int64_t n, int64_t k) {
   }
   p.off_ws = off;
   p.ws_bytes = p.tensor ? 0 : tcx_sm100_matmul_workspace_bytes(p.chunk_m, n, k, 1, 1, TCX_MATMUL_AUTO);
-  p.total = align_up(off + p.ws_bytes, 1024);
+  off = align_up(off + p.ws_bytes, 1024);
+  p.off_sk = off;
+  p.sk_slots = (p.tensor && use_pair(p.chunk_m, n, 1, sm_count())) ? std::min(sm_count() / 2, kMaxSkSlots) : 0;
+  p.total = align_up(off + static_cast<size_t>(p.sk_slots) * kSkSlotFloats * 4, 1024);
   return p;
 }
 
@@ -1553,8 +1966,11 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
   // raw mode as the device-buffer path takes it (the staging buffers are 1024-byte
   // aligned), so both paths run the same kernels and give identical results
   const bool raw = p.tensor && k % 4 == 0 && n % 4 == 0;
+  // a chunk's flag area starts as a copy of B's: B's inf / NaN flag, then zeros (the
+  // stream-K counters)
+  const size_t flag_bytes = p.sk_slots > 0 ? kSkCountOff + 8 * static_cast<size_t>(p.sk_slots) : sizeof(int);
   if (p.tensor) {  // B's split pre-pass once, shared by every chunk
-    if (cudaError_t e = cudaMemsetAsync(b_flag, 0, sizeof(int), comp); e != cudaSuccess)
+    if (cudaError_t e = cudaMemsetAsync(b_flag, 0, flag_bytes, comp); e != cudaSuccess)
       return fail(e, "matmul_host flag reset");
     if (raw) split_lo_launch(comp, nullptr, nullptr, 0, b_dev, b_planes, k * n / 4, b_flag, sms);
     else split_b(comp, b_dev, b_planes, 1, n, k, p.kp, b_flag, false, sms);
@@ -1582,13 +1998,14 @@ int tcx_sm100_matmul_host(const float* a_host, const float* b_host, float* c_hos
       // the chunk's flag starts as B's (inf / NaN anywhere in B), then A's split adds to it
       float* a_planes = reinterpret_cast<float*>(ws + p.off_ap[slot]);
       int* flag = reinterpret_cast<int*>(ws + p.off_flag[slot]);
-      if (cudaError_t e = cudaMemcpyAsync(flag, b_flag, sizeof(int), cudaMemcpyDeviceToDevice, comp); e != cudaSuccess)
+      if (cudaError_t e = cudaMemcpyAsync(flag, b_flag, flag_bytes, cudaMemcpyDeviceToDevice, comp); e != cudaSuccess)
         return fail(e, "matmul_host flag copy");
       if (raw) split_lo_launch(comp, a_dev, a_planes, rows * k / 4, nullptr, nullptr, 0, flag, sms);
       else split_a(comp, a_dev, a_planes, 1, rows, k, p.kp, flag, sms);
       if (int rc = launch_status("matmul_host split pre-pass")) return rc;
+      float* sk_area = p.sk_slots > 0 ? reinterpret_cast<float*>(ws + p.off_sk) : nullptr;
       if (int rc = gemm_planes(comp, a_planes, b_planes, 1, 1, rows, n, k, p.kp, 1, one, c_dev, nullptr,
-                               TCX_ACT_NONE, flag, a_dev, b_dev, false, sms, 1, nullptr, raw))
+                               TCX_ACT_NONE, flag, a_dev, b_dev, false, sms, 1, sk_area, raw, p.sk_slots))
         return rc;
     } else {
       const int rc = run_matmul(reinterpret_cast<tcx_stream_t>(comp), a_dev, b_dev, c_dev, rows, n, k, 1, nullptr,

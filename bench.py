@@ -303,20 +303,25 @@ class Timer:
     def __init__(self, torch, dist, world):
         self.torch, self.dist, self.world = torch, dist, world
 
-    # idle time before each timed region: a workload measured right after a power-capped
-    # one (the GEMMs draw the 1 kW limit) otherwise starts at the lowered SM clock the
-    # power limiter is still holding (measured: the fused attention kernel 0.22 -> 0.30 ms
-    # right after the bmm, back to 0.22 ms after 3 s idle)
-    rest_s = 1.0
+    # idle time before each workload's warm-up: a workload measured right after a
+    # power-capped one (the GEMMs draw the 1 kW limit) otherwise starts at the lowered SM
+    # clock the power limiter is still holding (measured: the fused attention kernel 0.22
+    # -> 0.30 ms right after the bmm, back to 0.22 ms after 3 s idle). The warm-up comes
+    # after the pause: a timed region that starts straight out of an idle pause is slow
+    # too (measured: softmax [16384, 4096] 84 -> 96 us, 2048^3 matmul 83 -> 88-98 us;
+    # three warm-up calls restore 84 / 83 us).
+    rest_s = 0.5
 
-    def run(self, step, steps, warmup, sampler=None):
+    def run(self, step, steps, warmup, sampler=None, before_timing=None):
         torch = self.torch
-        for _ in range(warmup):
-            step()
         torch.cuda.synchronize()
         time.sleep(self.rest_s)
+        for _ in range(max(warmup, 3)):
+            step()
         self.barrier()
         torch.cuda.synchronize()
+        if before_timing:
+            before_timing()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.time()
         start.record()
@@ -331,16 +336,16 @@ class Timer:
         ms = start.elapsed_time(end)
         return self.max_over_ranks(ms)
 
-    def run_hbm(self, step, steps, warmup, sampler, working_bytes):
+    def run_hbm(self, step, steps, warmup, sampler, working_bytes, before_timing=None):
         """Timing of an HBM-bound step: back to back (`run`) when the step's data is at
         least twice L2, so every step streams from HBM and pays the write-back of the
         previous step's output (the steady state); otherwise `run_flushed`."""
         l2 = self.torch.cuda.get_device_properties(self.torch.cuda.current_device()).L2_cache_size
         if working_bytes >= 2 * l2:
-            return self.run(step, steps, warmup, sampler)
-        return self.run_flushed(step, steps, warmup, sampler)
+            return self.run(step, steps, warmup, sampler, before_timing)
+        return self.run_flushed(step, steps, warmup, sampler, before_timing)
 
-    def run_flushed(self, step, steps, warmup, sampler=None):
+    def run_flushed(self, step, steps, warmup, sampler=None, before_timing=None):
         """Device time of `steps` calls of `step` with L2 emptied before each: a 256 MiB
         memset then a read of a second 256 MiB buffer (L2 ends up holding clean lines of
         the flush, so the step neither hits its own data nor pays the flush's
@@ -350,12 +355,14 @@ class Timer:
         if getattr(self, "flush", None) is None:
             self.flush = (torch.empty(256 << 20, dtype=torch.uint8, device="cuda"),
                           torch.ones(64 << 20, dtype=torch.float32, device="cuda"))
-        for _ in range(warmup):
-            step()
         torch.cuda.synchronize()
         time.sleep(self.rest_s)
+        for _ in range(max(warmup, 3)):
+            step()
         self.barrier()
         torch.cuda.synchronize()
+        if before_timing:
+            before_timing()
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         t0 = time.time()
         for start, end in events:
@@ -394,6 +401,13 @@ def read_timer(lib):
     for i in range(n.value):
         out[raw[i].decode()] = (int(launches[i]), float(total[i]))
     return out
+
+
+def hooks_on(lib):
+    """Clears the per-kernel device timing records and turns the hooks on (called right
+    before a timed region, after its warm-up)."""
+    read_timer(lib)
+    lib.tcx_sm100_timer_enable(1)
 
 
 def peaks():
@@ -457,12 +471,11 @@ def gpu_arm(args):
                                         ctypes.c_void_p(c.data_ptr()), size, size, size, 1, one, one, one, 0,
                                         None, 0, 0, ws, ws_bytes))
 
-    for _ in range(args.warmup):
-        step()
+    step()
     torch.cuda.synchronize()
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    ms = timer.run(step, args.steps, 0, sampler)
+
+    # the per-kernel device timing covers the timed steps only
+    ms = timer.run(step, args.steps, args.warmup, sampler, before_timing=lambda: hooks_on(lib))
     lib.tcx_sm100_timer_enable(0)
     kernels = read_timer(lib)
     ms_per_step = ms / args.steps
@@ -624,9 +637,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         of back-to-back kernels), then the per-kernel times from a shorter pass with the
         hooks on."""
         ms_ = timer.run_hbm(st, steps, 2, sampler, working_bytes) / steps
-        read_timer(lib)
-        lib.tcx_sm100_timer_enable(1)
-        timer.run_hbm(st, max(3, steps // 2), 1, None, working_bytes)
+        timer.run_hbm(st, max(3, steps // 2), 1, None, working_bytes, before_timing=lambda: hooks_on(lib))
         lib.tcx_sm100_timer_enable(0)
         return ms_, read_timer(lib)
 
@@ -830,9 +841,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         st()
         reps = max(5, steps) if size >= 2048 else 50
         ms = timer.run(st, reps, 3, sampler) / reps  # timing hooks off: no event records per launch
-        read_timer(lib)
-        lib.tcx_sm100_timer_enable(1)
-        timer.run(st, max(3, reps // 2), 1)
+        timer.run(st, max(3, reps // 2), 1, before_timing=lambda: hooks_on(lib))
         lib.tcx_sm100_timer_enable(0)
         kern = read_timer(lib)
         fl = 2.0 * size ** 3
@@ -867,9 +876,8 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
     def st():
         return ops.matmul(a, b, bias=bias, act="silu")
     st()
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    ms = timer.run(st, max(3, steps // 2), 1, sampler) / max(3, steps // 2)
+    ms = timer.run(st, max(3, steps // 2), 1, sampler) / max(3, steps // 2)  # timing hooks off
+    timer.run(st, max(3, steps // 2), 1, before_timing=lambda: hooks_on(lib))
     lib.tcx_sm100_timer_enable(0)
     kern = read_timer(lib)
     fl = 2.0 * nb * 2048 ** 3
@@ -903,9 +911,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
     st()
     n_att = max(3, steps // 2)
     ms = timer.run(st, n_att, 1, sampler) / n_att  # step time with the timing hooks off
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    timer.run(st, n_att, 1)
+    timer.run(st, n_att, 1, before_timing=lambda: hooks_on(lib))
     lib.tcx_sm100_timer_enable(0)
     kern = read_timer(lib)
     fl = 4.0 * heads * 2048 * 2048 * 128
@@ -935,9 +941,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         return ops.attention(q, k, v, amask)
     st_masked()
     ms_m = timer.run(st_masked, n_att, 1, sampler) / n_att
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    timer.run(st_masked, max(3, n_att // 2), 1)
+    timer.run(st_masked, max(3, n_att // 2), 1, before_timing=lambda: hooks_on(lib))
     lib.tcx_sm100_timer_enable(0)
     kern_m = read_timer(lib)
     fl_m = 4.0 * heads * 2048 * 2048 * 128
@@ -973,9 +977,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         return ops.softmax(ops.matmul(h, w2, bias=b2), axis=-1)
     mlp()
     eager_ms = timer.run(mlp, 50, 1, sampler) / 50  # timing hooks off
-    read_timer(lib)
-    lib.tcx_sm100_timer_enable(1)
-    timer.run(mlp, 20, 1)
+    timer.run(mlp, 20, 1, before_timing=lambda: hooks_on(lib))
     lib.tcx_sm100_timer_enable(0)
     kern = read_timer(lib)
     # the same forward replayed as one CUDA graph (no host work per op)

@@ -263,9 +263,13 @@ int tcx_sm100_fill(tcx_stream_t stream, void* output, int64_t count, uint32_t bi
 /* Scratch for tcx_sm100_matmul: the tf32 hi/lo split of both operands (K-major), or,
  * when k and n are multiples of 4 and both operands are 16-byte aligned, only their lo
  * terms in the operands' own layouts (the tensor cores then read the operands
- * themselves as the hi terms); the size covers either. lhs_batches / rhs_batches are
- * the operands' own batch counts (numel / (m*k), numel / (k*n)). Zero when the FFMA
- * kernel will be used. */
+ * themselves as the hi terms); the size covers either. It also covers the partial
+ * accumulators of small products split over k (split-K) or, for products large enough
+ * for the two-SM (CTA-pair) tiles, of tiles split between two SM pairs (stream-K: 256
+ * KiB per SM pair). A workspace sized before those areas existed is still accepted (no
+ * split is made then). lhs_batches / rhs_batches are the operands' own batch counts
+ * (numel / (m*k), numel / (k*n)). Zero when the FFMA kernel will be used. Calls that
+ * share one workspace must not overlap on the GPU. */
 size_t tcx_sm100_matmul_workspace_bytes(int64_t m, int64_t n, int64_t k,
                                         int64_t lhs_batches, int64_t rhs_batches, int path);
 

@@ -320,7 +320,7 @@ struct SingleTile {
   static constexpr int kStages = BN == 256 ? 2 : 3;
   static constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;
   static constexpr int kTmemCols = 2 * BN;  // two accumulators
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256 + kStoreStage;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 1024 + kStoreStage;  // slack, barriers, slices
   // instruction descriptor: kind::tf32, D f32, A/B tf32, both K-major, M = 128, N = BN;
   // the MN variant sets bit 16 (B MN-major, the raw mode)
   static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
@@ -594,7 +594,7 @@ struct PairOut {
   int col0, row0, batch;      // the share's column, row and batch in map_c
 };
 
-template <int MODE, typename Release>
+template <int MODE, int NCH = 4, typename Release>
 __device__ __forceinline__ void drain_pair(uint32_t tcol, float4* slice, int lane, const PairOut& o, const float* bias,
                                            int act, bool skip, Release release, float* part, const float* src,
                                            int nsrc, float4* ring, uint32_t ring_bars, int* err) {
@@ -613,11 +613,11 @@ __device__ __forceinline__ void drain_pair(uint32_t tcol, float4* slice, int lan
   uint32_t r0[32], r1[32];
   TCX_LD32(r0, tcol);
 #pragma unroll
-  for (int ci = 0; ci < 4; ++ci) {
+  for (int ci = 0; ci < NCH; ++ci) {
     uint32_t (&cur)[32] = (ci & 1) ? r1 : r0;
     uint32_t (&nxt)[32] = (ci & 1) ? r0 : r1;
     TCX_WAIT_LD32(cur);
-    if (ci + 1 < 4) {
+    if (ci + 1 < NCH) {
       TCX_LD32(nxt, tcol + static_cast<uint32_t>((ci + 1) * 32));
     } else {
       release();
@@ -692,10 +692,13 @@ template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_b_hi,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap map_c, const GemmArgs g) {
   using T = SingleTile<BN>;
   constexpr int kStages = T::kStages, kStageBytes = T::kStageBytes, kTileB = T::kTileB, kTmemCols = T::kTmemCols;
-  if (threadIdx.x == 0) prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
+  if (threadIdx.x == 0) {
+    prefetch_maps(map_a, map_b, map_a_hi, map_b_hi);
+    if (g.tma_out) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_c)) : "memory");
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -706,7 +709,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   uint64_t* drain = bars + 2 * kStages + 4;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float4* stage = reinterpret_cast<float4*>(smem + kStages * kStageBytes + 256) + ((threadIdx.x >> 5) - 2) * 256;
+  float4* stage = reinterpret_cast<float4*>(smem + kStages * kStageBytes + 1024) + ((threadIdx.x >> 5) - 2) * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -852,14 +855,31 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       const int rows_valid = static_cast<int>(g.m - row0 < 32 ? g.m - row0 : 32);
       const uint32_t tcol = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(acc * BN + part * (BN / 2));
-      drain_share<T::kChunks>(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, raw ? nullptr : g.bias,
-                  raw ? TCX_ACT_NONE : g.act, g.vec_store != 0, *abort_flag != 0, [&] {
-                    // all TMEM reads of this accumulator are done: hand it back to the MMA warp
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
-                  });
+      auto release = [&] {
+        // all TMEM reads of this accumulator are done: hand it back to the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+      };
+      if (g.tma_out) {
+        // TMA tile stores: map_c covers the output [batches][m][n], or with split-K the
+        // partial slices [splits][m][n]
+        PairOut o;
+        o.map_c = &map_c;
+        o.rows_valid = rows_valid;
+        o.cols_left = static_cast<int>(g.n - col0);
+        o.col0 = static_cast<int>(col0);
+        o.row0 = static_cast<int>(row0);
+        o.batch = static_cast<int>(raw ? split : batch);
+        drain_pair<kWhole, T::kChunks>(tcol, stage, lane, o, raw ? nullptr : g.bias, raw ? TCX_ACT_NONE : g.act,
+                                       *abort_flag != 0, release, nullptr, nullptr, 0, nullptr, 0, g.err);
+      } else {
+        drain_share<T::kChunks>(tcol, stage, lane, block, g.n, rows_valid, g.n - col0, col0, raw ? nullptr : g.bias,
+                                raw ? TCX_ACT_NONE : g.act, g.vec_store != 0, *abort_flag != 0, release);
+      }
     }
+    if (lane == 0) bulk_wait();  // this warp's bulk stores complete before the CTA exits
+    __syncwarp();
   }
 
   dependents_may_launch();  // the split-K reduce / fallback behind may start its set-up
@@ -1635,9 +1655,14 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
   g.tma_out = 0;
   alignas(64) CUtensorMap map_c;
   memset(&map_c, 0, sizeof(map_c));
-  if (pair) {
-    if (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0 && make_out_map(&map_c, output, batches, m, n))
+  if (g.splits > 1) {  // single-SM split-K: the stores go to the partial slices [splits][m][n]
+    if (n % 4 == 0 && reinterpret_cast<uintptr_t>(partial) % 16 == 0 && make_out_map(&map_c, partial, g.splits, m, n))
       g.tma_out = 1;
+  } else if (n % 4 == 0 && reinterpret_cast<uintptr_t>(output) % 16 == 0 &&
+             make_out_map(&map_c, output, batches, m, n)) {
+    g.tma_out = 1;
+  }
+  if (pair) {
     g.tiles_n = static_cast<int32_t>(ceil_div(n, kBN));
     g.tiles_m = static_cast<int32_t>(ceil_div(m, 2 * kHalf));
     int clusters = static_cast<int>(std::min<int64_t>(pair_tiles, sms / 2));
@@ -1675,10 +1700,10 @@ int gemm_planes(cudaStream_t s, float* wa, float* wb, int64_t nba, int64_t nbb, 
     // launched behind the pre-pass so that its set-up overlaps the pre-pass's tail
     if (bn == 128)
       launch_after(gemm_tf32x3_kernel<128>, grid, kGemmThreads, s, SingleTile<128>::kSmem, map_a, map_b, map_a_hi,
-                   map_b_hi, g);
+                   map_b_hi, map_c, g);
     else
       launch_after(gemm_tf32x3_kernel<256>, grid, kGemmThreads, s, SingleTile<256>::kSmem, map_a, map_b, map_a_hi,
-                   map_b_hi, g);
+                   map_b_hi, map_c, g);
   }
   if (int st = launch_status("tcgen05 matmul")) return st;
   if (g.splits > 1) {

@@ -419,7 +419,21 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "of fallback"
 
 
+# The bench's one JSON line goes to the process's original stdout; everything else that
+# writes to file descriptor 1 during the run (NCCL's version banner at communicator
+# creation, library messages) is sent to stderr, so stdout holds exactly that line.
+JSON_FD = 1
+
+
+def quiet_stdout():
+    global JSON_FD
+    sys.stdout.flush()
+    JSON_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
 def gpu_arm(args):
+    quiet_stdout()
     import torch
     import torch.distributed as dist
     from tensorcx_b200 import _abi, ops
@@ -603,7 +617,7 @@ def gpu_arm(args):
             "strong_scaling": {k: v["strong_scaling"]["efficiency_vs_n1"] for k, v in workloads.items()
                                if isinstance(v, dict) and "strong_scaling" in v} or None,
         }
-        print(json.dumps(line))
+        os.write(JSON_FD, (json.dumps(line) + "\n").encode())
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

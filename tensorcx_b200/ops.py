@@ -46,7 +46,14 @@ def _check_tensor(t: torch.Tensor, name: str = "input") -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream() -> ctypes.c_void_p:
+    """torch's current stream on the current device (the raw handle, without building a
+    torch.cuda.Stream object: ~0.2 us instead of ~3 us per op)."""
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(torch.cuda.current_device()))
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
@@ -64,6 +71,23 @@ def _workspace(nbytes: int, device, align: int = 1024):
 
 
 # -------------------------------------------------------------------- matmul
+_matmul_plans: dict = {}
+
+
+def _matmul_plan(lhs_shape, rhs_shape):
+    """make_matmul_plan for a shape pair with its ctypes metadata arrays, cached (a
+    failing plan raises each time and is not cached)."""
+    key = (tuple(lhs_shape), tuple(rhs_shape))
+    hit = _matmul_plans.get(key)
+    if hit is None:
+        p = plan.matmul(lhs_shape, rhs_shape)
+        hit = (p, i64_array(p.batch_shape), i64_array(p.lhs_batch_strides), i64_array(p.rhs_batch_strides))
+        if len(_matmul_plans) > 4096:
+            _matmul_plans.clear()
+        _matmul_plans[key] = hit
+    return hit
+
+
 def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = None,
            act: str = "none", path: str = "auto", out: torch.Tensor | None = None) -> torch.Tensor:
     """NumPy-semantics float32 matmul; optional fused epilogue act(C + bias[n])."""
@@ -72,7 +96,7 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
         raise ValueError("device mismatch for matmul")
     if lhs.dtype != torch.float32 or rhs.dtype != torch.float32:
         raise ValueError("matmul only supports float32 tensors")
-    p = plan.matmul(lhs.shape, rhs.shape)
+    p, shape_a, lstr_a, rstr_a = _matmul_plan(lhs.shape, rhs.shape)
     if out is None:
         out = torch.empty(p.output_shape, dtype=torch.float32, device=lhs.device)
     if bias is not None:
@@ -86,8 +110,7 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
     batches = plan.numel(p.batch_shape) if out.numel() else 0
     check(lib().tcx_sm100_matmul(
         _stream(), _ptr(lhs), _ptr(rhs), _ptr(out), p.m, p.n, p.k, batches,
-        i64_array(p.batch_shape), i64_array(p.lhs_batch_strides), i64_array(p.rhs_batch_strides),
-        len(p.batch_shape), _ptr(bias), ACT[act], MATMUL_PATH[path], ws, ws_bytes))
+        shape_a, lstr_a, rstr_a, len(p.batch_shape), _ptr(bias), ACT[act], MATMUL_PATH[path], ws, ws_bytes))
     del keep
     return out
 

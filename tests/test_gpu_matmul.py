@@ -237,6 +237,27 @@ def test_stream_k_tiles(tcx, oracle, lhs, rhs, act):
     np.testing.assert_array_equal(host(tcx.matmul(ad, bd, bias=biasd, act=act, path="tensor")), got)
 
 
+def test_stream_k_shape_with_nan_takes_ieee_path(tcx, oracle):
+    """A NaN in an operand of a stream-K-eligible product: the pre-pass raises the flag,
+    the pair kernel does no work (no partials, no counters) and the IEEE kernel behind
+    it computes the product; rows of both wave kinds against the oracle. The next call,
+    with the NaN replaced, runs stream-K again (its flag and counters reset per call)."""
+    rng = np.random.default_rng(21)
+    a = rng.uniform(-1, 1, (4096, 1024)).astype(np.float32)
+    b = rng.uniform(-1, 1, (1024, 4096)).astype(np.float32)
+    a[4000, 5] = np.nan
+    got = host(tcx.matmul(dev(a), dev(b)))
+    for rows in (slice(0, 64), slice(3990, 4010)):
+        expected = oracle.matmul(a, b, rows=rows, batches=[0])[0]
+        np.testing.assert_array_equal(np.isnan(got[rows]), np.isnan(expected))
+        fin = np.isfinite(expected)
+        np.testing.assert_allclose(got[rows][fin], expected[fin], rtol=1e-4, atol=1e-4)
+    a[4000, 5] = 0.5
+    got = host(tcx.matmul(dev(a), dev(b)))
+    rows = slice(4096 - 300, 4096)
+    frob_ok(got[rows], oracle.matmul(a, b, rows=rows, batches=[0])[0], 1024)
+
+
 def test_cta_pair_epilogue_and_linear(tcx, oracle):
     rng = np.random.default_rng(12)
     a = rng.uniform(-1, 1, (4, 520, 384)).astype(np.float32)

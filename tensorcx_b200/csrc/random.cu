@@ -25,8 +25,10 @@
 //
 // The kernel is bound by instruction issue (Philox-10 is ~40 integer instructions per
 // four values), not by the 4 bytes written per value: the round keys are computed once
-// per thread, the full blocks of an aligned output take a loop without bounds tests
-// (one 128-bit streaming store each), and the ragged ends another.
+// per thread, each round's two products are 32 x 32 -> 64-bit multiplies (high and low
+// halves from one product), the full blocks of an aligned output take a loop without
+// bounds tests, two blocks per iteration (one 128-bit streaming store each), and the
+// ragged ends another.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -57,8 +59,9 @@ __device__ __forceinline__ RoundKeys round_keys(uint2 k) {
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, const RoundKeys& rk) {
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t hi0 = __umulhi(kPhiloxM0, c.x), lo0 = kPhiloxM0 * c.x;
-    const uint32_t hi1 = __umulhi(kPhiloxM1, c.z), lo1 = kPhiloxM1 * c.z;
+    const uint64_t p0 = static_cast<uint64_t>(kPhiloxM0) * c.x, p1 = static_cast<uint64_t>(kPhiloxM1) * c.z;
+    const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
+    const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
     c = make_uint4(hi1 ^ c.y ^ rk.x[r], lo1, hi0 ^ c.w ^ rk.y[r], lo0);
   }
   return c;
@@ -130,7 +133,15 @@ random_kernel(float* __restrict__ out, int64_t count, uint64_t offset, uint2 key
   if constexpr (ALIGNED) {
     const uint64_t full = static_cast<uint64_t>(count) >> 2;
     float4* out4 = reinterpret_cast<float4*>(out);
-    for (uint64_t i = tid; i < full; i += stride) __stcs(out4 + i, block_values<NORMAL>(block_words(first_block + i, rk), a, b));
+    // two blocks per iteration (independent instruction streams); the second is computed
+    // past the end on the last iteration and not stored
+    for (uint64_t i = tid; i < full; i += 2 * stride) {
+      const uint64_t j = i + stride;
+      const float4 v0 = block_values<NORMAL>(block_words(first_block + i, rk), a, b);
+      const float4 v1 = block_values<NORMAL>(block_words(first_block + j, rk), a, b);
+      __stcs(out4 + i, v0);
+      if (j < full) __stcs(out4 + j, v1);
+    }
     const int rest = static_cast<int>(count & 3);
     if (rest && tid == 0) {
       const float4 v = block_values<NORMAL>(block_words(first_block + full, rk), a, b);

@@ -636,12 +636,14 @@ flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 // The leader's S and P·V issuers drive both SMs: every instruction does twice the work
 // of the single-SM kernel's, and a K stage holds two 32-feature chunks, so one barrier
 // wait covers 24 MMAs instead of 12. The leader's commits arrive on both CTAs' barriers
-// (one commit per CTA, no multicast), and both CTAs' softmax warps arrive on the
-// leader's P-ready and O-free barriers. Softmax, rescaling and the bounded waits are the
-// single-SM kernel's.
+// (one commit per CTA, no multicast), both CTAs' softmax warps arrive on the leader's
+// P-ready barriers and both CTAs' converter warps on its O-free barrier. Softmax,
+// rescaling and the bounded waits are the single-SM kernel's; the item epilogue is not:
+// the softmax warps hand each row's 1 / sum over shared memory and go on to the next
+// item, and the converter warps drain, normalize and store O.
 //   warp 0      TMA producer (Q and V on this CTA's barriers, K on the leader's)
 //   warp 1      S issuer (leader)          warp 6      P·V issuer (leader)
-//   warps 2-5   softmax and epilogue       warps 7-10  lo-term converters
+//   warps 2-5   softmax                    warps 7-10  lo-term converters, item epilogue
 //   warp 11     non-finite scan
 constexpr int kPQ = 2 * kFQ;                   // queries per pair item
 constexpr int kPKeys = kFK / 2;                // keys of a block per CTA (32)
@@ -655,7 +657,7 @@ constexpr int kPVHalf = 2 * (kMaxDv / 64) * kPVTile;  // 16 KB: a block's hi (or
 constexpr int kPVStage = 2 * kPVHalf;          // 32 KB: hi tiles, then lo tiles
 constexpr int kPairThreads = 384;
 constexpr int kConvWarp0 = 7, kScanWarp = 11;
-constexpr int kPairSmem = kQBytes + kPKStages * kPKStage + kPVStages * kPVStage + 1024 + 512;
+constexpr int kPairSmem = kQBytes + kPKStages * kPKStage + kPVStages * kPVStage + 1024 + 512 + 1024;
 static_assert(kPairSmem <= 232448, "shared memory per CTA");
 
 __device__ __forceinline__ void mma_tf32_pair_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
@@ -745,8 +747,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   uint64_t* q_empty = q_ready + 1;
   uint64_t* o_free = q_empty + 1;                // (the leader's: 8 softmax warps)
   uint64_t* drain = o_free + 1;                  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  uint64_t* l_ready = drain + 2;                 // [2] an item's row inverses written (4 softmax warps)
+  uint64_t* inv_free = l_ready + 2;              // [2] ... and read by the converters (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(inv_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* row_inv = reinterpret_cast<float*>(bars) + 128;  // [2][kFQ], past the 512-byte barrier area
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -772,6 +777,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     mbar_init(smem_u32(o_free), 8);
     mbar_init(smem_u32(&drain[0]), 1);
     mbar_init(smem_u32(&drain[1]), 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&l_ready[i]), 4); mbar_init(smem_u32(&inv_free[i]), 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -971,7 +977,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int row_in_tile = quarter * 32 + lane;
-    int64_t g = 0;
+    int64_t g = 0, sitem = 0;
     for (int64_t r = 0; r * ncl < items; ++r) {
       const int64_t w = snake_item_pair(r, items, cid, ncl);
       if (w < 0) continue;
@@ -1072,60 +1078,97 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(&p_full[buf]), 0));
       }
       if (aborted) break;
-      const int64_t gl = g - 1;
-      if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err,
-                        0x4a2))
+      // Hand the row's 1 / sum to the converter warps, which drain, normalize and store O
+      // once the item's last P·V has completed; the softmax moves on to the next item.
+      const int ib = static_cast<int>(sitem & 1);
+      if (sitem >= 2 && !wait_bounded(smem_u32(&inv_free[ib]), static_cast<uint32_t>(((sitem >> 1) - 1) & 1),
+                                      abort_flag, a.err, 0x4a2))
         break;
-      tc_fence_after();
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      float* orow = a.out + (b * a.L + query) * a.dv;
-      const int nch = a.dv / 32;
-      uint32_t o0[32], o1[32];
-      TCX_LD32(o0, tmem + lane_base + kColO);
-#pragma unroll
-      for (int ci = 0; ci < kMaxDv / 32; ++ci) {
-        if (ci >= nch) break;
-        uint32_t (&cur)[32] = (ci & 1) ? o1 : o0;
-        uint32_t (&nxt)[32] = (ci & 1) ? o0 : o1;
-        TCX_WAIT_LD32(cur);
-        if (ci + 1 < nch) TCX_LD32(nxt, tmem + lane_base + kColO + static_cast<uint32_t>((ci + 1) * 32));
-        if (row_ok) {
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(cur[e]), inv);
-          float* dst = orow + ci * 32;
-          if (a.vec8) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 8)
-              st_global_v8(dst + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-          }
-        }
-      }
-      tc_fence_before();
+      row_inv[ib * kFQ + row_in_tile] = l > 0.0f ? 1.0f / l : 0.0f;
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(o_free), 0));
+      if (lane == 0) mbar_arrive(smem_u32(&l_ready[ib]));
+      ++sitem;
     }
   } else if (warp >= kConvWarp0 && warp < kScanWarp) {
     // ------------------------------------------------ lo-term converters (both CTAs)
-    // The producer's Q and V fills in its order (K's lo terms come from the pre-pass).
+    // The producer's Q and V fills in its order (K's lo terms come from the pre-pass),
+    // and the output: after converting item i's Q, these warps drain item i - 1's O
+    // (its last P·V done, its row inverses handed over by the softmax warps), release
+    // the accumulator to the next item's P·V and store the rows; then item i's V.
     const int t = static_cast<int>(threadIdx.x) - kConvWarp0 * 32;
-    int64_t vf = 0, local = 0;
+    const int quarter = warp & 3;  // the TMEM lane quarter this warp may read
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int row_in_tile = quarter * 32 + lane;
+    int64_t vf = 0, local = 0, g_end = 0;
     uint32_t bad = 0;
     bool ok = true;
+    int64_t pb = 0;
+    int pqt = 0;
+    // O of item `it` (batch b, query tile qt), whose last key block is the g-th of this
+    // cluster's blocks (counted from 1)
+    auto drain_o = [&](int64_t it, int64_t b, int qt, int64_t gl) {
+      if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err,
+                        0x4b4))
+        return false;
+      const int ib = static_cast<int>(it & 1);
+      if (!wait_bounded(smem_u32(&l_ready[ib]), static_cast<uint32_t>((it >> 1) & 1), abort_flag, a.err, 0x4b5))
+        return false;
+      tc_fence_after();
+      const float inv = row_inv[ib * kFQ + row_in_tile];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&inv_free[ib]));
+      const int64_t query = static_cast<int64_t>(qt) * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile;
+      const bool row_ok = query < a.L;
+      float* orow = a.out + (b * a.L + query) * a.dv;
+      const int nch = a.dv / 32;
+      // two 32-column chunks at a time (registers): the accumulator is released after the
+      // last pair's TMEM load, before its stores
+      auto store_chunk = [&](const uint32_t (&oc)[32], int ci) {
+        if (!row_ok) return;
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__uint_as_float(oc[e]), inv);
+        float* dst = orow + ci * 32;
+        if (a.vec8) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8)
+            st_global_v8(dst + e, v[e], v[e + 1], v[e + 2], v[e + 3], v[e + 4], v[e + 5], v[e + 6], v[e + 7]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        }
+      };
+      for (int c0 = 0; c0 < nch; c0 += 2) {
+        const bool two = c0 + 1 < nch;
+        uint32_t o0[32], o1[32];
+        TCX_LD32(o0, tmem + lane_base + kColO + static_cast<uint32_t>(c0 * 32));
+        if (two) TCX_LD32(o1, tmem + lane_base + kColO + static_cast<uint32_t>((c0 + 1) * 32));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        TCX_TIE32(o0);
+        TCX_TIE32(o1);
+        if (c0 + 2 >= nch) {
+          // every TMEM read of O is done: the next item's first P·V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_rank(smem_u32(o_free), 0));
+        }
+        store_chunk(o0, c0);
+        if (two) store_chunk(o1, c0 + 1);
+      }
+      return true;
+    };
     for (int64_t r = 0; r * ncl < items && ok; ++r) {
       const int64_t w = snake_item_pair(r, items, cid, ncl);
       if (w < 0) continue;
       int64_t b; int qt, nkb;
       item_coords_pair(a, w, b, qt, nkb);
       if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x4b0)) break;
-      ++local;
       for (int c = 0; c < dchunks; ++c)
         write_lo(smem_u32(q_res + (2 * c) * kQTile), smem_u32(q_res + (2 * c + 1) * kQTile), kQTile, t, bad);
       publish_lo(smem_u32(q_ready), lane);
+      if (local > 0 && !(ok = drain_o(local - 1, pb, pqt, g_end - 1))) break;
+      ++local;
       auto conv_v = [&]() {
         const int s = static_cast<int>(vf % kPVStages);
         const uint32_t ph = static_cast<uint32_t>((vf / kPVStages) & 1);
@@ -1137,7 +1180,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         return true;
       };
       for (int j = 0; j < nkb && ok; ++j) ok = conv_v();
+      g_end += nkb;
+      pb = b;
+      pqt = qt;
     }
+    if (ok && local > 0) drain_o(local - 1, pb, pqt, g_end - 1);
     // every tile this CTA loaded was checked on the way: Q whole, V up to the last key
     // any item reaches (the pre-pass checked all of K)
     if (__any_sync(0xffffffffu, bad != 0) && lane == 0) atomicExch(a.flag, 1);

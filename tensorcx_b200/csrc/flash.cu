@@ -1393,7 +1393,10 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   // whole 32-column V chunks per CTA (Dv 64 or 128). Measured on [32, 2048, 2048, 128]
   // with the split pre-pass: 0.487 against 0.512 ms per call without a mask, 0.302
   // against 0.306 causal; with a float mask the pair is slower (0.674 against 0.636 ms
-  // kernel), its two SMs' softmax warps both gating every P·V.
+  // kernel), its two SMs' softmax warps both gating every P·V. Measured again with the
+  // pair reading q, k, v in place (no split pre-pass): masked calls 0.610 against 0.577 ms
+  // (float mask) and 0.531 against 0.487 ms (bool mask), so masks keep the single-SM
+  // kernel.
   auto aligned16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool pair = L > kFQ && mask_kind == 0 && dv % 64 == 0 && aligned16(q) && aligned16(k) && aligned16(v);
   if (pair) {

@@ -465,7 +465,8 @@ size_t tcx_sm100_attention_workspace_bytes(int64_t batches, int64_t queries, int
                                            int64_t v_batches, int32_t mask_kind) {
   if (batches < 0 || queries < 0 || keys < 0 || features < 0 || value_features < 0) return 0;
   if (flash_eligible(queries, keys, features, value_features, mask_kind, 0))
-    return flash_workspace_bytes(queries, keys, features, value_features, q_batches, k_batches, v_batches);
+    return flash_workspace_bytes(queries, keys, features, value_features, q_batches, k_batches, v_batches, batches,
+                                 mask_kind);
   const size_t scores = round_up(static_cast<size_t>(batches) * queries * keys * sizeof(float), 1024);
   const size_t g1 = tcx_sm100_matmul_workspace_bytes(queries, keys, features, q_batches, k_batches, TCX_MATMUL_AUTO);
   const size_t g2 = tcx_sm100_matmul_workspace_bytes(queries, value_features, keys, batches, v_batches,
@@ -514,7 +515,7 @@ int tcx_sm100_attention(tcx_stream_t stream, const float* q, const float* k, con
   }
   if (flash_eligible(queries, keys, features, value_features, mask_kind, batch_rank) &&
       reinterpret_cast<uintptr_t>(output) % 16 == 0) {
-    const size_t need = flash_workspace_bytes(queries, keys, features, value_features, qn, kn, vn);
+    const size_t need = flash_workspace_bytes(queries, keys, features, value_features, qn, kn, vn, batches, mask_kind);
     if (!workspace || workspace_bytes < need) return invalid("attention workspace is missing or too small");
     if (reinterpret_cast<uintptr_t>(workspace) % 1024) return invalid("attention workspace must be 1024-byte aligned");
     return attention_fused(s, q, k, v, mask, mask_kind, mask_strides, output, queries, keys, features,

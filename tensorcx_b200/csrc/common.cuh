@@ -156,7 +156,8 @@ void split_lo_planes(cudaStream_t s, const float* x, float* lo, int64_t n4, int*
 bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t value_features, int mask_kind,
                     int batch_rank);
 size_t flash_workspace_bytes(int64_t queries, int64_t keys, int64_t features, int64_t value_features,
-                             int64_t q_batches, int64_t k_batches, int64_t v_batches);
+                             int64_t q_batches, int64_t k_batches, int64_t v_batches, int64_t batches,
+                             int mask_kind);
 int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, const void* mask,
                     int mask_kind, const int64_t* mask_strides, float* out, int64_t L, int64_t S, int64_t d,
                     int64_t dv, int64_t batches, const int64_t* batch_shape, const int64_t* q_strides,

@@ -112,6 +112,15 @@ struct FlashArgs {
   int64_t v_planes;
   int64_t tail_row;
   int* flag;
+  // the CTA-pair kernel's work units: items whole (kv_split == 0) or cut into units of
+  // kv_split key blocks (when there are too few items for the SM pairs); a unit that is
+  // not a whole item leaves its unnormalized O rows in part_o [units][256][dv] and each
+  // row's reference maximum (log2 domain) and sum in part_ml [units][256][2], combined
+  // by flash_combine_kernel
+  int32_t kv_split;
+  int64_t units;
+  float* part_o;
+  float* part_ml;
 };
 
 __device__ __forceinline__ void batch_planes(const FlashArgs& a, int64_t b, int64_t& pq, int64_t& pk, int64_t& pv) {
@@ -686,6 +695,38 @@ __device__ __forceinline__ void item_coords_pair(const FlashArgs& a, int64_t w, 
   nkb = a.causal ? min(a.kv_blocks, (qt + 1) * (kPQ / kFK)) : a.kv_blocks;
 }
 
+// Key blocks of an item of query tile qt (256 queries): all, or up to the causal diagonal.
+__device__ __forceinline__ int item_blocks_pair(const FlashArgs& a, int qt) {
+  return a.causal ? min(a.kv_blocks, (qt + 1) * (kPQ / kFK)) : a.kv_blocks;
+}
+
+// Work unit u of the pair kernel: key blocks [j0, j1) of the item (batch b, query tile qt)
+// of nkb blocks. Units follow the item order (longest query tiles first); an item's units
+// are consecutive.
+__device__ __forceinline__ void unit_coords_pair(const FlashArgs& a, int64_t u, int64_t& b, int& qt, int& j0,
+                                                 int& j1, int& nkb) {
+  if (a.kv_split == 0) {
+    item_coords_pair(a, u, b, qt, nkb);
+    j0 = 0;
+    j1 = nkb;
+    return;
+  }
+  int64_t rest = u;
+  for (int r = 0; r < a.q_tiles; ++r) {
+    qt = a.q_tiles - 1 - r;
+    nkb = item_blocks_pair(a, qt);
+    const int per = (nkb + a.kv_split - 1) / a.kv_split;
+    const int64_t group = a.batches * per;
+    if (rest < group || r == a.q_tiles - 1) {
+      b = rest / per;
+      j0 = static_cast<int>(rest % per) * a.kv_split;
+      j1 = min(nkb, j0 + a.kv_split);
+      return;
+    }
+    rest -= group;
+  }
+}
+
 // The lo term of a float32 word x: x - trunc_tf32(x) (exact), rounded to tf32 (to
 // nearest, ties away from zero, as cvt.rna.tf32.f32) by adding half a tf32 ulp to the
 // magnitude bits and dropping the low 13.
@@ -793,7 +834,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int64_t items = a.batches * a.q_tiles;
+  const int64_t items = a.units;  // work units: items, or key ranges of items (kv_split)
   const int64_t cid = cluster_index(), ncl = cluster_count();
 
   if (warp == 0) {
@@ -804,8 +845,8 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       for (int64_t r = 0; r * ncl < items && ok; ++r) {
         const int64_t w = snake_item_pair(r, items, cid, ncl);
         if (w < 0) continue;
-        int64_t b; int qt, nkb;
-        item_coords_pair(a, w, b, qt, nkb);
+        int64_t b; int qt, j0, j1, nkb;
+        unit_coords_pair(a, w, b, qt, j0, j1, nkb);
         int64_t pq, pk, pv;
         batch_planes(a, b, pq, pk, pv);
         if (!wait_bounded(smem_u32(q_empty), static_cast<uint32_t>(local & 1) ^ 1u, abort_flag, a.err, 0x480)) break;
@@ -853,11 +894,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
                           static_cast<int>(pv));
           return true;
         };
-        for (int j = 0; j < nkb && ok; ++j) {
+        for (int j = j0; j < j1 && ok; ++j) {
           ok = load_k(j);
-          if (ok && j >= 1) ok = load_v(j - 1);
+          if (ok && j > j0) ok = load_v(j - 1);
         }
-        if (ok && nkb >= 1) ok = load_v(nkb - 1);
+        if (ok && j1 > j0) ok = load_v(j1 - 1);
       }
       if (!ok || *abort_flag) {  // Q and V fills land on this CTA's barriers, K on the leader's
         auto settle = [&](uint64_t* full, int stages, int64_t n, int site) {
@@ -883,12 +924,12 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       for (int64_t r = 0; r * ncl < items && ok; ++r) {
         const int64_t w = snake_item_pair(r, items, cid, ncl);
         if (w < 0) continue;
-        int64_t b; int qt, nkb;
-        item_coords_pair(a, w, b, qt, nkb);
+        int64_t b; int qt, j0, j1, nkb;
+        unit_coords_pair(a, w, b, qt, j0, j1, nkb);
         if (!wait_bounded(smem_u32(q_ready), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x490)) break;
         ++local;
         tc_fence_after();
-        for (int j = 0; j < nkb && ok; ++j, ++g) {
+        for (int j = j0; j < j1 && ok; ++j, ++g) {
           const int buf = static_cast<int>(g % kSBufs);
           if (g >= kSBufs) {
             if (!wait_bounded(smem_u32(&pv_done[buf]), static_cast<uint32_t>(((g - kSBufs) / kSBufs) & 1), abort_flag,
@@ -919,7 +960,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
           }
           if (!ok) break;
           commit_both(smem_u32(&s_full[buf]));
-          if (j == nkb - 1) commit_both(smem_u32(q_empty));
+          if (j == j1 - 1) commit_both(smem_u32(q_empty));
         }
       }
     }
@@ -933,16 +974,16 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       for (int64_t r = 0; r * ncl < items && ok; ++r) {
         const int64_t w = snake_item_pair(r, items, cid, ncl);
         if (w < 0) continue;
-        int64_t b; int qt, nkb;
-        item_coords_pair(a, w, b, qt, nkb);
+        int64_t b; int qt, j0, j1, nkb;
+        unit_coords_pair(a, w, b, qt, j0, j1, nkb);
         const int64_t item = local++;
-        for (int j = 0; j < nkb && ok; ++j, ++g) {
+        for (int j = j0; j < j1 && ok; ++j, ++g) {
           const int buf = static_cast<int>(g % kSBufs);
           if (!wait_bounded(smem_u32(&p_full[buf]), static_cast<uint32_t>((g / kSBufs) & 1), abort_flag, a.err, 0x494)) {
             ok = false;
             break;
           }
-          if (j == 0 && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x491)) {
+          if (j == j0 && !wait_bounded(smem_u32(o_free), static_cast<uint32_t>(item & 1) ^ 1u, abort_flag, a.err, 0x491)) {
             ok = false;
             break;
           }
@@ -960,7 +1001,7 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
               const uint64_t dv_hi = smem_desc_sw128_mn(v_hi + off, kPVTile);
               const uint64_t dv_lo = smem_desc_sw128_mn(v_lo + off, kPVTile);
               const uint32_t col = static_cast<uint32_t>(t * 8);
-              const uint32_t acc = (j == 0 && t == 0) ? 0u : 1u;
+              const uint32_t acc = (j == j0 && t == 0) ? 0u : 1u;
               mma_tf32_pair_ta(d_o, p_lo + col, dv_hi, id_o, acc);
               mma_tf32_pair_ta(d_o, p_hi + col, dv_lo, id_o, 1u);
               mma_tf32_pair_ta(d_o, p_hi + col, dv_hi, id_o, 1u);
@@ -981,14 +1022,14 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     for (int64_t r = 0; r * ncl < items; ++r) {
       const int64_t w = snake_item_pair(r, items, cid, ncl);
       if (w < 0) continue;
-      int64_t b; int qt, nkb;
-      item_coords_pair(a, w, b, qt, nkb);
+      int64_t b; int qt, j0, j1, nkb;
+      unit_coords_pair(a, w, b, qt, j0, j1, nkb);
       const int64_t query = static_cast<int64_t>(qt) * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile;
       const bool row_ok = query < a.L;
       const int64_t mrow = MK ? mask_offset(a, b) + (row_ok ? query : 0) * a.mq : 0;
       float m_use = -INFINITY, l = 0.0f;
       bool aborted = false;
-      for (int j = 0; j < nkb; ++j, ++g) {
+      for (int j = j0; j < j1; ++j, ++g) {
         const int buf = static_cast<int>(g % kSBufs);
         const uint32_t col_s = static_cast<uint32_t>(buf * 128), col_lo = col_s + kFK;
         const int64_t key0 = static_cast<int64_t>(j) * kFK;
@@ -1027,11 +1068,11 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         const bool need = mx > m_use + 8.0f;
         float alpha = 1.0f;
         if (need) {
-          alpha = j == 0 ? 0.0f : exp2f(m_use - mx);
+          alpha = j == j0 ? 0.0f : exp2f(m_use - mx);
           m_use = mx;
         }
         l = __fmul_rn(l, alpha);
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (j > j0 && __any_sync(0xffffffffu, need)) {
           const int64_t gp = g - 1;
           if (!wait_bounded(smem_u32(&pv_done[gp % kSBufs]), static_cast<uint32_t>((gp / kSBufs) & 1), abort_flag, a.err,
                             0x4a3)) {
@@ -1084,7 +1125,14 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       if (sitem >= 2 && !wait_bounded(smem_u32(&inv_free[ib]), static_cast<uint32_t>(((sitem >> 1) - 1) & 1),
                                       abort_flag, a.err, 0x4a2))
         break;
-      row_inv[ib * kFQ + row_in_tile] = l > 0.0f ? 1.0f / l : 0.0f;
+      if (j0 == 0 && j1 == nkb) {
+        row_inv[ib * kFQ + row_in_tile] = l > 0.0f ? 1.0f / l : 0.0f;
+      } else {  // a key range of the item: O stays unnormalized, the row's statistics go out
+        row_inv[ib * kFQ + row_in_tile] = 1.0f;
+        float* ml = a.part_ml + (w * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile) * 2;
+        ml[0] = m_use;
+        ml[1] = l;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&l_ready[ib]));
       ++sitem;
@@ -1102,11 +1150,13 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     int64_t vf = 0, local = 0, g_end = 0;
     uint32_t bad = 0;
     bool ok = true;
-    int64_t pb = 0;
+    int64_t pb = 0, pw = 0;
     int pqt = 0;
-    // O of item `it` (batch b, query tile qt), whose last key block is the g-th of this
-    // cluster's blocks (counted from 1)
-    auto drain_o = [&](int64_t it, int64_t b, int qt, int64_t gl) {
+    bool pwhole = true;
+    // O of this CTA's `it`-th unit (unit index uw: batch b, query tile qt; whole: the
+    // item's every key block, else a key range whose O goes to part_o), whose last key
+    // block is block gl of this cluster's sequence
+    auto drain_o = [&](int64_t it, int64_t uw, bool whole, int64_t b, int qt, int64_t gl) {
       if (!wait_bounded(smem_u32(&pv_done[gl % kSBufs]), static_cast<uint32_t>((gl / kSBufs) & 1), abort_flag, a.err,
                         0x4b4))
         return false;
@@ -1119,7 +1169,8 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       if (lane == 0) mbar_arrive(smem_u32(&inv_free[ib]));
       const int64_t query = static_cast<int64_t>(qt) * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile;
       const bool row_ok = query < a.L;
-      float* orow = a.out + (b * a.L + query) * a.dv;
+      float* orow = whole ? a.out + (b * a.L + query) * a.dv
+                          : a.part_o + (uw * kPQ + static_cast<int64_t>(rank) * kFQ + row_in_tile) * a.dv;
       const int nch = a.dv / 32;
       // two 32-column chunks at a time (registers): the accumulator is released after the
       // last pair's TMEM load, before its stores
@@ -1161,13 +1212,13 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     for (int64_t r = 0; r * ncl < items && ok; ++r) {
       const int64_t w = snake_item_pair(r, items, cid, ncl);
       if (w < 0) continue;
-      int64_t b; int qt, nkb;
-      item_coords_pair(a, w, b, qt, nkb);
+      int64_t b; int qt, j0, j1, nkb;
+      unit_coords_pair(a, w, b, qt, j0, j1, nkb);
       if (!wait_bounded(smem_u32(q_full), static_cast<uint32_t>(local & 1), abort_flag, a.err, 0x4b0)) break;
       for (int c = 0; c < dchunks; ++c)
         write_lo(smem_u32(q_res + (2 * c) * kQTile), smem_u32(q_res + (2 * c + 1) * kQTile), kQTile, t, bad);
       publish_lo(smem_u32(q_ready), lane);
-      if (local > 0 && !(ok = drain_o(local - 1, pb, pqt, g_end - 1))) break;
+      if (local > 0 && !(ok = drain_o(local - 1, pw, pwhole, pb, pqt, g_end - 1))) break;
       ++local;
       auto conv_v = [&]() {
         const int s = static_cast<int>(vf % kPVStages);
@@ -1179,12 +1230,14 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         publish_lo(smem_u32(&v_ready[s]), lane);
         return true;
       };
-      for (int j = 0; j < nkb && ok; ++j) ok = conv_v();
-      g_end += nkb;
+      for (int j = j0; j < j1 && ok; ++j) ok = conv_v();
+      g_end += j1 - j0;
       pb = b;
       pqt = qt;
+      pw = w;
+      pwhole = j0 == 0 && j1 == nkb;
     }
-    if (ok && local > 0) drain_o(local - 1, pb, pqt, g_end - 1);
+    if (ok && local > 0) drain_o(local - 1, pw, pwhole, pb, pqt, g_end - 1);
     // every tile this CTA loaded was checked on the way: Q whole, V up to the last key
     // any item reaches (the pre-pass checked all of K)
     if (__any_sync(0xffffffffu, bad != 0) && lane == 0) atomicExch(a.flag, 1);
@@ -1223,6 +1276,54 @@ flash_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
   cluster_sync_all();  // neither CTA leaves while the other may still touch its barriers
+}
+
+// Combines the units of the items the pair kernel cut into key ranges (kv_split): per
+// row, O = (sum_u 2^(m_u - M) O_u) / (sum_u 2^(m_u - M) l_u) with M the largest m_u
+// (log2 domain; a unit with no key for the row has m_u = -inf and weight 0). One warp per
+// row, launched behind the pair kernel (programmatic dependent: waits for its grid).
+constexpr int kCombineThreads = 256;
+
+__global__ void __launch_bounds__(kCombineThreads) flash_combine_kernel(const FlashArgs a) {
+  wait_for_prior_grid();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCombineThreads / 32);
+  const int64_t jobs = a.batches * a.q_tiles * kPQ;
+  for (int64_t job = static_cast<int64_t>(blockIdx.x) * (kCombineThreads / 32) + (threadIdx.x >> 5); job < jobs;
+       job += warps) {
+    const int64_t item = job / kPQ;
+    const int row = static_cast<int>(job % kPQ);
+    const int r = static_cast<int>(item / a.batches);
+    const int64_t b = item % a.batches;
+    const int qt = a.q_tiles - 1 - r;
+    const int per = (item_blocks_pair(a, qt) + a.kv_split - 1) / a.kv_split;
+    const int64_t query = static_cast<int64_t>(qt) * kPQ + row;
+    if (per == 1 || query >= a.L) continue;  // whole items were written by the pair kernel
+    int64_t u0 = b * per;  // the item's first unit: all units of the longer groups first
+    for (int rr = 0; rr < r; ++rr)
+      u0 += a.batches * ((item_blocks_pair(a, a.q_tiles - 1 - rr) + a.kv_split - 1) / a.kv_split);
+    float mx = -INFINITY;
+    for (int u = 0; u < per; ++u) mx = fmaxf(mx, __ldcg(a.part_ml + ((u0 + u) * kPQ + row) * 2));
+    float den = 0.0f, acc[kMaxDv / 32];
+#pragma unroll
+    for (int c = 0; c < kMaxDv / 32; ++c) acc[c] = 0.0f;
+    for (int u = 0; u < per; ++u) {
+      const float* ml = a.part_ml + ((u0 + u) * kPQ + row) * 2;
+      const float mu = __ldcg(ml);
+      const float wgt = mu == -INFINITY ? 0.0f : exp2f(__fsub_rn(mu, mx));
+      den = __fmaf_rn(wgt, __ldcg(ml + 1), den);
+      const float* o = a.part_o + ((u0 + u) * kPQ + row) * a.dv;
+#pragma unroll
+      for (int c = 0; c < kMaxDv / 32; ++c)
+        if (32 * c + lane < a.dv) acc[c] = __fmaf_rn(wgt, __ldcg(o + 32 * c + lane), acc[c]);
+    }
+    const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+    float* out = a.out + (b * a.L + query) * a.dv;
+#pragma unroll
+    for (int c = 0; c < kMaxDv / 32; ++c)
+      if (32 * c + lane < a.dv) out[32 * c + lane] = __fmul_rn(acc[c], inv);
+  }
+  dependents_may_launch();
 }
 
 // IEEE fallback, used only when the pre-pass or the pair kernel's scan saw inf / NaN
@@ -1318,18 +1419,28 @@ __global__ void __launch_bounds__(256) mask_scan(const float* __restrict__ m, in
 size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
 struct FlashLayout {
-  size_t off_flag, off_q, off_k, off_v, total;
+  size_t off_flag, off_q, off_k, off_v, off_po, off_pml, total;
   int64_t sp;
+  int64_t part_units;  // key-range units the partial areas hold (0: no split possible)
 };
 
-FlashLayout flash_layout(int64_t L, int64_t S, int64_t d, int64_t dv, int64_t nq, int64_t nk, int64_t nv) {
+// Unmasked products that may run on CTA pairs with fewer items (256 queries of one batch)
+// than twice the SM pairs get room for key-range units: at most two per SM pair beyond
+// one per item (the split keeps units >= total key blocks / (2 x pairs) blocks long).
+FlashLayout flash_layout(int64_t L, int64_t S, int64_t d, int64_t dv, int64_t nq, int64_t nk, int64_t nv,
+                         int64_t batches, int mask_kind) {
   FlashLayout f;
   f.sp = (S + kFC - 1) / kFC * kFC;
   f.off_flag = 0;
   f.off_q = 1024;
   f.off_k = round_up(f.off_q + static_cast<size_t>(2 * nq * L * d) * 4, 1024);
   f.off_v = round_up(f.off_k + static_cast<size_t>(2 * nk * S * d) * 4, 1024);
-  f.total = round_up(f.off_v + static_cast<size_t>(2 * nv * dv * f.sp) * 4, 1024);
+  f.off_po = round_up(f.off_v + static_cast<size_t>(2 * nv * dv * f.sp) * 4, 1024);
+  const int64_t pairs = sm_count() / 2;
+  const int64_t items = batches * ((L + kPQ - 1) / kPQ);
+  f.part_units = (mask_kind == 0 && dv % 64 == 0 && L > kFQ && items < 2 * pairs) ? 2 * pairs + items : 0;
+  f.off_pml = round_up(f.off_po + static_cast<size_t>(f.part_units * kPQ * dv) * 4, 1024);
+  f.total = round_up(f.off_pml + static_cast<size_t>(f.part_units * kPQ * 2) * 4, 1024);
   return f;
 }
 
@@ -1343,8 +1454,10 @@ bool flash_eligible(int64_t queries, int64_t keys, int64_t features, int64_t val
 }
 
 size_t flash_workspace_bytes(int64_t queries, int64_t keys, int64_t features, int64_t value_features,
-                             int64_t q_batches, int64_t k_batches, int64_t v_batches) {
-  return flash_layout(queries, keys, features, value_features, q_batches, k_batches, v_batches).total;
+                             int64_t q_batches, int64_t k_batches, int64_t v_batches, int64_t batches,
+                             int mask_kind) {
+  return flash_layout(queries, keys, features, value_features, q_batches, k_batches, v_batches, batches, mask_kind)
+      .total;
 }
 
 int attention_fused(cudaStream_t s, const float* q, const float* k, const float* v, const void* mask,
@@ -1380,7 +1493,11 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     if (v_strides[i]) nv *= batch_shape[i];
     ++fa.rank;
   }
-  const FlashLayout lay = flash_layout(L, S, d, dv, nq, nk, nv);
+  FlashLayout lay = flash_layout(L, S, d, dv, nq, nk, nv, batches, mask_kind);
+  if (workspace && workspace_bytes < lay.total && workspace_bytes >= lay.off_po) {
+    lay.part_units = 0;  // a workspace sized without the key-range partials: no split
+    lay.total = lay.off_po;
+  }
   if (!workspace || workspace_bytes < lay.total) return invalid("attention workspace is missing or too small");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int* flag = reinterpret_cast<int*>(ws + lay.off_flag);
@@ -1457,9 +1574,42 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
   fa.tail_row = causal ? std::min<int64_t>(S, static_cast<int64_t>(fa.q_tiles) * kPQ) : S;
   fa.flag = flag;
   const int64_t items = batches * fa.q_tiles;
+  fa.kv_split = 0;
+  fa.units = items;
+  fa.part_o = fa.part_ml = nullptr;
+  if (pair && items < sms && lay.part_units > 0) {
+    // Few items for the SM pairs (heads sharded over GPUs, short sequences) and the
+    // longest item more than three times the work per SM pair: cut the items' key blocks
+    // into units of >= 4 blocks, about two per SM pair, and combine the units' partial
+    // rows afterwards. Measured on [heads, 2048, 2048, 128] (per call): causal 4 heads
+    // 118 -> 71 µs; where the longest item is not that far above the average, the units'
+    // extra transitions, partial stores and the combining pass cost more than the balance
+    // gains (8 heads full 126 -> 179 µs, 16 heads causal 132 -> 186 µs), so those stay whole.
+    int64_t total = 0;
+    int longest = 0;
+    for (int qt = 0; qt < fa.q_tiles; ++qt) {
+      const int nkb = causal ? static_cast<int>(std::min<int64_t>(fa.kv_blocks, (qt + 1) * (kPQ / kFK))) : fa.kv_blocks;
+      total += batches * nkb;
+      longest = std::max(longest, nkb);
+    }
+    const int split = static_cast<int>(std::max<int64_t>(4, ceil_div(total, sms)));
+    if (split < longest && static_cast<int64_t>(longest) * (sms / 2) > 3 * total) {
+      int64_t units = 0;
+      for (int qt = 0; qt < fa.q_tiles; ++qt) {
+        const int nkb = causal ? static_cast<int>(std::min<int64_t>(fa.kv_blocks, (qt + 1) * (kPQ / kFK))) : fa.kv_blocks;
+        units += batches * ceil_div(nkb, split);
+      }
+      if (units <= lay.part_units) {
+        fa.kv_split = split;
+        fa.units = units;
+        fa.part_o = reinterpret_cast<float*>(ws + lay.off_po);
+        fa.part_ml = reinterpret_cast<float*>(ws + lay.off_pml);
+      }
+    }
+  }
   if (pair) {
     TimedLaunch timer("flash_tf32x3", s);
-    const int clusters = static_cast<int>(std::min<int64_t>(items, sms / 2));
+    const int clusters = static_cast<int>(std::min<int64_t>(fa.units, sms / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(kPairThreads);
@@ -1481,6 +1631,13 @@ int attention_fused(cudaStream_t s, const float* q, const float* k, const float*
     else flash_tf32x3_kernel<0><<<grid, kFlashThreads, kFlashSmem, s>>>(map_q, map_k, map_v, fa);
   }
   if (int st = launch_status("fused attention")) return st;
+  if (fa.kv_split > 0) {  // merge the key-range units' rows
+    TimedLaunch timer("flash_combine", s);
+    const int64_t rows = items * kPQ;
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(rows, kCombineThreads / 32), 4LL * sms));
+    launch_after(flash_combine_kernel, grid, kCombineThreads, s, 0, fa);
+    if (int st = launch_status("attention combine")) return st;
+  }
   {
     TimedLaunch timer("flash_rows_fallback", s);
     // idle unless a non-finite input was seen: a small grid (rows in a grid-stride loop)

@@ -524,6 +524,20 @@ def test_fused_attention(tcx, oracle, lq, lk, d, dv, causal):
         attn_check(got, oracle.attention(q, k, v, None, causal))
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_attention_key_range_units(tcx, oracle, causal):
+    """Fewer 256-query items than SM pairs (2 heads x 8 query tiles): the CTA-pair kernel
+    cuts each item's key blocks into units of 4 (the last query tiles into up to eight),
+    leaves each unit's unnormalized rows with their maxima and sums, and a combining
+    kernel merges them. Every row against the reference composite; a second call is bit
+    identical."""
+    q, k, v = gauss((2, 2048, 128), 23), gauss((2, 2048, 128), 24), gauss((2, 2048, 128), 25)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    got = host(tcx.attention(qd, kd, vd, is_causal=causal))
+    attn_check(got, oracle.attention(q, k, v, None, causal))
+    np.testing.assert_array_equal(host(tcx.attention(qd, kd, vd, is_causal=causal)), got)
+
+
 @pytest.mark.parametrize("scale", [None, 0.0, -0.3, 3.0])
 def test_fused_attention_broadcast_and_scale(tcx, oracle, scale):
     q, k, v = gauss((3, 2, 100, 64), 4), gauss((1, 2, 260, 64), 5), gauss((3, 1, 260, 32), 6)

@@ -334,7 +334,9 @@ int tcx_sm100_attention_softmax(tcx_stream_t stream, const float* scores, const 
  * attention_softmax(Q·Kᵀ, mask, scale, causal) · V. Without a mask, with features and
  * value_features multiples of 32 up to 128 and a 16-byte aligned output, one fused
  * tcgen05 kernel computes it (scores and probabilities stay in TMEM; the workspace holds
- * only the 3xTF32 split planes of q, k and v); otherwise the composite below runs. Inputs
+ * only the 3xTF32 split planes of q, k and v, or k's lo terms, and for products with few
+ * 256-query items the partial rows of items cut into key ranges); otherwise the
+ * composite below runs. Inputs
  * holding inf / NaN are computed by an IEEE row kernel (decided on the device).
  * q [batch..., queries, features],
  * k [batch..., keys, features], v [batch..., keys, value_features], each batch-broadcast

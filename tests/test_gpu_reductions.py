@@ -1,6 +1,6 @@
 """GPU parity of the reduction kernels against the CPU oracle, through the C ABI.
 
-Bars (SURVEY numeric contract): int32 sum/max and every argmax/min index bit-exact;
+Bars: int32 sum/max and every argmax/min index bit-exact;
 row sum/mean/max bit-exact where the reference test demands it
 (tests/python/test_cuda_primitives.py:114-125: widths 255..65536); fp32 full-tensor
 sum/mean within 1e-5 relative of the CPU result (and reported against the exact sum).

@@ -1858,12 +1858,14 @@ struct HostPlan {
 };
 
 // Row chunks of A (and C). The PCIe uploads are the floor of the whole call; chunks
-// of 512 rows keep each chunk's GEMM (B split once) about as long as the next chunk's
+// of 256 rows keep each chunk's GEMM (B split once) about as long as the next chunk's
 // upload, and keep the tail that nothing overlaps (the last GEMM and download) short.
-// Measured at 8192^3: 512-row chunks 11.6 ms per call, 1024 rows 12.1, 2048 rows 13.3.
+// Measured at 8192^3 on one B200, the variants interleaved in one process: 256-row
+// chunks 11.02-11.31 ms per call, 512 rows 11.25-11.64, 1024 rows 11.55, 128 rows 16.1
+// (the per-chunk launches no longer hide behind the uploads).
 HostPlan host_plan(int64_t m, int64_t n, int64_t k) {
   HostPlan p;
-  p.chunk_m = m >= 2048 ? 512 : m;
+  p.chunk_m = m >= 2048 ? 256 : m;
   p.chunks = (m + p.chunk_m - 1) / p.chunk_m;
   p.kp = (k + kBK - 1) / kBK * kBK;
   p.tensor = use_tensor(p.chunk_m, n, k, TCX_MATMUL_AUTO);

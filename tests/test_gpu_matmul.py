@@ -168,13 +168,14 @@ def test_linear_fused(tcx, oracle, path, shape):
 
 
 @pytest.mark.parametrize("m,n,k", [(4096, 1024, 512), (1000, 300, 70), (5, 7, 3), (2048, 2048, 0),
-                                   (2048, 5000, 512)])
+                                   (2048, 5000, 512), (512, 9728, 256)])
 def test_matmul_host_pipeline(tcx, oracle, m, n, k):
     """Host-buffer matmul (chunked upload / GEMM / download pipeline) against the CPU
     oracle on sampled rows and against the device-buffer path (the same 3xTF32 products;
     the chunks' tiles split k differently from the whole product's when stream-K
     applies, so the two agree within the tolerance, not bit for bit); repeatable bit
-    for bit. (2048, 5000, 512): each 512-row chunk is a CTA-pair product."""
+    for bit. (2048, 5000, 512): 256-row chunks through the single-SM kernel's TMA-store
+    epilogue; (512, 9728, 256): one chunk, a CTA-pair product."""
     rng = np.random.default_rng(m + n)
     a = torch.from_numpy(rng.uniform(-1, 1, (m, k)).astype(np.float32)).pin_memory()
     b = torch.from_numpy(rng.uniform(-1, 1, (k, n)).astype(np.float32)).pin_memory()

@@ -65,6 +65,7 @@ def parse():
     p.add_argument("--path", default="auto")
     p.add_argument("--repeat", type=int, default=3)
     p.add_argument("--causal", action="store_true")
+    p.add_argument("--kernels", action="store_true", help="with --case: device time per kernel as well")
     return p.parse_args()
 
 
@@ -72,7 +73,7 @@ def run_case(a):
     """One hot-path workload called `--repeat` times on cuda:0 after one untimed call;
     prints the mean device time per call (CUDA events on the current stream).
 
-        python bench.py --case matmul --size 4096 [--path tensor|ffma] [--repeat 3]
+        python bench.py --case matmul --size 4096 [--path tensor|ffma] [--repeat 3] [--kernels]
         python bench.py --case bmm --batch 64 --size 2048
         python bench.py --case softmax|rmsnorm|layernorm --rows 16384 --cols 4096
         python bench.py --case sum|max|min|argmax|mean --n 268435456 [--int32]
@@ -131,6 +132,17 @@ def run_case(a):
     e.record()
     torch.cuda.synchronize()
     print(f"{w}: {s.elapsed_time(e) / a.repeat:.4f} ms per call")
+    if a.kernels:  # device time per kernel, the calls queued behind a device spin
+        from tensorcx_b200 import _abi
+        lib = _abi.lib()
+        step = queued(torch, fn)
+        hooks_on(lib)
+        for _ in range(a.repeat):
+            step()
+        torch.cuda.synchronize()
+        lib.tcx_sm100_timer_enable(0)
+        for name, (count, total) in read_timer(lib).items():
+            print(f"  {name}: {count} launches, {total / max(count, 1) * 1e3:.2f} us per launch")
 
 
 def dist_env():
@@ -408,6 +420,23 @@ def hooks_on(lib):
     before a timed region, after its warm-up)."""
     read_timer(lib)
     lib.tcx_sm100_timer_enable(1)
+
+
+# ~0.1 ms of device spin at the B200's clocks
+SPIN_CYCLES = 200_000
+
+
+def queued(torch, step):
+    """`step` behind a short device spin on the current stream. The timing hooks record an
+    event before and after each launch; on an idle GPU the start event completes at once
+    and the pair then also spans the host's own launch of the kernel (a few microseconds,
+    the whole duration of a small product's kernels). Behind the spin the host enqueues
+    the step's events and launches while the GPU is still busy, so each pair brackets the
+    kernel's device time."""
+    def run():
+        torch.cuda._sleep(SPIN_CYCLES)
+        step()
+    return run
 
 
 def peaks():
@@ -855,7 +884,8 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         st()
         reps = max(5, steps) if size >= 2048 else 50
         ms = timer.run(st, reps, 3, sampler) / reps  # timing hooks off: no event records per launch
-        timer.run(st, max(3, reps // 2), 1, before_timing=lambda: hooks_on(lib))
+        # per-kernel device times, with the host's launches queued ahead of the GPU
+        timer.run(queued(torch, st), max(3, reps // 2), 1, before_timing=lambda: hooks_on(lib))
         lib.tcx_sm100_timer_enable(0)
         kern = read_timer(lib)
         fl = 2.0 * size ** 3
@@ -873,7 +903,8 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
                 "ms_per_step": graph_ms, "value": world * fl / (graph_ms * 1e-3) / 1e12},
             "config": f"fp32 [{size},{size}] x [{size},{size}], U(-1,1), per-rank replica, split pre-pass + GEMM "
                       "(+ split-K reduce when the tiles fill few SMs) per step, called from Python "
-                      "(graph_replay: the same call captured as a CUDA graph)",
+                      "(graph_replay: the same call captured as a CUDA graph; kernels_ms: event pairs per "
+                      "launch with the calls queued behind a 0.1 ms device spin, i.e. device time)",
             "kernels_ms": {name: round(t / max(c, 1), 4) for name, (c, t) in kern.items()},
             "roofline": {"bound": "tensor", "achieved": fl / (k_avg * 1e-3) / 1e12 if k_avg else None,
                          "peak": peak_3x, "unit": "TFLOP/s",

@@ -745,7 +745,7 @@ def secondary(args, torch, dist, lib, ops, timer, world, rank, hbm_peak, peak_3x
         from tensorcx_b200.collective import PeerReduction
         peer = PeerReduction()
     combine = ("in the reduction kernel over NVLink peer memory" if peer else
-               "NCCL all_gather + the combine kernel" if world > 1 else "the combine kernel")
+               "by NCCL all_gather + the combine kernel" if world > 1 else "by the combine kernel")
     for name, x, op in [("sum_f32_2^28", xf, "sum"), ("mean_f32_2^28", xf, "mean"), ("max_f32_2^28", xf, "max"),
                         ("min_f32_2^28", xf, "min"), ("argmax_f32_2^28", xf, "argmax"),
                         ("sum_i32_2^28", xi, "sum"), ("max_i32_2^28", xi, "max")]:

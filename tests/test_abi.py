@@ -57,6 +57,26 @@ def test_abi_version_and_errors():
         _abi.check(_abi.INVALID_ARGUMENT)
 
 
+def test_more_entry_points_reject_bad_arguments_before_cuda():
+    """Unsupported ops, negative or empty extents and missing buffers come back as
+    TCX_INVALID_ARGUMENT with a message, before any CUDA call (this runs without a GPU)."""
+    lib = _abi.lib()
+    cases = [
+        # no-allocation full reduction: op / dtype checked first, then the count
+        (lambda: lib.tcx_sm100_reduce_all_noalloc(None, 99, 0, None, 4, None), b"op"),
+        (lambda: lib.tcx_sm100_reduce_all_noalloc(None, _abi.OP["sum"], 0, None, -1, None), b"negative"),
+        (lambda: lib.tcx_sm100_reduce_partial(None, _abi.OP["sum"], 0, None, 0, 0, None, None, 0), b"non-empty"),
+        (lambda: lib.tcx_sm100_affine_norm(None, _abi.OP["layernorm"], None, None, -1, 4, 1, 1e-5, None, None),
+         b"negative"),
+        (lambda: lib.tcx_sm100_affine_norm(None, _abi.OP["softmax"], None, None, 1, 4, 1, 1e-5, None, None),
+         b"rmsnorm"),
+        (lambda: lib.tcx_sm100_copy_to_device(None, None, None, 16), b"buffer"),
+    ]
+    for call, word in cases:
+        assert call() == _abi.INVALID_ARGUMENT
+        assert word in lib.tcx_sm100_last_error(), lib.tcx_sm100_last_error()
+
+
 def test_workspace_queries():
     lib = _abi.lib()
     assert lib.tcx_sm100_matmul_workspace_bytes(8192, 8192, 8192, 1, 1, 0) >= 4 * 4 * 8192 * 8192

@@ -99,6 +99,15 @@ def matmul(lhs: torch.Tensor, rhs: torch.Tensor, *, bias: torch.Tensor | None = 
     p, shape_a, lstr_a, rstr_a = _matmul_plan(lhs.shape, rhs.shape)
     if out is None:
         out = torch.empty(p.output_shape, dtype=torch.float32, device=lhs.device)
+    else:
+        # the kernels write every element of out and read the operands while doing so
+        _check_tensor(out, "out")
+        if out.device != lhs.device or out.dtype != torch.float32 or tuple(out.shape) != tuple(p.output_shape):
+            raise ValueError(f"out must be a float32 tensor of shape {tuple(p.output_shape)} on {lhs.device}")
+        for t in (lhs, rhs):
+            if t.numel() and out.numel() and out.data_ptr() < t.data_ptr() + t.numel() * 4 and \
+                    t.data_ptr() < out.data_ptr() + out.numel() * 4:
+                raise ValueError("out must not overlap the operands")
     if bias is not None:
         _check_tensor(bias, "bias")
         if bias.shape != (p.n,) or bias.dtype != torch.float32:

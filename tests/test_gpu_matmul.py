@@ -354,3 +354,24 @@ def test_skinny_batched_and_linear(tcx, oracle):
     w = rng.uniform(-0.05, 0.05, (20, 300)).astype(np.float32)
     bias = rng.normal(size=20).astype(np.float32)
     frob_ok(host(tcx.linear(dev(x), dev(w), dev(bias))), oracle.linear(x, w, bias), 300)
+
+
+def test_out_tensor_checked_and_filled(tcx):
+    """A caller-provided `out` receives the same result as a fresh output; an `out` of the
+    wrong shape or dtype, non-contiguous, or overlapping an operand is refused before any
+    launch."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.rand(300, 200, device="cuda", generator=g)
+    b = torch.rand(200, 260, device="cuda", generator=g)
+    want = tcx.matmul(a, b)
+    out = torch.full((300, 260), float("nan"), device="cuda")
+    got = tcx.matmul(a, b, out=out)
+    torch.cuda.synchronize()
+    assert got is out and torch.equal(out, want)
+    for bad in (torch.empty(300, 261, device="cuda"), torch.empty(300, 260, dtype=torch.float64, device="cuda"),
+                torch.empty(260, 300, device="cuda").t()):
+        with pytest.raises(ValueError):
+            tcx.matmul(a, b, out=bad)
+    sq = torch.rand(256, 256, device="cuda", generator=g)
+    with pytest.raises(ValueError):
+        tcx.matmul(sq, sq.clone(), out=sq)

@@ -42,6 +42,11 @@ def _check_tensor(t: torch.Tensor, name: str = "input") -> None:
         raise TypeError(f"{name} must be a tensor")
     if not t.is_cuda:
         raise ValueError("device mismatch: tensors must be on the CUDA device")
+    # the kernels launch on the current device's stream: a tensor of another GPU would be
+    # read there through its device address
+    if t.device.index is not None and t.device.index != torch.cuda.current_device():
+        raise ValueError(f"device mismatch: {name} is on {t.device} but the current device is "
+                         f"cuda:{torch.cuda.current_device()} (use torch.cuda.device)")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
 

@@ -375,3 +375,15 @@ def test_out_tensor_checked_and_filled(tcx):
     sq = torch.rand(256, 256, device="cuda", generator=g)
     with pytest.raises(ValueError):
         tcx.matmul(sq, sq.clone(), out=sq)
+
+
+def test_tensor_on_another_device_is_refused(tcx):
+    """Kernels launch on the current device: an operand of another GPU is an error, and
+    the same call under that device's guard runs."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    a = torch.ones(4, 4, device="cuda:1")
+    with pytest.raises(ValueError):
+        tcx.matmul(a, a)
+    with torch.cuda.device(1):
+        assert float(tcx.matmul(a, a)[0, 0].item()) == 4.0
